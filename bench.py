@@ -1,0 +1,327 @@
+#!/usr/bin/env python3
+"""Decode benchmark: batch-1 greedy decode tokens/s of the Llama-3-8B-shaped
+Q4_K model on 1..8 B200s (tensor parallel).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one greedy decode token (embedding, 32 layers, output norm, LM head,
+argmax, token advance) at context 512 + W + i.  The model is synthetic
+(seeded N(0, 0.02) weights quantised to Q4_K, Q8_0 embedding/output; there is
+no checkpoint or dataset on this path).  Every step reads the whole 4.5 GB of
+weights, far larger than the 126 MB L2, so no flush is needed between steps.
+
+Prints one JSON line on rank 0.  `value` is device-timed (CUDA events on the
+engine stream, max over ranks); `e2e` goes through the public C ABI call
+rf_decode_step with the token in pinned host memory every step; `roofline` is
+the dominant kernel (the fused gate/up + SwiGLU Q4_K GEMV) timed with events
+over every layer in turn; `cpu_baseline` is the reference's CPU path (the
+oracle port, reference threading) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "batch-1 decode tokens/s (Llama-3-8B Q4_K)"
+UNIT = "tokens/s"
+PROMPT_LEN = 512
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return ws, rank, local
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.dev), "-lms", "200"], stdout=self.tmp,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.proc or not self.tmp:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.tmp.flush()
+        rows = []
+        with open(self.tmp.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def algorithmic_bytes(spec, tp: int, ctx: float):
+    """Weight + activation bytes one decode token must move (per rank), per SURVEY 8(d):
+    matrices M*K*b (b = GGUF bytes/element), KV f16 at context ctx, vectors 4 bytes/elem."""
+    from ramforge_b200 import synth
+    bpe = {synth.Q4_K: 144 / 256, synth.Q8_0: 34 / 32, synth.Q4_0: 18 / 32}
+    d, ff, hd = spec.n_embd, spec.n_ff, spec.head_dim
+    q, kv = spec.n_heads * hd, spec.n_kv_heads * hd
+    b = bpe[spec.layer_type]
+    layer_w = (d * (q + 2 * kv) + q * d + 2 * d * ff + ff * d) * b / tp
+    lm = spec.vocab_size * d * bpe[spec.out_type] / tp
+    kv_bytes = spec.n_layers * 2 * (kv / tp) * 2 * ctx
+    gateup = 2 * (ff / tp) * d * b + 4 * d + 4 * ff / tp
+    return spec.n_layers * layer_w + lm + kv_bytes, gateup
+
+
+def make_model(spec, world, rank):
+    """GGUF image of the benchmark model: in memory for 1 rank; shared through
+    /dev/shm for several ranks (rank 0 writes, the others map it)."""
+    from ramforge_b200 import synth
+    if world == 1:
+        return synth.gguf_bytes(spec)
+    import torch.distributed as dist
+    path = f"/dev/shm/ramforge_b200_{spec.name}_s{spec.seed}.gguf"
+    if rank == 0 and not os.path.exists(path):
+        g = synth.gguf_bytes(spec)
+        tmp = path + f".tmp{os.getpid()}"
+        g.tofile(tmp)
+        os.replace(tmp, path)
+    dist.barrier()
+    return path
+
+
+def cpu_baseline(gguf, spec):
+    """Reference CPU path (oracle port): one full decode token (32 layers + LM head)
+    at position 0 with the reference's dispatch (Q4_K/Q8_0 matvecs single-threaded,
+    compute_dispatch.rs:219-254)."""
+    from oracle import oracle as orc
+    m = orc.OracleModel(gguf, kv_f16=True, max_seq=8, threads=1)
+    t0 = time.perf_counter()
+    fh = m.forward(1, 0)
+    orc.argmax(m.logits(fh))
+    dt = time.perf_counter() - t0
+    m.close()
+    return {"value": 1.0 / dt, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": "1 greedy decode token of the same model (32 layers + LM head, position 0), oracle port "
+                      "with the reference's threading (Q4_K/Q8_0 matvecs single-threaded)",
+            "seconds": dt}
+
+
+def run_reference(args, spec):
+    """--impl reference: the reference's CPU implementation (oracle port, its own
+    threading) on this workload.  A step is a bounded sample: one layer of a token
+    forward (layer i mod 32, no commit) plus 1/32 of the LM head rows, so
+    tokens/s = 1 / (32 * mean step time)."""
+    from oracle import oracle as orc
+    from ramforge_b200 import synth
+    t_gen = time.perf_counter()
+    g = synth.gguf_bytes(spec)
+    gen_s = time.perf_counter() - t_gen
+    m = orc.OracleModel(g, kv_f16=True, max_seq=8, threads=1)
+    L, V = spec.n_layers, spec.vocab_size
+    hidden = np.asarray(synth.normal(9, 9, spec.n_embd), np.float32)
+
+    def step(i):
+        layer = i % L
+        m.layer_step(layer, 0, hidden)
+        r0 = layer * V // L
+        m.logits_rows(hidden, r0, (layer + 1) * V // L)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    dt = time.perf_counter() - t0
+    per_step = dt / args.steps
+    value = 1.0 / (per_step * L)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(spec, args, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "port",
+                         "sample": "per step: one layer of a decode token (layer i mod 32) + 1/32 of the LM-head "
+                                   "rows; reference threading (Q4_K/Q8_0 single-threaded)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "model_generation_s": gen_s,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(spec, args, tp):
+    return {"workload": "llama-3-8b-shape Q4_K batch-1 greedy decode (BASELINE configs[3])",
+            "layers": spec.n_layers, "dim": spec.n_embd, "heads": f"{spec.n_heads}q/{spec.n_kv_heads}kv",
+            "ffn": spec.n_ff, "vocab": spec.vocab_size, "weights": "Q4_K layers, Q8_0 token_embd/output",
+            "kv_cache": "f16", "prompt_tokens": PROMPT_LEN, "decode_context": f"{PROMPT_LEN + args.warmup}.."
+            f"{PROMPT_LEN + args.warmup + args.steps}", "parallelism": f"tp{tp}",
+            "l2": "no flush: every step streams 4.5 GB of weights (> 126 MB L2)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_env()
+
+    from ramforge_b200 import synth
+    spec = synth.LLAMA3_8B
+
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, spec)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=600))
+    from ramforge_b200 import DecodeEngine, tp_unique_id
+
+    t0 = time.perf_counter()
+    gguf = make_model(spec, world, rank)
+    gen_s = time.perf_counter() - t0
+    nccl_id = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    e2e_steps = args.steps
+    max_seq = PROMPT_LEN + args.warmup + max(args.steps, e2e_steps) + 16
+    t0 = time.perf_counter()
+    eng = DecodeEngine(gguf, device=local, max_seq_len=max_seq, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    load_s = time.perf_counter() - t0
+    prompt = np.random.default_rng(3).integers(0, spec.vocab_size, PROMPT_LEN).tolist()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # prefill (token by token, like the reference: inference.rs:578-592) + warm-up
+    first = int(eng.generate(prompt, 1)[0])
+    toks, _ = eng.decode_timed(first, args.warmup)
+    nxt = int(toks[-1])
+    barrier()
+    with ClockSampler(local) as clk:
+        toks, dev_ms = eng.decode_timed(nxt, args.steps)
+        barrier()
+    dev_ms = max_over_ranks(dev_ms)
+    clocks = clk.summary()
+    value = args.steps / (dev_ms / 1e3)
+
+    # e2e: same positions again through rf_decode_step (pinned H2D token+pos, D2H token, sync)
+    eng.kv_reset()
+    first = int(eng.generate(prompt, 1)[0])
+    tok = first
+    for _ in range(args.warmup):
+        tok = eng.decode_step(tok)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        tok = eng.decode_step(tok)
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e = {"value": e2e_steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+           "api": "rf_decode_step (token + position in, next token out)"}
+
+    # dominant kernel: gate/up + SwiGLU GEMV, timed over every layer (weights >> L2)
+    kms = eng.bench_layer_kernels(iters=3)
+    kms = [max_over_ranks(k) for k in kms]
+    ctx_mean = PROMPT_LEN + args.warmup + args.steps / 2
+    step_bytes, gateup_bytes = algorithmic_bytes(spec, world, ctx_mean)
+    peak, peak_kind = measured_peaks()
+    achieved = gateup_bytes / (kms[3] / 1e3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "gemv_kernel<Q4_K, EpiSwiGLU> (ffn gate/up + SwiGLU)",
+                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": gateup_bytes,
+                "ms_per_launch": kms[3], "traffic": None}
+    step_gbs = step_bytes / (dev_ms / args.steps / 1e3) / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(spec, args, world), "clocks": clocks, "e2e": e2e,
+        "gpu_launches": args.steps * eng.step_kernel_count, "roofline": roofline,
+        "step_roofline": {"bytes_per_token_per_gpu": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak},
+        "kernel_ms": dict(zip(["qkv_rope", "attention", "wo_residual", "gateup_swiglu", "down_residual"], kms)),
+        "setup_s": {"model_generation": gen_s, "engine_load": load_s},
+    }
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(gguf, spec)
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

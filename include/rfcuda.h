@@ -1,0 +1,230 @@
+/*
+ * rfcuda.h - C ABI of librfcuda.so, the B200 (sm_100a) decode engine that
+ * replaces RAMforge's legacy CPU executor on the per-token hot path.
+ *
+ * Conventions (mirroring the reference's Rust contracts):
+ *   - every call returns int: RF_OK (0) or a negative RF_E* code; the reason is
+ *     in rf_last_error() (thread-local), never a panic or abort
+ *     (reference: Result<_, String> throughout, e.g. streaming_model.rs:909-919);
+ *   - the caller owns host buffers (activations, logits); the engine owns device
+ *     weights, the KV cache and its scratch (reference: caller-owned &mut [f32]
+ *     scratch in model_executor.rs:102-121, model-owned persistent weights);
+ *   - one host thread drives one engine (reference: one thread per engine,
+ *     layer cache behind a Mutex, streaming_model.rs:141);
+ *   - matrices use the ggml convention ne0 = input (row length), ne1 = output
+ *     rows, rows stored contiguously (reference: compute.rs:7-15).
+ * Reference paths are crates/<crate>/src/<file>:<line> in NeonMC23/RAMforge.
+ */
+#ifndef RFCUDA_H
+#define RFCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RF_ABI_VERSION 1
+
+/* status codes */
+#define RF_OK 0
+#define RF_EINVAL (-1)       /* bad argument / shape / position (arity mismatch errors) */
+#define RF_ENOMEM (-2)       /* byte budget exceeded or a device/pinned allocation failed */
+#define RF_ECUDA (-3)        /* CUDA runtime error */
+#define RF_EFORMAT (-4)      /* malformed GGUF / unsupported tensor type */
+#define RF_ESTATE (-5)       /* wrong state, e.g. layer not loaded, KV cache full */
+#define RF_EUNSUPPORTED (-6) /* valid request this build does not implement */
+#define RF_ENCCL (-7)        /* NCCL (tensor-parallel) failure */
+#define RF_ETIMEOUT (-8)     /* a bounded device-side wait gave up */
+
+/* ggml tensor type ids (types.rs:238-270) accepted by the engine */
+#define RF_TYPE_F32 0
+#define RF_TYPE_F16 1
+#define RF_TYPE_Q4_0 2
+#define RF_TYPE_Q8_0 8
+#define RF_TYPE_Q4_K 12
+
+/* per-layer tensor roles, the nine tensors of StreamingLayerWeights
+ * (model_executor.rs:33-48; names blk.N.<role>.weight, model.rs:182-192) */
+#define RF_ROLE_ATTN_NORM 0
+#define RF_ROLE_ATTN_Q 1
+#define RF_ROLE_ATTN_K 2
+#define RF_ROLE_ATTN_V 3
+#define RF_ROLE_ATTN_OUTPUT 4
+#define RF_ROLE_FFN_NORM 5
+#define RF_ROLE_FFN_GATE 6
+#define RF_ROLE_FFN_UP 7
+#define RF_ROLE_FFN_DOWN 8
+/* persistent tensors (persistent.rs:20-80) */
+#define RF_ROLE_TOKEN_EMBD 16
+#define RF_ROLE_OUTPUT_NORM 17
+#define RF_ROLE_OUTPUT 18
+
+/* LlamaConfig (runtime/src/model.rs:25-37); head_dim = n_embd / n_heads (model.rs:148). */
+typedef struct rf_model_config {
+  uint32_t vocab_size, context_length, n_embd, n_layers, n_ff, n_heads, n_kv_heads, head_dim;
+  float rms_eps, rope_theta;
+} rf_model_config;
+
+/* GPU runtime configuration: the reference's RuntimeConfig (runtime_config.rs:15-23)
+ * plus the device-side knobs.  Zero-initialise and set what you need. */
+typedef struct rf_runtime_config {
+  int device;                 /* CUDA ordinal */
+  int tp_rank, tp_size;       /* tensor parallelism (tp_size 0/1 = single GPU) */
+  const uint8_t* nccl_id;     /* 128-byte id from rf_tp_unique_id (tp_size > 1) */
+  uint32_t max_seq_len;       /* KV capacity in positions; 0 = context_length */
+  uint64_t vram_budget_bytes; /* byte budget for everything the engine allocates; 0 = device free memory */
+  int ring_slots;             /* out-of-core VRAM ring depth; 0 = all layers resident */
+  int kv_f32;                 /* 1 = f32 KV cache (reference format); 0 = f16 (default) */
+  int disable_graphs;         /* 1 = launch kernels eagerly instead of replaying a CUDA graph */
+} rf_runtime_config;
+
+/* One host tensor handed to rf_layer_load / rf_persistent_load. */
+typedef struct rf_tensor_view {
+  int role;          /* RF_ROLE_* */
+  int ggml_type;     /* RF_TYPE_* */
+  uint64_t ne0, ne1; /* ne1 = 1 for vectors */
+  const void* host;  /* GGUF block bytes */
+  uint64_t bytes;
+} rf_tensor_view;
+
+/* ResidencyStats (residency.rs:7-40) for the device weight store and ring. */
+typedef struct rf_residency_stats {
+  uint64_t layer_loads, layer_releases, cache_hits, cache_misses, evictions;
+  uint64_t peak_bytes, h2d_bytes;
+} rf_residency_stats;
+
+/* One rank's slice of a tensor-parallel engine: Q/K/V and gate/up are split by
+ * rows (KV head groups, FFN rows), Wo/Wdown by columns, the LM head by vocab rows. */
+typedef struct rf_tp_shard {
+  uint32_t q_heads, q_head_offset, kv_heads, kv_head_offset;
+  uint32_t ff_rows, ff_offset, vocab_rows, vocab_offset;
+} rf_tp_shard;
+
+typedef struct rf_engine rf_engine;
+
+const char* rf_last_error(void);
+int rf_abi_version(void);
+
+/* ---- host-only helpers (no GPU needed) ------------------------------------ */
+/* parse_gguf_file (gguf.rs:196) + LlamaConfig::from_gguf (model.rs:40-161) on an
+ * in-memory GGUF image. */
+int rf_gguf_read_config(const void* gguf, uint64_t len, rf_model_config* out);
+/* The shard an engine of tp_size ranks gives rank tp_rank (RF_EINVAL when the
+ * model does not split evenly or a slice would cut a quant block of `ggml_type`). */
+int rf_tp_shard_plan(const rf_model_config* cfg, int tp_size, int tp_rank, int ggml_type, rf_tp_shard* out);
+
+/* ---- engine lifecycle -------------------------------------------------- */
+/* Empty engine for explicit layer/persistent loads (StreamingLlamaModel::load
+ * without a data source, streaming_model.rs:156-182). */
+int rf_engine_create(const rf_model_config* cfg, const rf_runtime_config* rt, rf_engine** out);
+/* Parse a GGUF image in host memory (parse_gguf_file gguf.rs:196 +
+ * LlamaConfig::from_gguf model.rs:40 + validate_required_tensors model.rs:168),
+ * upload persistent weights and, when rt->ring_slots == 0, every layer.  The
+ * image must stay alive while the engine may stream layers from it. */
+int rf_engine_create_from_gguf(const void* gguf, uint64_t len, const rf_runtime_config* rt, rf_engine** out);
+/* Same, from a file path (GgufDataSource::open, datasource.rs:97); the file is mapped. */
+int rf_engine_create_from_file(const char* path, const rf_runtime_config* rt, rf_engine** out);
+void rf_engine_destroy(rf_engine* e);
+int rf_engine_config(const rf_engine* e, rf_model_config* out);
+
+/* ---- weights (layer load/compute/release) --------------------------------- */
+/* Persistent weight upload (PersistentWeight, persistent.rs:20-80). */
+int rf_persistent_load(rf_engine* e, const rf_tensor_view* view);
+/* load_layer (streaming_model.rs:581-847): copies and packs the nine tensors of one
+ * layer into device memory, charging the byte budget "layer:<i>:weights". */
+int rf_layer_load(rf_engine* e, int layer, const rf_tensor_view* views, int n_views);
+/* load_layer from the engine's own GGUF source (engines created from a GGUF). */
+int rf_layer_load_gguf(rf_engine* e, int layer);
+/* release_layer (streaming_model.rs:849-873): frees the layer and its charge. */
+int rf_layer_release(rf_engine* e, int layer);
+int rf_layer_is_resident(const rf_engine* e, int layer);
+/* ModelExecutor::execute_layer (model_executor.rs:102-236) on the engine's
+ * device hidden state at position pos (== KV length). The layer's K/V is written
+ * at slot pos and becomes history when rf_kv_commit advances the length
+ * (the deferred commit of streaming_model.rs:1289-1295). */
+int rf_layer_compute(rf_engine* e, int layer, uint32_t pos);
+
+/* ---- hidden state, token forward, logits ----------------------------------- */
+/* hidden <- token_embd row (get_embedding, tensor.rs:701 / persistent.rs:80). */
+int rf_embed(rf_engine* e, uint32_t token);
+int rf_hidden_write(rf_engine* e, const float* host, uint32_t n);
+int rf_hidden_read(rf_engine* e, float* host, uint32_t n);
+/* KvCache::increment_seq_len (kv_cache.rs:415). */
+int rf_kv_commit(rf_engine* e);
+/* forward_single_streaming (streaming_model.rs:909-1305): pos must equal the KV
+ * length (else RF_EINVAL, streaming_model.rs:921); final_hidden (n_embd floats,
+ * output-normed) may be NULL. */
+int rf_forward_token(rf_engine* e, uint32_t token, uint32_t pos, float* final_hidden);
+/* compute_logits (streaming_model.rs:1334-1371) on the last forward's hidden plus the
+ * greedy pick (Sampler::sample_checked greedy branch, sampling.rs:45-56: first
+ * maximum wins).  logits (vocab floats) and argmax may each be NULL. */
+int rf_compute_logits(rf_engine* e, float* logits, uint32_t* argmax);
+/* One greedy decode step at pos = KV length: forward(token) + logits + argmax,
+ * replayed as one CUDA graph. */
+int rf_decode_step(rf_engine* e, uint32_t token, uint32_t* next_token);
+/* generate_impl greedy path (inference.rs:445-759): prompt token by token, then
+ * n_new greedy tokens into out (n_new entries). */
+int rf_generate(rf_engine* e, const uint32_t* prompt, uint32_t n_prompt, uint32_t n_new, uint32_t* out);
+
+/* ---- measurement hooks (the Profiler's per-event timers, profile.rs:8-60) --------- */
+/* Kernels one decode step launches: 5 per layer + embedding, output norm, LM head
+ * with argmax, token advance. */
+int rf_step_kernel_count(const rf_engine* e, uint32_t* out);
+/* n_steps greedy decode steps from `token` at pos = KV length, token fed back on
+ * the device (rf_generate's loop), bracketed by CUDA events on the engine stream:
+ * *device_ms = their elapsed device time.  out_tokens (n_steps) may be NULL. */
+int rf_decode_timed(rf_engine* e, uint32_t token, uint32_t n_steps, uint32_t* out_tokens, float* device_ms);
+/* Average device time per launch of each per-layer kernel class
+ * (0 QKV+RoPE, 1 attention, 2 Wo+residual, 3 gate/up+SwiGLU, 4 down+residual),
+ * each class launched over every resident layer in turn, `iters` rounds, with
+ * events on the engine stream.  Runs at pos = KV length without committing. */
+int rf_bench_layer_kernels(rf_engine* e, uint32_t iters, float* avg_ms5);
+
+/* ---- KV cache (KvCache, kv_cache.rs:20-510) ------------------------------------ */
+int rf_kv_reset(rf_engine* e);                        /* clear (kv_cache.rs clear / inference.rs:405-409) */
+int rf_kv_seq_len(const rf_engine* e, uint32_t* out); /* seq_len */
+/* get_k_range / get_v_range (kv_cache.rs:452-480): positions [start,end) of this
+ * rank's KV heads as f32 in the reference layout [pos][kv_head][head_dim]. */
+int rf_kv_read(const rf_engine* e, int layer, int which_v, uint32_t start, uint32_t end, float* host);
+
+/* ---- byte budget and residency (MemoryBudget memory.rs:39-388, StagingPlan
+ *      staging_plan.rs:46-77, should_keep_resident persistent.rs:468) ----------- */
+int rf_budget_total(const rf_engine* e, uint64_t* out);
+int rf_budget_used(const rf_engine* e, uint64_t* out);
+int rf_budget_available(const rf_engine* e, uint64_t* out);
+/* Choose which layers stay resident (mask[i] != 0) and the ring depth used for the
+ * others; vram_weight_budget_bytes caps resident layer weights plus ring slots. */
+int rf_set_residency_plan(rf_engine* e, const uint8_t* resident_mask, int ring_slots,
+                          uint64_t vram_weight_budget_bytes);
+int rf_residency_stats_get(const rf_engine* e, rf_residency_stats* out);
+
+/* ---- tensor parallelism -------------------------------------------------------- */
+/* 128-byte NCCL unique id for rank 0 to distribute (ncclGetUniqueId). */
+int rf_tp_unique_id(uint8_t* out128);
+
+/* ---- standalone ops on device pointers (benchmark configs 2 and 3) ---------------
+ * A packed matrix is the device form of one GGUF weight (quantized_matvec_dispatch,
+ * compute_dispatch.rs:90-254 / quantized_matvec_reference compute.rs:185-229). */
+typedef struct rf_matrix rf_matrix;
+/* Pack GGUF block bytes (host or device pointer, `on_device`) of an out x in
+ * matrix of ggml_type on the current device. */
+int rf_matrix_create(int ggml_type, const void* gguf_bytes, uint64_t bytes, int on_device, uint32_t n_out,
+                     uint32_t n_in, rf_matrix** out);
+void rf_matrix_destroy(rf_matrix* m);
+uint64_t rf_matrix_device_bytes(const rf_matrix* m);
+/* y[b][out] = W . x[b][in] for b < batch (1..8); dX, dY device pointers; stream
+ * is a cudaStream_t (NULL = legacy default stream). */
+int rf_qmatvec(const rf_matrix* m, const float* dX, float* dY, int batch, void* stream);
+/* Single-token GQA decode attention (attention_reference compute.rs:461-547)
+ * for `batch` sequences: dQ [batch][H][hd] f32, dK/dV [batch][KV][ctx][hd] f16,
+ * dOut [batch][H][hd] f32; softmax over all ctx positions with scale 1/sqrt(hd).
+ * Split-K scratch comes from a per-device workspace the library allocates once. */
+int rf_decode_attention(const float* dQ, const uint16_t* dK, const uint16_t* dV, int ctx, int n_heads,
+                        int n_kv_heads, int head_dim, int batch, float* dOut, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RFCUDA_H */

@@ -1,0 +1,275 @@
+// rf_common.cpp - errors, byte budget, GGUF parsing, LlamaConfig, host packing.
+#include "rf_common.h"
+
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <thread>
+
+namespace rf {
+
+static thread_local std::string g_err;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+const char* last_error() { return g_err.c_str(); }
+
+// ---- Budget ----------------------------------------------------------------
+// MemoryBudget::allocate (memory.rs:93-122) / release (memory.rs:131-152).
+int Budget::allocate(const std::string& name, uint64_t bytes) {
+  if (bytes == 0) return set_error(RF_EINVAL, "invalid allocation size 0 for '%s'", name.c_str());
+  if (charges_.count(name)) return set_error(RF_EINVAL, "allocation '%s' already exists", name.c_str());
+  if (!can_allocate(bytes))
+    return set_error(RF_ENOMEM,
+                     "insufficient VRAM budget for '%s': requested %llu, available %llu (total %llu, used %llu)",
+                     name.c_str(), (unsigned long long)bytes, (unsigned long long)available(),
+                     (unsigned long long)total_, (unsigned long long)used_);
+  charges_[name] = bytes;
+  used_ += bytes;
+  peak_ = std::max(peak_, used_);
+  return RF_OK;
+}
+int Budget::release(const std::string& name) {
+  auto it = charges_.find(name);
+  if (it == charges_.end()) return set_error(RF_EINVAL, "allocation '%s' not found", name.c_str());
+  used_ -= it->second;
+  charges_.erase(it);
+  return RF_OK;
+}
+
+// ---- GGUF ---------------------------------------------------------------------
+namespace {
+struct Reader {
+  const uint8_t* p;
+  uint64_t len, pos = 0;
+  bool err = false;
+  bool take(void* dst, uint64_t n) {
+    if (err || pos + n > len || pos + n < pos) {
+      err = true;
+      return false;
+    }
+    if (dst) memcpy(dst, p + pos, n);
+    pos += n;
+    return true;
+  }
+  uint32_t u32() { uint32_t v = 0; take(&v, 4); return v; }
+  uint64_t u64() { uint64_t v = 0; take(&v, 8); return v; }
+  bool str(std::string* s) {
+    uint64_t n = u64();
+    if (err || n > 10ull * 1024 * 1024 || pos + n > len) { err = true; return false; }  // MAX_STRING_LEN (gguf.rs:12)
+    if (s) s->assign((const char*)p + pos, n);
+    pos += n;
+    return true;
+  }
+};
+
+// read_metadata_value (gguf.rs:130-151); integer/float views as MetadataValue::as_u64
+// (types.rs:86-98) and the get_f32_arch match (runtime/src/model.rs:79-98).
+void read_scalar(Reader& r, uint32_t t, GgufMeta* m) {
+  uint8_t b1 = 0; uint16_t b2 = 0; uint32_t b4 = 0; uint64_t b8 = 0;
+  switch (t) {
+    case 0: r.take(&b1, 1); m->u = b1; m->has_u = true; break;
+    case 1: r.take(&b1, 1); m->u = (uint64_t)(int64_t)(int8_t)b1; m->has_u = true; break;
+    case 2: r.take(&b2, 2); m->u = b2; m->has_u = true; break;
+    case 3: r.take(&b2, 2); m->u = (uint64_t)(int64_t)(int16_t)b2; m->has_u = true; break;
+    case 4: r.take(&b4, 4); m->u = b4; m->has_u = true; m->f = b4; m->has_f = true; break;
+    case 5: r.take(&b4, 4); m->u = (uint64_t)(int64_t)(int32_t)b4; m->has_u = true; m->f = (int32_t)b4; m->has_f = true; break;
+    case 6: { float f = 0; r.take(&f, 4); m->f = f; m->has_f = true; break; }
+    case 7: r.take(&b1, 1); break;
+    case 8: r.str(&m->str); break;
+    case 10: r.take(&b8, 8); m->u = b8; m->has_u = true; m->f = (double)b8; m->has_f = true; break;
+    case 11: r.take(&b8, 8); m->u = b8; m->has_u = true; m->f = (double)(int64_t)b8; m->has_f = true; break;
+    case 12: { double d = 0; r.take(&d, 8); m->f = d; m->has_f = true; break; }
+    default: r.err = true;
+  }
+}
+
+bool type_info(uint32_t type, uint64_t* qk, uint64_t* bsz) {
+  switch (type) {  // GgmlType::type_info (types.rs:354-376) for the types the engine runs
+    case T_F32: *qk = 1; *bsz = 4; return true;
+    case T_F16: *qk = 1; *bsz = 2; return true;
+    case T_Q4_0: *qk = 32; *bsz = 18; return true;
+    case T_Q8_0: *qk = 32; *bsz = 34; return true;
+    case T_Q4_K: *qk = 256; *bsz = 144; return true;
+    case 6: *qk = 32; *bsz = 22; return true;    // Q5_0 (parsed, not executed)
+    case 14: *qk = 256; *bsz = 210; return true; // Q6_K (parsed, not executed)
+    default: return false;
+  }
+}
+}  // namespace
+
+const GgufTensor* Gguf::find(const std::string& n) const {
+  for (auto& t : tensors)
+    if (t.name == n) return &t;
+  return nullptr;
+}
+
+int parse_gguf(const uint8_t* p, uint64_t len, Gguf* g) {
+  Reader r{p, len};
+  char magic[4];
+  if (!r.take(magic, 4) || memcmp(magic, "GGUF", 4)) return set_error(RF_EFORMAT, "invalid GGUF magic");
+  g->version = r.u32();
+  if (g->version < 1 || g->version > 3) return set_error(RF_EFORMAT, "unsupported GGUF version %u", g->version);
+  const uint64_t nt = r.u64(), nkv = r.u64();
+  if (r.err || nt > 10000000ull || nkv > 100000ull) return set_error(RF_EFORMAT, "GGUF header counts out of range");
+  for (uint64_t i = 0; i < nkv; i++) {
+    std::string key;
+    r.str(&key);
+    GgufMeta m;
+    m.vtype = r.u32();
+    if (r.err) return set_error(RF_EFORMAT, "truncated GGUF metadata");
+    if (m.vtype == 9) {  // read_array_value (gguf.rs:153-194)
+      const uint32_t at = r.u32();
+      const uint64_t n = r.u64();
+      if (at == 9 || n > 10000000ull) return set_error(RF_EFORMAT, "unsupported GGUF array");
+      m.arr_len = n;
+      for (uint64_t j = 0; j < n && !r.err; j++) {
+        GgufMeta tmp;
+        read_scalar(r, at, &tmp);
+      }
+    } else {
+      read_scalar(r, m.vtype, &m);
+    }
+    if (r.err) return set_error(RF_EFORMAT, "truncated or invalid GGUF metadata value for '%s'", key.c_str());
+    g->meta[key] = m;
+  }
+  auto al = g->meta.find("general.alignment");
+  g->alignment = (al != g->meta.end() && al->second.has_u) ? al->second.u : 32;  // gguf.rs:251-255
+  g->tensors.resize(nt);
+  for (auto& t : g->tensors) {
+    r.str(&t.name);
+    const uint32_t nd = r.u32();
+    if (r.err || nd > 8) return set_error(RF_EFORMAT, "invalid tensor info");  // MAX_DIMENSIONS (gguf.rs:13)
+    t.dims.resize(nd);
+    for (auto& d : t.dims) d = r.u64();
+    t.type = r.u32();
+    t.offset = r.u64();
+    if (r.err) return set_error(RF_EFORMAT, "truncated tensor info");
+  }
+  uint64_t ds = r.pos;
+  if (g->alignment && ds % g->alignment) ds += g->alignment - ds % g->alignment;  // align_offset (model.rs:197)
+  g->data_start = ds;
+  for (auto& t : g->tensors) {
+    uint64_t ne = 1, qk = 0, bsz = 0;
+    for (auto d : t.dims) ne *= d;
+    if (!type_info(t.type, &qk, &bsz)) continue;  // unknown types stay unresolved
+    t.nbytes = (ne + qk - 1) / qk * bsz;
+    if (ds + t.offset + t.nbytes > len || ds + t.offset < ds)
+      return set_error(RF_EFORMAT, "tensor '%s' extends past the end of the GGUF image", t.name.c_str());
+    t.data = p + ds + t.offset;
+  }
+  return RF_OK;
+}
+
+int llama_config_from_gguf(const Gguf& g, rf_model_config* c) {
+  auto arch_it = g.meta.find("general.architecture");
+  std::string arch = arch_it != g.meta.end() ? arch_it->second.str : "unknown";
+  if (arch != "llama" && arch != "qwen2")
+    return set_error(RF_EFORMAT, "unsupported execution architecture '%s' (supported: [llama, qwen2])",
+                     arch.c_str());
+  const char* pre[4] = {arch.c_str(), "llama", "qwen2", "general"};
+  auto get_u = [&](const char* sfx, uint64_t* v) {  // get_u64_arch (model.rs:54-77)
+    for (auto pf : pre) {
+      auto it = g.meta.find(std::string(pf) + "." + sfx);
+      if (it != g.meta.end() && it->second.has_u) { *v = it->second.u; return true; }
+    }
+    return false;
+  };
+  auto get_f = [&](const char* sfx, float* v) {  // get_f32_arch (model.rs:79-98)
+    for (auto pf : pre) {
+      auto it = g.meta.find(std::string(pf) + "." + sfx);
+      if (it != g.meta.end() && it->second.has_f) { *v = (float)it->second.f; return true; }
+    }
+    return false;
+  };
+  uint64_t v = 0;
+  memset(c, 0, sizeof *c);
+  if (get_u("vocab_size", &v)) c->vocab_size = (uint32_t)v;
+  else {
+    auto t = g.meta.find("tokenizer.ggml.tokens");
+    if (t == g.meta.end()) return set_error(RF_EFORMAT, "missing vocab_size (tried %s.vocab_size)", arch.c_str());
+    c->vocab_size = (uint32_t)t->second.arr_len;
+  }
+  if (!get_u("context_length", &v)) return set_error(RF_EFORMAT, "missing %s.context_length", arch.c_str());
+  c->context_length = (uint32_t)v;
+  if (!get_u("embedding_length", &v)) return set_error(RF_EFORMAT, "missing %s.embedding_length", arch.c_str());
+  c->n_embd = (uint32_t)v;
+  if (!get_u("block_count", &v)) return set_error(RF_EFORMAT, "missing %s.block_count", arch.c_str());
+  c->n_layers = (uint32_t)v;
+  if (!get_u("feed_forward_length", &v) && !get_u("intermediate_size", &v))
+    return set_error(RF_EFORMAT, "missing %s.feed_forward_length", arch.c_str());
+  c->n_ff = (uint32_t)v;
+  if (!get_u("attention.head_count", &v)) return set_error(RF_EFORMAT, "missing %s.attention.head_count", arch.c_str());
+  c->n_heads = (uint32_t)v;
+  c->n_kv_heads = get_u("attention.head_count_kv", &v) ? (uint32_t)v : c->n_heads;
+  if (!get_f("attention.layer_norm_rms_epsilon", &c->rms_eps) && !get_f("attention.layer_norm_epsilon", &c->rms_eps))
+    c->rms_eps = 1e-5f;  // model.rs:142-144
+  if (!get_f("rope.freq_base", &c->rope_theta)) c->rope_theta = 10000.0f;  // model.rs:146
+  if (c->n_heads == 0 || c->n_kv_heads == 0) return set_error(RF_EFORMAT, "zero attention heads");
+  c->head_dim = c->n_embd / c->n_heads;  // model.rs:148
+  return RF_OK;
+}
+
+// ---- host packing ---------------------------------------------------------------
+int host_packed_init(int type, uint32_t M, uint32_t K, HostPacked* out) {
+  if (!packed_geometry(type, M, K, &out->geo))
+    return set_error(RF_EINVAL, "type %d cannot hold a %u x %u matrix", type, M, K);
+  out->qs.assign(out->geo.qs_stride * M, 0);
+  out->sc.assign(out->geo.sc_stride * M, 0);
+  return RF_OK;
+}
+
+int pack_rows(const uint8_t* src, uint64_t src_row_bytes, uint32_t src_blk_off, const std::vector<int>& src_rows,
+              HostPacked* out, uint32_t dst_row0, uint32_t dst_row_step) {
+  const PackedMat& g = out->geo;
+  const uint32_t qk = block_elems(g.type), bsz = block_bytes(g.type), nblk = g.K / qk;
+  if ((uint64_t)(src_blk_off + nblk) * bsz > src_row_bytes)
+    return set_error(RF_EINVAL, "packing slice exceeds the source row");
+  const size_t n = src_rows.size();
+  if (n && (uint64_t)dst_row0 + (uint64_t)(n - 1) * dst_row_step >= g.M)
+    return set_error(RF_EINVAL, "packing rows exceed the destination");
+  auto work = [&](size_t a, size_t b) {
+    for (size_t r = a; r < b; r++) {
+      const uint8_t* s = src + (uint64_t)src_rows[r] * src_row_bytes + (uint64_t)src_blk_off * bsz;
+      const uint64_t dr = dst_row0 + (uint64_t)r * dst_row_step;
+      uint8_t* q = out->qs.data() + dr * g.qs_stride;
+      uint8_t* c = g.sc_stride ? out->sc.data() + dr * g.sc_stride : nullptr;
+      switch (g.type) {
+        case T_F32:
+        case T_F16: memcpy(q, s, (size_t)nblk * bsz); break;
+        case T_Q8_0:
+          for (uint32_t b = 0; b < nblk; b++, s += 34) { memcpy(c + 2 * b, s, 2); memcpy(q + 32 * b, s + 2, 32); }
+          break;
+        case T_Q4_0:
+          for (uint32_t b = 0; b < nblk; b++, s += 18) { memcpy(c + 2 * b, s, 2); memcpy(q + 16 * b, s + 2, 16); }
+          break;
+        case T_Q4_K:
+          for (uint32_t b = 0; b < nblk; b++, s += 144) { memcpy(c + 16 * b, s, 16); memcpy(q + 128 * b, s + 16, 128); }
+          break;
+      }
+    }
+  };
+  const size_t nt = std::min<size_t>(std::max(1u, std::thread::hardware_concurrency()), 32);
+  if (n < 256 || nt <= 1) {
+    work(0, n);
+  } else {
+    std::vector<std::thread> ts;
+    const size_t per = (n + nt - 1) / nt;
+    for (size_t t = 0; t < nt; t++) {
+      const size_t a = t * per, b = std::min(n, a + per);
+      if (a < b) ts.emplace_back(work, a, b);
+    }
+    for (auto& t : ts) t.join();
+  }
+  return RF_OK;
+}
+
+}  // namespace rf

@@ -1,0 +1,1160 @@
+// rf_engine.cu - the decode engine behind include/rfcuda.h.
+//
+// One engine drives one GPU (one tensor-parallel rank).  Everything the decode
+// step touches lives in HBM: packed layer weights, persistent embedding /
+// output weights, the f16 KV cache (head-major [kv_head][pos][head_dim] so a
+// CTA reads one head's history contiguously), activation scratch and the
+// step's inputs (token id, position) as device words.  Because the position is
+// a device word, the whole token step - embedding, every layer, output norm,
+// LM head with argmax and the token/position advance - is one CUDA graph that
+// is replayed unchanged for every token.
+#include <dlfcn.h>
+#include <fcntl.h>
+#include <math.h>
+#include <nccl.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "rf_common.h"
+
+using namespace rf;
+
+// ---------------------------------------------------------------------------
+// NCCL, loaded on demand (only tensor-parallel engines need it)
+// ---------------------------------------------------------------------------
+namespace {
+struct NcclApi {
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  const char* (*errStr)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+NcclApi* nccl() {
+  static NcclApi api;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (h) {
+      api.getUniqueId = (decltype(api.getUniqueId))dlsym(h, "ncclGetUniqueId");
+      api.commInitRank = (decltype(api.commInitRank))dlsym(h, "ncclCommInitRank");
+      api.allReduce = (decltype(api.allReduce))dlsym(h, "ncclAllReduce");
+      api.allGather = (decltype(api.allGather))dlsym(h, "ncclAllGather");
+      api.commDestroy = (decltype(api.commDestroy))dlsym(h, "ncclCommDestroy");
+      api.errStr = (decltype(api.errStr))dlsym(h, "ncclGetErrorString");
+      api.ok = api.getUniqueId && api.commInitRank && api.allReduce && api.allGather && api.commDestroy && api.errStr;
+    }
+  }
+  return api.ok ? &api : nullptr;
+}
+#define RF_NCCL(expr)                                                                           \
+  do {                                                                                          \
+    ncclResult_t _r = (expr);                                                                   \
+    if (_r != ncclSuccess) return set_error(RF_ENCCL, "%s failed: %s", #expr, nccl()->errStr(_r)); \
+  } while (0)
+
+inline uint64_t align256(uint64_t x) { return (x + 255) & ~255ull; }
+
+const char* kRoleNames[9] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
+                             "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+
+struct Layer {
+  bool resident = false;
+  void* block = nullptr;
+  uint64_t bytes = 0;
+  PackedMat qkv{}, wo{}, gateup{}, down{};
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+};
+
+struct StepIO {  // device words read by the step kernels
+  uint32_t token;
+  int pos;
+};
+}  // namespace
+
+struct rf_engine {
+  rf_model_config cfg{};
+  rf_runtime_config rt{};
+  int dev = 0;
+  int tp = 1, rank = 0;
+  // local (this rank's) shard geometry
+  uint32_t qh_local = 0, kvh_local = 0, q_local = 0, kv_local = 0, ff_local = 0;
+  uint32_t qh_off = 0, kvh_off = 0, ff_off = 0, vocab_local = 0, vocab_off = 0, vocab_chunk = 0;
+  uint32_t max_seq = 0, seq_len = 0;
+  int max_splits = 0;
+  Budget budget;
+  cudaStream_t stream = nullptr;
+  // GGUF source (optional)
+  Gguf gguf;
+  const uint8_t* src = nullptr;
+  uint64_t src_len = 0;
+  void* map_addr = nullptr;
+  uint64_t map_len = 0;
+  // persistent weights
+  PackedMat embd{}, out{};
+  bool tied = false, have_embd = false, have_out = false, have_onorm = false;
+  void* embd_block = nullptr;
+  void* out_block = nullptr;
+  float* out_norm = nullptr;
+  std::vector<Layer> layers;
+  std::vector<uint8_t> plan_resident;  // residency plan (1 = keep resident)
+  // KV cache
+  void* kv_block = nullptr;
+  std::vector<void*> kc, vc;
+  // scratch
+  void* scratch = nullptr;
+  float *hidden = nullptr, *final_hidden = nullptr, *partial = nullptr, *q = nullptr, *k_cur = nullptr,
+        *v_cur = nullptr, *att = nullptr, *act = nullptr, *logits = nullptr, *logits_all = nullptr,
+        *attn_part = nullptr;
+  unsigned* attn_counters = nullptr;
+  StepIO* d_io = nullptr;
+  uint32_t* d_hist = nullptr;  // token produced at each position (device-side greedy history)
+  unsigned long long* d_key = nullptr;
+  float2* rope_cs = nullptr;
+  // pinned host words
+  StepIO* h_io = nullptr;
+  uint32_t* h_tok = nullptr;
+  unsigned long long* h_key = nullptr;
+  // graphs
+  cudaGraphExec_t g_forward = nullptr, g_decode = nullptr;
+  // NCCL
+  ncclComm_t comm = nullptr;
+  rf_residency_stats stats{};
+};
+
+namespace {
+
+int dev_alloc(rf_engine* e, const std::string& charge, uint64_t bytes, void** out) {
+  RF_TRY(e->budget.allocate(charge, bytes));
+  cudaError_t err = cudaMalloc(out, bytes);
+  if (err != cudaSuccess) {
+    e->budget.release(charge);
+    *out = nullptr;
+    return set_error(RF_ENOMEM, "cudaMalloc(%llu) for '%s' failed: %s", (unsigned long long)bytes, charge.c_str(),
+                     cudaGetErrorString(err));
+  }
+  return RF_OK;
+}
+void dev_free(rf_engine* e, const std::string& charge, void** p) {
+  if (*p) {
+    cudaFree(*p);
+    *p = nullptr;
+    e->budget.release(charge);
+  }
+}
+
+void drop_graphs(rf_engine* e) {
+  if (e->g_forward) cudaGraphExecDestroy(e->g_forward);
+  if (e->g_decode) cudaGraphExecDestroy(e->g_decode);
+  e->g_forward = e->g_decode = nullptr;
+}
+
+// Build the RoPE (cos, sin) table on the host with the reference's f32
+// expression: angle = theta^(-2i/hd) * pos (compute.rs:446-450), evaluated by the
+// same glibc powf/cosf/sinf the Rust f32 methods call.
+std::vector<float2> rope_table(uint32_t max_seq, uint32_t hd, float theta) {
+  const uint32_t half = hd / 2;
+  std::vector<float> inv(half);
+  for (uint32_t i = 0; i < half; i++) {
+    const float ex = -2.0f * (float)i / (float)hd;
+    inv[i] = powf(theta, ex);
+  }
+  std::vector<float2> t((size_t)max_seq * half);
+  for (uint32_t p = 0; p < max_seq; p++)
+    for (uint32_t i = 0; i < half; i++) {
+      const float angle = inv[i] * (float)p;
+      t[(size_t)p * half + i] = make_float2(cosf(angle), sinf(angle));
+    }
+  return t;
+}
+
+int validate_config(const rf_model_config& c, int tp) {
+  if (!c.n_embd || !c.n_layers || !c.n_heads || !c.n_kv_heads || !c.vocab_size || !c.n_ff)
+    return set_error(RF_EINVAL, "model config has a zero dimension");
+  if (c.n_heads % c.n_kv_heads) return set_error(RF_EINVAL, "GQA requires n_heads %% n_kv_heads == 0");
+  if (!c.head_dim || c.head_dim % 2 || c.head_dim > 128)
+    return set_error(RF_EUNSUPPORTED, "head_dim %u unsupported (even, <= 128)", c.head_dim);
+  const uint32_t G = c.n_heads / c.n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return set_error(RF_EUNSUPPORTED, "GQA group %u unsupported", G);
+  if (c.n_kv_heads % tp || c.n_ff % tp) return set_error(RF_EINVAL, "tp %d must divide n_kv_heads and n_ff", tp);
+  return RF_OK;
+}
+
+int shard_plan(const rf_model_config& c, int tp, int rank, int block, rf_tp_shard* o) {
+  if (tp < 1 || rank < 0 || rank >= tp) return set_error(RF_EINVAL, "tp_rank %d / tp_size %d invalid", rank, tp);
+  RF_TRY(validate_config(c, tp));
+  const uint32_t G = c.n_heads / c.n_kv_heads;
+  o->kv_heads = c.n_kv_heads / tp;
+  o->kv_head_offset = o->kv_heads * rank;
+  o->q_heads = o->kv_heads * G;
+  o->q_head_offset = o->kv_head_offset * G;
+  o->ff_rows = c.n_ff / tp;
+  o->ff_offset = o->ff_rows * rank;
+  const uint32_t chunk = (c.vocab_size + tp - 1) / tp;
+  o->vocab_offset = std::min(c.vocab_size, chunk * rank);
+  o->vocab_rows = std::min(c.vocab_size, o->vocab_offset + chunk) - o->vocab_offset;
+  if (tp > 1 && block > 1) {  // row-parallel column slices must not cut a quant block
+    const uint32_t q_cols = o->q_heads * c.head_dim;
+    if (q_cols % block || o->ff_rows % block)
+      return set_error(RF_EINVAL, "tp %d: shard widths (%u attention columns, %u FFN columns) are not multiples of "
+                       "the %d-element quant block", tp, q_cols, o->ff_rows, block);
+  }
+  return RF_OK;
+}
+
+int setup_geometry(rf_engine* e) {
+  const rf_model_config& c = e->cfg;
+  e->tp = e->rt.tp_size > 1 ? e->rt.tp_size : 1;
+  e->rank = e->tp > 1 ? e->rt.tp_rank : 0;
+  rf_tp_shard sh{};
+  RF_TRY(shard_plan(c, e->tp, e->rank, 1, &sh));
+  e->kvh_local = sh.kv_heads;
+  e->kvh_off = sh.kv_head_offset;
+  e->qh_local = sh.q_heads;
+  e->qh_off = sh.q_head_offset;
+  e->q_local = e->qh_local * c.head_dim;
+  e->kv_local = e->kvh_local * c.head_dim;
+  e->ff_local = sh.ff_rows;
+  e->ff_off = sh.ff_offset;
+  e->vocab_chunk = (c.vocab_size + e->tp - 1) / e->tp;
+  e->vocab_off = sh.vocab_offset;
+  e->vocab_local = sh.vocab_rows;
+  e->max_seq = e->rt.max_seq_len ? e->rt.max_seq_len : c.context_length;
+  if (!e->max_seq) return set_error(RF_EINVAL, "max_seq_len is zero");
+  e->max_splits = std::max<int>(32, (int)((e->max_seq + 511) / 512));
+  return RF_OK;
+}
+
+int engine_init_device(rf_engine* e) {
+  const rf_model_config& c = e->cfg;
+  RF_CUDA(cudaSetDevice(e->dev));
+  RF_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  size_t free_b = 0, total_b = 0;
+  RF_CUDA(cudaMemGetInfo(&free_b, &total_b));
+  e->budget = Budget(e->rt.vram_budget_bytes ? e->rt.vram_budget_bytes : (uint64_t)free_b);
+  e->layers.assign(c.n_layers, Layer{});
+  e->plan_resident.assign(c.n_layers, 1);
+  // KV cache: per layer K and V, [kv_head_local][max_seq][head_dim]
+  const uint64_t esz = e->rt.kv_f32 ? 4 : 2;
+  const uint64_t per = align256((uint64_t)e->kvh_local * e->max_seq * c.head_dim * esz);
+  RF_TRY(dev_alloc(e, "kv_cache", per * 2 * c.n_layers, &e->kv_block));
+  e->kc.resize(c.n_layers);
+  e->vc.resize(c.n_layers);
+  for (uint32_t l = 0; l < c.n_layers; l++) {
+    e->kc[l] = (uint8_t*)e->kv_block + per * (2 * l);
+    e->vc[l] = (uint8_t*)e->kv_block + per * (2 * l + 1);
+  }
+  // scratch
+  const uint32_t G = c.n_heads / c.n_kv_heads;
+  const uint64_t part_f = attn_part_floats(1, e->kvh_local, e->max_splits, G, c.head_dim);
+  struct Item { void** p; uint64_t bytes; };
+  const uint64_t vl_pad = (uint64_t)e->vocab_chunk;
+  std::vector<Item> items = {
+      {(void**)&e->hidden, 4ull * c.n_embd},        {(void**)&e->final_hidden, 4ull * c.n_embd},
+      {(void**)&e->partial, 4ull * c.n_embd},       {(void**)&e->q, 4ull * e->q_local},
+      {(void**)&e->k_cur, 4ull * e->kv_local},      {(void**)&e->v_cur, 4ull * e->kv_local},
+      {(void**)&e->att, 4ull * e->q_local},         {(void**)&e->act, 4ull * e->ff_local},
+      {(void**)&e->logits, 4ull * vl_pad},          {(void**)&e->logits_all, 4ull * vl_pad * e->tp},
+      {(void**)&e->attn_part, 4ull * part_f},       {(void**)&e->attn_counters, 4ull * e->kvh_local},
+      {(void**)&e->d_io, sizeof(StepIO)},           {(void**)&e->d_key, 8},
+      {(void**)&e->d_hist, 4ull * e->max_seq},
+      {(void**)&e->rope_cs, 8ull * e->max_seq * (c.head_dim / 2)}};
+  uint64_t total = 0;
+  for (auto& it : items) total += align256(it.bytes);
+  RF_TRY(dev_alloc(e, "scratch:activations", total, &e->scratch));
+  RF_CUDA(cudaMemset(e->scratch, 0, total));
+  uint64_t off = 0;
+  for (auto& it : items) {
+    *it.p = (uint8_t*)e->scratch + off;
+    off += align256(it.bytes);
+  }
+  auto tab = rope_table(e->max_seq, c.head_dim, c.rope_theta);
+  RF_CUDA(cudaMemcpy(e->rope_cs, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  RF_CUDA(cudaMallocHost((void**)&e->h_io, sizeof(StepIO)));
+  RF_CUDA(cudaMallocHost((void**)&e->h_tok, 4 * 4096));
+  RF_CUDA(cudaMallocHost((void**)&e->h_key, 8));
+  if (e->tp > 1) {
+    if (!nccl()) return set_error(RF_ENCCL, "tensor parallelism needs libnccl.so.2, which could not be loaded");
+    if (!e->rt.nccl_id) return set_error(RF_EINVAL, "tp_size > 1 requires nccl_id");
+    ncclUniqueId id;
+    memcpy(&id, e->rt.nccl_id, sizeof id);
+    RF_NCCL(nccl()->commInitRank(&e->comm, e->tp, id, e->rank));
+  }
+  return RF_OK;
+}
+
+// ---- weight packing ----------------------------------------------------------------
+struct View {
+  int type = -1;
+  uint64_t ne0 = 0, ne1 = 0, bytes = 0;
+  const uint8_t* host = nullptr;
+};
+
+int check_view(const View& v, const char* what, uint64_t ne0, uint64_t ne1) {
+  if (!v.host) return set_error(RF_EINVAL, "missing tensor %s", what);
+  if (v.ne0 != ne0 || v.ne1 != ne1)
+    return set_error(RF_EINVAL, "%s shape mismatch: expected [%llu, %llu], got [%llu, %llu]", what,
+                     (unsigned long long)ne0, (unsigned long long)ne1, (unsigned long long)v.ne0,
+                     (unsigned long long)v.ne1);
+  const int qk = block_elems(v.type);
+  if (!qk) return set_error(RF_EFORMAT, "%s: tensor type %d is not supported by the engine", what, v.type);
+  if (ne0 % qk) return set_error(RF_EFORMAT, "%s: row length %llu not a multiple of %d", what, (unsigned long long)ne0, qk);
+  const uint64_t need = ne0 / qk * block_bytes(v.type) * ne1;
+  if (v.bytes < need)
+    return set_error(RF_EINVAL, "%s truncated: expected %llu bytes, got %llu", what, (unsigned long long)need,
+                     (unsigned long long)v.bytes);
+  return RF_OK;
+}
+
+uint64_t row_bytes_of(const View& v) { return v.ne0 / block_elems(v.type) * block_bytes(v.type); }
+
+// f32 copy of a norm vector (F32 or F16 storage; TensorData F16 rows are f32 after load)
+int norm_to_f32(const View& v, uint32_t n, std::vector<float>* out) {
+  out->resize(n);
+  if (v.type == T_F32) memcpy(out->data(), v.host, 4ull * n);
+  else if (v.type == T_F16) {
+    for (uint32_t i = 0; i < n; i++) {
+      uint16_t h;
+      memcpy(&h, v.host + 2ull * i, 2);
+      const float f = __half2float(__ushort_as_half(h));
+      (*out)[i] = (h & 0x7C00u) ? f : f * 0.5f;  // reference f16 decode (tensor.rs:1017-1041)
+    }
+  } else {
+    return set_error(RF_EUNSUPPORTED, "norm weights of type %d are not supported", v.type);
+  }
+  return RF_OK;
+}
+
+std::vector<int> iota_rows(uint32_t start, uint32_t n) {
+  std::vector<int> r(n);
+  for (uint32_t i = 0; i < n; i++) r[i] = (int)(start + i);
+  return r;
+}
+// Packed order pairing dimension i with i+hd/2 of every head in [h0, h0+nh).
+std::vector<int> rope_pair_rows(uint32_t h0, uint32_t nh, uint32_t hd) {
+  std::vector<int> r;
+  r.reserve((size_t)nh * hd);
+  const uint32_t half = hd / 2;
+  for (uint32_t h = 0; h < nh; h++)
+    for (uint32_t i = 0; i < half; i++) {
+      r.push_back((int)((h0 + h) * hd + i));
+      r.push_back((int)((h0 + h) * hd + i + half));
+    }
+  return r;
+}
+
+int upload_packed(const HostPacked& hp, uint8_t* base, uint64_t* off, PackedMat* dst) {
+  *dst = hp.geo;
+  dst->qs = base + *off;
+  RF_CUDA(cudaMemcpy(dst->qs, hp.qs.data(), hp.qs.size(), cudaMemcpyHostToDevice));
+  *off += align256(hp.qs.size());
+  dst->sc = base + *off;
+  if (!hp.sc.empty()) RF_CUDA(cudaMemcpy(dst->sc, hp.sc.data(), hp.sc.size(), cudaMemcpyHostToDevice));
+  *off += align256(hp.sc.size() ? hp.sc.size() : 16);
+  return RF_OK;
+}
+uint64_t packed_bytes(const HostPacked& hp) { return align256(hp.qs.size()) + align256(hp.sc.size() ? hp.sc.size() : 16); }
+
+int load_layer_views(rf_engine* e, int l, const View* v /*[9]*/) {
+  const rf_model_config& c = e->cfg;
+  const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
+  RF_TRY(check_view(v[0], "attn_norm", c.n_embd, 1));
+  RF_TRY(check_view(v[1], "attn_q", c.n_embd, qd));
+  RF_TRY(check_view(v[2], "attn_k", c.n_embd, kvd));
+  RF_TRY(check_view(v[3], "attn_v", c.n_embd, kvd));
+  RF_TRY(check_view(v[4], "attn_output", qd, c.n_embd));
+  RF_TRY(check_view(v[5], "ffn_norm", c.n_embd, 1));
+  RF_TRY(check_view(v[6], "ffn_gate", c.n_embd, c.n_ff));
+  RF_TRY(check_view(v[7], "ffn_up", c.n_embd, c.n_ff));
+  RF_TRY(check_view(v[8], "ffn_down", c.n_ff, c.n_embd));
+  if (v[1].type != v[2].type || v[1].type != v[3].type)
+    return set_error(RF_EUNSUPPORTED, "layer %d: Q/K/V of different types are not supported", l);
+  if (v[6].type != v[7].type) return set_error(RF_EUNSUPPORTED, "layer %d: gate/up of different types", l);
+  const uint32_t qk_o = block_elems(v[4].type), qk_d = block_elems(v[8].type);
+  if ((e->qh_off * hd) % qk_o || e->q_local % qk_o || e->ff_off % qk_d || e->ff_local % qk_d)
+    return set_error(RF_EINVAL, "tensor-parallel shard of layer %d does not fall on block boundaries", l);
+  HostPacked qkv, wo, gu, dn;
+  RF_TRY(host_packed_init(v[1].type, e->q_local + 2 * e->kv_local, c.n_embd, &qkv));
+  RF_TRY(pack_rows(v[1].host, row_bytes_of(v[1]), 0, rope_pair_rows(e->qh_off, e->qh_local, hd), &qkv, 0, 1));
+  RF_TRY(pack_rows(v[2].host, row_bytes_of(v[2]), 0, rope_pair_rows(e->kvh_off, e->kvh_local, hd), &qkv, e->q_local, 1));
+  RF_TRY(pack_rows(v[3].host, row_bytes_of(v[3]), 0, iota_rows(e->kvh_off * hd, e->kv_local), &qkv,
+                   e->q_local + e->kv_local, 1));
+  RF_TRY(host_packed_init(v[4].type, c.n_embd, e->q_local, &wo));
+  RF_TRY(pack_rows(v[4].host, row_bytes_of(v[4]), e->qh_off * hd / qk_o, iota_rows(0, c.n_embd), &wo, 0, 1));
+  RF_TRY(host_packed_init(v[6].type, 2 * e->ff_local, c.n_embd, &gu));
+  RF_TRY(pack_rows(v[6].host, row_bytes_of(v[6]), 0, iota_rows(e->ff_off, e->ff_local), &gu, 0, 2));
+  RF_TRY(pack_rows(v[7].host, row_bytes_of(v[7]), 0, iota_rows(e->ff_off, e->ff_local), &gu, 1, 2));
+  RF_TRY(host_packed_init(v[8].type, c.n_embd, e->ff_local, &dn));
+  RF_TRY(pack_rows(v[8].host, row_bytes_of(v[8]), e->ff_off / qk_d, iota_rows(0, c.n_embd), &dn, 0, 1));
+  std::vector<float> an, fn;
+  RF_TRY(norm_to_f32(v[0], c.n_embd, &an));
+  RF_TRY(norm_to_f32(v[5], c.n_embd, &fn));
+  const uint64_t total = packed_bytes(qkv) + packed_bytes(wo) + packed_bytes(gu) + packed_bytes(dn) +
+                         2 * align256(4ull * c.n_embd);
+  Layer& L = e->layers[l];
+  const std::string charge = "layer:" + std::to_string(l) + ":weights";
+  RF_TRY(dev_alloc(e, charge, total, &L.block));
+  uint8_t* base = (uint8_t*)L.block;
+  uint64_t off = 0;
+  int rc = upload_packed(qkv, base, &off, &L.qkv);
+  if (!rc) rc = upload_packed(wo, base, &off, &L.wo);
+  if (!rc) rc = upload_packed(gu, base, &off, &L.gateup);
+  if (!rc) rc = upload_packed(dn, base, &off, &L.down);
+  if (!rc) {
+    L.attn_norm = (float*)(base + off);
+    off += align256(4ull * c.n_embd);
+    L.ffn_norm = (float*)(base + off);
+    cudaError_t ce = cudaMemcpy(L.attn_norm, an.data(), 4ull * c.n_embd, cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(L.ffn_norm, fn.data(), 4ull * c.n_embd, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) rc = set_error(RF_ECUDA, "norm upload failed: %s", cudaGetErrorString(ce));
+  }
+  if (rc) {  // release_layer on every error path (streaming_model.rs:1170-1270)
+    dev_free(e, charge, &L.block);
+    return rc;
+  }
+  L.bytes = total;
+  L.resident = true;
+  e->stats.layer_loads++;
+  e->stats.h2d_bytes += total;
+  e->stats.peak_bytes = e->budget.peak();
+  drop_graphs(e);
+  return RF_OK;
+}
+
+View view_from_gguf(const GgufTensor* t) {
+  View v;
+  if (!t) return v;
+  v.type = (int)t->type;
+  v.ne0 = t->dims.size() > 0 ? t->dims[0] : 1;
+  v.ne1 = t->dims.size() > 1 ? t->dims[1] : 1;
+  v.bytes = t->nbytes;
+  v.host = t->data;
+  return v;
+}
+
+int load_persistent(rf_engine* e, int role, const View& v) {
+  const rf_model_config& c = e->cfg;
+  if (role == RF_ROLE_OUTPUT_NORM) {
+    RF_TRY(check_view(v, "output_norm", c.n_embd, 1));
+    std::vector<float> w;
+    RF_TRY(norm_to_f32(v, c.n_embd, &w));
+    void* p = nullptr;
+    if (!e->out_norm) {
+      RF_TRY(dev_alloc(e, "persistent:output_norm", 4ull * c.n_embd, &p));
+      e->out_norm = (float*)p;
+    }
+    RF_CUDA(cudaMemcpy(e->out_norm, w.data(), 4ull * c.n_embd, cudaMemcpyHostToDevice));
+    e->have_onorm = true;
+  } else if (role == RF_ROLE_TOKEN_EMBD || role == RF_ROLE_OUTPUT) {
+    const bool is_embd = role == RF_ROLE_TOKEN_EMBD;
+    // get_embedding expects [n_embd, vocab] (tensor.rs:706-714)
+    RF_TRY(check_view(v, is_embd ? "token_embd" : "output", c.n_embd, c.vocab_size));
+    HostPacked hp;
+    const uint32_t rows = is_embd ? c.vocab_size : e->vocab_local;
+    const uint32_t r0 = is_embd ? 0 : e->vocab_off;
+    RF_TRY(host_packed_init(v.type, rows, c.n_embd, &hp));
+    RF_TRY(pack_rows(v.host, row_bytes_of(v), 0, iota_rows(r0, rows), &hp, 0, 1));
+    const std::string charge = is_embd ? "persistent:token_embd" : "persistent:output";
+    void** blk = is_embd ? &e->embd_block : &e->out_block;
+    dev_free(e, charge, blk);
+    RF_TRY(dev_alloc(e, charge, packed_bytes(hp), blk));
+    uint64_t off = 0;
+    RF_TRY(upload_packed(hp, (uint8_t*)*blk, &off, is_embd ? &e->embd : &e->out));
+    if (is_embd) e->have_embd = true;
+    else { e->have_out = true; e->tied = false; }
+    e->stats.h2d_bytes += packed_bytes(hp);
+  } else {
+    return set_error(RF_EINVAL, "unknown persistent role %d", role);
+  }
+  drop_graphs(e);
+  return RF_OK;
+}
+
+// The LM head matrix: output.weight, or the tied embedding rows of this rank
+// (compute_logits uses token_embd when output.weight is absent, streaming_model.rs:1353).
+int lm_head(rf_engine* e, PackedMat* W) {
+  if (e->have_out) { *W = e->out; return RF_OK; }
+  if (!e->have_embd) return set_error(RF_ESTATE, "no output or token_embd weights loaded");
+  *W = e->embd;
+  W->M = e->vocab_local;
+  W->qs = e->embd.qs + (uint64_t)e->vocab_off * e->embd.qs_stride;
+  W->sc = e->embd.sc + (uint64_t)e->vocab_off * e->embd.sc_stride;
+  return RF_OK;
+}
+
+int release_layer_impl(rf_engine* e, int l) {
+  Layer& L = e->layers[l];
+  if (!L.resident) return set_error(RF_ESTATE, "layer %d is not loaded", l);
+  dev_free(e, "layer:" + std::to_string(l) + ":weights", &L.block);
+  L = Layer{};
+  e->stats.layer_releases++;
+  drop_graphs(e);
+  return RF_OK;
+}
+
+int load_layer_gguf(rf_engine* e, int l) {
+  if (!e->src) return set_error(RF_ESTATE, "engine has no GGUF source");
+  View v[9];
+  for (int j = 0; j < 9; j++) {
+    const std::string name = "blk." + std::to_string(l) + "." + kRoleNames[j] + ".weight";
+    const GgufTensor* t = e->gguf.find(name);
+    if (!t || !t->data) return set_error(RF_EFORMAT, "missing tensor '%s'", name.c_str());
+    v[j] = view_from_gguf(t);
+  }
+  return load_layer_views(e, l, v);
+}
+
+// ---- the step ----------------------------------------------------------------------
+// One layer: execute_layer's block order (model_executor.rs:147-233) as five
+// fused kernels.  Row-parallel projections finish with a sum over ranks.
+// Kernel class k of layer l: 0 QKV+RoPE+KV append, 1 attention, 2 Wo+residual,
+// 3 gate/up+SwiGLU, 4 down+residual (2 and 4 end with the rank all-reduce).
+int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
+  const rf_model_config& c = e->cfg;
+  Layer& L = e->layers[l];
+  const Launch La{e->stream, pdl};
+  if (k == 0) {
+    RopeQKVArgs ra{};
+    ra.q_rows = e->q_local;
+    ra.kv_rows = e->kv_local;
+    ra.head_dim = c.head_dim;
+    ra.max_seq = e->max_seq;
+    ra.rope_cs = e->rope_cs;
+    ra.d_pos = &e->d_io->pos;
+    ra.q_out = e->q;
+    ra.k_cur = e->k_cur;
+    ra.v_cur = e->v_cur;
+    ra.kcache = e->kc[l];
+    ra.vcache = e->vc[l];
+    ra.kv_f32 = e->rt.kv_f32;
+    RF_CUDA(gemv_qkv_rope(La, L.qkv, e->hidden, L.attn_norm, c.rms_eps, ra));
+  } else if (k == 1) {
+    AttnArgs aa{};
+    aa.q = e->q;
+    aa.kc = e->kc[l];
+    aa.vc = e->vc[l];
+    aa.head_stride = (uint64_t)e->max_seq * c.head_dim;
+    aa.batch_stride = 0;
+    aa.k_cur = e->k_cur;
+    aa.v_cur = e->v_cur;
+    aa.d_nhist = &e->d_io->pos;
+    aa.n_heads = (int)e->qh_local;
+    aa.n_kv_heads = (int)e->kvh_local;
+    aa.head_dim = (int)c.head_dim;
+    aa.batch = 1;
+    aa.max_splits = e->max_splits;
+    aa.part = e->attn_part;
+    aa.counters = e->attn_counters;
+    aa.out = e->att;
+    aa.kv_f32 = e->rt.kv_f32;
+    RF_CUDA(launch_attention(La, aa));
+  } else if (k == 2 || k == 4) {
+    const PackedMat& W = k == 2 ? L.wo : L.down;
+    const float* x = k == 2 ? e->att : e->act;
+    if (e->tp == 1) {
+      RF_CUDA(gemv_residual(La, W, x, e->hidden, e->hidden));
+    } else {
+      RF_CUDA(gemv_residual(La, W, x, e->rank == 0 ? e->hidden : nullptr, e->partial));
+      RF_NCCL(nccl()->allReduce(e->partial, e->hidden, c.n_embd, ncclFloat32, ncclSum, e->comm, e->stream));
+    }
+  } else {
+    RF_CUDA(gemv_swiglu(La, L.gateup, e->hidden, L.ffn_norm, c.rms_eps, e->act));
+  }
+  return RF_OK;
+}
+
+int enqueue_layer(rf_engine* e, int l, bool pdl) {
+  for (int k = 0; k < 5; k++) RF_TRY(enqueue_layer_kernel(e, l, k, pdl));
+  return RF_OK;
+}
+
+bool all_resident(const rf_engine* e) {
+  for (auto& L : e->layers)
+    if (!L.resident) return false;
+  return true;
+}
+
+// embedding -> every layer -> output RMSNorm into final_hidden.
+int enqueue_forward(rf_engine* e, bool pdl) {
+  const Launch La{e->stream, pdl};
+  RF_CUDA(launch_embed(La, e->embd, &e->d_io->token, e->hidden, e->d_key));
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++) RF_TRY(enqueue_layer(e, (int)l, pdl));
+  RF_CUDA(launch_rmsnorm(La, e->hidden, e->out_norm, e->cfg.rms_eps, e->cfg.n_embd, e->final_hidden));
+  return RF_OK;
+}
+
+// LM head + greedy argmax (+ rank max) on final_hidden.
+int enqueue_logits(rf_engine* e, bool pdl, bool want_logits) {
+  PackedMat W;
+  RF_TRY(lm_head(e, &W));
+  const Launch La{e->stream, pdl};
+  RF_CUDA(cudaMemsetAsync(e->d_key, 0, 8, e->stream));
+  RF_CUDA(gemv_argmax(La, W, e->final_hidden, nullptr, 0.f, want_logits ? e->logits : nullptr, e->d_key,
+                      e->vocab_off));
+  if (e->tp > 1) RF_NCCL(nccl()->allReduce(e->d_key, e->d_key, 1, ncclUint64, ncclMax, e->comm, e->stream));
+  return RF_OK;
+}
+
+int enqueue_decode(rf_engine* e, bool pdl) {
+  RF_TRY(enqueue_forward(e, pdl));
+  RF_TRY(enqueue_logits(e, pdl, false));
+  RF_CUDA(launch_finalize(Launch{e->stream, pdl}, e->d_key, &e->d_io->token, &e->d_io->pos, e->d_hist, (int)e->max_seq));
+  return RF_OK;
+}
+
+int ensure_ready(rf_engine* e) {
+  if (!e->have_embd) return set_error(RF_ESTATE, "token_embd is not loaded");
+  if (!e->have_onorm) return set_error(RF_ESTATE, "output_norm is not loaded");
+  if (!all_resident(e)) {
+    if (!e->src) return set_error(RF_ESTATE, "a layer is not resident and the engine has no GGUF source");
+  }
+  return RF_OK;
+}
+
+// Make every layer resident, loading from the GGUF source where needed.
+// Layers the residency plan marks non-resident are loaded for the step and
+// released afterwards (load -> compute -> release, streaming_model.rs:1081-1270).
+int run_stepwise(rf_engine* e, bool decode) {
+  const Launch La{e->stream, false};
+  RF_CUDA(launch_embed(La, e->embd, &e->d_io->token, e->hidden, e->d_key));
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
+    bool loaded_now = false;
+    if (!e->layers[l].resident) {
+      e->stats.cache_misses++;
+      RF_TRY(load_layer_gguf(e, (int)l));
+      loaded_now = true;
+    } else {
+      e->stats.cache_hits++;
+    }
+    RF_TRY(enqueue_layer(e, (int)l, false));
+    if (loaded_now && !e->plan_resident[l]) {
+      RF_CUDA(cudaStreamSynchronize(e->stream));
+      RF_TRY(release_layer_impl(e, (int)l));
+    }
+  }
+  RF_CUDA(launch_rmsnorm(La, e->hidden, e->out_norm, e->cfg.rms_eps, e->cfg.n_embd, e->final_hidden));
+  if (decode) {
+    RF_TRY(enqueue_logits(e, false, false));
+    RF_CUDA(launch_finalize(La, e->d_key, &e->d_io->token, &e->d_io->pos, e->d_hist, (int)e->max_seq));
+  }
+  return RF_OK;
+}
+
+int capture(rf_engine* e, bool decode, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  RF_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = decode ? enqueue_decode(e, true) : enqueue_forward(e, true);
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return set_error(RF_ECUDA, "graph capture failed: %s", cudaGetErrorString(ce));
+  ce = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (ce != cudaSuccess) return set_error(RF_ECUDA, "graph instantiate failed: %s", cudaGetErrorString(ce));
+  return RF_OK;
+}
+
+// Launch one token step (forward, or decode = forward + logits + advance).
+int launch_step(rf_engine* e, bool decode) {
+  if (!all_resident(e)) return run_stepwise(e, decode);
+  if (e->rt.disable_graphs) return decode ? enqueue_decode(e, true) : enqueue_forward(e, true);
+  cudaGraphExec_t* g = decode ? &e->g_decode : &e->g_forward;
+  if (!*g) RF_TRY(capture(e, decode, g));
+  e->stats.cache_hits += e->cfg.n_layers;
+  RF_CUDA(cudaGraphLaunch(*g, e->stream));
+  return RF_OK;
+}
+
+int set_io(rf_engine* e, uint32_t token, uint32_t pos) {
+  e->h_io->token = token;
+  e->h_io->pos = (int)pos;
+  RF_CUDA(cudaMemcpyAsync(e->d_io, e->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, e->stream));
+  return RF_OK;
+}
+
+int check_step(rf_engine* e, uint32_t token, uint32_t pos) {
+  if (pos != e->seq_len)
+    return set_error(RF_EINVAL, "KV position/history mismatch: position %u requires cache history %u, got %u", pos,
+                     pos, e->seq_len);
+  if (e->seq_len >= e->max_seq) return set_error(RF_ESTATE, "KV cache full (%u positions)", e->max_seq);
+  if (token >= e->cfg.vocab_size)
+    return set_error(RF_EINVAL, "token_id %u out of bounds for vocab %u", token, e->cfg.vocab_size);
+  return ensure_ready(e);
+}
+
+// n greedy decode steps starting from `token` at pos = KV length.  Each step's
+// argmax is the next step's token on the device (finalize_kernel), and lands in
+// d_hist[pos]; the host copies the n tokens once at the end.  With device_ms the
+// n steps are bracketed by events on the engine stream.
+int decode_loop(rf_engine* e, uint32_t token, uint32_t n, uint32_t* out, float* device_ms) {
+  if (n == 0) {
+    if (device_ms) *device_ms = 0.f;
+    return RF_OK;
+  }
+  if ((uint64_t)e->seq_len + n > e->max_seq) return set_error(RF_ESTATE, "KV cache full");
+  const uint32_t p0 = e->seq_len;
+  RF_TRY(set_io(e, token, p0));
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (device_ms) {
+    RF_CUDA(cudaEventCreate(&a));
+    RF_CUDA(cudaEventCreate(&b));
+    RF_CUDA(cudaEventRecord(a, e->stream));
+  }
+  int rc = RF_OK;
+  for (uint32_t t = 0; t < n && !rc; t++) {
+    rc = launch_step(e, true);
+    if (!rc) e->seq_len++;
+  }
+  if (device_ms && !rc) {
+    cudaError_t ce = cudaEventRecord(b, e->stream);
+    if (ce == cudaSuccess) ce = cudaEventSynchronize(b);
+    if (ce == cudaSuccess) ce = cudaEventElapsedTime(device_ms, a, b);
+    if (ce != cudaSuccess) rc = set_error(RF_ECUDA, "decode timing failed: %s", cudaGetErrorString(ce));
+  }
+  if (a) cudaEventDestroy(a);
+  if (b) cudaEventDestroy(b);
+  if (rc) return rc;
+  if (out) RF_CUDA(cudaMemcpyAsync(out, e->d_hist + p0, 4ull * n, cudaMemcpyDeviceToHost, e->stream));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  return RF_OK;
+}
+
+int engine_finish_create(rf_engine* e) {
+  RF_TRY(setup_geometry(e));
+  RF_TRY(engine_init_device(e));
+  return RF_OK;
+}
+
+int create_from_image(const uint8_t* p, uint64_t len, const rf_runtime_config* rt, rf_engine* e) {
+  e->rt = rt ? *rt : rf_runtime_config{};
+  e->dev = e->rt.device;
+  e->src = p;
+  e->src_len = len;
+  RF_TRY(parse_gguf(p, len, &e->gguf));
+  RF_TRY(llama_config_from_gguf(e->gguf, &e->cfg));
+  // validate_required_tensors (model.rs:168-200)
+  for (const char* n : {"token_embd.weight", "output_norm.weight"})
+    if (!e->gguf.find(n)) return set_error(RF_EFORMAT, "Unsupported or incomplete model: missing tensor '%s'", n);
+  RF_TRY(engine_finish_create(e));
+  RF_TRY(load_persistent(e, RF_ROLE_TOKEN_EMBD, view_from_gguf(e->gguf.find("token_embd.weight"))));
+  RF_TRY(load_persistent(e, RF_ROLE_OUTPUT_NORM, view_from_gguf(e->gguf.find("output_norm.weight"))));
+  if (const GgufTensor* o = e->gguf.find("output.weight")) RF_TRY(load_persistent(e, RF_ROLE_OUTPUT, view_from_gguf(o)));
+  else e->tied = true;
+  if (e->rt.ring_slots == 0)
+    for (uint32_t l = 0; l < e->cfg.n_layers; l++) RF_TRY(load_layer_gguf(e, (int)l));
+  return RF_OK;
+}
+
+void destroy(rf_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->dev);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  drop_graphs(e);
+  for (size_t l = 0; l < e->layers.size(); l++)
+    if (e->layers[l].block) cudaFree(e->layers[l].block);
+  if (e->embd_block) cudaFree(e->embd_block);
+  if (e->out_block) cudaFree(e->out_block);
+  if (e->out_norm) cudaFree(e->out_norm);
+  if (e->kv_block) cudaFree(e->kv_block);
+  if (e->scratch) cudaFree(e->scratch);
+  if (e->h_io) cudaFreeHost(e->h_io);
+  if (e->h_tok) cudaFreeHost(e->h_tok);
+  if (e->h_key) cudaFreeHost(e->h_key);
+  if (e->comm && nccl()) nccl()->commDestroy(e->comm);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  if (e->map_addr) munmap(e->map_addr, e->map_len);
+  delete e;
+}
+
+#define ENGINE_GUARD(e)                                                \
+  do {                                                                 \
+    if (!(e)) return set_error(RF_EINVAL, "null engine");              \
+    cudaError_t _se = cudaSetDevice((e)->dev);                         \
+    if (_se != cudaSuccess)                                            \
+      return set_error(RF_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(_se)); \
+  } while (0)
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char* rf_last_error(void) { return last_error(); }
+int rf_abi_version(void) { return RF_ABI_VERSION; }
+
+int rf_gguf_read_config(const void* gguf, uint64_t len, rf_model_config* out) {
+  if (!gguf || !out) return set_error(RF_EINVAL, "null argument");
+  Gguf g;
+  RF_TRY(parse_gguf((const uint8_t*)gguf, len, &g));
+  return llama_config_from_gguf(g, out);
+}
+
+int rf_tp_shard_plan(const rf_model_config* cfg, int tp_size, int tp_rank, int ggml_type, rf_tp_shard* out) {
+  if (!cfg || !out) return set_error(RF_EINVAL, "null argument");
+  rf_model_config c = *cfg;
+  if (!c.head_dim && c.n_heads) c.head_dim = c.n_embd / c.n_heads;
+  const int block = block_elems(ggml_type);
+  if (!block) return set_error(RF_EINVAL, "unknown ggml type %d", ggml_type);
+  return shard_plan(c, tp_size, tp_rank, block, out);
+}
+
+int rf_engine_create(const rf_model_config* cfg, const rf_runtime_config* rt, rf_engine** out) {
+  if (!cfg || !out) return set_error(RF_EINVAL, "null argument");
+  *out = nullptr;
+  rf_engine* e = new rf_engine();
+  e->cfg = *cfg;
+  if (!e->cfg.head_dim && e->cfg.n_heads) e->cfg.head_dim = e->cfg.n_embd / e->cfg.n_heads;
+  e->rt = rt ? *rt : rf_runtime_config{};
+  e->dev = e->rt.device;
+  int rc = engine_finish_create(e);
+  if (rc) { destroy(e); return rc; }
+  *out = e;
+  return RF_OK;
+}
+
+int rf_engine_create_from_gguf(const void* gguf, uint64_t len, const rf_runtime_config* rt, rf_engine** out) {
+  if (!gguf || !out) return set_error(RF_EINVAL, "null argument");
+  *out = nullptr;
+  rf_engine* e = new rf_engine();
+  int rc = create_from_image((const uint8_t*)gguf, len, rt, e);
+  if (rc) { destroy(e); return rc; }
+  *out = e;
+  return RF_OK;
+}
+
+int rf_engine_create_from_file(const char* path, const rf_runtime_config* rt, rf_engine** out) {
+  if (!path || !out) return set_error(RF_EINVAL, "null argument");
+  *out = nullptr;
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) return set_error(RF_EINVAL, "cannot open '%s'", path);
+  struct stat st;
+  if (fstat(fd, &st) != 0 || st.st_size <= 0) { close(fd); return set_error(RF_EFORMAT, "cannot stat '%s'", path); }
+  void* m = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (m == MAP_FAILED) return set_error(RF_EFORMAT, "cannot map '%s'", path);
+  rf_engine* e = new rf_engine();
+  e->map_addr = m;
+  e->map_len = (uint64_t)st.st_size;
+  int rc = create_from_image((const uint8_t*)m, (uint64_t)st.st_size, rt, e);
+  if (rc) { destroy(e); return rc; }
+  *out = e;
+  return RF_OK;
+}
+
+void rf_engine_destroy(rf_engine* e) { destroy(e); }
+
+int rf_engine_config(const rf_engine* e, rf_model_config* out) {
+  if (!e || !out) return set_error(RF_EINVAL, "null argument");
+  *out = e->cfg;
+  return RF_OK;
+}
+
+int rf_persistent_load(rf_engine* e, const rf_tensor_view* v) {
+  ENGINE_GUARD(e);
+  if (!v) return set_error(RF_EINVAL, "null view");
+  View w;
+  w.type = v->ggml_type;
+  w.ne0 = v->ne0;
+  w.ne1 = v->ne1 ? v->ne1 : 1;
+  w.bytes = v->bytes;
+  w.host = (const uint8_t*)v->host;
+  return load_persistent(e, v->role, w);
+}
+
+int rf_layer_load(rf_engine* e, int layer, const rf_tensor_view* views, int n_views) {
+  ENGINE_GUARD(e);
+  if (layer < 0 || layer >= (int)e->cfg.n_layers) return set_error(RF_EINVAL, "layer %d out of range", layer);
+  if (!views || n_views <= 0) return set_error(RF_EINVAL, "no tensor views");
+  if (e->layers[layer].resident) return set_error(RF_ESTATE, "layer %d is already loaded", layer);
+  View v[9];
+  for (int i = 0; i < n_views; i++) {
+    const rf_tensor_view& t = views[i];
+    if (t.role < 0 || t.role > 8) return set_error(RF_EINVAL, "view %d has role %d (not a layer tensor)", i, t.role);
+    v[t.role].type = t.ggml_type;
+    v[t.role].ne0 = t.ne0;
+    v[t.role].ne1 = t.ne1 ? t.ne1 : 1;
+    v[t.role].bytes = t.bytes;
+    v[t.role].host = (const uint8_t*)t.host;
+  }
+  return load_layer_views(e, layer, v);
+}
+
+int rf_layer_load_gguf(rf_engine* e, int layer) {
+  ENGINE_GUARD(e);
+  if (layer < 0 || layer >= (int)e->cfg.n_layers) return set_error(RF_EINVAL, "layer %d out of range", layer);
+  if (e->layers[layer].resident) return set_error(RF_ESTATE, "layer %d is already loaded", layer);
+  return load_layer_gguf(e, layer);
+}
+
+int rf_layer_release(rf_engine* e, int layer) {
+  ENGINE_GUARD(e);
+  if (layer < 0 || layer >= (int)e->cfg.n_layers) return set_error(RF_EINVAL, "layer %d out of range", layer);
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  return release_layer_impl(e, layer);
+}
+
+int rf_layer_is_resident(const rf_engine* e, int layer) {
+  if (!e || layer < 0 || layer >= (int)e->cfg.n_layers) return 0;
+  return e->layers[layer].resident ? 1 : 0;
+}
+
+int rf_layer_compute(rf_engine* e, int layer, uint32_t pos) {
+  ENGINE_GUARD(e);
+  if (layer < 0 || layer >= (int)e->cfg.n_layers) return set_error(RF_EINVAL, "layer %d out of range", layer);
+  if (!e->layers[layer].resident) return set_error(RF_ESTATE, "layer %d is not loaded", layer);
+  if (pos != e->seq_len)
+    return set_error(RF_EINVAL, "KV position/history mismatch: position %u, history %u", pos, e->seq_len);
+  if (e->seq_len >= e->max_seq) return set_error(RF_ESTATE, "KV cache full");
+  e->h_io->pos = (int)pos;
+  RF_CUDA(cudaMemcpyAsync(&e->d_io->pos, &e->h_io->pos, 4, cudaMemcpyHostToDevice, e->stream));
+  RF_TRY(enqueue_layer(e, layer, false));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  return RF_OK;
+}
+
+int rf_embed(rf_engine* e, uint32_t token) {
+  ENGINE_GUARD(e);
+  if (!e->have_embd) return set_error(RF_ESTATE, "token_embd is not loaded");
+  if (token >= e->cfg.vocab_size) return set_error(RF_EINVAL, "token_id %u out of bounds", token);
+  e->h_io->token = token;
+  RF_CUDA(cudaMemcpyAsync(&e->d_io->token, &e->h_io->token, 4, cudaMemcpyHostToDevice, e->stream));
+  RF_CUDA(launch_embed(Launch{e->stream, false}, e->embd, &e->d_io->token, e->hidden, e->d_key));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  return RF_OK;
+}
+
+int rf_hidden_write(rf_engine* e, const float* host, uint32_t n) {
+  ENGINE_GUARD(e);
+  if (!host || n != e->cfg.n_embd) return set_error(RF_EINVAL, "hidden size mismatch: expected %u", e->cfg.n_embd);
+  RF_CUDA(cudaMemcpy(e->hidden, host, 4ull * n, cudaMemcpyHostToDevice));
+  return RF_OK;
+}
+
+int rf_hidden_read(rf_engine* e, float* host, uint32_t n) {
+  ENGINE_GUARD(e);
+  if (!host || n != e->cfg.n_embd) return set_error(RF_EINVAL, "hidden size mismatch: expected %u", e->cfg.n_embd);
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  RF_CUDA(cudaMemcpy(host, e->hidden, 4ull * n, cudaMemcpyDeviceToHost));
+  return RF_OK;
+}
+
+int rf_kv_commit(rf_engine* e) {
+  ENGINE_GUARD(e);
+  if (e->seq_len >= e->max_seq) return set_error(RF_ESTATE, "KV cache full");
+  e->seq_len++;
+  return RF_OK;
+}
+
+int rf_forward_token(rf_engine* e, uint32_t token, uint32_t pos, float* final_hidden) {
+  ENGINE_GUARD(e);
+  RF_TRY(check_step(e, token, pos));
+  RF_TRY(set_io(e, token, pos));
+  RF_TRY(launch_step(e, false));
+  e->seq_len++;
+  if (final_hidden) {
+    RF_CUDA(cudaMemcpyAsync(final_hidden, e->final_hidden, 4ull * e->cfg.n_embd, cudaMemcpyDeviceToHost, e->stream));
+  }
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  return RF_OK;
+}
+
+int rf_compute_logits(rf_engine* e, float* logits, uint32_t* argmax) {
+  ENGINE_GUARD(e);
+  RF_TRY(enqueue_logits(e, false, logits != nullptr));
+  if (logits) {
+    if (e->tp > 1) {
+      RF_NCCL(nccl()->allGather(e->logits, e->logits_all, e->vocab_chunk, ncclFloat32, e->comm, e->stream));
+      RF_CUDA(cudaMemcpyAsync(logits, e->logits_all, 4ull * e->cfg.vocab_size, cudaMemcpyDeviceToHost, e->stream));
+    } else {
+      RF_CUDA(cudaMemcpyAsync(logits, e->logits, 4ull * e->cfg.vocab_size, cudaMemcpyDeviceToHost, e->stream));
+    }
+  }
+  RF_CUDA(cudaMemcpyAsync(e->h_key, e->d_key, 8, cudaMemcpyDeviceToHost, e->stream));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  if (argmax) *argmax = ~(uint32_t)(*e->h_key & 0xFFFFFFFFull);
+  return RF_OK;
+}
+
+int rf_decode_step(rf_engine* e, uint32_t token, uint32_t* next_token) {
+  ENGINE_GUARD(e);
+  RF_TRY(check_step(e, token, e->seq_len));
+  RF_TRY(set_io(e, token, e->seq_len));
+  RF_TRY(launch_step(e, true));
+  e->seq_len++;
+  RF_CUDA(cudaMemcpyAsync(e->h_tok, &e->d_io->token, 4, cudaMemcpyDeviceToHost, e->stream));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  if (next_token) *next_token = e->h_tok[0];
+  return RF_OK;
+}
+
+int rf_generate(rf_engine* e, const uint32_t* prompt, uint32_t n_prompt, uint32_t n_new, uint32_t* out) {
+  ENGINE_GUARD(e);
+  if (!prompt || n_prompt == 0) return set_error(RF_EINVAL, "empty prompt");
+  if (n_new && !out) return set_error(RF_EINVAL, "null output");
+  if ((uint64_t)e->seq_len + n_prompt + n_new > e->max_seq + 1ull)
+    return set_error(RF_ESTATE, "prompt + generation exceed the KV capacity %u", e->max_seq);
+  for (uint32_t i = 0; i < n_prompt; i++)
+    if (prompt[i] >= e->cfg.vocab_size) return set_error(RF_EINVAL, "token_id %u out of bounds", prompt[i]);
+  RF_TRY(ensure_ready(e));
+  // prompt tokens except the last: forward only (inference.rs:578-592)
+  for (uint32_t i = 0; i + 1 < n_prompt; i++) {
+    RF_TRY(set_io(e, prompt[i], e->seq_len));
+    RF_TRY(launch_step(e, false));
+    e->seq_len++;
+  }
+  if (n_new == 0) {
+    RF_TRY(set_io(e, prompt[n_prompt - 1], e->seq_len));
+    RF_TRY(launch_step(e, false));
+    e->seq_len++;
+    RF_CUDA(cudaStreamSynchronize(e->stream));
+    return RF_OK;
+  }
+  // The last prompt token and every generated token but the last go through
+  // decode steps whose argmax feeds the next step on the device (the reference
+  // forwards each sampled token except the final one, inference.rs:595-712).
+  return decode_loop(e, prompt[n_prompt - 1], n_new, out, nullptr);
+}
+
+int rf_decode_timed(rf_engine* e, uint32_t token, uint32_t n_steps, uint32_t* out_tokens, float* device_ms) {
+  ENGINE_GUARD(e);
+  if (token >= e->cfg.vocab_size) return set_error(RF_EINVAL, "token_id %u out of bounds", token);
+  if ((uint64_t)e->seq_len + n_steps > e->max_seq)
+    return set_error(RF_ESTATE, "%u steps exceed the KV capacity %u at length %u", n_steps, e->max_seq, e->seq_len);
+  RF_TRY(ensure_ready(e));
+  return decode_loop(e, token, n_steps, out_tokens, device_ms);
+}
+
+int rf_step_kernel_count(const rf_engine* e, uint32_t* out) {
+  if (!e || !out) return set_error(RF_EINVAL, "null argument");
+  *out = 5u * e->cfg.n_layers + 4u;  // embed, 5 per layer, output norm, LM head, advance
+  return RF_OK;
+}
+
+int rf_bench_layer_kernels(rf_engine* e, uint32_t iters, float* avg_ms5) {
+  ENGINE_GUARD(e);
+  if (!avg_ms5 || iters == 0) return set_error(RF_EINVAL, "bad arguments");
+  if (!all_resident(e)) return set_error(RF_ESTATE, "every layer must be resident");
+  if (e->seq_len >= e->max_seq) return set_error(RF_ESTATE, "KV cache full");
+  e->h_io->pos = (int)e->seq_len;
+  RF_CUDA(cudaMemcpyAsync(&e->d_io->pos, &e->h_io->pos, 4, cudaMemcpyHostToDevice, e->stream));
+  cudaEvent_t a, b;
+  RF_CUDA(cudaEventCreate(&a));
+  RF_CUDA(cudaEventCreate(&b));
+  int rc = RF_OK;
+  for (int k = 0; k < 5 && !rc; k++) {
+    cudaEventRecord(a, e->stream);
+    for (uint32_t it = 0; it < iters && !rc; it++)
+      for (uint32_t l = 0; l < e->cfg.n_layers && !rc; l++) rc = enqueue_layer_kernel(e, (int)l, k);
+    cudaEventRecord(b, e->stream);
+    cudaError_t ce = cudaEventSynchronize(b);
+    float ms = 0.f;
+    if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, a, b);
+    if (ce != cudaSuccess && !rc) rc = set_error(RF_ECUDA, "kernel timing failed: %s", cudaGetErrorString(ce));
+    avg_ms5[k] = ms / (float)(iters * e->cfg.n_layers);
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  return rc;
+}
+
+int rf_kv_reset(rf_engine* e) {
+  ENGINE_GUARD(e);
+  e->seq_len = 0;
+  return RF_OK;
+}
+
+int rf_kv_seq_len(const rf_engine* e, uint32_t* out) {
+  if (!e || !out) return set_error(RF_EINVAL, "null argument");
+  *out = e->seq_len;
+  return RF_OK;
+}
+
+int rf_kv_read(const rf_engine* ec, int layer, int which_v, uint32_t start, uint32_t end, float* host) {
+  rf_engine* e = const_cast<rf_engine*>(ec);
+  ENGINE_GUARD(e);
+  if (layer < 0 || layer >= (int)e->cfg.n_layers || start > end || end > e->seq_len || !host)
+    return set_error(RF_EINVAL, "KV read range [%u,%u) of layer %d invalid (history %u)", start, end, layer, e->seq_len);
+  if (end == start) return RF_OK;
+  const uint64_t n = (uint64_t)(end - start) * e->kvh_local * e->cfg.head_dim;
+  float* tmp = nullptr;
+  RF_CUDA(cudaMalloc(&tmp, n * 4));
+  cudaError_t ce = launch_kv_gather(which_v ? e->vc[layer] : e->kc[layer], e->rt.kv_f32, e->kvh_local, e->max_seq,
+                                    e->cfg.head_dim, start, end, tmp, e->stream);
+  if (ce == cudaSuccess) ce = cudaMemcpyAsync(host, tmp, n * 4, cudaMemcpyDeviceToHost, e->stream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
+  cudaFree(tmp);
+  if (ce != cudaSuccess) return set_error(RF_ECUDA, "KV read failed: %s", cudaGetErrorString(ce));
+  return RF_OK;
+}
+
+int rf_budget_total(const rf_engine* e, uint64_t* out) {
+  if (!e || !out) return set_error(RF_EINVAL, "null argument");
+  *out = e->budget.total();
+  return RF_OK;
+}
+int rf_budget_used(const rf_engine* e, uint64_t* out) {
+  if (!e || !out) return set_error(RF_EINVAL, "null argument");
+  *out = e->budget.used();
+  return RF_OK;
+}
+int rf_budget_available(const rf_engine* e, uint64_t* out) {
+  if (!e || !out) return set_error(RF_EINVAL, "null argument");
+  *out = e->budget.available();
+  return RF_OK;
+}
+
+int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uint64_t vram_weight_budget_bytes) {
+  ENGINE_GUARD(e);
+  if (!mask) return set_error(RF_EINVAL, "null residency mask");
+  if (ring_slots < 0) return set_error(RF_EINVAL, "ring_slots must be >= 0");
+  uint64_t resident_bytes = 0;
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++)
+    if (mask[l] && e->layers[l].resident) resident_bytes += e->layers[l].bytes;
+  if (vram_weight_budget_bytes && resident_bytes > vram_weight_budget_bytes)
+    return set_error(RF_ENOMEM, "resident layers need %llu bytes, weight budget is %llu",
+                     (unsigned long long)resident_bytes, (unsigned long long)vram_weight_budget_bytes);
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
+    e->plan_resident[l] = mask[l] ? 1 : 0;
+    if (!mask[l] && e->layers[l].resident) {
+      RF_TRY(release_layer_impl(e, (int)l));
+      e->stats.evictions++;
+    }
+  }
+  e->rt.ring_slots = ring_slots;
+  return RF_OK;
+}
+
+int rf_residency_stats_get(const rf_engine* e, rf_residency_stats* out) {
+  if (!e || !out) return set_error(RF_EINVAL, "null argument");
+  *out = e->stats;
+  out->peak_bytes = e->budget.peak();
+  return RF_OK;
+}
+
+int rf_tp_unique_id(uint8_t* out128) {
+  if (!out128) return set_error(RF_EINVAL, "null argument");
+  if (!nccl()) return set_error(RF_ENCCL, "libnccl.so.2 could not be loaded");
+  ncclUniqueId id;
+  RF_NCCL(nccl()->getUniqueId(&id));
+  memcpy(out128, &id, sizeof id);
+  return RF_OK;
+}
+
+}  // extern "C"

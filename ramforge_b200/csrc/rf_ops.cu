@@ -1,0 +1,167 @@
+// rf_ops.cu - standalone device-pointer ops of include/rfcuda.h: packed
+// matrices + quantized matvec (benchmark config 2) and batched GQA decode
+// attention (benchmark config 3).
+#include <mutex>
+#include <unordered_map>
+
+#include "rf_common.h"
+
+using namespace rf;
+
+struct rf_matrix {
+  PackedMat m{};
+  void* block = nullptr;
+  uint64_t bytes = 0;
+  int device = 0;
+};
+
+namespace {
+// Per-device split-K workspace for rf_decode_attention: partial sums and the
+// per-(sequence, KV head) arrival counters (zero at rest; the last CTA of a
+// head resets its counter).  Grown on demand, never shrunk.
+struct AttnWorkspace {
+  float* part = nullptr;
+  size_t part_floats = 0;
+  unsigned* counters = nullptr;
+  size_t n_counters = 0;
+};
+std::mutex g_ws_mu;
+std::unordered_map<int, AttnWorkspace> g_ws;
+
+int workspace(int dev, size_t part_floats, size_t n_counters, AttnWorkspace** out) {
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  AttnWorkspace& w = g_ws[dev];
+  if (w.part_floats < part_floats) {
+    if (w.part) cudaFree(w.part);
+    w.part = nullptr;
+    w.part_floats = 0;
+    RF_CUDA(cudaMalloc(&w.part, part_floats * sizeof(float)));
+    w.part_floats = part_floats;
+  }
+  if (w.n_counters < n_counters) {
+    if (w.counters) cudaFree(w.counters);
+    w.counters = nullptr;
+    w.n_counters = 0;
+    RF_CUDA(cudaMalloc(&w.counters, n_counters * sizeof(unsigned)));
+    RF_CUDA(cudaMemset(w.counters, 0, n_counters * sizeof(unsigned)));
+    w.n_counters = n_counters;
+  }
+  *out = &w;
+  return RF_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int rf_matrix_create(int type, const void* bytes, uint64_t nbytes, int on_device, uint32_t n_out, uint32_t n_in,
+                     rf_matrix** out) {
+  if (!bytes || !out) return set_error(RF_EINVAL, "null argument");
+  *out = nullptr;
+  PackedMat g;
+  if (!packed_geometry(type, n_out, n_in, &g))
+    return set_error(RF_EINVAL, "type %d cannot hold a %u x %u matrix", type, n_out, n_in);
+  const uint64_t row_bytes = (uint64_t)(n_in / block_elems(type)) * block_bytes(type);
+  if (nbytes < row_bytes * n_out)
+    return set_error(RF_EINVAL, "weight truncated: expected %llu bytes, got %llu",
+                     (unsigned long long)(row_bytes * n_out), (unsigned long long)nbytes);
+  rf_matrix* m = new rf_matrix();
+  cudaGetDevice(&m->device);
+  const uint64_t qs_b = (g.qs_stride * n_out + 255) & ~255ull, sc_b = (g.sc_stride * n_out + 255) & ~255ull;
+  m->bytes = qs_b + (sc_b ? sc_b : 256);
+  cudaError_t ce = cudaMalloc(&m->block, m->bytes);
+  if (ce != cudaSuccess) {
+    delete m;
+    return set_error(RF_ENOMEM, "cudaMalloc(%llu) failed: %s", (unsigned long long)qs_b, cudaGetErrorString(ce));
+  }
+  m->m = g;
+  m->m.qs = (uint8_t*)m->block;
+  m->m.sc = (uint8_t*)m->block + qs_b;
+  if (on_device) {
+    ce = launch_pack((const uint8_t*)bytes, nullptr, m->m, 0);
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+  } else {
+    HostPacked hp;
+    std::vector<int> rows(n_out);
+    for (uint32_t r = 0; r < n_out; r++) rows[r] = (int)r;
+    int rc = host_packed_init(type, n_out, n_in, &hp);
+    if (!rc) rc = pack_rows((const uint8_t*)bytes, row_bytes, 0, rows, &hp, 0, 1);
+    if (rc) {
+      cudaFree(m->block);
+      delete m;
+      return rc;
+    }
+    ce = cudaMemcpy(m->m.qs, hp.qs.data(), hp.qs.size(), cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess && !hp.sc.empty()) ce = cudaMemcpy(m->m.sc, hp.sc.data(), hp.sc.size(), cudaMemcpyHostToDevice);
+  }
+  if (ce != cudaSuccess) {
+    cudaFree(m->block);
+    delete m;
+    return set_error(RF_ECUDA, "packing failed: %s", cudaGetErrorString(ce));
+  }
+  *out = m;
+  return RF_OK;
+}
+
+void rf_matrix_destroy(rf_matrix* m) {
+  if (!m) return;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(m->device);
+  cudaFree(m->block);
+  cudaSetDevice(cur);
+  delete m;
+}
+
+uint64_t rf_matrix_device_bytes(const rf_matrix* m) { return m ? m->bytes : 0; }
+
+int rf_qmatvec(const rf_matrix* m, const float* dX, float* dY, int batch, void* stream) {
+  if (!m || !dX || !dY) return set_error(RF_EINVAL, "null argument");
+  if (batch < 1 || batch > 8) return set_error(RF_EINVAL, "batch %d out of range 1..8", batch);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (batch == 1) {
+    RF_CUDA(gemv_store(Launch{s, false}, m->m, dX, nullptr, 0.f, dY));
+    return RF_OK;
+  }
+  if (m->m.K != m->m.Kp)
+    return set_error(RF_EUNSUPPORTED, "batched matvec needs n_in to be a multiple of %u", m->m.Kp - m->m.K + m->m.K);
+  RF_CUDA(gemv_batched(s, m->m, dX, batch, dY));
+  return RF_OK;
+}
+
+int rf_decode_attention(const float* dQ, const uint16_t* dK, const uint16_t* dV, int ctx, int n_heads, int n_kv_heads,
+                        int head_dim, int batch, float* dOut, void* stream) {
+  if (!dQ || !dK || !dV || !dOut) return set_error(RF_EINVAL, "null argument");
+  if (ctx <= 0 || batch <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || head_dim <= 0 || head_dim > 128)
+    return set_error(RF_EINVAL, "invalid attention shape");
+  const int G = n_heads / n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return set_error(RF_EUNSUPPORTED, "GQA group %d unsupported", G);
+  int dev = 0;
+  RF_CUDA(cudaGetDevice(&dev));
+  const int max_splits = std::max(32, (ctx + 511) / 512);
+  AttnWorkspace* w = nullptr;
+  RF_TRY(workspace(dev, attn_part_floats(batch, n_kv_heads, max_splits, G, head_dim),
+                   (size_t)batch * n_kv_heads, &w));
+  AttnArgs a{};
+  a.q = dQ;
+  a.kc = dK;
+  a.vc = dV;
+  a.head_stride = (uint64_t)ctx * head_dim;
+  a.batch_stride = (uint64_t)n_kv_heads * ctx * head_dim;
+  a.k_cur = nullptr;
+  a.v_cur = nullptr;
+  a.d_nhist = nullptr;
+  a.nhist = ctx;
+  a.n_heads = n_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.batch = batch;
+  a.max_splits = max_splits;
+  a.part = w->part;
+  a.counters = w->counters;
+  a.out = dOut;
+  a.kv_f32 = 0;
+  RF_CUDA(launch_attention(Launch{(cudaStream_t)stream, false}, a));
+  return RF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,120 @@
+"""GPU parity of the standalone kernels against the CPU oracle.
+
+Tolerances: quantized matvec max|y - y_ref| <= 2e-4 * max|y_ref| (f32
+reassociation only: the engine sums per sub-block and across lanes, the
+reference sums sequentially); attention max|o - o_ref| <= 1e-4 * max|o_ref| + 1e-6;
+embedding rows and per-element dequantisation are bit-exact.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from ramforge_b200 import QMatrix, decode_attention, synth
+
+pytestmark = pytest.mark.gpu
+THREADS = min(32, os.cpu_count() or 8)
+
+
+def torch_mod():
+    import torch
+    return torch
+
+
+def _weights(gtype, M, K, seed=1):
+    w = synth.normal(seed, 100 + gtype, M * K, std=0.02).reshape(M, K)
+    return synth.quantize(gtype, w)
+
+
+def _run_qmv(gtype, M, K, batch=1, seed=1, raw=None):
+    torch = torch_mod()
+    raw = _weights(gtype, M, K, seed) if raw is None else raw
+    x = synth.normal(seed, 7, batch * K, std=1.0).reshape(batch, K)
+    m = QMatrix(gtype, raw, M, K)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty(batch, M, device="cuda")
+    m.matvec(dx.data_ptr(), dy.data_ptr(), batch)
+    torch.cuda.synchronize()
+    y = dy.cpu().numpy()
+    for b in range(batch):
+        ref = orc.matvec(gtype, raw, K, M, x[b], threads=THREADS)
+        err = np.abs(y[b] - ref).max()
+        assert err <= 2e-4 * np.abs(ref).max() + 1e-6, (gtype, M, K, b, err, np.abs(ref).max())
+    m.close()
+
+
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.F16, synth.F32])
+@pytest.mark.parametrize("M,K", [(1, 256), (7, 512), (33, 768), (130, 2304), (257, 4096)])
+def test_qmatvec_small_shapes(gtype, M, K):
+    _run_qmv(gtype, M, K)
+
+
+@pytest.mark.parametrize("gtype,M,K", [(synth.Q8_0, 5, 32), (synth.Q4_0, 3, 32), (synth.Q4_0, 2, 96),
+                                       (synth.Q8_0, 9, 160), (synth.F32, 3, 8), (synth.F32, 2, 12)])
+def test_qmatvec_ragged_rows_padded_to_units(gtype, M, K):
+    _run_qmv(gtype, M, K)
+
+
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K])
+@pytest.mark.parametrize("M,K", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
+def test_qmatvec_config2_shapes(gtype, M, K):
+    _run_qmv(gtype, M, K)
+
+
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K])
+@pytest.mark.parametrize("batch", [4, 8])
+def test_qmatvec_batched(gtype, batch):
+    _run_qmv(gtype, 1024, 4096, batch=batch)
+
+
+def test_qmatvec_subnormal_scales_follow_reference_decode():
+    # A Q8_0 block whose f16 scale is subnormal: the reference decodes it at half
+    # its IEEE value (quant.rs:40-65); the GPU must agree.
+    raw = bytearray(_weights(synth.Q8_0, 4, 64))
+    for r in range(4):
+        raw[r * 68:r * 68 + 2] = (0x0155 + r).to_bytes(2, "little")
+    _run_qmv(synth.Q8_0, 4, 64, raw=np.frombuffer(bytes(raw), np.uint8))
+
+
+@pytest.mark.parametrize("ctx", [1, 5, 512, 2048, 8192, 32768])
+@pytest.mark.parametrize("batch", [1, 8])
+def test_decode_attention_config3(ctx, batch):
+    torch = torch_mod()
+    H, KV, hd = 32, 8, 128
+    if ctx == 32768 and batch == 8:
+        batch = 2  # oracle time; the kernel path is the same
+    q = synth.normal(2, 1, batch * H * hd).reshape(batch, H, hd)
+    k = synth.normal(2, 2, batch * KV * ctx * hd).reshape(batch, KV, ctx, hd).astype(np.float16)
+    v = synth.normal(2, 3, batch * KV * ctx * hd).reshape(batch, KV, ctx, hd).astype(np.float16)
+    dq = torch.from_numpy(q).cuda()
+    dk = torch.from_numpy(k.view(np.uint16)).cuda()
+    dv = torch.from_numpy(v.view(np.uint16)).cuda()
+    do = torch.empty(batch, H, hd, device="cuda")
+    decode_attention(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ctx, H, KV, hd, batch, do.data_ptr())
+    torch.cuda.synchronize()
+    out = do.cpu().numpy()
+    for b in range(batch):
+        # reference layout [pos][kv_head][hd]: history = first ctx-1 positions, current = last
+        kk = k[b].astype(np.float32).transpose(1, 0, 2)
+        vv = v[b].astype(np.float32).transpose(1, 0, 2)
+        ref = orc.attention(q[b], kk[:-1], vv[:-1], kk[-1], vv[-1], ctx - 1, H, KV, hd)
+        err = np.abs(out[b].reshape(-1) - ref).max()
+        assert err <= 1e-4 * np.abs(ref).max() + 1e-6, (ctx, b, err)
+
+
+def test_decode_attention_repeated_calls_reuse_workspace():
+    torch = torch_mod()
+    H, KV, hd, ctx = 32, 8, 128, 3000
+    q = torch.randn(1, H, hd, device="cuda")
+    k = torch.randn(1, KV, ctx, hd, device="cuda").half()
+    v = torch.randn(1, KV, ctx, hd, device="cuda").half()
+    outs = []
+    for _ in range(3):
+        o = torch.empty(1, H, hd, device="cuda")
+        decode_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ctx, H, KV, hd, 1, o.data_ptr())
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    ref = torch.softmax((q.view(1, KV, 4, hd) @ k.float().transpose(-1, -2)) / hd ** 0.5, -1) @ v.float()
+    assert torch.allclose(outs[0], ref.view(1, H, hd), atol=1e-4, rtol=1e-4)
