@@ -196,6 +196,24 @@ def run_reference(args, spec):
     print(json.dumps(line), flush=True)
 
 
+def run_profile(args, spec):
+    """--profile: the same model shape (optionally fewer layers) run eagerly for a
+    handful of launches, so an ncu capture of it stays small and ends by itself:
+    4 prompt tokens, then 2 greedy decode steps (5 kernels per layer + 4)."""
+    import torch
+    from ramforge_b200 import DecodeEngine, synth
+    if args.layers:
+        spec = synth.scaled(spec, name=f"{spec.name}-{args.layers}l", n_layers=args.layers)
+    torch.cuda.set_device(0)
+    g = synth.gguf_bytes(spec)
+    eng = DecodeEngine(g, device=0, max_seq_len=64, disable_graphs=True)
+    first = int(eng.generate([11, 22, 33, 44], 1)[0])
+    toks, ms = eng.decode_timed(first, 2)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_run": spec.name, "layers": spec.n_layers, "tokens": toks.tolist(), "ms": ms}))
+    eng.close()
+
+
 def workload_config(spec, args, tp):
     return {"workload": "llama-3-8b-shape Q4_K batch-1 greedy decode (BASELINE configs[3])",
             "layers": spec.n_layers, "dim": spec.n_embd, "heads": f"{spec.n_heads}q/{spec.n_kv_heads}kv",
@@ -212,6 +230,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="small eager run for ncu captures")
+    ap.add_argument("--layers", type=int, default=0, help="with --profile: layer count of the model")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -222,6 +242,9 @@ def main():
     if args.impl == "reference":
         if rank == 0:
             run_reference(args, spec)
+        return
+    if args.profile:
+        run_profile(args, spec)
         return
 
     import torch

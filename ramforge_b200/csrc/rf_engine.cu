@@ -233,7 +233,7 @@ int setup_geometry(rf_engine* e) {
   e->vocab_local = sh.vocab_rows;
   e->max_seq = e->rt.max_seq_len ? e->rt.max_seq_len : c.context_length;
   if (!e->max_seq) return set_error(RF_EINVAL, "max_seq_len is zero");
-  e->max_splits = std::max<int>(32, (int)((e->max_seq + 511) / 512));
+  e->max_splits = std::max<int>(64, (int)((e->max_seq + 511) / 512));
   return RF_OK;
 }
 
@@ -282,7 +282,8 @@ int engine_init_device(rf_engine* e) {
   }
   auto tab = rope_table(e->max_seq, c.head_dim, c.rope_theta);
   RF_CUDA(cudaMemcpy(e->rope_cs, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
-  RF_CUDA(cudaMallocHost((void**)&e->h_io, sizeof(StepIO)));
+  // one pinned {token, pos} slot per position: asynchronous steps never share a source slot
+  RF_CUDA(cudaMallocHost((void**)&e->h_io, sizeof(StepIO) * (e->max_seq + 1)));
   RF_CUDA(cudaMallocHost((void**)&e->h_tok, 4 * 4096));
   RF_CUDA(cudaMallocHost((void**)&e->h_key, 8));
   if (e->tp > 1) {
@@ -679,10 +680,14 @@ int launch_step(rf_engine* e, bool decode) {
   return RF_OK;
 }
 
+// Queue the step inputs.  The copy reads pinned slot `pos`, which no other
+// in-flight step uses (positions are distinct until the KV cache is reset, and
+// every entry point that reuses positions synchronises before returning).
 int set_io(rf_engine* e, uint32_t token, uint32_t pos) {
-  e->h_io->token = token;
-  e->h_io->pos = (int)pos;
-  RF_CUDA(cudaMemcpyAsync(e->d_io, e->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, e->stream));
+  StepIO* slot = e->h_io + std::min<uint32_t>(pos, e->max_seq);
+  slot->token = token;
+  slot->pos = (int)pos;
+  RF_CUDA(cudaMemcpyAsync(e->d_io, slot, sizeof(StepIO), cudaMemcpyHostToDevice, e->stream));
   return RF_OK;
 }
 

@@ -104,31 +104,63 @@ __device__ void stage_x(const float* __restrict__ x, const float* __restrict__ n
                         float* sx, float* sxs, float* sred, bool need_xs) {
   float rms = 1.f;
   if (nw) rms = rms_of(block_sumsq(x, K, sred), K, eps);
-  for (int e = threadIdx.x; e < Kp; e += GEMV_THREADS) {
+  // warp w stages 32-element chunks w, w+8, ...: coalesced loads, and the chunk
+  // sums sum(x) that the Q4_K min term needs come from one shuffle reduction
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int c = warp; c * 32 < Kp; c += GEMV_WARPS) {
+    const int e = c * 32 + lane;
     float v = 0.f;
     if (e < K) {
-      float xv = x[e];
+      const float xv = x[e];
       v = nw ? xv / rms * nw[e] : xv;
     }
-    sx[swz<EPU>(e)] = v;
+    if (e < Kp) sx[swz<EPU>(e)] = v;
+    if (need_xs) {
+      float s = v;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) sxs[c] = s;
+    }
   }
   __syncthreads();
-  if (need_xs) {
-    for (int g = threadIdx.x; g < Kp / 32; g += GEMV_THREADS) {
-      float s = 0.f;
-      for (int l = 0; l < 32; l++) s += sx[swz<EPU>(g * 32 + l)];
-      sxs[g] = s;
-    }
-    __syncthreads();
-  }
 }
 
 // ---------------------------------------------------------------------------
-// per-unit dot products: 32 bytes of one row against its EPU activations
+// per-unit dot products: 32 bytes of each of R rows against the unit's EPU
+// activations, accumulated into acc[R].  x is read one 16-byte chunk at a time
+// and reused across the rows, so only a few activations are live at once.
 // ---------------------------------------------------------------------------
 // XA(c) returns the float4 of unit-relative elements [4c, 4c+4).
 template <int FMT>
 struct UnitDot;
+
+// Q4_K super-block header fields of sub-block pair i = u%4 (get_scale_min,
+// quant.rs:216-226, for j = 2i and 2i+1): d*sc and dmin*m for both sub-blocks.
+__device__ __forceinline__ void q4k_scales(const uint8_t* sc_row, int u, float& d1, float& mn1, float& d2,
+                                           float& mn2) {
+  const uint4 h = __ldg(reinterpret_cast<const uint4*>(sc_row + (size_t)(u >> 2) * 16));
+  const float d = h2f(h.x & 0xFFFFu), dmin = h2f(h.x >> 16);
+  const int i = u & 3;
+  uint32_t sc0, m0, sc1, m1;
+  if (i < 2) {
+    const uint32_t a = h.y >> (16 * i), b = h.z >> (16 * i);  // s[2i], s[2i+1] / s[2i+4], s[2i+5]
+    sc0 = a & 63u;
+    sc1 = (a >> 8) & 63u;
+    m0 = b & 63u;
+    m1 = (b >> 8) & 63u;
+  } else {
+    const int k = i - 2;  // j = 4+2k, 5+2k: low 4 bits in s[8+2k], s[9+2k]; high 2 bits in s[2k..], s[4+2k..]
+    const uint32_t lo = h.w >> (16 * k), hs = h.y >> (16 * k), hm = h.z >> (16 * k);
+    sc0 = (lo & 0xFu) | (((hs >> 6) & 3u) << 4);
+    sc1 = ((lo >> 8) & 0xFu) | (((hs >> 14) & 3u) << 4);
+    m0 = ((lo >> 4) & 0xFu) | (((hm >> 6) & 3u) << 4);
+    m1 = ((lo >> 12) & 0xFu) | (((hm >> 14) & 3u) << 4);
+  }
+  d1 = d * (float)sc0;
+  mn1 = dmin * (float)m0;
+  d2 = d * (float)sc1;
+  mn2 = dmin * (float)m1;
+}
 
 template <>
 struct UnitDot<T_Q4_K> {
@@ -138,43 +170,34 @@ struct UnitDot<T_Q4_K> {
   // (low nibble, sub-block 2i) and element 32+l (high nibble, sub-block 2i+1).
   // value = d*sc*q - dmin*m (quant.rs:235-248), summed as
   // (d*sc) * sum(q*x) - (dmin*m) * sum(x).
-  template <class XA>
-  __device__ __forceinline__ static float dot(const uint32_t (&w)[8], XA xa, const uint8_t* sc_row, int u,
-                                              float xs_lo, float xs_hi) {
-    const uint4 h = __ldg(reinterpret_cast<const uint4*>(sc_row + (size_t)(u >> 2) * 16));
-    const float d = h2f(h.x & 0xFFFFu), dmin = h2f(h.x >> 16);
-    const int i = u & 3;
-    // get_scale_min (quant.rs:216-226) for j = 2i, 2i+1
-    uint32_t sc0, m0, sc1, m1;
-    if (i < 2) {
-      const uint32_t a = h.y >> (16 * i), b = h.z >> (16 * i);  // bytes s[2i], s[2i+1] / s[2i+4], s[2i+5]
-      sc0 = a & 63u; sc1 = (a >> 8) & 63u;
-      m0 = b & 63u; m1 = (b >> 8) & 63u;
-    } else {
-      const int k = i - 2;  // j = 4+2k, 5+2k: low parts in s[8+2k], s[9+2k]; high bits in s[2k..], s[4+2k..]
-      const uint32_t lo = h.w >> (16 * k), hs = h.y >> (16 * k), hm = h.z >> (16 * k);
-      sc0 = (lo & 0xFu) | (((hs >> 6) & 3u) << 4);
-      sc1 = ((lo >> 8) & 0xFu) | (((hs >> 14) & 3u) << 4);
-      m0 = ((lo >> 4) & 0xFu) | (((hm >> 6) & 3u) << 4);
-      m1 = ((lo >> 12) & 0xFu) | (((hm >> 14) & 3u) << 4);
-    }
-    const float d1 = d * (float)sc0, mn1 = dmin * (float)m0;
-    const float d2 = d * (float)sc1, mn2 = dmin * (float)m1;
-    float lo0 = 0.f, lo1 = 0.f, hi0 = 0.f, hi1 = 0.f;
+  template <int R, class XA>
+  __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&srow)[R],
+                                               int u, float xs_lo, float xs_hi, float (&acc)[R]) {
+    float lo[R], hi[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) lo[r] = hi[r] = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      const uint32_t v = w[k];
       const float4 a = xa(k), b = xa(8 + k);
-      lo0 = fmaf(nib<0>(v, 0), a.x, lo0);
-      lo1 = fmaf(nib<0>(v, 8), a.y, lo1);
-      lo0 = fmaf(nib<0>(v, 16), a.z, lo0);
-      lo1 = fmaf(nib<0>(v, 24), a.w, lo1);
-      hi0 = fmaf(nib<0>(v, 4), b.x, hi0);
-      hi1 = fmaf(nib<0>(v, 12), b.y, hi1);
-      hi0 = fmaf(nib<0>(v, 20), b.z, hi0);
-      hi1 = fmaf(nib<0>(v, 28), b.w, hi1);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint32_t v = w[r][k];
+        lo[r] = fmaf(nib<0>(v, 0), a.x, lo[r]);
+        hi[r] = fmaf(nib<0>(v, 4), b.x, hi[r]);
+        lo[r] = fmaf(nib<0>(v, 8), a.y, lo[r]);
+        hi[r] = fmaf(nib<0>(v, 12), b.y, hi[r]);
+        lo[r] = fmaf(nib<0>(v, 16), a.z, lo[r]);
+        hi[r] = fmaf(nib<0>(v, 20), b.z, hi[r]);
+        lo[r] = fmaf(nib<0>(v, 24), a.w, lo[r]);
+        hi[r] = fmaf(nib<0>(v, 28), b.w, hi[r]);
+      }
     }
-    return d1 * (lo0 + lo1) - mn1 * xs_lo + (d2 * (hi0 + hi1) - mn2 * xs_hi);
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      float d1, mn1, d2, mn2;
+      q4k_scales(srow[r], u, d1, mn1, d2, mn2);
+      acc[r] += d1 * lo[r] - mn1 * xs_lo + (d2 * hi[r] - mn2 * xs_hi);
+    }
   }
 };
 
@@ -184,33 +207,41 @@ struct UnitDot<T_Q4_0> {
   static constexpr bool NEED_XS = false;
   // Unit u = blocks 2u, 2u+1: block byte j holds element j (low) and 16+j (high);
   // value (q-8)*d (quant.rs:104-112).
-  template <class XA>
-  __device__ __forceinline__ static float dot(const uint32_t (&w)[8], XA xa, const uint8_t* sc_row, int u,
-                                              float, float) {
-    const uint32_t dd = __ldg(reinterpret_cast<const uint32_t*>(sc_row) + u);
-    float s0a = 0.f, s0b = 0.f, s1a = 0.f, s1b = 0.f;
+  template <int R, class XA>
+  __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&srow)[R],
+                                               int u, float, float, float (&acc)[R]) {
+    float s0[R], s1[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) s0[r] = s1[r] = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
-      const uint32_t v0 = w[k], v1 = w[4 + k];
       const float4 a = xa(k), b = xa(4 + k), c = xa(8 + k), e = xa(12 + k);
-      s0a = fmaf(nib<8>(v0, 0), a.x, s0a);
-      s0b = fmaf(nib<8>(v0, 8), a.y, s0b);
-      s0a = fmaf(nib<8>(v0, 16), a.z, s0a);
-      s0b = fmaf(nib<8>(v0, 24), a.w, s0b);
-      s0a = fmaf(nib<8>(v0, 4), b.x, s0a);
-      s0b = fmaf(nib<8>(v0, 12), b.y, s0b);
-      s0a = fmaf(nib<8>(v0, 20), b.z, s0a);
-      s0b = fmaf(nib<8>(v0, 28), b.w, s0b);
-      s1a = fmaf(nib<8>(v1, 0), c.x, s1a);
-      s1b = fmaf(nib<8>(v1, 8), c.y, s1b);
-      s1a = fmaf(nib<8>(v1, 16), c.z, s1a);
-      s1b = fmaf(nib<8>(v1, 24), c.w, s1b);
-      s1a = fmaf(nib<8>(v1, 4), e.x, s1a);
-      s1b = fmaf(nib<8>(v1, 12), e.y, s1b);
-      s1a = fmaf(nib<8>(v1, 20), e.z, s1a);
-      s1b = fmaf(nib<8>(v1, 28), e.w, s1b);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint32_t v0 = w[r][k], v1 = w[r][4 + k];
+        s0[r] = fmaf(nib<8>(v0, 0), a.x, s0[r]);
+        s0[r] = fmaf(nib<8>(v0, 8), a.y, s0[r]);
+        s0[r] = fmaf(nib<8>(v0, 16), a.z, s0[r]);
+        s0[r] = fmaf(nib<8>(v0, 24), a.w, s0[r]);
+        s0[r] = fmaf(nib<8>(v0, 4), b.x, s0[r]);
+        s0[r] = fmaf(nib<8>(v0, 12), b.y, s0[r]);
+        s0[r] = fmaf(nib<8>(v0, 20), b.z, s0[r]);
+        s0[r] = fmaf(nib<8>(v0, 28), b.w, s0[r]);
+        s1[r] = fmaf(nib<8>(v1, 0), c.x, s1[r]);
+        s1[r] = fmaf(nib<8>(v1, 8), c.y, s1[r]);
+        s1[r] = fmaf(nib<8>(v1, 16), c.z, s1[r]);
+        s1[r] = fmaf(nib<8>(v1, 24), c.w, s1[r]);
+        s1[r] = fmaf(nib<8>(v1, 4), e.x, s1[r]);
+        s1[r] = fmaf(nib<8>(v1, 12), e.y, s1[r]);
+        s1[r] = fmaf(nib<8>(v1, 20), e.z, s1[r]);
+        s1[r] = fmaf(nib<8>(v1, 28), e.w, s1[r]);
+      }
     }
-    return h2f(dd & 0xFFFFu) * (s0a + s0b) + h2f(dd >> 16) * (s1a + s1b);
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const uint32_t dd = __ldg(reinterpret_cast<const uint32_t*>(srow[r]) + u);
+      acc[r] += h2f(dd & 0xFFFFu) * s0[r] + h2f(dd >> 16) * s1[r];
+    }
   }
 };
 
@@ -219,21 +250,27 @@ struct UnitDot<T_Q8_0> {
   static constexpr int EPU = 32;
   static constexpr bool NEED_XS = false;
   // Unit u = block u: 32 signed bytes, value q*d (quant.rs:176-180).
-  template <class XA>
-  __device__ __forceinline__ static float dot(const uint32_t (&w)[8], XA xa, const uint8_t* sc_row, int u,
-                                              float, float) {
-    const float d = h2f(__ldg(reinterpret_cast<const unsigned short*>(sc_row) + u));
-    float s0 = 0.f, s1 = 0.f;
+  template <int R, class XA>
+  __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&srow)[R],
+                                               int u, float, float, float (&acc)[R]) {
+    float s0[R], s1[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) s0[r] = s1[r] = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      const uint32_t v = w[k];
       const float4 a = xa(k);
-      s0 = fmaf(sbyte_f(v, 0), a.x, s0);
-      s1 = fmaf(sbyte_f(v, 8), a.y, s1);
-      s0 = fmaf(sbyte_f(v, 16), a.z, s0);
-      s1 = fmaf(sbyte_f(v, 24), a.w, s1);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint32_t v = w[r][k];
+        s0[r] = fmaf(sbyte_f(v, 0), a.x, s0[r]);
+        s1[r] = fmaf(sbyte_f(v, 8), a.y, s1[r]);
+        s0[r] = fmaf(sbyte_f(v, 16), a.z, s0[r]);
+        s1[r] = fmaf(sbyte_f(v, 24), a.w, s1[r]);
+      }
     }
-    return d * (s0 + s1);
+#pragma unroll
+    for (int r = 0; r < R; r++)
+      acc[r] += h2f(__ldg(reinterpret_cast<const unsigned short*>(srow[r]) + u)) * (s0[r] + s1[r]);
   }
 };
 
@@ -241,18 +278,21 @@ template <>
 struct UnitDot<T_F16> {
   static constexpr int EPU = 16;
   static constexpr bool NEED_XS = false;
-  template <class XA>
-  __device__ __forceinline__ static float dot(const uint32_t (&w)[8], XA xa, const uint8_t*, int, float, float) {
-    float s = 0.f;
+  template <int R, class XA>
+  __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&)[R], int,
+                                               float, float, float (&acc)[R]) {
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       const float4 a = xa(k);
-      s = fmaf(h2f(w[2 * k] & 0xFFFFu), a.x, s);
-      s = fmaf(h2f(w[2 * k] >> 16), a.y, s);
-      s = fmaf(h2f(w[2 * k + 1] & 0xFFFFu), a.z, s);
-      s = fmaf(h2f(w[2 * k + 1] >> 16), a.w, s);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        float s = acc[r];
+        s = fmaf(h2f(w[r][2 * k] & 0xFFFFu), a.x, s);
+        s = fmaf(h2f(w[r][2 * k] >> 16), a.y, s);
+        s = fmaf(h2f(w[r][2 * k + 1] & 0xFFFFu), a.z, s);
+        acc[r] = fmaf(h2f(w[r][2 * k + 1] >> 16), a.w, s);
+      }
     }
-    return s;
   }
 };
 
@@ -260,18 +300,21 @@ template <>
 struct UnitDot<T_F32> {
   static constexpr int EPU = 8;
   static constexpr bool NEED_XS = false;
-  template <class XA>
-  __device__ __forceinline__ static float dot(const uint32_t (&w)[8], XA xa, const uint8_t*, int, float, float) {
-    float s = 0.f;
+  template <int R, class XA>
+  __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&)[R], int,
+                                               float, float, float (&acc)[R]) {
 #pragma unroll
     for (int k = 0; k < 2; k++) {
       const float4 a = xa(k);
-      s = fmaf(__uint_as_float(w[4 * k]), a.x, s);
-      s = fmaf(__uint_as_float(w[4 * k + 1]), a.y, s);
-      s = fmaf(__uint_as_float(w[4 * k + 2]), a.z, s);
-      s = fmaf(__uint_as_float(w[4 * k + 3]), a.w, s);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        float s = acc[r];
+        s = fmaf(__uint_as_float(w[r][4 * k]), a.x, s);
+        s = fmaf(__uint_as_float(w[r][4 * k + 1]), a.y, s);
+        s = fmaf(__uint_as_float(w[r][4 * k + 2]), a.z, s);
+        acc[r] = fmaf(__uint_as_float(w[r][4 * k + 3]), a.w, s);
+      }
     }
-    return s;
   }
 };
 
@@ -398,68 +441,68 @@ struct EpiArgmax {
 // ---------------------------------------------------------------------------
 // Each warp owns groups of R consecutive packed rows; its lanes stride over the
 // 32-byte units of those rows (unit u by lane u % 32), so one warp-wide load
-// instruction reads 1 KB of contiguous weights per row.  x lives in shared
-// memory; the first unit of the first group is loaded before waiting on the
-// previous kernel (weights never depend on it).
+// instruction reads 1 KB of contiguous weights per row.  A lane keeps R x CH
+// units (256 bytes) in flight: HBM needs tens of KB outstanding per SM to reach
+// its bandwidth, and the grid is two 8-warp CTAs per SM.  The first chunk of a
+// warp's first group is loaded before waiting on the previous kernel (weights
+// never depend on it), and the next group's first chunk is loaded before the
+// current group's reduction.  x lives in shared memory.
 template <int FMT, int R, class Epi>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(PackedMat W, const float* __restrict__ x,
-                                                            const float* __restrict__ nw, float eps, Epi epi) {
+__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(PackedMat W, const float* __restrict__ x,
+                                                               const float* __restrict__ nw, float eps, Epi epi) {
   using D = UnitDot<FMT>;
   constexpr int EPU = D::EPU;
+  constexpr int CH = 8 / R;  // units per row in flight per lane
   extern __shared__ __align__(16) float smem[];
   float* sx = smem;
   float* sxs = smem + W.Kp;
   float* sred = sxs + W.Kp / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n_groups = (int)((W.M + R - 1) / R);
-  int g = blockIdx.x * GEMV_WARPS + warp;
   const int units = (int)W.units;
+  const int nch = (units + 32 * CH - 1) / (32 * CH);
+  const int gstride = gridDim.x * GEMV_WARPS;
+  int g = blockIdx.x * GEMV_WARPS + warp;
 
-  uint32_t wpre[R][8];
-  const bool pre = g < n_groups && lane < units;
-  if (pre) {
+  uint32_t w[CH][R][8];
+  auto load = [&](int grp, int c) {
 #pragma unroll
     for (int r = 0; r < R; r++) {
-      const uint32_t row = min((uint32_t)(g * R + r), W.M - 1);
-      ldg256(W.qs + (size_t)row * W.qs_stride + (size_t)lane * 32, wpre[r]);
+      const uint8_t* q = W.qs + (size_t)min((uint32_t)(grp * R + r), W.M - 1) * W.qs_stride;
+#pragma unroll
+      for (int j = 0; j < CH; j++) {
+        const int u = (c * CH + j) * 32 + lane;
+        if (u < units) ldg256(q + (size_t)u * 32, w[j][r]);
+      }
     }
-  }
+  };
+  if (g < n_groups) load(g, 0);
   griddep_wait();
   stage_x<EPU>(x, nw, eps, (int)W.K, (int)W.Kp, sx, sxs, sred, D::NEED_XS);
   griddep_launch();
 
-  bool first = true;
-  for (; g < n_groups; g += gridDim.x * GEMV_WARPS) {
+  for (; g < n_groups; g += gstride) {
     float acc[R];
-#pragma unroll
-    for (int r = 0; r < R; r++) acc[r] = 0.f;
-    const uint8_t* qrow[R];
     const uint8_t* srow[R];
 #pragma unroll
     for (int r = 0; r < R; r++) {
-      const uint32_t row = min((uint32_t)(g * R + r), W.M - 1);
-      qrow[r] = W.qs + (size_t)row * W.qs_stride;
-      srow[r] = W.sc + (size_t)row * W.sc_stride;
+      acc[r] = 0.f;
+      srow[r] = W.sc + (size_t)min((uint32_t)(g * R + r), W.M - 1) * W.sc_stride;
     }
-    for (int u = lane; u < units; u += 32) {
-      uint32_t w[R][8];
-      if (first && pre) {
+    for (int c = 0; c < nch; c++) {
+      if (c > 0) load(g, c);
 #pragma unroll
-        for (int r = 0; r < R; r++)
-#pragma unroll
-          for (int k = 0; k < 8; k++) w[r][k] = wpre[r][k];
-      } else {
-#pragma unroll
-        for (int r = 0; r < R; r++) ldg256(qrow[r] + (size_t)u * 32, w[r]);
+      for (int j = 0; j < CH; j++) {
+        const int u = (c * CH + j) * 32 + lane;
+        if (u < units) {
+          auto xa = [&](int k) { return ldx<EPU>(sx, u, k); };
+          const float xs_lo = D::NEED_XS ? sxs[2 * u] : 0.f;
+          const float xs_hi = D::NEED_XS ? sxs[2 * u + 1] : 0.f;
+          D::template accum<R>(w[j], xa, srow, u, xs_lo, xs_hi, acc);
+        }
       }
-      first = false;
-      auto xa = [&](int c) { return ldx<EPU>(sx, u, c); };
-      const float xs_lo = D::NEED_XS ? sxs[2 * u] : 0.f;
-      const float xs_hi = D::NEED_XS ? sxs[2 * u + 1] : 0.f;
-#pragma unroll
-      for (int r = 0; r < R; r++) acc[r] += D::dot(w[r], xa, srow[r], u, xs_lo, xs_hi);
     }
-    first = false;
+    if (g + gstride < n_groups) load(g + gstride, 0);
 #pragma unroll
     for (int r = 0; r < R; r++) {
 #pragma unroll
@@ -484,9 +527,10 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_batched_kernel(PackedMat W,
     for (int b = 0; b < B; b++) acc[b] = 0.f;
     const uint8_t* q = W.qs + (size_t)row * W.qs_stride;
     const uint8_t* s = W.sc + (size_t)row * W.sc_stride;
+    const uint8_t* const srow[1] = {s};
     for (int u = lane; u < units; u += 32) {
-      uint32_t w[8];
-      ldg256(q + (size_t)u * 32, w);
+      uint32_t w[1][8];
+      ldg256(q + (size_t)u * 32, w[0]);
 #pragma unroll
       for (int b = 0; b < B; b++) {
         const float* xb = x + (size_t)b * W.Kp + (size_t)u * EPU;
@@ -496,7 +540,9 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_batched_kernel(PackedMat W,
 #pragma unroll 8
           for (int l = 0; l < 32; l++) { xs_lo += xb[l]; xs_hi += xb[32 + l]; }
         }
-        acc[b] += D::dot(w, xa, s, u, xs_lo, xs_hi);
+        float a1[1] = {acc[b]};
+        D::template accum<1>(w, xa, srow, u, xs_lo, xs_hi, a1);
+        acc[b] = a1[0];
       }
     }
 #pragma unroll
@@ -553,14 +599,14 @@ static cudaError_t run_gemv_t(const Launch& L, const PackedMat& W, const float* 
   }
   const int groups = (int)((W.M + R - 1) / R);
   int blocks = (groups + GEMV_WARPS - 1) / GEMV_WARPS;
-  int per_sm = smem <= 56 * 1024 ? 4 : (smem <= 110 * 1024 ? 2 : 1);
+  const int per_sm = smem <= 110 * 1024 ? 2 : 1;  // persistent: 2 CTAs (16 warps) per SM
   blocks = std::max(1, std::min(blocks, num_sms() * per_sm));
   return launch_k(L, k, dim3(blocks), dim3(GEMV_THREADS), smem, W, x, nw, eps, epi);
 }
 
 template <int R, class Epi>
-static cudaError_t run_gemv(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
-                            Epi epi) {
+static cudaError_t run_gemv_r(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
+                              Epi epi) {
   switch (W.type) {
     case T_Q4_K: return run_gemv_t<T_Q4_K, R>(L, W, x, nw, eps, epi);
     case T_Q4_0: return run_gemv_t<T_Q4_0, R>(L, W, x, nw, eps, epi);
@@ -571,23 +617,33 @@ static cudaError_t run_gemv(const Launch& L, const PackedMat& W, const float* x,
   }
 }
 
+// Rows per warp group: 4 when a row has at most 64 units (every lane then holds
+// 2 units of each of 4 rows), else 2 (4 units of each of 2 rows).  Both are even,
+// which the RoPE and SwiGLU row pairs need.
+template <class Epi>
+static cudaError_t run_gemv(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
+                            Epi epi) {
+  if (W.units <= 64) return run_gemv_r<4>(L, W, x, nw, eps, epi);
+  return run_gemv_r<2>(L, W, x, nw, eps, epi);
+}
+
 cudaError_t gemv_store(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps, float* y) {
-  return run_gemv<2>(L, W, x, nw, eps, EpiStore{y});
+  return run_gemv(L, W, x, nw, eps, EpiStore{y});
 }
 cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const float* x, const float* res, float* out) {
-  return run_gemv<2>(L, W, x, nullptr, 0.f, EpiResidual{res, out});
+  return run_gemv(L, W, x, nullptr, 0.f, EpiResidual{res, out});
 }
 cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
                           const RopeQKVArgs& a) {
-  return run_gemv<2>(L, W, x, nw, eps, EpiRope{a});
+  return run_gemv(L, W, x, nw, eps, EpiRope{a});
 }
 cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
                         float* act) {
-  return run_gemv<2>(L, W, x, nw, eps, EpiSwiGLU{act});
+  return run_gemv(L, W, x, nw, eps, EpiSwiGLU{act});
 }
 cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
                         float* logits, unsigned long long* key, uint32_t row_offset) {
-  return run_gemv<2>(L, W, x, nw, eps, EpiArgmax{logits, key, row_offset, 0ull});
+  return run_gemv(L, W, x, nw, eps, EpiArgmax{logits, key, row_offset, 0ull});
 }
 
 template <int FMT>
@@ -803,12 +859,17 @@ cudaError_t launch_kv_gather(const void* cache, int kv_f32, uint32_t kvh, uint32
 // ---------------------------------------------------------------------------
 // attention_reference (compute.rs:461-547) for one query token: query head h
 // reads KV head h*KV/H (contiguous groups of G = H/KV heads), so one CTA loads
-// each K/V row once for its G heads.  A CTA covers a chunk of positions; the
-// last CTA of a head to finish merges the chunk partials (max-rescaled sums).
+// each K/V row once for its G heads.  A CTA covers a chunk of about 32+
+// positions; each warp takes ATT_UNROLL consecutive positions at a time and
+// issues all their row loads before using any (lane i holds dims
+// [i*DPL, i*DPL+DPL) of every row), so a CTA's pass over K and over V each cost
+// one memory round trip.  The last CTA of a head to finish merges the chunk
+// partials (max-rescaled sums); nothing waits on another CTA.
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_WARPS = ATT_THREADS / 32;
 constexpr int ATT_MAX_CHUNK = 512;
-constexpr int ATT_MIN_CHUNK = 64;
+constexpr int ATT_MIN_CHUNK = 32;
+constexpr int ATT_UNROLL = 8;
 
 __host__ __device__ inline int attn_nsplit(int ctx, int max_splits) {
   int s = (ctx + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK;
@@ -820,16 +881,30 @@ size_t attn_part_floats(int batch, int n_kv_heads, int max_splits, int G, int hd
   return (size_t)batch * n_kv_heads * max_splits * G * (hd + 2);
 }
 
-template <typename KT>
-__device__ __forceinline__ float kv_load(const KT* p);
-template <>
-__device__ __forceinline__ float kv_load<__half>(const __half* p) { return __half2float(*p); }
-template <>
-__device__ __forceinline__ float kv_load<float>(const float* p) { return *p; }
+// DPL consecutive elements of one K/V row into f32 registers (zero past hd).
+template <int DPL>
+__device__ __forceinline__ void load_row(const __half* p, int d0, int hd, float (&v)[DPL]) {
+  if (DPL == 4 && d0 + 4 <= hd) {
+    const uint2 r = __ldg(reinterpret_cast<const uint2*>(p + d0));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    v[0] = a.x; v[1] = a.y; v[2 % DPL] = b.x; v[3 % DPL] = b.y;
+  } else if (DPL == 2 && d0 + 2 <= hd) {
+    const float2 a = __half22float2(__ldg(reinterpret_cast<const __half2*>(p + d0)));
+    v[0] = a.x; v[1 % DPL] = a.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < DPL; i++) v[i] = d0 + i < hd ? __half2float(p[d0 + i]) : 0.f;
+  }
+}
+template <int DPL>
+__device__ __forceinline__ void load_row(const float* p, int d0, int hd, float (&v)[DPL]) {
+#pragma unroll
+  for (int i = 0; i < DPL; i++) v[i] = d0 + i < hd ? p[d0 + i] : 0.f;
+}
 
 template <int DPL, int G, typename KT>
 __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(AttnArgs a) {
-  __shared__ float sq[G][DPL * 32];
   __shared__ float ssc[G][ATT_MAX_CHUNK];
   __shared__ float sred[ATT_WARPS][G][DPL * 32];
   __shared__ float sm[G], sl[G];
@@ -856,35 +931,43 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(AttnArgs a) {
     return;
   }
   const int p0 = split * chunk, p1 = min(ctx, p0 + chunk);
+  const int d0 = lane * DPL;
   const float* qb = a.q + ((size_t)b * a.n_heads + h0) * hd;
-  for (int t = threadIdx.x; t < G * DPL * 32; t += ATT_THREADS) {
-    const int h = t / (DPL * 32), d = t % (DPL * 32);
-    sq[h][d] = d < hd ? qb[(size_t)h * hd + d] : 0.f;
-  }
-  __syncthreads();
+  float qr[G][DPL];
+#pragma unroll
+  for (int h = 0; h < G; h++)
+#pragma unroll
+    for (int i = 0; i < DPL; i++) qr[h][i] = d0 + i < hd ? qb[(size_t)h * hd + d0 + i] : 0.f;
   const KT* kb = reinterpret_cast<const KT*>(a.kc) + (size_t)b * a.batch_stride + (size_t)kvh * a.head_stride;
   const KT* vb = reinterpret_cast<const KT*>(a.vc) + (size_t)b * a.batch_stride + (size_t)kvh * a.head_stride;
-  const float inv_div = sqrtf((float)hd);  // score = dot / sqrt(hd)  (compute.rs:530)
-  const int d0 = lane * DPL;
+  const float* kcur = has_cur ? a.k_cur + (size_t)kvh * hd : nullptr;
+  const float* vcur = has_cur ? a.v_cur + (size_t)kvh * hd : nullptr;
+  const float div = sqrtf((float)hd);  // score = dot / sqrt(hd)  (compute.rs:530)
 
   // pass 1: scores
-  for (int p = p0 + warp; p < p1; p += ATT_WARPS) {
-    float k[DPL];
-    if (p < nhist) {
+  for (int p = p0 + warp * ATT_UNROLL; p < p1; p += ATT_WARPS * ATT_UNROLL) {
+    float k[ATT_UNROLL][DPL];
 #pragma unroll
-      for (int i = 0; i < DPL; i++) k[i] = d0 + i < hd ? kv_load<KT>(kb + (size_t)p * hd + d0 + i) : 0.f;
-    } else {
+    for (int t = 0; t < ATT_UNROLL; t++) {
+      const int pp = p + t;
+      if (pp < min(p1, nhist)) load_row<DPL>(kb + (size_t)pp * hd, d0, hd, k[t]);
+      else if (pp < p1) load_row<DPL>(kcur, d0, hd, k[t]);
+      else {
 #pragma unroll
-      for (int i = 0; i < DPL; i++) k[i] = d0 + i < hd ? a.k_cur[(size_t)kvh * hd + d0 + i] : 0.f;
+        for (int i = 0; i < DPL; i++) k[t][i] = 0.f;
+      }
     }
 #pragma unroll
-    for (int h = 0; h < G; h++) {
-      float s = 0.f;
+    for (int t = 0; t < ATT_UNROLL; t++) {
 #pragma unroll
-      for (int i = 0; i < DPL; i++) s = fmaf(sq[h][d0 + i], k[i], s);
+      for (int h = 0; h < G; h++) {
+        float s = 0.f;
 #pragma unroll
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) ssc[h][p - p0] = s / inv_div;
+        for (int i = 0; i < DPL; i++) s = fmaf(qr[h][i], k[t][i], s);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0 && p + t < p1) ssc[h][p + t - p0] = s / div;
+      }
     }
   }
   __syncthreads();
@@ -903,7 +986,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(AttnArgs a) {
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) { sm[h] = m; sl[h] = l; }
+    if (lane == 0) {
+      sm[h] = m;
+      sl[h] = l;
+    }
   }
   __syncthreads();
   // pass 2: sum_p e_p * v_p
@@ -912,20 +998,28 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(AttnArgs a) {
   for (int h = 0; h < G; h++)
 #pragma unroll
     for (int i = 0; i < DPL; i++) acc[h][i] = 0.f;
-  for (int p = p0 + warp; p < p1; p += ATT_WARPS) {
-    float v[DPL];
-    if (p < nhist) {
+  for (int p = p0 + warp * ATT_UNROLL; p < p1; p += ATT_WARPS * ATT_UNROLL) {
+    float v[ATT_UNROLL][DPL];
 #pragma unroll
-      for (int i = 0; i < DPL; i++) v[i] = d0 + i < hd ? kv_load<KT>(vb + (size_t)p * hd + d0 + i) : 0.f;
-    } else {
+    for (int t = 0; t < ATT_UNROLL; t++) {
+      const int pp = p + t;
+      if (pp < min(p1, nhist)) load_row<DPL>(vb + (size_t)pp * hd, d0, hd, v[t]);
+      else if (pp < p1) load_row<DPL>(vcur, d0, hd, v[t]);
+      else {
 #pragma unroll
-      for (int i = 0; i < DPL; i++) v[i] = d0 + i < hd ? a.v_cur[(size_t)kvh * hd + d0 + i] : 0.f;
+        for (int i = 0; i < DPL; i++) v[t][i] = 0.f;
+      }
     }
 #pragma unroll
-    for (int h = 0; h < G; h++) {
-      const float e = ssc[h][p - p0];
+    for (int t = 0; t < ATT_UNROLL; t++) {
+      if (p + t < p1) {
 #pragma unroll
-      for (int i = 0; i < DPL; i++) acc[h][i] = fmaf(e, v[i], acc[h][i]);
+        for (int h = 0; h < G; h++) {
+          const float e = ssc[h][p + t - p0];
+#pragma unroll
+          for (int i = 0; i < DPL; i++) acc[h][i] = fmaf(e, v[t][i], acc[h][i]);
+        }
+      }
     }
   }
 #pragma unroll

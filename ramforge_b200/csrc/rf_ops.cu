@@ -137,7 +137,7 @@ int rf_decode_attention(const float* dQ, const uint16_t* dK, const uint16_t* dV,
   if (G != 1 && G != 2 && G != 4 && G != 8) return set_error(RF_EUNSUPPORTED, "GQA group %d unsupported", G);
   int dev = 0;
   RF_CUDA(cudaGetDevice(&dev));
-  const int max_splits = std::max(32, (ctx + 511) / 512);
+  const int max_splits = std::max(64, (ctx + 511) / 512);
   AttnWorkspace* w = nullptr;
   RF_TRY(workspace(dev, attn_part_floats(batch, n_kv_heads, max_splits, G, head_dim),
                    (size_t)batch * n_kv_heads, &w));
