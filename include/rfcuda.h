@@ -223,6 +223,19 @@ int rf_qmatvec(const rf_matrix* m, const float* dX, float* dY, int batch, void* 
  * Split-K scratch comes from a per-device workspace the library allocates once. */
 int rf_decode_attention(const float* dQ, const uint16_t* dK, const uint16_t* dV, int ctx, int n_heads,
                         int n_kv_heads, int head_dim, int batch, float* dOut, void* stream);
+/* rf_decode_attention that allocates no device memory.  No counterpart in the
+ * reference.  For callers that cannot call cudaMalloc: processes whose device
+ * memory is already owned by another allocator (a framework's caching pool or
+ * a fixed arena), where a fresh cudaMalloc fails or fragments that pool, and
+ * latency-critical loops that cannot afford the device synchronisation
+ * cudaMalloc/cudaFree may imply.  The split-K scratch is a fixed 16 MiB
+ * array in the library, held on every GPU that loads it until exit; shapes
+ * that need more return RF_EINVAL.  The first call on a device looks the array
+ * up, so make it before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU race.  Same arguments and results as
+ * rf_decode_attention. */
+int rf_decode_attention_noalloc(const float* dQ, const uint16_t* dK, const uint16_t* dV, int ctx, int n_heads,
+                                int n_kv_heads, int head_dim, int batch, float* dOut, void* stream);
 
 #ifdef __cplusplus
 }

@@ -31,7 +31,7 @@ EXPORTS = [
     "rf_decode_step", "rf_generate", "rf_kv_reset", "rf_kv_seq_len", "rf_kv_read", "rf_budget_total",
     "rf_budget_used", "rf_budget_available", "rf_set_residency_plan", "rf_residency_stats_get",
     "rf_step_kernel_count", "rf_decode_timed", "rf_bench_layer_kernels", "rf_tp_unique_id", "rf_matrix_create", "rf_matrix_destroy", "rf_matrix_device_bytes", "rf_qmatvec",
-    "rf_decode_attention",
+    "rf_decode_attention", "rf_decode_attention_noalloc",
 ]
 
 
@@ -125,6 +125,7 @@ def lib():
             "rf_matrix_device_bytes": (c_u64, [vp]),
             "rf_qmatvec": (c_int, [vp, vp, vp, c_int, vp]),
             "rf_decode_attention": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp, vp]),
+            "rf_decode_attention_noalloc": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

@@ -28,6 +28,33 @@ struct AttnWorkspace {
 std::mutex g_ws_mu;
 std::unordered_map<int, AttnWorkspace> g_ws;
 
+// Fixed scratch of rf_decode_attention_noalloc: the split-K partial sums
+// followed by the per-(sequence, KV head) arrival counters, 16 MiB per device
+// that loads this library, held until the process exits.  Device code could
+// name it directly; host code must ask the runtime for its device address.
+constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;  // 16 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once
+// per device, with that device current).
+int noalloc_scratch(int dev, float** out) {
+  if (dev < 0 || dev >= kMaxDevices) return set_error(RF_EINVAL, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    cudaError_t ce = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (ce != cudaSuccess || !p)
+      return set_error(RF_ECUDA, "cudaGetSymbolAddress(no-allocation scratch) failed: %s", cudaGetErrorString(ce));
+    g_noalloc_addr[dev] = (float*)p;
+  }
+  *out = g_noalloc_addr[dev];
+  return RF_OK;
+}
+
 int workspace(int dev, size_t part_floats, size_t n_counters, AttnWorkspace** out) {
   std::lock_guard<std::mutex> lk(g_ws_mu);
   AttnWorkspace& w = g_ws[dev];
@@ -160,6 +187,60 @@ int rf_decode_attention(const float* dQ, const uint16_t* dK, const uint16_t* dV,
   a.counters = w->counters;
   a.out = dOut;
   a.kv_f32 = 0;
+  RF_CUDA(launch_attention(Launch{(cudaStream_t)stream, false}, a));
+  return RF_OK;
+}
+
+// rf_decode_attention for callers that cannot allocate device memory: the
+// split-K partials and counters live in g_noalloc_scratch instead of a
+// workspace grown with cudaMalloc.  The first call on a device looks up the
+// array's device address (cudaGetSymbolAddress, with that device current);
+// make that first call before any stream capture.  Calls share the array: the
+// counters are cleared (cudaMemsetAsync, no allocation) before every launch,
+// and calls that overlap on the GPU race on the scratch.  Shapes whose scratch
+// exceeds kNoAllocScratchFloats are rejected with RF_EINVAL.
+int rf_decode_attention_noalloc(const float* dQ, const uint16_t* dK, const uint16_t* dV, int ctx, int n_heads,
+                                int n_kv_heads, int head_dim, int batch, float* dOut, void* stream) {
+  if (!dQ || !dK || !dV || !dOut) return set_error(RF_EINVAL, "null argument");
+  if (ctx <= 0 || batch <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || head_dim <= 0 || head_dim > 128)
+    return set_error(RF_EINVAL, "invalid attention shape");
+  const int G = n_heads / n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return set_error(RF_EUNSUPPORTED, "GQA group %d unsupported", G);
+  int dev = 0;
+  RF_CUDA(cudaGetDevice(&dev));
+  float* scratch = nullptr;
+  RF_TRY(noalloc_scratch(dev, &scratch));
+  const size_t n_counters = (size_t)batch * n_kv_heads;
+  const size_t per_split = attn_part_floats(batch, n_kv_heads, 1, G, head_dim);
+  const int min_splits = (ctx + 511) / 512;  // every split covers at most 512 positions
+  int max_splits = std::max(64, min_splits);
+  if (per_split * (size_t)max_splits + n_counters > kNoAllocScratchFloats) {
+    const size_t fit = per_split ? (kNoAllocScratchFloats - std::min(n_counters, kNoAllocScratchFloats)) / per_split : 0;
+    if (fit < (size_t)min_splits)
+      return set_error(RF_EINVAL,
+                       "rf_decode_attention_noalloc: batch %d x %d KV heads x ctx %d needs %zu bytes of scratch; "
+                       "its fixed scratch holds %zu bytes",
+                       batch, n_kv_heads, ctx, (per_split * (size_t)min_splits + n_counters) * 4,
+                       kNoAllocScratchFloats * 4);
+    max_splits = (int)std::min<size_t>(fit, (size_t)max_splits);
+  }
+  unsigned* counters = reinterpret_cast<unsigned*>(scratch + per_split * (size_t)max_splits);
+  RF_CUDA(cudaMemsetAsync(counters, 0, n_counters * sizeof(unsigned), (cudaStream_t)stream));
+  AttnArgs a{};
+  a.q = dQ;
+  a.kc = dK;
+  a.vc = dV;
+  a.head_stride = (uint64_t)ctx * head_dim;
+  a.batch_stride = (uint64_t)n_kv_heads * ctx * head_dim;
+  a.nhist = ctx;
+  a.n_heads = n_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.batch = batch;
+  a.max_splits = max_splits;
+  a.part = scratch;
+  a.counters = counters;
+  a.out = dOut;
   RF_CUDA(launch_attention(Launch{(cudaStream_t)stream, false}, a));
   return RF_OK;
 }
