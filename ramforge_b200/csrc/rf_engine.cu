@@ -74,6 +74,7 @@ struct Layer {
   void* block = nullptr;
   uint64_t bytes = 0;
   PackedMat qkv{}, wo{}, gateup{}, down{};
+  GemvMaps mq{}, mo{}, mg{}, md{};  // TMA descriptors of the four matrices
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
 };
@@ -108,6 +109,7 @@ struct rf_engine {
   void* embd_block = nullptr;
   void* out_block = nullptr;
   float* out_norm = nullptr;
+  GemvMaps lm_maps{};  // TMA descriptors of the LM-head matrix (output or this rank's tied rows)
   std::vector<Layer> layers;
   std::vector<uint8_t> plan_resident;  // residency plan (1 = keep resident)
   // KV cache
@@ -425,6 +427,10 @@ int load_layer_views(rf_engine* e, int l, const View* v /*[9]*/) {
     dev_free(e, charge, &L.block);
     return rc;
   }
+  make_gemv_maps(L.qkv, &L.mq);  // not TMA-eligible: the register-streaming GEMV runs instead
+  make_gemv_maps(L.wo, &L.mo);
+  make_gemv_maps(L.gateup, &L.mg);
+  make_gemv_maps(L.down, &L.md);
   L.bytes = total;
   L.resident = true;
   e->stats.layer_loads++;
@@ -444,6 +450,8 @@ View view_from_gguf(const GgufTensor* t) {
   v.host = t->data;
   return v;
 }
+
+int lm_head(rf_engine* e, PackedMat* W);
 
 int load_persistent(rf_engine* e, int role, const View& v) {
   const rf_model_config& c = e->cfg;
@@ -479,6 +487,8 @@ int load_persistent(rf_engine* e, int role, const View& v) {
   } else {
     return set_error(RF_EINVAL, "unknown persistent role %d", role);
   }
+  PackedMat lm;
+  if (lm_head(e, &lm) == RF_OK) make_gemv_maps(lm, &e->lm_maps);
   drop_graphs(e);
   return RF_OK;
 }
@@ -540,7 +550,7 @@ int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
     ra.kcache = e->kc[l];
     ra.vcache = e->vc[l];
     ra.kv_f32 = e->rt.kv_f32;
-    RF_CUDA(gemv_qkv_rope(La, L.qkv, e->hidden, L.attn_norm, c.rms_eps, ra));
+    RF_CUDA(gemv_qkv_rope(La, L.qkv, &L.mq, e->hidden, L.attn_norm, c.rms_eps, ra));
   } else if (k == 1) {
     AttnArgs aa{};
     aa.q = e->q;
@@ -563,15 +573,16 @@ int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
     RF_CUDA(launch_attention(La, aa));
   } else if (k == 2 || k == 4) {
     const PackedMat& W = k == 2 ? L.wo : L.down;
+    const GemvMaps* M = k == 2 ? &L.mo : &L.md;
     const float* x = k == 2 ? e->att : e->act;
     if (e->tp == 1) {
-      RF_CUDA(gemv_residual(La, W, x, e->hidden, e->hidden));
+      RF_CUDA(gemv_residual(La, W, M, x, e->hidden, e->hidden));
     } else {
-      RF_CUDA(gemv_residual(La, W, x, e->rank == 0 ? e->hidden : nullptr, e->partial));
+      RF_CUDA(gemv_residual(La, W, M, x, e->rank == 0 ? e->hidden : nullptr, e->partial));
       RF_NCCL(nccl()->allReduce(e->partial, e->hidden, c.n_embd, ncclFloat32, ncclSum, e->comm, e->stream));
     }
   } else {
-    RF_CUDA(gemv_swiglu(La, L.gateup, e->hidden, L.ffn_norm, c.rms_eps, e->act));
+    RF_CUDA(gemv_swiglu(La, L.gateup, &L.mg, e->hidden, L.ffn_norm, c.rms_eps, e->act));
   }
   return RF_OK;
 }
@@ -602,7 +613,7 @@ int enqueue_logits(rf_engine* e, bool pdl, bool want_logits) {
   RF_TRY(lm_head(e, &W));
   const Launch La{e->stream, pdl};
   RF_CUDA(cudaMemsetAsync(e->d_key, 0, 8, e->stream));
-  RF_CUDA(gemv_argmax(La, W, e->final_hidden, nullptr, 0.f, want_logits ? e->logits : nullptr, e->d_key,
+  RF_CUDA(gemv_argmax(La, W, &e->lm_maps, e->final_hidden, nullptr, 0.f, want_logits ? e->logits : nullptr, e->d_key,
                       e->vocab_off));
   if (e->tp > 1) RF_NCCL(nccl()->allReduce(e->d_key, e->d_key, 1, ncclUint64, ncclMax, e->comm, e->stream));
   return RF_OK;

@@ -99,67 +99,85 @@ __device__ float block_sumsq(const float* __restrict__ x, int n, float* sred) {
 // rms = sqrt(sum/n + eps); y = x / rms * w   (compute.rs:312-317)
 __device__ __forceinline__ float rms_of(float ss, int n, float eps) { return sqrtf(ss / (float)n + eps); }
 
-template <int EPU>
-__device__ void stage_x(const float* __restrict__ x, const float* __restrict__ nw, float eps, int K, int Kp,
-                        float* sx, float* sxs, float* sred, bool need_xs) {
-  float rms = 1.f;
-  if (nw) rms = rms_of(block_sumsq(x, K, sred), K, eps);
-  // warp w stages 32-element chunks w, w+8, ...: coalesced loads, and the chunk
-  // sums sum(x) that the Q4_K min term needs come from one shuffle reduction
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int c = warp; c * 32 < Kp; c += GEMV_WARPS) {
-    const int e = c * 32 + lane;
-    float v = 0.f;
-    if (e < K) {
-      const float xv = x[e];
-      v = nw ? xv / rms * nw[e] : xv;
-    }
-    if (e < Kp) sx[swz<EPU>(e)] = v;
-    if (need_xs) {
-      float s = v;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) sxs[c] = s;
-    }
-  }
-  __syncthreads();
-}
-
 // ---------------------------------------------------------------------------
 // per-unit dot products: 32 bytes of each of R rows against the unit's EPU
-// activations, accumulated into acc[R].  x is read one 16-byte chunk at a time
-// and reused across the rows, so only a few activations are live at once.
+// activations, accumulated into acc[R].
+//
+// Quant fields are never shifted down or converted.  A 4- or 8-bit field masked
+// in place inside a 32-bit word, bits [off, off+n) with off + n <= 24, is read
+// as an f32 whose value is exactly q * 2^(off-149) (a subnormal, or a normal
+// number with exponent field 1 - the bit pattern and the value are linear in
+// that range).  Shared memory holds x pre-multiplied by 2^(85-off) for the field
+// position each element is decoded from, so every product is exactly
+// q * x * 2^-64 and one packed fma.rn.f32x2 accumulates two elements; the 2^64 is
+// folded into the block scale.  Per 8 quants of Q4: 1 shift, 8 masks, 4 FFMA2.
 // ---------------------------------------------------------------------------
-// XA(c) returns the float4 of unit-relative elements [4c, 4c+4).
+constexpr float kTwo64 = 18446744073709551616.0f;  // 2^64
+
+// Field offset (bit position inside its 32-bit word, after the one 8-bit shift
+// that brings byte 3's fields below bit 24) of the element at unit-relative
+// index l; EPU-specific layouts below.
+template <int FMT>
+__device__ __forceinline__ int field_off(int l);
+template <>
+__device__ __forceinline__ int field_off<T_Q4_K>(int l) {  // byte l%32 of the unit; high nibble for l >= 32
+  const int b = l & 3;
+  return (b < 3 ? 8 * b : 16) + (l >= 32 ? 4 : 0);
+}
+template <>
+__device__ __forceinline__ int field_off<T_Q4_0>(int l) {  // block byte (l%32)%16; high nibble for (l%32) >= 16
+  const int b = l & 3;
+  return (b < 3 ? 8 * b : 16) + ((l & 31) >= 16 ? 4 : 0);
+}
+template <>
+__device__ __forceinline__ int field_off<T_Q8_0>(int l) {  // byte l of the block
+  const int b = l & 3;
+  return b < 3 ? 8 * b : 16;
+}
+template <>
+__device__ __forceinline__ int field_off<T_F16>(int) { return 85; }  // scale 1: weights are real floats
+template <>
+__device__ __forceinline__ int field_off<T_F32>(int) { return 85; }
+
+// 2^(85 - off): exact power-of-two pre-scale of x for a field at bit `off`
+// (85 - off >= 65 for quant fields; 0 for float weights).
+__device__ __forceinline__ float prescale(int off) { return __int_as_float((127 + 149 - 64 - off) << 23); }
+
+__device__ __forceinline__ float as_f(uint32_t bits) { return __uint_as_float(bits); }
+
+// Scale words come from global memory (read-only path) or from a shared-memory stage.
+template <bool SMEM, class T>
+__device__ __forceinline__ T ld_scale(const T* p) {
+  if constexpr (SMEM) return *p;
+  else return __ldg(p);
+}
+
 template <int FMT>
 struct UnitDot;
 
 // Q4_K super-block header fields of sub-block pair i = u%4 (get_scale_min,
-// quant.rs:216-226, for j = 2i and 2i+1): d*sc and dmin*m for both sub-blocks.
+// quant.rs:216-226, for j = 2i and 2i+1): d*sc and dmin*m of both sub-blocks,
+// with d*sc carrying the 2^64 of the scaled products.  Branch-free: lanes of a
+// warp decode different i.
+template <bool SMEM>
 __device__ __forceinline__ void q4k_scales(const uint8_t* sc_row, int u, float& d1, float& mn1, float& d2,
                                            float& mn2) {
-  const uint4 h = __ldg(reinterpret_cast<const uint4*>(sc_row + (size_t)(u >> 2) * 16));
-  const float d = h2f(h.x & 0xFFFFu), dmin = h2f(h.x >> 16);
+  const uint4 h = ld_scale<SMEM>(reinterpret_cast<const uint4*>(sc_row + (size_t)(u >> 2) * 16));
+  const float d = h2f(h.x & 0xFFFFu) * kTwo64, dmin = h2f(h.x >> 16);
   const int i = u & 3;
-  uint32_t sc0, m0, sc1, m1;
-  if (i < 2) {
-    const uint32_t a = h.y >> (16 * i), b = h.z >> (16 * i);  // s[2i], s[2i+1] / s[2i+4], s[2i+5]
-    sc0 = a & 63u;
-    sc1 = (a >> 8) & 63u;
-    m0 = b & 63u;
-    m1 = (b >> 8) & 63u;
-  } else {
-    const int k = i - 2;  // j = 4+2k, 5+2k: low 4 bits in s[8+2k], s[9+2k]; high 2 bits in s[2k..], s[4+2k..]
-    const uint32_t lo = h.w >> (16 * k), hs = h.y >> (16 * k), hm = h.z >> (16 * k);
-    sc0 = (lo & 0xFu) | (((hs >> 6) & 3u) << 4);
-    sc1 = ((lo >> 8) & 0xFu) | (((hs >> 14) & 3u) << 4);
-    m0 = ((lo >> 4) & 0xFu) | (((hm >> 6) & 3u) << 4);
-    m1 = ((lo >> 12) & 0xFu) | (((hm >> 14) & 3u) << 4);
-  }
-  d1 = d * (float)sc0;
-  mn1 = dmin * (float)m0;
-  d2 = d * (float)sc1;
-  mn2 = dmin * (float)m1;
+  const int sh = (i & 1) * 16;
+  const uint32_t y = (h.y >> sh) & 0xFFFFu;  // s[2i'], s[2i'+1]      (i' = i & 1)
+  const uint32_t z = (h.z >> sh) & 0xFFFFu;  // s[2i'+4], s[2i'+5]
+  const uint32_t w = (h.w >> sh) & 0xFFFFu;  // s[2i'+8], s[2i'+9]
+  // j < 4: sc = s[j] & 63, m = s[j+4] & 63; j >= 4: low 4 bits from s[j+4], high 2 from s[j-4] / s[j]
+  const uint32_t sc_lo = y & 0x3F3Fu, m_lo = z & 0x3F3Fu;
+  const uint32_t sc_hi = (w & 0x0F0Fu) | ((y >> 2) & 0x3030u);
+  const uint32_t m_hi = ((w >> 4) & 0x0F0Fu) | ((z >> 2) & 0x3030u);
+  const uint32_t sc = i >= 2 ? sc_hi : sc_lo, m = i >= 2 ? m_hi : m_lo;
+  d1 = d * (float)(sc & 0xFFu);
+  d2 = d * (float)(sc >> 8);
+  mn1 = dmin * (float)(m & 0xFFu);
+  mn2 = dmin * (float)(m >> 8);
 }
 
 template <>
@@ -170,33 +188,29 @@ struct UnitDot<T_Q4_K> {
   // (low nibble, sub-block 2i) and element 32+l (high nibble, sub-block 2i+1).
   // value = d*sc*q - dmin*m (quant.rs:235-248), summed as
   // (d*sc) * sum(q*x) - (dmin*m) * sum(x).
-  template <int R, class XA>
+  template <int R, class XA, bool SMEM = false>
   __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&srow)[R],
                                                int u, float xs_lo, float xs_hi, float (&acc)[R]) {
-    float lo[R], hi[R];
+    float2 lo[R], hi[R];
 #pragma unroll
-    for (int r = 0; r < R; r++) lo[r] = hi[r] = 0.f;
+    for (int r = 0; r < R; r++) lo[r] = hi[r] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 8; k++) {
       const float4 a = xa(k), b = xa(8 + k);
 #pragma unroll
       for (int r = 0; r < R; r++) {
-        const uint32_t v = w[r][k];
-        lo[r] = fmaf(nib<0>(v, 0), a.x, lo[r]);
-        hi[r] = fmaf(nib<0>(v, 4), b.x, hi[r]);
-        lo[r] = fmaf(nib<0>(v, 8), a.y, lo[r]);
-        hi[r] = fmaf(nib<0>(v, 12), b.y, hi[r]);
-        lo[r] = fmaf(nib<0>(v, 16), a.z, lo[r]);
-        hi[r] = fmaf(nib<0>(v, 20), b.z, hi[r]);
-        lo[r] = fmaf(nib<0>(v, 24), a.w, lo[r]);
-        hi[r] = fmaf(nib<0>(v, 28), b.w, hi[r]);
+        const uint32_t v = w[r][k], t = v >> 8;
+        lo[r] = __ffma2_rn(make_float2(as_f(v & 0xFu), as_f(v & 0xF00u)), make_float2(a.x, a.y), lo[r]);
+        lo[r] = __ffma2_rn(make_float2(as_f(v & 0xF0000u), as_f(t & 0xF0000u)), make_float2(a.z, a.w), lo[r]);
+        hi[r] = __ffma2_rn(make_float2(as_f(v & 0xF0u), as_f(v & 0xF000u)), make_float2(b.x, b.y), hi[r]);
+        hi[r] = __ffma2_rn(make_float2(as_f(v & 0xF00000u), as_f(t & 0xF00000u)), make_float2(b.z, b.w), hi[r]);
       }
     }
 #pragma unroll
     for (int r = 0; r < R; r++) {
       float d1, mn1, d2, mn2;
-      q4k_scales(srow[r], u, d1, mn1, d2, mn2);
-      acc[r] += d1 * lo[r] - mn1 * xs_lo + (d2 * hi[r] - mn2 * xs_hi);
+      q4k_scales<SMEM>(srow[r], u, d1, mn1, d2, mn2);
+      acc[r] += d1 * (lo[r].x + lo[r].y) - mn1 * xs_lo + (d2 * (hi[r].x + hi[r].y) - mn2 * xs_hi);
     }
   }
 };
@@ -204,43 +218,36 @@ struct UnitDot<T_Q4_K> {
 template <>
 struct UnitDot<T_Q4_0> {
   static constexpr int EPU = 64;
-  static constexpr bool NEED_XS = false;
+  static constexpr bool NEED_XS = true;
   // Unit u = blocks 2u, 2u+1: block byte j holds element j (low) and 16+j (high);
-  // value (q-8)*d (quant.rs:104-112).
-  template <int R, class XA>
+  // value (q-8)*d (quant.rs:104-112), summed as d * (sum(q*x) - 8*sum(x)).
+  template <int R, class XA, bool SMEM = false>
   __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&srow)[R],
-                                               int u, float, float, float (&acc)[R]) {
-    float s0[R], s1[R];
+                                               int u, float xs0, float xs1, float (&acc)[R]) {
+    float2 s0[R], s1[R];
 #pragma unroll
-    for (int r = 0; r < R; r++) s0[r] = s1[r] = 0.f;
+    for (int r = 0; r < R; r++) s0[r] = s1[r] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       const float4 a = xa(k), b = xa(4 + k), c = xa(8 + k), e = xa(12 + k);
 #pragma unroll
       for (int r = 0; r < R; r++) {
-        const uint32_t v0 = w[r][k], v1 = w[r][4 + k];
-        s0[r] = fmaf(nib<8>(v0, 0), a.x, s0[r]);
-        s0[r] = fmaf(nib<8>(v0, 8), a.y, s0[r]);
-        s0[r] = fmaf(nib<8>(v0, 16), a.z, s0[r]);
-        s0[r] = fmaf(nib<8>(v0, 24), a.w, s0[r]);
-        s0[r] = fmaf(nib<8>(v0, 4), b.x, s0[r]);
-        s0[r] = fmaf(nib<8>(v0, 12), b.y, s0[r]);
-        s0[r] = fmaf(nib<8>(v0, 20), b.z, s0[r]);
-        s0[r] = fmaf(nib<8>(v0, 28), b.w, s0[r]);
-        s1[r] = fmaf(nib<8>(v1, 0), c.x, s1[r]);
-        s1[r] = fmaf(nib<8>(v1, 8), c.y, s1[r]);
-        s1[r] = fmaf(nib<8>(v1, 16), c.z, s1[r]);
-        s1[r] = fmaf(nib<8>(v1, 24), c.w, s1[r]);
-        s1[r] = fmaf(nib<8>(v1, 4), e.x, s1[r]);
-        s1[r] = fmaf(nib<8>(v1, 12), e.y, s1[r]);
-        s1[r] = fmaf(nib<8>(v1, 20), e.z, s1[r]);
-        s1[r] = fmaf(nib<8>(v1, 28), e.w, s1[r]);
+        const uint32_t v0 = w[r][k], t0 = v0 >> 8, v1 = w[r][4 + k], t1 = v1 >> 8;
+        s0[r] = __ffma2_rn(make_float2(as_f(v0 & 0xFu), as_f(v0 & 0xF00u)), make_float2(a.x, a.y), s0[r]);
+        s0[r] = __ffma2_rn(make_float2(as_f(v0 & 0xF0000u), as_f(t0 & 0xF0000u)), make_float2(a.z, a.w), s0[r]);
+        s0[r] = __ffma2_rn(make_float2(as_f(v0 & 0xF0u), as_f(v0 & 0xF000u)), make_float2(b.x, b.y), s0[r]);
+        s0[r] = __ffma2_rn(make_float2(as_f(v0 & 0xF00000u), as_f(t0 & 0xF00000u)), make_float2(b.z, b.w), s0[r]);
+        s1[r] = __ffma2_rn(make_float2(as_f(v1 & 0xFu), as_f(v1 & 0xF00u)), make_float2(c.x, c.y), s1[r]);
+        s1[r] = __ffma2_rn(make_float2(as_f(v1 & 0xF0000u), as_f(t1 & 0xF0000u)), make_float2(c.z, c.w), s1[r]);
+        s1[r] = __ffma2_rn(make_float2(as_f(v1 & 0xF0u), as_f(v1 & 0xF000u)), make_float2(e.x, e.y), s1[r]);
+        s1[r] = __ffma2_rn(make_float2(as_f(v1 & 0xF00000u), as_f(t1 & 0xF00000u)), make_float2(e.z, e.w), s1[r]);
       }
     }
 #pragma unroll
     for (int r = 0; r < R; r++) {
-      const uint32_t dd = __ldg(reinterpret_cast<const uint32_t*>(srow[r]) + u);
-      acc[r] += h2f(dd & 0xFFFFu) * s0[r] + h2f(dd >> 16) * s1[r];
+      const uint32_t dd = ld_scale<SMEM>(reinterpret_cast<const uint32_t*>(srow[r]) + u);
+      const float d0 = h2f(dd & 0xFFFFu), d1 = h2f(dd >> 16);
+      acc[r] += d0 * ((s0[r].x + s0[r].y) * kTwo64 - 8.f * xs0) + d1 * ((s1[r].x + s1[r].y) * kTwo64 - 8.f * xs1);
     }
   }
 };
@@ -248,29 +255,30 @@ struct UnitDot<T_Q4_0> {
 template <>
 struct UnitDot<T_Q8_0> {
   static constexpr int EPU = 32;
-  static constexpr bool NEED_XS = false;
-  // Unit u = block u: 32 signed bytes, value q*d (quant.rs:176-180).
-  template <int R, class XA>
+  static constexpr bool NEED_XS = true;
+  // Unit u = block u: 32 signed bytes, value q*d (quant.rs:176-180).  Bytes are
+  // biased to q+128 (xor 0x80) and summed as d * (sum((q+128)*x) - 128*sum(x)).
+  template <int R, class XA, bool SMEM = false>
   __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&srow)[R],
-                                               int u, float, float, float (&acc)[R]) {
-    float s0[R], s1[R];
+                                               int u, float xs, float, float (&acc)[R]) {
+    float2 s[R];
 #pragma unroll
-    for (int r = 0; r < R; r++) s0[r] = s1[r] = 0.f;
+    for (int r = 0; r < R; r++) s[r] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 8; k++) {
       const float4 a = xa(k);
 #pragma unroll
       for (int r = 0; r < R; r++) {
-        const uint32_t v = w[r][k];
-        s0[r] = fmaf(sbyte_f(v, 0), a.x, s0[r]);
-        s1[r] = fmaf(sbyte_f(v, 8), a.y, s1[r]);
-        s0[r] = fmaf(sbyte_f(v, 16), a.z, s0[r]);
-        s1[r] = fmaf(sbyte_f(v, 24), a.w, s1[r]);
+        const uint32_t v = w[r][k] ^ 0x80808080u, t = v >> 8;
+        s[r] = __ffma2_rn(make_float2(as_f(v & 0xFFu), as_f(v & 0xFF00u)), make_float2(a.x, a.y), s[r]);
+        s[r] = __ffma2_rn(make_float2(as_f(v & 0xFF0000u), as_f(t & 0xFF0000u)), make_float2(a.z, a.w), s[r]);
       }
     }
 #pragma unroll
-    for (int r = 0; r < R; r++)
-      acc[r] += h2f(__ldg(reinterpret_cast<const unsigned short*>(srow[r]) + u)) * (s0[r] + s1[r]);
+    for (int r = 0; r < R; r++) {
+      const float d = h2f(ld_scale<SMEM>(reinterpret_cast<const unsigned short*>(srow[r]) + u));
+      acc[r] += d * ((s[r].x + s[r].y) * kTwo64 - 128.f * xs);
+    }
   }
 };
 
@@ -278,7 +286,7 @@ template <>
 struct UnitDot<T_F16> {
   static constexpr int EPU = 16;
   static constexpr bool NEED_XS = false;
-  template <int R, class XA>
+  template <int R, class XA, bool SMEM = false>
   __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&)[R], int,
                                                float, float, float (&acc)[R]) {
 #pragma unroll
@@ -300,7 +308,7 @@ template <>
 struct UnitDot<T_F32> {
   static constexpr int EPU = 8;
   static constexpr bool NEED_XS = false;
-  template <int R, class XA>
+  template <int R, class XA, bool SMEM = false>
   __device__ __forceinline__ static void accum(const uint32_t (&w)[R][8], XA xa, const uint8_t* const (&)[R], int,
                                                float, float, float (&acc)[R]) {
 #pragma unroll
@@ -318,6 +326,38 @@ struct UnitDot<T_F32> {
   }
 };
 
+// Stage the activation vector into shared memory: optional RMSNorm
+// (rms_norm_reference, compute.rs:291-319), the per-field pre-scale of the
+// weight format, the unit swizzle, and (formats with a min/bias term) the
+// unscaled sum of every 32 consecutive elements.
+template <int FMT>
+__device__ void stage_x(const float* __restrict__ x, const float* __restrict__ nw, float eps, int K, int Kp,
+                        float* sx, float* sxs, float* sred) {
+  using D = UnitDot<FMT>;
+  constexpr int EPU = D::EPU;
+  float rms = 1.f;
+  if (nw) rms = rms_of(block_sumsq(x, K, sred), K, eps);
+  // warp w stages 32-element chunks w, w+8, ...: coalesced loads, and the chunk
+  // sums come from one shuffle reduction
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int c = warp; c * 32 < Kp; c += GEMV_WARPS) {
+    const int e = c * 32 + lane;
+    float v = 0.f;
+    if (e < K) {
+      const float xv = x[e];
+      v = nw ? xv / rms * nw[e] : xv;
+    }
+    if (e < Kp) sx[swz<EPU>(e)] = v * prescale(field_off<FMT>(e % EPU));
+    if (D::NEED_XS) {
+      float s = v;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) sxs[c] = s;
+    }
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // epilogues (called by lane 0 of a warp with the R finished row sums)
 // ---------------------------------------------------------------------------
@@ -327,6 +367,7 @@ struct EpiStore {
     for (int i = 0; i < n; i++) y[row0 + i] = v[i];
   }
   __device__ void finish() {}
+  __device__ void flush() {}
 };
 
 struct EpiResidual {
@@ -336,6 +377,7 @@ struct EpiResidual {
     for (int i = 0; i < n; i++) out[row0 + i] = res ? res[row0 + i] + v[i] : v[i];
   }
   __device__ void finish() {}
+  __device__ void flush() {}
 };
 
 struct EpiRope {
@@ -387,6 +429,7 @@ struct EpiRope {
     }
   }
   __device__ void finish() {}
+  __device__ void flush() {}
 };
 
 struct EpiSwiGLU {
@@ -401,6 +444,7 @@ struct EpiSwiGLU {
     }
   }
   __device__ void finish() {}
+  __device__ void flush() {}
 };
 
 // Order-preserving 64-bit key: high word = float bits mapped to unsigned order,
@@ -423,6 +467,10 @@ struct EpiArgmax {
       const unsigned long long k = argmax_key(v[i], row_offset + row0 + i);
       best = k > best ? k : best;
     }
+  }
+  // barrier-free end of kernel: every thread that saw rows merges its own best
+  __device__ void flush() {
+    if (best) atomicMax(key, best);
   }
   __device__ void finish() {
     __shared__ unsigned long long sb[GEMV_WARPS];
@@ -478,7 +526,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(PackedMat W, cons
   };
   if (g < n_groups) load(g, 0);
   griddep_wait();
-  stage_x<EPU>(x, nw, eps, (int)W.K, (int)W.Kp, sx, sxs, sred, D::NEED_XS);
+  stage_x<FMT>(x, nw, eps, (int)W.K, (int)W.Kp, sx, sxs, sred);
   griddep_launch();
 
   for (; g < n_groups; g += gstride) {
@@ -496,8 +544,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(PackedMat W, cons
         const int u = (c * CH + j) * 32 + lane;
         if (u < units) {
           auto xa = [&](int k) { return ldx<EPU>(sx, u, k); };
-          const float xs_lo = D::NEED_XS ? sxs[2 * u] : 0.f;
-          const float xs_hi = D::NEED_XS ? sxs[2 * u + 1] : 0.f;
+          const float xs_lo = D::NEED_XS ? sxs[u * (EPU / 32)] : 0.f;
+          const float xs_hi = (D::NEED_XS && EPU == 64) ? sxs[2 * u + 1] : 0.f;
           D::template accum<R>(w[j], xa, srow, u, xs_lo, xs_hi, acc);
         }
       }
@@ -511,6 +559,221 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(PackedMat W, cons
     if (lane == 0) epi(g * R, acc, min(R, (int)W.M - g * R));
   }
   epi.finish();
+}
+
+// ---------------------------------------------------------------------------
+// the TMA-pipelined GEMV (quantized formats)
+// ---------------------------------------------------------------------------
+// One persistent CTA per SM (two when shared memory allows).  Warp 8 is the
+// producer: its lane 0 streams 64-row x 16-unit weight tiles, with their scale
+// headers, into a ring of shared-memory stages through 2D TMA loads (no cluster
+// multicast) that complete on per-stage mbarriers.  Warps 0-7 consume: thread t
+// handles rows 4*(t/16) .. +3 of the tile and unit t%16 of the chunk, so every x
+// chunk read from shared memory serves four rows.  Bytes in flight per SM are
+// the ring (tens of KB), independent of registers, and scale headers arrive with
+// their weights instead of as dependent loads.  The first stages are requested
+// before waiting on the previous kernel (weights never depend on it).
+//
+// Every mbarrier wait is bounded (kWaitLimitCycles); on expiry the thread sets
+// g_rf_error and returns, and the producer first waits, again bounded, for the
+// copies it has in flight.  No wait depends on another CTA or another GPU.
+constexpr int TMA_TR = 64;    // rows per tile
+constexpr int TMA_NU = 16;    // 32-byte units per row per chunk
+constexpr int TMA_CONSUMERS = 256;
+constexpr int TMA_THREADS = TMA_CONSUMERS + 32;
+constexpr long long kWaitLimitCycles = 4000000000LL;  // about 2 s at 1.9 GHz
+
+__device__ unsigned g_rf_error;  // nonzero after a bounded wait gave up
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for phase `parity` of `bar`; false when the limit expired.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > kWaitLimitCycles) return false;
+  return true;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Block-wide sum of squares over NT threads (every thread of the block).
+template <int NT>
+__device__ float block_sumsq_nt(const float* __restrict__ x, int n, float* sred) {
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += NT) {
+    const float v = x[i];
+    s = fmaf(v, v, s);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < NT / 32; w++) t += sred[w];
+    sred[32] = t;
+  }
+  __syncthreads();
+  const float r = sred[32];
+  __syncthreads();
+  return r;
+}
+
+// stage_x for NT threads over Kc >= Kp elements (zero beyond K).
+template <int FMT, int NT>
+__device__ void stage_x_nt(const float* __restrict__ x, const float* __restrict__ nw, float eps, int K, int Kc,
+                           float* sx, float* sxs, float* sred) {
+  using D = UnitDot<FMT>;
+  constexpr int EPU = D::EPU;
+  float rms = 1.f;
+  if (nw) rms = rms_of(block_sumsq_nt<NT>(x, K, sred), K, eps);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int c = warp; c * 32 < Kc; c += NT / 32) {
+    const int e = c * 32 + lane;
+    float v = 0.f;
+    if (e < K) {
+      const float xv = x[e];
+      v = nw ? xv / rms * nw[e] : xv;
+    }
+    sx[swz<EPU>(e)] = v * prescale(field_off<FMT>(e % EPU));
+    if (D::NEED_XS) {
+      float s = v;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) sxs[c] = s;
+    }
+  }
+  __syncthreads();
+}
+
+template <int FMT, class Epi>
+__global__ void __launch_bounds__(TMA_THREADS, 1)
+    gemv_tma_kernel(const __grid_constant__ CUtensorMap tm_qs, const __grid_constant__ CUtensorMap tm_sc, PackedMat W,
+                    const float* __restrict__ x, const float* __restrict__ nw, float eps, int nstages,
+                    uint32_t sc_chunk_bytes, Epi epi) {
+  using D = UnitDot<FMT>;
+  constexpr int EPU = D::EPU;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const uint32_t qs_tile = TMA_TR * TMA_NU * 32;
+  const uint32_t sc_tile = TMA_TR * sc_chunk_bytes;
+  const uint32_t stage_bytes = (qs_tile + sc_tile + 127) & ~127u;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + nstages;
+  uint8_t* stages = smem_raw + 128;
+  const int units = (int)W.units;
+  const int nch = (units + TMA_NU - 1) / TMA_NU;
+  const int Kc = nch * TMA_NU * EPU;
+  float* sx = reinterpret_cast<float*>(stages + (size_t)nstages * stage_bytes);
+  float* sxs = sx + Kc;
+  float* sred = sxs + Kc / 32;
+  const int ntiles = (int)((W.M + TMA_TR - 1) / TMA_TR);
+  const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total = my_tiles * nch;
+  const bool producer = tid == TMA_CONSUMERS;
+
+  if (producer) {
+    for (int i = 0; i < nstages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], TMA_CONSUMERS / 32);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  auto issue = [&](int k) {
+    const int slot = k % nstages;
+    const int t = (int)blockIdx.x + (k / nch) * (int)gridDim.x, c = k % nch;
+    uint8_t* st = stages + (size_t)slot * stage_bytes;
+    mbar_expect_tx(&full[slot], qs_tile + sc_tile);
+    tma_load_2d(st, &tm_qs, c * TMA_NU * 8, t * TMA_TR, &full[slot]);
+    tma_load_2d(st + qs_tile, &tm_sc, c * (int)(sc_chunk_bytes / 4), t * TMA_TR, &full[slot]);
+  };
+  if (producer)
+    for (int k = 0; k < min(nstages, total); k++) issue(k);
+  griddep_wait();
+  stage_x_nt<FMT, TMA_THREADS>(x, nw, eps, (int)W.K, Kc, sx, sxs, sred);
+  griddep_launch();
+
+  if (tid >= TMA_CONSUMERS) {  // producer warp
+    if (lane == 0) {
+      for (int k = nstages; k < total; k++) {
+        const int slot = k % nstages;
+        if (!mbar_wait(&empty[slot], ((k / nstages) - 1) & 1)) {
+          atomicExch(&g_rf_error, 1u);
+          for (int j = max(0, k - nstages); j < k; j++)  // let the copies in flight land
+            if (!mbar_wait(&full[j % nstages], (j / nstages) & 1)) break;
+          return;
+        }
+        issue(k);
+      }
+    }
+    return;
+  }
+  const int g = tid >> 4, s = tid & 15;
+  int k = 0;
+  for (int ti = 0; ti < my_tiles; ti++) {
+    const int t = (int)blockIdx.x + ti * (int)gridDim.x;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < nch; c++, k++) {
+      const int slot = k % nstages;
+      if (!mbar_wait(&full[slot], (k / nstages) & 1)) {
+        atomicExch(&g_rf_error, 2u);
+        return;
+      }
+      const uint8_t* st = stages + (size_t)slot * stage_bytes;
+      const int u = c * TMA_NU + s;
+      if (u < units) {
+        uint32_t w[4][8];
+        const uint8_t* srow[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          const uint4* p = reinterpret_cast<const uint4*>(st + (size_t)(4 * g + r) * (TMA_NU * 32) + s * 32);
+          const uint4 a = p[0], b = p[1];
+          w[r][0] = a.x; w[r][1] = a.y; w[r][2] = a.z; w[r][3] = a.w;
+          w[r][4] = b.x; w[r][5] = b.y; w[r][6] = b.z; w[r][7] = b.w;
+          srow[r] = st + qs_tile + (size_t)(4 * g + r) * sc_chunk_bytes;
+        }
+        auto xa = [&](int kk) { return ldx<EPU>(sx, u, kk); };
+        const float xs_lo = D::NEED_XS ? sxs[u * (EPU / 32)] : 0.f;
+        const float xs_hi = (D::NEED_XS && EPU == 64) ? sxs[2 * u + 1] : 0.f;
+        D::template accum<4, decltype(xa), true>(w, xa, srow, s, xs_lo, xs_hi, acc);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+#pragma unroll
+      for (int o = 8; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    }
+    const int row0 = t * TMA_TR + 4 * g;
+    if (s == 0 && row0 < (int)W.M) epi(row0, acc, min(4, (int)W.M - row0));
+  }
+  epi.flush();
 }
 
 // Batched variant for the standalone op: x[b][K] read through L1, R = 1.
@@ -534,11 +797,19 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_batched_kernel(PackedMat W,
 #pragma unroll
       for (int b = 0; b < B; b++) {
         const float* xb = x + (size_t)b * W.Kp + (size_t)u * EPU;
-        auto xa = [&](int c) { return __ldg(reinterpret_cast<const float4*>(xb) + c); };
+        auto xa = [&](int c) {
+          const float4 f = __ldg(reinterpret_cast<const float4*>(xb) + c);
+          return make_float4(f.x * prescale(field_off<FMT>(4 * c)), f.y * prescale(field_off<FMT>(4 * c + 1)),
+                             f.z * prescale(field_off<FMT>(4 * c + 2)), f.w * prescale(field_off<FMT>(4 * c + 3)));
+        };
         float xs_lo = 0.f, xs_hi = 0.f;
         if (D::NEED_XS) {
 #pragma unroll 8
-          for (int l = 0; l < 32; l++) { xs_lo += xb[l]; xs_hi += xb[32 + l]; }
+          for (int l = 0; l < 32; l++) xs_lo += xb[l];
+          if (EPU == 64) {
+#pragma unroll 8
+            for (int l = 0; l < 32; l++) xs_hi += xb[32 + l];
+          }
         }
         float a1[1] = {acc[b]};
         D::template accum<1>(w, xa, srow, u, xs_lo, xs_hi, a1);
@@ -617,33 +888,115 @@ static cudaError_t run_gemv_r(const Launch& L, const PackedMat& W, const float* 
   }
 }
 
-// Rows per warp group: 4 when a row has at most 64 units (every lane then holds
-// 2 units of each of 4 rows), else 2 (4 units of each of 2 rows).  Both are even,
-// which the RoPE and SwiGLU row pairs need.
+constexpr size_t kMaxSmem = 227 * 1024;
+
+template <int FMT, class Epi>
+static cudaError_t run_gemv_tma_t(const Launch& L, const PackedMat& W, const GemvMaps& m, const float* x,
+                                  const float* nw, float eps, Epi epi) {
+  constexpr int EPU = UnitDot<FMT>::EPU;
+  auto k = gemv_tma_kernel<FMT, Epi>;
+  const int nch = (int)((W.units + TMA_NU - 1) / TMA_NU);
+  const size_t Kc = (size_t)nch * TMA_NU * EPU;
+  const size_t x_bytes = (Kc + Kc / 32 + 40) * sizeof(float);
+  const size_t stage_bytes = ((size_t)TMA_TR * TMA_NU * 32 + (size_t)TMA_TR * m.sc_chunk_bytes + 127) & ~(size_t)127;
+  if (128 + 2 * stage_bytes + x_bytes > kMaxSmem) return cudaErrorInvalidValue;
+  const int nstages = (int)std::min<size_t>(6, (kMaxSmem - 128 - x_bytes) / stage_bytes);
+  const size_t smem = 128 + (size_t)nstages * stage_bytes + x_bytes;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int ntiles = (int)((W.M + TMA_TR - 1) / TMA_TR);
+  const int blocks = std::max(1, std::min(ntiles, num_sms()));
+  return launch_k(L, k, dim3(blocks), dim3(TMA_THREADS), smem, m.qs, m.sc, W, x, nw, eps, nstages,
+                  m.sc_chunk_bytes, epi);
+}
+
+// Rows per warp group of the register-streaming GEMV: 4 when a row has at most
+// 64 units (every lane then holds 2 units of each of 4 rows), else 2 (4 units of
+// each of 2 rows).  Both are even, which the RoPE and SwiGLU row pairs need.
 template <class Epi>
-static cudaError_t run_gemv(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
-                            Epi epi) {
+static cudaError_t run_gemv(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x,
+                            const float* nw, float eps, Epi epi) {
+  if (maps && maps->ok) {
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (W.type) {
+      case T_Q4_K: e = run_gemv_tma_t<T_Q4_K>(L, W, *maps, x, nw, eps, epi); break;
+      case T_Q4_0: e = run_gemv_tma_t<T_Q4_0>(L, W, *maps, x, nw, eps, epi); break;
+      case T_Q8_0: e = run_gemv_tma_t<T_Q8_0>(L, W, *maps, x, nw, eps, epi); break;
+    }
+    if (e != cudaErrorInvalidValue) return e;  // too large for shared memory: fall through
+  }
   if (W.units <= 64) return run_gemv_r<4>(L, W, x, nw, eps, epi);
   return run_gemv_r<2>(L, W, x, nw, eps, epi);
 }
 
-cudaError_t gemv_store(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps, float* y) {
-  return run_gemv(L, W, x, nw, eps, EpiStore{y});
+cudaError_t gemv_store(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* nw,
+                       float eps, float* y) {
+  return run_gemv(L, W, maps, x, nw, eps, EpiStore{y});
 }
-cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const float* x, const float* res, float* out) {
-  return run_gemv(L, W, x, nullptr, 0.f, EpiResidual{res, out});
+cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* res,
+                          float* out) {
+  return run_gemv(L, W, maps, x, nullptr, 0.f, EpiResidual{res, out});
 }
-cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
-                          const RopeQKVArgs& a) {
-  return run_gemv(L, W, x, nw, eps, EpiRope{a});
+cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x,
+                          const float* nw, float eps, const RopeQKVArgs& a) {
+  return run_gemv(L, W, maps, x, nw, eps, EpiRope{a});
 }
-cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
-                        float* act) {
-  return run_gemv(L, W, x, nw, eps, EpiSwiGLU{act});
+cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* nw,
+                        float eps, float* act) {
+  return run_gemv(L, W, maps, x, nw, eps, EpiSwiGLU{act});
 }
-cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const float* x, const float* nw, float eps,
-                        float* logits, unsigned long long* key, uint32_t row_offset) {
-  return run_gemv(L, W, x, nw, eps, EpiArgmax{logits, key, row_offset, 0ull});
+cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* nw,
+                        float eps, float* logits, unsigned long long* key, uint32_t row_offset) {
+  return run_gemv(L, W, maps, x, nw, eps, EpiArgmax{logits, key, row_offset, 0ull});
+}
+
+// ---- TMA descriptors ----------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+// 2D map over rows of `row_bytes` (uint32 elements), box = box_words x TMA_TR rows.
+static bool encode_rows(CUtensorMap* tm, void* base, uint64_t row_bytes, uint64_t stride, uint32_t rows,
+                        uint32_t box_words) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || row_bytes % 4 || stride % 16 || ((uintptr_t)base & 15) || box_words == 0 || box_words > 256)
+    return false;
+  const cuuint64_t dims[2] = {row_bytes / 4, rows};
+  const cuuint64_t strides[1] = {stride};
+  const cuuint32_t box[2] = {box_words, (cuuint32_t)TMA_TR};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_gemv_maps(const PackedMat& W, GemvMaps* out) {
+  out->ok = false;
+  uint32_t sc_chunk = 0;
+  switch (W.type) {
+    case T_Q4_K: sc_chunk = TMA_NU / 4 * 16; break;  // one 16-byte header per 4 units
+    case T_Q4_0: sc_chunk = TMA_NU * 4; break;       // two f16 scales per unit
+    case T_Q8_0: sc_chunk = TMA_NU * 2; break;       // one f16 scale per unit
+    default: return false;
+  }
+  if (!encode_rows(&out->qs, W.qs, W.qs_stride, W.qs_stride, W.M, TMA_NU * 8)) return false;
+  if (!encode_rows(&out->sc, W.sc, W.sc_stride, W.sc_stride, W.M, sc_chunk / 4)) return false;
+  out->sc_chunk_bytes = sc_chunk;
+  out->ok = true;
+  return true;
 }
 
 template <int FMT>
@@ -870,6 +1223,7 @@ constexpr int ATT_WARPS = ATT_THREADS / 32;
 constexpr int ATT_MAX_CHUNK = 512;
 constexpr int ATT_MIN_CHUNK = 32;
 constexpr int ATT_UNROLL = 8;
+constexpr int ATT_MERGE_SPLITS = 64;  // merges of up to this many splits take the parallel path
 
 __host__ __device__ inline int attn_nsplit(int ctx, int max_splits) {
   int s = (ctx + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK;
@@ -908,6 +1262,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(AttnArgs a) {
   __shared__ float ssc[G][ATT_MAX_CHUNK];
   __shared__ float sred[ATT_WARPS][G][DPL * 32];
   __shared__ float sm[G], sl[G];
+  __shared__ float s_w[ATT_MERGE_SPLITS][G];
   __shared__ int s_last;
   const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1064,18 +1419,62 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(AttnArgs a) {
   }
   __threadfence();
   const float* pall = a.part + slot * (size_t)G * (hd + 2);
-  for (int t = threadIdx.x; t < G * hd; t += ATT_THREADS) {
-    const int h = t / hd, d = t % hd;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(pall + ((size_t)s * G + h) * (hd + 2) + hd));
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < nsplit; s++) {
-      const float* ps = pall + ((size_t)s * G + h) * (hd + 2);
-      const float sc = expf(__ldcg(ps + hd) - M);
-      L = fmaf(sc, __ldcg(ps + hd + 1), L);
-      O = fmaf(sc, __ldcg(ps + d), O);
+  if (nsplit <= ATT_MERGE_SPLITS) {
+    // one warp per head: split weights exp(m_s - M) / sum_s exp(m_s - M) l_s in one load round
+    for (int h = warp; h < G; h += ATT_WARPS) {
+      float ms[ATT_MERGE_SPLITS / 32], ls[ATT_MERGE_SPLITS / 32];
+      float M = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) {
+        const int sp = lane + 32 * j;
+        const float* ps = pall + ((size_t)sp * G + h) * (hd + 2);
+        ms[j] = sp < nsplit ? __ldcg(ps + hd) : -INFINITY;
+        ls[j] = sp < nsplit ? __ldcg(ps + hd + 1) : 0.f;
+        M = fmaxf(M, ms[j]);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float L = 0.f;
+#pragma unroll
+      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) {
+        ms[j] = lane + 32 * j < nsplit ? expf(ms[j] - M) : 0.f;
+        L = fmaf(ms[j], ls[j], L);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+#pragma unroll
+      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) s_w[lane + 32 * j][h] = ms[j] / L;
     }
-    out_b[(size_t)h * hd + d] = O / L;
+    __syncthreads();
+    // every output element: sum_s w_s * O_s, eight independent loads at a time
+    for (int t = threadIdx.x; t < G * hd; t += ATT_THREADS) {
+      const int h = t / hd, d = t % hd;
+      float O = 0.f;
+      for (int s0 = 0; s0 < nsplit; s0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          v[j] = s0 + j < nsplit ? __ldcg(pall + ((size_t)(s0 + j) * G + h) * (hd + 2) + d) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          if (s0 + j < nsplit) O = fmaf(s_w[s0 + j][h], v[j], O);
+      }
+      out_b[(size_t)h * hd + d] = O;
+    }
+  } else {
+    for (int t = threadIdx.x; t < G * hd; t += ATT_THREADS) {
+      const int h = t / hd, d = t % hd;
+      float M = -INFINITY;
+      for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(pall + ((size_t)s * G + h) * (hd + 2) + hd));
+      float L = 0.f, O = 0.f;
+      for (int s = 0; s < nsplit; s++) {
+        const float* ps = pall + ((size_t)s * G + h) * (hd + 2);
+        const float sc = expf(__ldcg(ps + hd) - M);
+        L = fmaf(sc, __ldcg(ps + hd + 1), L);
+        O = fmaf(sc, __ldcg(ps + d), O);
+      }
+      out_b[(size_t)h * hd + d] = O / L;
+    }
   }
   if (threadIdx.x == 0) a.counters[(size_t)b * a.n_kv_heads + kvh] = 0u;
   griddep_launch();

@@ -1,5 +1,6 @@
 // rf_kernels.cuh - device data layouts and kernel launchers of the decode engine.
 #pragma once
+#include <cuda.h>  // CUtensorMap (types only; the encoder is fetched from the driver at run time)
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -66,6 +67,18 @@ inline uint32_t padded_k(int type, uint32_t K) {
 }
 bool packed_geometry(int type, uint32_t M, uint32_t K, PackedMat* out);  // fills all but pointers
 
+// TMA descriptors of a packed quantized matrix for the pipelined GEMV: 64-row x
+// 16-unit boxes of qs (512 B per row) and the matching scale bytes.  ok == false
+// (F32/F16, or rows whose scale stride is not a multiple of 16 bytes) selects the
+// register-streaming GEMV instead.
+struct GemvMaps {
+  CUtensorMap qs, sc;
+  uint32_t sc_chunk_bytes;
+  bool ok;
+};
+// Builds the descriptors for the device pointers in W (false: not TMA-eligible).
+bool make_gemv_maps(const PackedMat& W, GemvMaps* out);
+
 // ---- launch helpers -------------------------------------------------------
 // Every engine kernel is launched with programmatic dependent launch so its
 // weight prefetch overlaps the previous kernel's tail.
@@ -81,10 +94,10 @@ cudaError_t launch_pack(const uint8_t* gguf, const int* src_row_of, PackedMat ds
 // ---- GEMV families -------------------------------------------------------
 // All take x (f32, K elements) and optionally RMSNorm it on the fly with
 // norm_w/eps (rms_norm_reference, compute.rs:291-319).
-cudaError_t gemv_store(const Launch& L, const PackedMat& W, const float* x, const float* norm_w, float eps,
+cudaError_t gemv_store(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* norm_w, float eps,
                        float* y);
 // out[row] = (res ? res[row] : 0) + (W.x)[row]   (residual add, model_executor.rs:213-215, 231-233)
-cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const float* x, const float* res, float* out);
+cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* res, float* out);
 
 struct RopeQKVArgs {
   uint32_t q_rows, kv_rows, head_dim, max_seq;
@@ -98,14 +111,14 @@ struct RopeQKVArgs {
   int kv_f32;
 };
 // Fused: RMSNorm(attn_norm) -> packed [Q;K;V] matvec -> RoPE on Q/K pairs -> K/V append.
-cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const float* x, const float* norm_w, float eps,
+cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* norm_w, float eps,
                           const RopeQKVArgs& a);
 // Fused: RMSNorm(ffn_norm) -> packed [gate_j; up_j] matvec -> act[j] = silu(g)*u.
-cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const float* x, const float* norm_w, float eps,
+cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* norm_w, float eps,
                         float* act);
 // Fused LM head: optional RMSNorm(output_norm) -> logits (nullable) -> packed
 // argmax key (atomicMax of (ordered value, ~global_row)).
-cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const float* x, const float* norm_w, float eps,
+cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* norm_w, float eps,
                         float* logits, unsigned long long* key, uint32_t row_offset);
 // Batched standalone GEMV: y[b][row] for b < batch (x read through L1).
 cudaError_t gemv_batched(cudaStream_t s, const PackedMat& W, const float* x, int batch, float* y);

@@ -10,6 +10,7 @@ using namespace rf;
 
 struct rf_matrix {
   PackedMat m{};
+  GemvMaps maps{};
   void* block = nullptr;
   uint64_t bytes = 0;
   int device = 0;
@@ -125,6 +126,7 @@ int rf_matrix_create(int type, const void* bytes, uint64_t nbytes, int on_device
     delete m;
     return set_error(RF_ECUDA, "packing failed: %s", cudaGetErrorString(ce));
   }
+  make_gemv_maps(m->m, &m->maps);
   *out = m;
   return RF_OK;
 }
@@ -146,7 +148,7 @@ int rf_qmatvec(const rf_matrix* m, const float* dX, float* dY, int batch, void* 
   if (batch < 1 || batch > 8) return set_error(RF_EINVAL, "batch %d out of range 1..8", batch);
   cudaStream_t s = (cudaStream_t)stream;
   if (batch == 1) {
-    RF_CUDA(gemv_store(Launch{s, false}, m->m, dX, nullptr, 0.f, dY));
+    RF_CUDA(gemv_store(Launch{s, false}, m->m, &m->maps, dX, nullptr, 0.f, dY));
     return RF_OK;
   }
   if (m->m.K != m->m.Kp)
