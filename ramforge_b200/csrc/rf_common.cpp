@@ -222,8 +222,8 @@ int llama_config_from_gguf(const Gguf& g, rf_model_config* c) {
 int host_packed_init(int type, uint32_t M, uint32_t K, HostPacked* out) {
   if (!packed_geometry(type, M, K, &out->geo))
     return set_error(RF_EINVAL, "type %d cannot hold a %u x %u matrix", type, M, K);
-  out->qs.assign(out->geo.qs_stride * M, 0);
-  out->sc.assign(out->geo.sc_stride * M, 0);
+  out->qs.assign(packed_qs_bytes(out->geo), 0);
+  out->sc.assign(packed_sc_bytes(out->geo), 0);
   return RF_OK;
 }
 
@@ -236,23 +236,32 @@ int pack_rows(const uint8_t* src, uint64_t src_row_bytes, uint32_t src_blk_off, 
   const size_t n = src_rows.size();
   if (n && (uint64_t)dst_row0 + (uint64_t)(n - 1) * dst_row_step >= g.M)
     return set_error(RF_EINVAL, "packing rows exceed the destination");
+  uint8_t* Q = out->qs.data();
+  uint8_t* C = out->sc.data();
   auto work = [&](size_t a, size_t b) {
     for (size_t r = a; r < b; r++) {
       const uint8_t* s = src + (uint64_t)src_rows[r] * src_row_bytes + (uint64_t)src_blk_off * bsz;
-      const uint64_t dr = dst_row0 + (uint64_t)r * dst_row_step;
-      uint8_t* q = out->qs.data() + dr * g.qs_stride;
-      uint8_t* c = g.sc_stride ? out->sc.data() + dr * g.sc_stride : nullptr;
+      const uint32_t dr = (uint32_t)(dst_row0 + (uint64_t)r * dst_row_step);
       switch (g.type) {
         case T_F32:
-        case T_F16: memcpy(q, s, (size_t)nblk * bsz); break;
+        case T_F16: memcpy(Q + qs_byte_off(g, dr, 0), s, (size_t)nblk * bsz); break;
         case T_Q8_0:
-          for (uint32_t b = 0; b < nblk; b++, s += 34) { memcpy(c + 2 * b, s, 2); memcpy(q + 32 * b, s + 2, 32); }
+          for (uint32_t k = 0; k < nblk; k++, s += 34) {
+            memcpy(C + sc_byte_off(g, dr, 2ull * k), s, 2);
+            memcpy(Q + qs_byte_off(g, dr, 32ull * k), s + 2, 32);
+          }
           break;
         case T_Q4_0:
-          for (uint32_t b = 0; b < nblk; b++, s += 18) { memcpy(c + 2 * b, s, 2); memcpy(q + 16 * b, s + 2, 16); }
+          for (uint32_t k = 0; k < nblk; k++, s += 18) {
+            memcpy(C + sc_byte_off(g, dr, 2ull * k), s, 2);
+            memcpy(Q + qs_byte_off(g, dr, 16ull * k), s + 2, 16);
+          }
           break;
         case T_Q4_K:
-          for (uint32_t b = 0; b < nblk; b++, s += 144) { memcpy(c + 16 * b, s, 16); memcpy(q + 128 * b, s + 16, 128); }
+          for (uint32_t k = 0; k < nblk; k++, s += 144) {
+            memcpy(C + sc_byte_off(g, dr, 16ull * k), s, 16);
+            for (int p = 0; p < 4; p++) memcpy(Q + qs_byte_off(g, dr, 128ull * k + 32 * p), s + 16 + 32 * p, 32);
+          }
           break;
       }
     }

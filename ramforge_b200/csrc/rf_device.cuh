@@ -1,0 +1,144 @@
+// rf_device.cuh - device helpers and launch plumbing shared by the kernel
+// translation units (rf_kernels.cu, rf_gemv.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <utility>
+
+#include "rf_kernels.cuh"
+
+namespace rf {
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Streaming loads of weights (read once per token: no L1 allocation).
+__device__ __forceinline__ void ldg256(const uint8_t* p, uint32_t (&w)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void ldg128(const uint8_t* p, uint32_t (&w)[4]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+               : "l"(p));
+}
+__device__ __forceinline__ void ldg64(const uint8_t* p, uint32_t (&w)[2]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v2.b32 {%0,%1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "l"(p));
+}
+
+// f16 -> f32 as the reference decodes block scales and F16 tensors
+// (quant.rs:40-65, tensor.rs:1017-1041): IEEE for normal numbers, but a
+// subnormal half comes out at half its IEEE value (the normalising loop's
+// exponent is one short).  The engine reproduces that for bit-parity.
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+  const float f = __half2float(__ushort_as_half((unsigned short)bits16));
+  return (bits16 & 0x7C00u) ? f : f * 0.5f;
+}
+
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+
+// Block-wide sum of squares of x[0..n).  Threads 0..255 accumulate elements
+// i, i+256, ... and warps 0..7 are summed in order, whatever the block size
+// (NT >= 256, a multiple of 32), so every kernel that normalises the same vector
+// produces bit-identical results.  sred holds at least 33 floats.
+template <int NT>
+__device__ __forceinline__ float block_sumsq_n(const float* __restrict__ x, int n, float* sred) {
+  static_assert(NT >= GEMV_THREADS && NT % 32 == 0, "block too small");
+  float s = 0.f;
+  if (threadIdx.x < GEMV_THREADS)
+    for (int i = threadIdx.x; i < n; i += GEMV_THREADS) {
+      const float v = x[i];
+      s = fmaf(v, v, s);
+    }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0 && threadIdx.x < GEMV_THREADS) sred[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < GEMV_WARPS; w++) t += sred[w];
+    sred[32] = t;
+  }
+  __syncthreads();
+  const float r = sred[32];
+  __syncthreads();
+  return r;
+}
+__device__ __forceinline__ float block_sumsq(const float* __restrict__ x, int n, float* sred) {
+  return block_sumsq_n<GEMV_THREADS>(x, n, sred);
+}
+
+// Block-wide sum of squares of x[0..n) (n a multiple of 4, x 16-byte aligned,
+// not written while the kernel runs): thread t takes float4s t, t+NT, ... in
+// order, then warps and warp partials are summed in a fixed order.  Up to four
+// loads per thread are in flight at once.
+template <int NT>
+__device__ __forceinline__ float block_sumsq_v4(const float* __restrict__ x, int n, float* sred) {
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const int nq = n / 4;
+  float s = 0.f;
+  for (int q0 = threadIdx.x; q0 < nq; q0 += 4 * NT) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) v[u] = q0 + u * NT < nq ? __ldg(x4 + q0 + u * NT) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      s = fmaf(v[u].x, v[u].x, s);
+      s = fmaf(v[u].y, v[u].y, s);
+      s = fmaf(v[u].z, v[u].z, s);
+      s = fmaf(v[u].w, v[u].w, s);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < NT / 32; w++) t += sred[w];
+    sred[32] = t;
+  }
+  __syncthreads();
+  const float r = sred[32];
+  __syncthreads();
+  return r;
+}
+
+// RMSNorm scale given the sum of squares: rms = sqrt(sum/n + eps), and the
+// normalised element is x / rms * w   (compute.rs:312-317).
+__device__ __forceinline__ float rms_of(float ss, int n, float eps) { return sqrtf(ss / (float)n + eps); }
+
+inline int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(const Launch& L, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = L.stream;
+  cudaLaunchAttribute attr[1];
+  if (L.pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
+}  // namespace rf

@@ -74,7 +74,6 @@ struct Layer {
   void* block = nullptr;
   uint64_t bytes = 0;
   PackedMat qkv{}, wo{}, gateup{}, down{};
-  GemvMaps mq{}, mo{}, mg{}, md{};  // TMA descriptors of the four matrices
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
 };
@@ -109,7 +108,6 @@ struct rf_engine {
   void* embd_block = nullptr;
   void* out_block = nullptr;
   float* out_norm = nullptr;
-  GemvMaps lm_maps{};  // TMA descriptors of the LM-head matrix (output or this rank's tied rows)
   std::vector<Layer> layers;
   std::vector<uint8_t> plan_resident;  // residency plan (1 = keep resident)
   // KV cache
@@ -121,6 +119,7 @@ struct rf_engine {
         *v_cur = nullptr, *att = nullptr, *act = nullptr, *logits = nullptr, *logits_all = nullptr,
         *attn_part = nullptr;
   unsigned* attn_counters = nullptr;
+  GemvScratch gws{};  // split-K partials + tile counters of the quantized GEMV
   StepIO* d_io = nullptr;
   uint32_t* d_hist = nullptr;  // token produced at each position (device-side greedy history)
   unsigned long long* d_key = nullptr;
@@ -194,6 +193,13 @@ int validate_config(const rf_model_config& c, int tp) {
   return RF_OK;
 }
 
+// Vocabulary rows per rank: an even split rounded up to whole 64-row tiles of
+// the packed LM head, so every shard starts on a tile (the last one is shorter).
+uint32_t vocab_chunk_of(const rf_model_config& c, int tp) {
+  if (tp <= 1) return c.vocab_size;
+  return ((c.vocab_size + tp - 1) / tp + QT_ROWS - 1) / QT_ROWS * QT_ROWS;
+}
+
 int shard_plan(const rf_model_config& c, int tp, int rank, int block, rf_tp_shard* o) {
   if (tp < 1 || rank < 0 || rank >= tp) return set_error(RF_EINVAL, "tp_rank %d / tp_size %d invalid", rank, tp);
   RF_TRY(validate_config(c, tp));
@@ -204,9 +210,12 @@ int shard_plan(const rf_model_config& c, int tp, int rank, int block, rf_tp_shar
   o->q_head_offset = o->kv_head_offset * G;
   o->ff_rows = c.n_ff / tp;
   o->ff_offset = o->ff_rows * rank;
-  const uint32_t chunk = (c.vocab_size + tp - 1) / tp;
+  const uint32_t chunk = vocab_chunk_of(c, tp);
   o->vocab_offset = std::min(c.vocab_size, chunk * rank);
   o->vocab_rows = std::min(c.vocab_size, o->vocab_offset + chunk) - o->vocab_offset;
+  if (o->vocab_rows == 0)
+    return set_error(RF_EINVAL, "tp %d: a vocabulary of %u rows leaves rank %d no whole 64-row tile", tp,
+                     c.vocab_size, rank);
   if (tp > 1 && block > 1) {  // row-parallel column slices must not cut a quant block
     const uint32_t q_cols = o->q_heads * c.head_dim;
     if (q_cols % block || o->ff_rows % block)
@@ -230,7 +239,7 @@ int setup_geometry(rf_engine* e) {
   e->kv_local = e->kvh_local * c.head_dim;
   e->ff_local = sh.ff_rows;
   e->ff_off = sh.ff_offset;
-  e->vocab_chunk = (c.vocab_size + e->tp - 1) / e->tp;
+  e->vocab_chunk = vocab_chunk_of(c, e->tp);
   e->vocab_off = sh.vocab_offset;
   e->vocab_local = sh.vocab_rows;
   e->max_seq = e->rt.max_seq_len ? e->rt.max_seq_len : c.context_length;
@@ -261,6 +270,22 @@ int engine_init_device(rf_engine* e) {
   // scratch
   const uint32_t G = c.n_heads / c.n_kv_heads;
   const uint64_t part_f = attn_part_floats(1, e->kvh_local, e->max_splits, G, c.head_dim);
+  // GEMV split-K scratch for any matrix this rank can hold, sized for the
+  // smallest chunk (128 elements, Q8_0)
+  uint64_t gpart = 0;
+  uint32_t gcnt = 0;
+  const uint32_t shapes[5][2] = {{e->q_local + 2 * e->kv_local, c.n_embd},
+                                 {c.n_embd, e->q_local},
+                                 {2 * e->ff_local, c.n_embd},
+                                 {c.n_embd, e->ff_local},
+                                 {e->vocab_local, c.n_embd}};
+  for (auto& sh : shapes) {
+    const uint64_t mp = (sh[0] + QT_ROWS - 1) / QT_ROWS * QT_ROWS;
+    gpart = std::max<uint64_t>(gpart, mp * ((sh[1] + 127) / 128));
+    gcnt = std::max<uint32_t>(gcnt, (uint32_t)(mp / QT_ROWS));
+  }
+  e->gws.part_floats = gpart;
+  e->gws.n_cnt = gcnt;
   struct Item { void** p; uint64_t bytes; };
   const uint64_t vl_pad = (uint64_t)e->vocab_chunk;
   std::vector<Item> items = {
@@ -270,6 +295,7 @@ int engine_init_device(rf_engine* e) {
       {(void**)&e->att, 4ull * e->q_local},         {(void**)&e->act, 4ull * e->ff_local},
       {(void**)&e->logits, 4ull * vl_pad},          {(void**)&e->logits_all, 4ull * vl_pad * e->tp},
       {(void**)&e->attn_part, 4ull * part_f},       {(void**)&e->attn_counters, 4ull * e->kvh_local},
+      {(void**)&e->gws.part, 4ull * gpart},         {(void**)&e->gws.cnt, 4ull * gcnt},
       {(void**)&e->d_io, sizeof(StepIO)},           {(void**)&e->d_key, 8},
       {(void**)&e->d_hist, 4ull * e->max_seq},
       {(void**)&e->rope_cs, 8ull * e->max_seq * (c.head_dim / 2)}};
@@ -358,6 +384,7 @@ std::vector<int> rope_pair_rows(uint32_t h0, uint32_t nh, uint32_t hd) {
   return r;
 }
 
+// Device image of a packed matrix: qs | sc (each 256-byte aligned).
 int upload_packed(const HostPacked& hp, uint8_t* base, uint64_t* off, PackedMat* dst) {
   *dst = hp.geo;
   dst->qs = base + *off;
@@ -366,6 +393,7 @@ int upload_packed(const HostPacked& hp, uint8_t* base, uint64_t* off, PackedMat*
   dst->sc = base + *off;
   if (!hp.sc.empty()) RF_CUDA(cudaMemcpy(dst->sc, hp.sc.data(), hp.sc.size(), cudaMemcpyHostToDevice));
   *off += align256(hp.sc.size() ? hp.sc.size() : 16);
+  dst->sub_scales = has_subnormal_scales(hp.geo, hp.sc.data()) ? 1 : 0;
   return RF_OK;
 }
 uint64_t packed_bytes(const HostPacked& hp) { return align256(hp.qs.size()) + align256(hp.sc.size() ? hp.sc.size() : 16); }
@@ -427,10 +455,6 @@ int load_layer_views(rf_engine* e, int l, const View* v /*[9]*/) {
     dev_free(e, charge, &L.block);
     return rc;
   }
-  make_gemv_maps(L.qkv, &L.mq);  // not TMA-eligible: the register-streaming GEMV runs instead
-  make_gemv_maps(L.wo, &L.mo);
-  make_gemv_maps(L.gateup, &L.mg);
-  make_gemv_maps(L.down, &L.md);
   L.bytes = total;
   L.resident = true;
   e->stats.layer_loads++;
@@ -487,8 +511,6 @@ int load_persistent(rf_engine* e, int role, const View& v) {
   } else {
     return set_error(RF_EINVAL, "unknown persistent role %d", role);
   }
-  PackedMat lm;
-  if (lm_head(e, &lm) == RF_OK) make_gemv_maps(lm, &e->lm_maps);
   drop_graphs(e);
   return RF_OK;
 }
@@ -498,8 +520,15 @@ int load_persistent(rf_engine* e, int role, const View& v) {
 int lm_head(rf_engine* e, PackedMat* W) {
   if (e->have_out) { *W = e->out; return RF_OK; }
   if (!e->have_embd) return set_error(RF_ESTATE, "no output or token_embd weights loaded");
+  // rows [vocab_off, vocab_off + vocab_local) of the embedding: whole 64-row
+  // tiles (shard_plan aligns vocabulary shards), so the sub-matrix is a suffix of
+  // the same layout
+  if (is_tiled(e->embd.type) && e->vocab_off % QT_ROWS)
+    return set_error(RF_ESTATE, "vocabulary shard offset %u is not a multiple of %d rows", e->vocab_off, QT_ROWS);
   *W = e->embd;
   W->M = e->vocab_local;
+  if (is_tiled(W->type)) W->Mp = (W->M + QT_ROWS - 1) / QT_ROWS * QT_ROWS;
+  else W->Mp = W->M;
   W->qs = e->embd.qs + (uint64_t)e->vocab_off * e->embd.qs_stride;
   W->sc = e->embd.sc + (uint64_t)e->vocab_off * e->embd.sc_stride;
   return RF_OK;
@@ -550,7 +579,7 @@ int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
     ra.kcache = e->kc[l];
     ra.vcache = e->vc[l];
     ra.kv_f32 = e->rt.kv_f32;
-    RF_CUDA(gemv_qkv_rope(La, L.qkv, &L.mq, e->hidden, L.attn_norm, c.rms_eps, ra));
+    RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, ra));
   } else if (k == 1) {
     AttnArgs aa{};
     aa.q = e->q;
@@ -573,16 +602,15 @@ int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
     RF_CUDA(launch_attention(La, aa));
   } else if (k == 2 || k == 4) {
     const PackedMat& W = k == 2 ? L.wo : L.down;
-    const GemvMaps* M = k == 2 ? &L.mo : &L.md;
     const float* x = k == 2 ? e->att : e->act;
     if (e->tp == 1) {
-      RF_CUDA(gemv_residual(La, W, M, x, e->hidden, e->hidden));
+      RF_CUDA(gemv_residual(La, W, &e->gws, x, e->hidden, e->hidden));
     } else {
-      RF_CUDA(gemv_residual(La, W, M, x, e->rank == 0 ? e->hidden : nullptr, e->partial));
+      RF_CUDA(gemv_residual(La, W, &e->gws, x, e->rank == 0 ? e->hidden : nullptr, e->partial));
       RF_NCCL(nccl()->allReduce(e->partial, e->hidden, c.n_embd, ncclFloat32, ncclSum, e->comm, e->stream));
     }
   } else {
-    RF_CUDA(gemv_swiglu(La, L.gateup, &L.mg, e->hidden, L.ffn_norm, c.rms_eps, e->act));
+    RF_CUDA(gemv_swiglu(La, L.gateup, &e->gws, e->hidden, L.ffn_norm, c.rms_eps, e->act));
   }
   return RF_OK;
 }
@@ -613,7 +641,7 @@ int enqueue_logits(rf_engine* e, bool pdl, bool want_logits) {
   RF_TRY(lm_head(e, &W));
   const Launch La{e->stream, pdl};
   RF_CUDA(cudaMemsetAsync(e->d_key, 0, 8, e->stream));
-  RF_CUDA(gemv_argmax(La, W, &e->lm_maps, e->final_hidden, nullptr, 0.f, want_logits ? e->logits : nullptr, e->d_key,
+  RF_CUDA(gemv_argmax(La, W, &e->gws, e->final_hidden, nullptr, 0.f, want_logits ? e->logits : nullptr, e->d_key,
                       e->vocab_off));
   if (e->tp > 1) RF_NCCL(nccl()->allReduce(e->d_key, e->d_key, 1, ncclUint64, ncclMax, e->comm, e->stream));
   return RF_OK;

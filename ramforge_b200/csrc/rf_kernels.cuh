@@ -1,6 +1,5 @@
 // rf_kernels.cuh - device data layouts and kernel launchers of the decode engine.
 #pragma once
-#include <cuda.h>  // CUtensorMap (types only; the encoder is fetched from the driver at run time)
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -13,26 +12,64 @@ enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12 };
 // Packed device form of one GGUF matrix (n_out rows of n_in elements).
 //
 // GGUF interleaves per-block scales with quants (Q8_0: 34-byte blocks, Q4_K:
-// 144-byte super-blocks), which leaves quants at 2- or 16-byte alignment.  The
-// engine splits every row into two byte streams at load time, without changing
-// a single bit of either:
-//   qs : the quant bytes of the row, blocks concatenated in GGUF order, padded to
-//        a multiple of 32 bytes so each lane reads one 256-bit "unit" per load;
-//   sc : the per-block scale bytes of the row (Q8_0/Q4_0: the f16 d of every 32
-//        elements; Q4_K: the 16-byte {d, dmin, scales[12]} header of every
-//        256 elements).
-// A unit covers EPU elements: Q8_0 32 (one block), Q4_0 64 (two blocks), Q4_K
-// 64 (one sub-block pair of a super-block), F16 16, F32 8.
+// 144-byte super-blocks).  The engine splits every row into two byte streams at
+// load time and reorders them, without changing a single bit of either:
+//   qs : the quant bytes;
+//   sc : the per-block scale bytes (Q8_0/Q4_0: the f16 d of every 32 elements;
+//        Q4_K: the 16-byte {d, dmin, scales[12]} header of every 256 elements).
+//
+// Quantized types (Q4_K, Q4_0, Q8_0) use the tiled layout the GEMV streams:
+// rows are grouped in tiles of 64 (the row count padded with zero rows), every
+// row is cut into chunks of 128 quant bytes (256 elements for Q4_K/Q4_0, 128 for
+// Q8_0; the row length padded with zero blocks), and one "item" = (tile, chunk)
+// is 8 KiB of contiguous qs:
+//   qs[((tile*nk + chunk)*4 + piece)*2048 + (row%64)*32 + byte%32]
+// where piece = 32-byte quarter of the chunk, so one warp-wide 256-bit load reads
+// 1 KiB of consecutive bytes (piece `p` of 32 consecutive rows).  The scale
+// bytes of an item are contiguous too: sc[((tile*nk + chunk)*64 + row%64)*SB + b]
+// with SB = 16 (Q4_K header; Q4_0: eight f16) or 8 (Q8_0: four f16) bytes.
+//
+// F32/F16 tensors stay row-major (qs_stride bytes per row, no sc).
 struct PackedMat {
   int type;
   uint32_t M, K;        // rows, logical row length
-  uint32_t Kp;          // row length padded to a whole number of units / blocks
+  uint32_t Kp;          // row length padded to whole chunks (F32/F16: whole 32-byte units)
   uint32_t units;       // 32-byte units per row
-  uint64_t qs_stride;   // bytes per row of qs
-  uint64_t sc_stride;   // bytes per row of sc (0 for F32/F16)
+  uint64_t qs_stride;   // quant bytes per row (padded)
+  uint64_t sc_stride;   // scale bytes per row (padded; 0 for F32/F16)
+  uint32_t Mp;          // rows padded to the 64-row tile (F32/F16: M)
+  uint32_t nk;          // chunks per row (0 for F32/F16)
+  uint32_t sbytes;      // scale bytes per row per chunk (0 for F32/F16)
   uint8_t* qs;
   uint8_t* sc;
+  // Nonzero when some block scale is a subnormal half: the GEMV then decodes
+  // scales the reference's way (h2f) instead of with the hardware conversion.
+  // Set at load time (the host scans, or reads back the pack kernel's flag).
+  int sub_scales;
 };
+
+constexpr int QT_ROWS = 64;          // rows per tile
+constexpr int QT_CHUNK_BYTES = 128;  // quant bytes per row per chunk
+constexpr int QT_ITEM_BYTES = QT_ROWS * QT_CHUNK_BYTES;
+
+__host__ __device__ inline bool is_tiled(int type) { return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0; }
+__host__ __device__ inline int chunk_elems(int type) { return type == T_Q8_0 ? 128 : 256; }
+__host__ __device__ inline int chunk_scale_bytes(int type) { return type == T_Q8_0 ? 8 : 16; }
+
+// Byte b (0 <= b < qs_stride) of row r's quant bytes.
+__host__ __device__ inline uint64_t qs_byte_off(const PackedMat& W, uint32_t r, uint64_t b) {
+  if (!is_tiled(W.type)) return (uint64_t)r * W.qs_stride + b;
+  const uint64_t item = (uint64_t)(r / QT_ROWS) * W.nk + b / QT_CHUNK_BYTES;
+  return (item * 4 + (b / 32) % 4) * (QT_ROWS * 32) + (uint64_t)(r % QT_ROWS) * 32 + b % 32;
+}
+// Byte b (0 <= b < sc_stride) of row r's scale bytes.
+__host__ __device__ inline uint64_t sc_byte_off(const PackedMat& W, uint32_t r, uint64_t b) {
+  const uint64_t item = (uint64_t)(r / QT_ROWS) * W.nk + b / W.sbytes;
+  return (item * QT_ROWS + r % QT_ROWS) * W.sbytes + b % W.sbytes;
+}
+// Device bytes of the two streams.
+inline uint64_t packed_qs_bytes(const PackedMat& W) { return (uint64_t)W.Mp * W.qs_stride; }
+inline uint64_t packed_sc_bytes(const PackedMat& W) { return (uint64_t)W.Mp * W.sc_stride; }
 
 __host__ __device__ inline int elems_per_unit(int type) {
   switch (type) {
@@ -60,24 +97,24 @@ __host__ __device__ inline int block_bytes(int type) {
     default: return 0;
   }
 }
-// Padded row length for a type: a multiple of the unit and of the block.
+// Padded row length for a type: whole chunks (quantized) or whole units (F32/F16).
 inline uint32_t padded_k(int type, uint32_t K) {
-  uint32_t q = (uint32_t)(type == T_Q4_K ? 256 : elems_per_unit(type));
+  const uint32_t q = (uint32_t)(is_tiled(type) ? chunk_elems(type) : elems_per_unit(type));
   return (K + q - 1) / q * q;
 }
 bool packed_geometry(int type, uint32_t M, uint32_t K, PackedMat* out);  // fills all but pointers
 
-// TMA descriptors of a packed quantized matrix for the pipelined GEMV: 64-row x
-// 16-unit boxes of qs (512 B per row) and the matching scale bytes.  ok == false
-// (F32/F16, or rows whose scale stride is not a multiple of 16 bytes) selects the
-// register-streaming GEMV instead.
-struct GemvMaps {
-  CUtensorMap qs, sc;
-  uint32_t sc_chunk_bytes;
-  bool ok;
+// Split-K scratch of the quantized GEMV: partial row sums of tiles whose chunks
+// are spread over several warps, and one arrival counter per tile (zero at rest:
+// the warp that completes a tile resets it).  Kernels of one stream may share it.
+struct GemvScratch {
+  float* part;
+  unsigned* cnt;
+  uint64_t part_floats;
+  uint32_t n_cnt;
 };
-// Builds the descriptors for the device pointers in W (false: not TMA-eligible).
-bool make_gemv_maps(const PackedMat& W, GemvMaps* out);
+// Scratch a matrix needs (0 / 0 for F32/F16).
+void gemv_scratch_need(const PackedMat& W, uint64_t* part_floats, uint32_t* n_cnt);
 
 // ---- launch helpers -------------------------------------------------------
 // Every engine kernel is launched with programmatic dependent launch so its
@@ -88,16 +125,21 @@ struct Launch {
 };
 
 // Repack GGUF rows (device bytes) into a PackedMat. src_row_of[dst] selects the
-// GGUF row for each packed row (NULL = identity).
-cudaError_t launch_pack(const uint8_t* gguf, const int* src_row_of, PackedMat dst, cudaStream_t s);
+// GGUF row for each packed row (NULL = identity).  *d_sub (device word, may be
+// NULL) is set to 1 when a block scale is a subnormal half, else 0.
+cudaError_t launch_pack(const uint8_t* gguf, const int* src_row_of, PackedMat dst, unsigned* d_sub, cudaStream_t s);
+// Host scan of packed scale bytes: true when any block scale is a subnormal half.
+bool has_subnormal_scales(const PackedMat& W, const uint8_t* sc_host);
 
 // ---- GEMV families -------------------------------------------------------
 // All take x (f32, K elements) and optionally RMSNorm it on the fly with
-// norm_w/eps (rms_norm_reference, compute.rs:291-319).
-cudaError_t gemv_store(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* norm_w, float eps,
-                       float* y);
+// norm_w/eps (rms_norm_reference, compute.rs:291-319).  Quantized matrices need
+// the split-K scratch (gemv_scratch_need); F32/F16 ones ignore it.
+cudaError_t gemv_store(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x, const float* norm_w,
+                       float eps, float* y);
 // out[row] = (res ? res[row] : 0) + (W.x)[row]   (residual add, model_executor.rs:213-215, 231-233)
-cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* res, float* out);
+cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x, const float* res,
+                          float* out);
 
 struct RopeQKVArgs {
   uint32_t q_rows, kv_rows, head_dim, max_seq;
@@ -111,17 +153,19 @@ struct RopeQKVArgs {
   int kv_f32;
 };
 // Fused: RMSNorm(attn_norm) -> packed [Q;K;V] matvec -> RoPE on Q/K pairs -> K/V append.
-cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* norm_w, float eps,
-                          const RopeQKVArgs& a);
+cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
+                          const float* norm_w, float eps, const RopeQKVArgs& a);
 // Fused: RMSNorm(ffn_norm) -> packed [gate_j; up_j] matvec -> act[j] = silu(g)*u.
-cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* norm_w, float eps,
-                        float* act);
+cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
+                        const float* norm_w, float eps, float* act);
 // Fused LM head: optional RMSNorm(output_norm) -> logits (nullable) -> packed
 // argmax key (atomicMax of (ordered value, ~global_row)).
-cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const GemvMaps* maps, const float* x, const float* norm_w, float eps,
-                        float* logits, unsigned long long* key, uint32_t row_offset);
-// Batched standalone GEMV: y[b][row] for b < batch (x read through L1).
-cudaError_t gemv_batched(cudaStream_t s, const PackedMat& W, const float* x, int batch, float* y);
+cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
+                        const float* norm_w, float eps, float* logits, unsigned long long* key, uint32_t row_offset);
+// Batched standalone GEMV: y[b][row] = (W . x[b])[row] for b < batch, x[b] at
+// x + b*K, y[b] at y + b*M.
+cudaError_t gemv_batched(cudaStream_t s, const PackedMat& W, const GemvScratch* ws, const float* x, int batch,
+                         float* y);
 
 // ---- attention -------------------------------------------------------------
 struct AttnArgs {

@@ -10,7 +10,6 @@ using namespace rf;
 
 struct rf_matrix {
   PackedMat m{};
-  GemvMaps maps{};
   void* block = nullptr;
   uint64_t bytes = 0;
   int device = 0;
@@ -56,6 +55,41 @@ int noalloc_scratch(int dev, float** out) {
   return RF_OK;
 }
 
+// Per-device split-K scratch of rf_qmatvec (GemvScratch), grown on demand.
+struct GemvWorkspace {
+  float* part = nullptr;
+  uint64_t part_floats = 0;
+  unsigned* cnt = nullptr;
+  uint32_t n_cnt = 0;
+};
+std::mutex g_gws_mu;
+std::unordered_map<int, GemvWorkspace> g_gws;
+
+int gemv_workspace(int dev, const PackedMat& W, GemvScratch* out) {
+  uint64_t pf = 0;
+  uint32_t nc = 0;
+  gemv_scratch_need(W, &pf, &nc);
+  std::lock_guard<std::mutex> lk(g_gws_mu);
+  GemvWorkspace& w = g_gws[dev];
+  if (w.part_floats < pf) {
+    if (w.part) cudaFree(w.part);
+    w.part = nullptr;
+    w.part_floats = 0;
+    RF_CUDA(cudaMalloc(&w.part, pf * sizeof(float)));
+    w.part_floats = pf;
+  }
+  if (w.n_cnt < nc) {
+    if (w.cnt) cudaFree(w.cnt);
+    w.cnt = nullptr;
+    w.n_cnt = 0;
+    RF_CUDA(cudaMalloc(&w.cnt, nc * sizeof(unsigned)));
+    RF_CUDA(cudaMemset(w.cnt, 0, nc * sizeof(unsigned)));
+    w.n_cnt = nc;
+  }
+  *out = GemvScratch{w.part, w.cnt, w.part_floats, w.n_cnt};
+  return RF_OK;
+}
+
 int workspace(int dev, size_t part_floats, size_t n_counters, AttnWorkspace** out) {
   std::lock_guard<std::mutex> lk(g_ws_mu);
   AttnWorkspace& w = g_ws[dev];
@@ -94,19 +128,24 @@ int rf_matrix_create(int type, const void* bytes, uint64_t nbytes, int on_device
                      (unsigned long long)(row_bytes * n_out), (unsigned long long)nbytes);
   rf_matrix* m = new rf_matrix();
   cudaGetDevice(&m->device);
-  const uint64_t qs_b = (g.qs_stride * n_out + 255) & ~255ull, sc_b = (g.sc_stride * n_out + 255) & ~255ull;
-  m->bytes = qs_b + (sc_b ? sc_b : 256);
+  // qs | sc | one word for the pack kernel's subnormal-scale flag
+  const uint64_t qs_b = (packed_qs_bytes(g) + 255) & ~255ull, sc_b = (packed_sc_bytes(g) + 255) & ~255ull;
+  m->bytes = qs_b + (sc_b ? sc_b : 256) + 256;
   cudaError_t ce = cudaMalloc(&m->block, m->bytes);
   if (ce != cudaSuccess) {
     delete m;
-    return set_error(RF_ENOMEM, "cudaMalloc(%llu) failed: %s", (unsigned long long)qs_b, cudaGetErrorString(ce));
+    return set_error(RF_ENOMEM, "cudaMalloc(%llu) failed: %s", (unsigned long long)m->bytes, cudaGetErrorString(ce));
   }
   m->m = g;
   m->m.qs = (uint8_t*)m->block;
   m->m.sc = (uint8_t*)m->block + qs_b;
+  unsigned* flag = (unsigned*)((uint8_t*)m->block + qs_b + (sc_b ? sc_b : 256));
   if (on_device) {
-    ce = launch_pack((const uint8_t*)bytes, nullptr, m->m, 0);
+    ce = launch_pack((const uint8_t*)bytes, nullptr, m->m, flag, 0);
     if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    unsigned f = 0;
+    if (ce == cudaSuccess) ce = cudaMemcpy(&f, flag, sizeof f, cudaMemcpyDeviceToHost);
+    m->m.sub_scales = f ? 1 : 0;
   } else {
     HostPacked hp;
     std::vector<int> rows(n_out);
@@ -120,13 +159,13 @@ int rf_matrix_create(int type, const void* bytes, uint64_t nbytes, int on_device
     }
     ce = cudaMemcpy(m->m.qs, hp.qs.data(), hp.qs.size(), cudaMemcpyHostToDevice);
     if (ce == cudaSuccess && !hp.sc.empty()) ce = cudaMemcpy(m->m.sc, hp.sc.data(), hp.sc.size(), cudaMemcpyHostToDevice);
+    m->m.sub_scales = has_subnormal_scales(hp.geo, hp.sc.data()) ? 1 : 0;
   }
   if (ce != cudaSuccess) {
     cudaFree(m->block);
     delete m;
     return set_error(RF_ECUDA, "packing failed: %s", cudaGetErrorString(ce));
   }
-  make_gemv_maps(m->m, &m->maps);
   *out = m;
   return RF_OK;
 }
@@ -147,13 +186,12 @@ int rf_qmatvec(const rf_matrix* m, const float* dX, float* dY, int batch, void* 
   if (!m || !dX || !dY) return set_error(RF_EINVAL, "null argument");
   if (batch < 1 || batch > 8) return set_error(RF_EINVAL, "batch %d out of range 1..8", batch);
   cudaStream_t s = (cudaStream_t)stream;
-  if (batch == 1) {
-    RF_CUDA(gemv_store(Launch{s, false}, m->m, &m->maps, dX, nullptr, 0.f, dY));
-    return RF_OK;
-  }
-  if (m->m.K != m->m.Kp)
-    return set_error(RF_EUNSUPPORTED, "batched matvec needs n_in to be a multiple of %u", m->m.Kp - m->m.K + m->m.K);
-  RF_CUDA(gemv_batched(s, m->m, dX, batch, dY));
+  int cur = 0;
+  RF_CUDA(cudaGetDevice(&cur));
+  if (cur != m->device) return set_error(RF_EINVAL, "matrix lives on device %d, current device is %d", m->device, cur);
+  GemvScratch ws{};
+  RF_TRY(gemv_workspace(cur, m->m, &ws));
+  RF_CUDA(gemv_batched(s, m->m, &ws, dX, batch, dY));
   return RF_OK;
 }
 
