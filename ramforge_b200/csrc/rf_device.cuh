@@ -38,6 +38,50 @@ __device__ __forceinline__ float h2f(uint32_t bits16) {
   return (bits16 & 0x7C00u) ? f : f * 0.5f;
 }
 
+// Element e of packed row `row`, dequantised exactly as the reference does it
+// (embedding rows, parity dumps).
+__device__ __forceinline__ float dequant_elem(const PackedMat& W, uint32_t row, uint32_t e) {
+  const uint8_t* q = W.qs;
+  const uint8_t* c = W.sc;
+  switch (W.type) {
+    case T_F32: return reinterpret_cast<const float*>(q + (uint64_t)row * W.qs_stride)[e];
+    case T_F16: return h2f(reinterpret_cast<const unsigned short*>(q + (uint64_t)row * W.qs_stride)[e]);
+    case T_Q8_0: {  // q*d (quant.rs:176-180)
+      const uint8_t* sp = c + sc_byte_off(W, row, 2ull * (e / 32));
+      const float d = h2f(sp[0] | (sp[1] << 8));
+      return __fmul_rn((float)(int8_t)q[qs_byte_off(W, row, e)], d);
+    }
+    case T_Q4_0: {  // (q-8)*d (quant.rs:104-112)
+      const uint32_t b = e / 32, j = e % 32;
+      const uint8_t byte = q[qs_byte_off(W, row, (uint64_t)b * 16 + (j & 15))];
+      const int v = (j < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
+      const uint8_t* sp = c + sc_byte_off(W, row, 2ull * b);
+      const float d = h2f(sp[0] | (sp[1] << 8));
+      return __fmul_rn((float)v, d);
+    }
+    case T_Q4_K: {  // d1*q - min1 (quant.rs:228-254)
+      const uint32_t sb = e / 256, r = e % 256, gi = r / 64, t = r % 64;
+      const uint8_t byte = q[qs_byte_off(W, row, (uint64_t)sb * 128 + gi * 32 + (t & 31))];
+      const uint32_t nq = t < 32 ? (byte & 0xF) : (byte >> 4);
+      const uint8_t* h = c + sc_byte_off(W, row, (uint64_t)sb * 16);
+      const float d = h2f(h[0] | (h[1] << 8)), dmin = h2f(h[2] | (h[3] << 8));
+      const uint8_t* s = h + 4;
+      const int j = (int)(2 * gi + (t >= 32));
+      uint32_t sc, m;
+      if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+      } else {
+        sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+      }
+      const float d1 = __fmul_rn(d, (float)sc), mn = __fmul_rn(dmin, (float)m);
+      return __fsub_rn(__fmul_rn(d1, (float)nq), mn);
+    }
+  }
+  return 0.f;
+}
+
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 
@@ -72,10 +116,10 @@ __device__ __forceinline__ float block_sumsq(const float* __restrict__ x, int n,
   return block_sumsq_n<GEMV_THREADS>(x, n, sred);
 }
 
-// Block-wide sum of squares of x[0..n) (n a multiple of 4, x 16-byte aligned,
-// not written while the kernel runs): thread t takes float4s t, t+NT, ... in
-// order, then warps and warp partials are summed in a fixed order.  Up to four
-// loads per thread are in flight at once.
+// Block-wide sum of squares of x[0..n) (n a multiple of 4, x 16-byte aligned).
+// x is read through L2, so it may have been written earlier by the same kernel.
+// Thread t takes float4s t, t+NT, ... in order, then warps and warp partials are
+// summed in a fixed order.  Up to four loads per thread are in flight at once.
 template <int NT>
 __device__ __forceinline__ float block_sumsq_v4(const float* __restrict__ x, int n, float* sred) {
   const float4* x4 = reinterpret_cast<const float4*>(x);
@@ -84,7 +128,7 @@ __device__ __forceinline__ float block_sumsq_v4(const float* __restrict__ x, int
   for (int q0 = threadIdx.x; q0 < nq; q0 += 4 * NT) {
     float4 v[4];
 #pragma unroll
-    for (int u = 0; u < 4; u++) v[u] = q0 + u * NT < nq ? __ldg(x4 + q0 + u * NT) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < 4; u++) v[u] = q0 + u * NT < nq ? __ldcg(x4 + q0 + u * NT) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int u = 0; u < 4; u++) {
       s = fmaf(v[u].x, v[u].x, s);

@@ -130,6 +130,18 @@ struct rf_engine {
   unsigned long long* h_key = nullptr;
   // graphs
   cudaGraphExec_t g_forward = nullptr, g_decode = nullptr;
+  // persistent step kernel: per-layer matrix table (host copy + device copy),
+  // its shared memory (0 = not applicable), barrier word and error word
+  bool step_enabled = false;  // opt-in (rf_set_step_kernel): the per-kernel graph is faster today
+  bool step_dirty = true;
+  size_t step_smem = 0;
+  std::vector<StepLayer> h_step_layers;
+  StepLayer* d_step_layers = nullptr;
+  unsigned* d_bar = nullptr;
+  unsigned* d_err = nullptr;
+  bool step_used = false;  // the step kernel ran since the last error check
+  bool step_profile = false;
+  unsigned long long* d_stamps = nullptr;  // barrier completion times of the last profiled step
   // NCCL
   ncclComm_t comm = nullptr;
   rf_residency_stats stats{};
@@ -160,6 +172,7 @@ void drop_graphs(rf_engine* e) {
   if (e->g_forward) cudaGraphExecDestroy(e->g_forward);
   if (e->g_decode) cudaGraphExecDestroy(e->g_decode);
   e->g_forward = e->g_decode = nullptr;
+  e->step_dirty = true;
 }
 
 // Build the RoPE (cos, sin) table on the host with the reference's f32
@@ -296,6 +309,9 @@ int engine_init_device(rf_engine* e) {
       {(void**)&e->logits, 4ull * vl_pad},          {(void**)&e->logits_all, 4ull * vl_pad * e->tp},
       {(void**)&e->attn_part, 4ull * part_f},       {(void**)&e->attn_counters, 4ull * e->kvh_local},
       {(void**)&e->gws.part, 4ull * gpart},         {(void**)&e->gws.cnt, 4ull * gcnt},
+      {(void**)&e->d_bar, 4},                       {(void**)&e->d_err, 4},
+      {(void**)&e->d_stamps, 8ull * (5 * c.n_layers + 8)},
+      {(void**)&e->d_step_layers, sizeof(StepLayer) * c.n_layers},
       {(void**)&e->d_io, sizeof(StepIO)},           {(void**)&e->d_key, 8},
       {(void**)&e->d_hist, 4ull * e->max_seq},
       {(void**)&e->rope_cs, 8ull * e->max_seq * (c.head_dim / 2)}};
@@ -561,45 +577,57 @@ int load_layer_gguf(rf_engine* e, int l) {
 // fused kernels.  Row-parallel projections finish with a sum over ranks.
 // Kernel class k of layer l: 0 QKV+RoPE+KV append, 1 attention, 2 Wo+residual,
 // 3 gate/up+SwiGLU, 4 down+residual (2 and 4 end with the rank all-reduce).
+// QKV epilogue arguments of layer l: RoPE on the packed Q/K pairs, K/V append at
+// the step position.
+RopeQKVArgs rope_args(rf_engine* e, int l) {
+  RopeQKVArgs ra{};
+  ra.q_rows = e->q_local;
+  ra.kv_rows = e->kv_local;
+  ra.head_dim = e->cfg.head_dim;
+  ra.max_seq = e->max_seq;
+  ra.rope_cs = e->rope_cs;
+  ra.d_pos = &e->d_io->pos;
+  ra.q_out = e->q;
+  ra.k_cur = e->k_cur;
+  ra.v_cur = e->v_cur;
+  ra.kcache = e->kc[l];
+  ra.vcache = e->vc[l];
+  ra.kv_f32 = e->rt.kv_f32;
+  return ra;
+}
+
+// Attention of layer l over the history (length = the step position) and the
+// current K/V.
+AttnArgs attn_args(rf_engine* e, int l) {
+  AttnArgs aa{};
+  aa.q = e->q;
+  aa.kc = e->kc[l];
+  aa.vc = e->vc[l];
+  aa.head_stride = (uint64_t)e->max_seq * e->cfg.head_dim;
+  aa.batch_stride = 0;
+  aa.k_cur = e->k_cur;
+  aa.v_cur = e->v_cur;
+  aa.d_nhist = &e->d_io->pos;
+  aa.n_heads = (int)e->qh_local;
+  aa.n_kv_heads = (int)e->kvh_local;
+  aa.head_dim = (int)e->cfg.head_dim;
+  aa.batch = 1;
+  aa.max_splits = e->max_splits;
+  aa.part = e->attn_part;
+  aa.counters = e->attn_counters;
+  aa.out = e->att;
+  aa.kv_f32 = e->rt.kv_f32;
+  return aa;
+}
+
 int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
   const rf_model_config& c = e->cfg;
   Layer& L = e->layers[l];
   const Launch La{e->stream, pdl};
   if (k == 0) {
-    RopeQKVArgs ra{};
-    ra.q_rows = e->q_local;
-    ra.kv_rows = e->kv_local;
-    ra.head_dim = c.head_dim;
-    ra.max_seq = e->max_seq;
-    ra.rope_cs = e->rope_cs;
-    ra.d_pos = &e->d_io->pos;
-    ra.q_out = e->q;
-    ra.k_cur = e->k_cur;
-    ra.v_cur = e->v_cur;
-    ra.kcache = e->kc[l];
-    ra.vcache = e->vc[l];
-    ra.kv_f32 = e->rt.kv_f32;
-    RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, ra));
+    RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, rope_args(e, l)));
   } else if (k == 1) {
-    AttnArgs aa{};
-    aa.q = e->q;
-    aa.kc = e->kc[l];
-    aa.vc = e->vc[l];
-    aa.head_stride = (uint64_t)e->max_seq * c.head_dim;
-    aa.batch_stride = 0;
-    aa.k_cur = e->k_cur;
-    aa.v_cur = e->v_cur;
-    aa.d_nhist = &e->d_io->pos;
-    aa.n_heads = (int)e->qh_local;
-    aa.n_kv_heads = (int)e->kvh_local;
-    aa.head_dim = (int)c.head_dim;
-    aa.batch = 1;
-    aa.max_splits = e->max_splits;
-    aa.part = e->attn_part;
-    aa.counters = e->attn_counters;
-    aa.out = e->att;
-    aa.kv_f32 = e->rt.kv_f32;
-    RF_CUDA(launch_attention(La, aa));
+    RF_CUDA(launch_attention(La, attn_args(e, l)));
   } else if (k == 2 || k == 4) {
     const PackedMat& W = k == 2 ? L.wo : L.down;
     const float* x = k == 2 ? e->att : e->act;
@@ -708,9 +736,102 @@ int capture(rf_engine* e, bool decode, cudaGraphExec_t* out) {
   return RF_OK;
 }
 
+StepArgs step_args(rf_engine* e, bool decode) {
+  const rf_model_config& c = e->cfg;
+  StepArgs a{};
+  a.layers = e->d_step_layers;
+  a.n_layers = (int)c.n_layers;
+  a.decode = decode ? 1 : 0;
+  a.embd = e->embd;
+  lm_head(e, &a.lm);
+  a.out_norm = e->out_norm;
+  a.eps = c.rms_eps;
+  a.n_embd = c.n_embd;
+  a.q_rows = e->q_local;
+  a.kv_rows = e->kv_local;
+  a.head_dim = c.head_dim;
+  a.max_seq = e->max_seq;
+  a.n_heads = e->qh_local;
+  a.n_kv_heads = e->kvh_local;
+  a.rope_cs = e->rope_cs;
+  a.hidden = e->hidden;
+  a.final_hidden = e->final_hidden;
+  a.q = e->q;
+  a.k_cur = e->k_cur;
+  a.v_cur = e->v_cur;
+  a.att = e->att;
+  a.act = e->act;
+  a.logits = nullptr;
+  a.d_token = &e->d_io->token;
+  a.d_pos = &e->d_io->pos;
+  a.hist = e->d_hist;
+  a.hist_len = (int)e->max_seq;
+  a.key = e->d_key;
+  a.vocab_off = e->vocab_off;
+  a.gws = e->gws;
+  a.attn_part = e->attn_part;
+  a.attn_counters = e->attn_counters;
+  a.max_splits = e->max_splits;
+  a.bar = e->d_bar;
+  a.err = e->d_err;
+  a.stamps = e->step_profile ? e->d_stamps : nullptr;
+  return a;
+}
+
+// Decide whether the persistent step kernel runs the step (one GPU, every layer
+// resident, f16 KV cache, an instantiated shape) and refresh its layer table.
+int prepare_step_kernel(rf_engine* e) {
+  if (!e->step_dirty) return RF_OK;
+  e->step_smem = 0;
+  e->step_dirty = false;
+  if (!e->step_enabled || e->tp > 1 || e->rt.kv_f32 || !all_resident(e) || !e->have_embd || !e->have_onorm)
+    return RF_OK;
+  PackedMat lm;
+  if (lm_head(e, &lm) != RF_OK) return RF_OK;
+  const rf_model_config& c = e->cfg;
+  e->h_step_layers.assign(c.n_layers, StepLayer{});
+  for (uint32_t l = 0; l < c.n_layers; l++) {
+    const Layer& L = e->layers[l];
+    StepLayer& S = e->h_step_layers[l];
+    S.qkv = L.qkv;
+    S.wo = L.wo;
+    S.gateup = L.gateup;
+    S.down = L.down;
+    S.attn_norm = L.attn_norm;
+    S.ffn_norm = L.ffn_norm;
+    S.rope = rope_args(e, (int)l);
+    S.attn = attn_args(e, (int)l);
+  }
+  RF_CUDA(cudaMemcpy(e->d_step_layers, e->h_step_layers.data(), sizeof(StepLayer) * c.n_layers,
+                     cudaMemcpyHostToDevice));
+  e->step_smem = step_kernel_smem(step_args(e, true), e->h_step_layers[0]);
+  return RF_OK;
+}
+
+bool step_kernel_active(rf_engine* e) { return prepare_step_kernel(e) == RF_OK && e->step_smem > 0; }
+
+// After a synchronisation: a step-kernel barrier that gave up fails the call.
+int check_step_kernel(rf_engine* e) {
+  if (!e->step_used) return RF_OK;
+  e->step_used = false;
+  unsigned err = 0;
+  RF_CUDA(cudaMemcpy(&err, e->d_err, sizeof err, cudaMemcpyDeviceToHost));
+  if (err) {
+    RF_CUDA(cudaMemset(e->d_err, 0, sizeof err));
+    return set_error(RF_ETIMEOUT, "a grid barrier of the step kernel timed out (error word 0x%x)", err);
+  }
+  return RF_OK;
+}
+
 // Launch one token step (forward, or decode = forward + logits + advance).
 int launch_step(rf_engine* e, bool decode) {
   if (!all_resident(e)) return run_stepwise(e, decode);
+  if (step_kernel_active(e)) {
+    RF_CUDA(launch_step_kernel(e->stream, step_args(e, decode), e->h_step_layers[0], e->step_smem));
+    e->step_used = true;
+    e->stats.cache_hits += e->cfg.n_layers;
+    return RF_OK;
+  }
   if (e->rt.disable_graphs) return decode ? enqueue_decode(e, true) : enqueue_forward(e, true);
   cudaGraphExec_t* g = decode ? &e->g_decode : &e->g_forward;
   if (!*g) RF_TRY(capture(e, decode, g));
@@ -774,7 +895,7 @@ int decode_loop(rf_engine* e, uint32_t token, uint32_t n, uint32_t* out, float* 
   if (rc) return rc;
   if (out) RF_CUDA(cudaMemcpyAsync(out, e->d_hist + p0, 4ull * n, cudaMemcpyDeviceToHost, e->stream));
   RF_CUDA(cudaStreamSynchronize(e->stream));
-  return RF_OK;
+  return check_step_kernel(e);
 }
 
 int engine_finish_create(rf_engine* e) {
@@ -1015,7 +1136,7 @@ int rf_forward_token(rf_engine* e, uint32_t token, uint32_t pos, float* final_hi
     RF_CUDA(cudaMemcpyAsync(final_hidden, e->final_hidden, 4ull * e->cfg.n_embd, cudaMemcpyDeviceToHost, e->stream));
   }
   RF_CUDA(cudaStreamSynchronize(e->stream));
-  return RF_OK;
+  return check_step_kernel(e);
 }
 
 int rf_compute_logits(rf_engine* e, float* logits, uint32_t* argmax) {
@@ -1043,6 +1164,7 @@ int rf_decode_step(rf_engine* e, uint32_t token, uint32_t* next_token) {
   e->seq_len++;
   RF_CUDA(cudaMemcpyAsync(e->h_tok, &e->d_io->token, 4, cudaMemcpyDeviceToHost, e->stream));
   RF_CUDA(cudaStreamSynchronize(e->stream));
+  RF_TRY(check_step_kernel(e));
   if (next_token) *next_token = e->h_tok[0];
   return RF_OK;
 }
@@ -1067,7 +1189,7 @@ int rf_generate(rf_engine* e, const uint32_t* prompt, uint32_t n_prompt, uint32_
     RF_TRY(launch_step(e, false));
     e->seq_len++;
     RF_CUDA(cudaStreamSynchronize(e->stream));
-    return RF_OK;
+    return check_step_kernel(e);
   }
   // The last prompt token and every generated token but the last go through
   // decode steps whose argmax feeds the next step on the device (the reference
@@ -1084,9 +1206,54 @@ int rf_decode_timed(rf_engine* e, uint32_t token, uint32_t n_steps, uint32_t* ou
   return decode_loop(e, token, n_steps, out_tokens, device_ms);
 }
 
-int rf_step_kernel_count(const rf_engine* e, uint32_t* out) {
-  if (!e || !out) return set_error(RF_EINVAL, "null argument");
-  *out = 5u * e->cfg.n_layers + 4u;  // embed, 5 per layer, output norm, LM head, advance
+int rf_step_kernel_count(const rf_engine* ec, uint32_t* out) {
+  if (!ec || !out) return set_error(RF_EINVAL, "null argument");
+  rf_engine* e = const_cast<rf_engine*>(ec);
+  if (all_resident(e) && step_kernel_active(e)) *out = 1u;  // the persistent step kernel
+  else *out = 5u * e->cfg.n_layers + 4u;  // embed, 5 per layer, output norm, LM head, advance
+  return RF_OK;
+}
+
+int rf_set_step_kernel(rf_engine* e, int enable) {
+  ENGINE_GUARD(e);
+  e->step_enabled = enable != 0;
+  e->step_dirty = true;
+  return RF_OK;
+}
+
+int rf_step_profile(rf_engine* e, int enable) {
+  ENGINE_GUARD(e);
+  e->step_profile = enable != 0;
+  if (e->step_profile) RF_CUDA(cudaMemset(e->d_stamps, 0, 8ull * (5 * e->cfg.n_layers + 8)));
+  return RF_OK;
+}
+
+int rf_step_phase_times(rf_engine* e, float* us, uint32_t n, uint32_t* n_out) {
+  ENGINE_GUARD(e);
+  if (!us || !n_out) return set_error(RF_EINVAL, "null argument");
+  const uint32_t nb = 5 * e->cfg.n_layers + 8;
+  std::vector<unsigned long long> t(nb);
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  RF_CUDA(cudaMemcpy(t.data(), e->d_stamps, 8ull * nb, cudaMemcpyDeviceToHost));
+  uint32_t k = 0;
+  for (uint32_t i = 1; i < nb && t[i] >= t[i - 1] && t[i] && k < n; i++) us[k++] = (float)(t[i] - t[i - 1]) * 1e-3f;
+  *n_out = k;
+  return RF_OK;
+}
+
+int rf_selftest_barrier(int device, uint32_t phantom_arrivals, uint32_t* err_word) {
+  if (!err_word) return set_error(RF_EINVAL, "null argument");
+  RF_CUDA(cudaSetDevice(device));
+  unsigned w = 0;
+  RF_CUDA(barrier_selftest(phantom_arrivals, &w));
+  *err_word = w;
+  return RF_OK;
+}
+
+int rf_step_kernel_active(rf_engine* e, int* out) {
+  ENGINE_GUARD(e);
+  if (!out) return set_error(RF_EINVAL, "null argument");
+  *out = all_resident(e) && step_kernel_active(e) ? 1 : 0;
   return RF_OK;
 }
 

@@ -1,548 +1,18 @@
-// rf_gemv.cu - batch-1 matrix-vector products of the decode engine and their
-// fused epilogues (RoPE + KV append, SwiGLU, residual add, greedy argmax).
-//
-// Batch-1 decode reads every weight byte once per token for one multiply-add
-// per element, so the GEMV is bound by HBM bandwidth when its instruction
-// stream is lean enough.  For 4-bit weights on B200 it is not automatically:
-// HBM delivers ~12e12 Q4_K weights/s, and at 16 integer ops per clock per SM
-// sub-partition a dequantise-and-FMA loop may spend only ~1.1 integer
-// instructions per weight.  The quantized kernel is built around that budget:
-//
-//  * One lane owns two rows (r and r+32 of a 64-row tile) and walks the tile's
-//    128-byte chunks.  Every activation load is then the same address across the
-//    warp (a shared-memory broadcast), every scale header is decoded once per row
-//    per chunk, and no cross-lane reduction is needed.
-//  * Weights are read with 256-bit loads from the tiled layout (rf_kernels.cuh),
-//    so each warp-wide load is 1 KiB of consecutive bytes; the next chunk's
-//    pieces are loaded while the current one is multiplied.
-//  * A quant field masked in place inside its 32-bit word (bits [off, off+n),
-//    off + n <= 24) reads as the float q * 2^(off-149); shared memory holds x
-//    pre-multiplied by 2^(85-off) for the field position each element comes from,
-//    so every product is exactly q * x * 2^-64 and one packed fma.rn.f32x2 takes
-//    two elements.  The top byte of a word is brought down with one byte-permute
-//    shared by two words: 17 integer ops per 16 Q4 weights.
-//  * Work is split "stream-K": the (tile, chunk) items of the matrix are cut into
-//    equal contiguous ranges, one per warp of a persistent grid, so every SM gets
-//    the same number of bytes whatever the matrix shape.  A tile whose chunks span
-//    several warps is finished by the last of them to arrive (arrival counter),
-//    which sums the partials in chunk order: results do not depend on timing, and
-//    nothing waits on another warp or CTA.
+// rf_gemv.cu - standalone GEMV kernels and launchers of the decode engine
+// (quantized matrices: the routine of rf_gemv.cuh over one kernel launch;
+// F32/F16 matrices: a plain row-major kernel).
 #include <algorithm>
 
-#include "rf_device.cuh"
+#include "rf_gemv.cuh"
 
 namespace rf {
-
-constexpr float kTwo64 = 18446744073709551616.0f;  // 2^64
-__device__ __forceinline__ float as_f(uint32_t bits) { return __uint_as_float(bits); }
-__device__ __forceinline__ float2 ff2(float a, float b) { return make_float2(a, b); }
-// 2^(85 - off): exact pre-scale of x for a field at bit `off`.
-__device__ __forceinline__ float prescale(int off) { return __int_as_float((212 - off) << 23); }
-
-// ---------------------------------------------------------------------------
-// epilogues: called with the finished values of rows [row0, row0+n), n <= 2 and
-// row0 even, so RoPE and SwiGLU row pairs arrive together.
-// ---------------------------------------------------------------------------
-struct EpiStore {
-  float* y;
-  __device__ void operator()(int row0, const float* v, int n) {
-    for (int i = 0; i < n; i++) y[row0 + i] = v[i];
-  }
-  __device__ void flush() {}
-};
-
-struct EpiResidual {
-  const float* res;
-  float* out;
-  __device__ void operator()(int row0, const float* v, int n) {
-    for (int i = 0; i < n; i++) out[row0 + i] = res ? res[row0 + i] + v[i] : v[i];
-  }
-  __device__ void flush() {}
-};
-
-struct EpiRope {
-  RopeQKVArgs a;
-  // Q and K rows are packed as pairs (i, i+hd/2) of each head so that the
-  // half-split rotation (compute.rs:440-456) happens in registers; V rows are in
-  // natural order.
-  __device__ void operator()(int row0, const float* v, int n) {
-    const int pos = *a.d_pos;
-    const uint32_t half = a.head_dim / 2;
-    const uint32_t p = (uint32_t)row0;
-    if (p < a.q_rows + a.kv_rows) {
-      if (n < 2) return;
-      const bool isq = p < a.q_rows;
-      const uint32_t j = (isq ? p : p - a.q_rows) / 2;
-      const uint32_t h = j / half, i = j % half;
-      const float2 cs = a.rope_cs[(size_t)pos * half + i];
-      const float x0 = v[0], x1 = v[1];
-      // first*cos - second*sin ; first*sin + second*cos, one rounding per op
-      const float o0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-      const float o1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-      const uint32_t e0 = h * a.head_dim + i, e1 = e0 + half;
-      if (isq) {
-        a.q_out[e0] = o0;
-        a.q_out[e1] = o1;
-      } else {
-        a.k_cur[e0] = o0;
-        a.k_cur[e1] = o1;
-        const size_t c0 = ((size_t)h * a.max_seq + pos) * a.head_dim + i;
-        if (a.kv_f32) {
-          ((float*)a.kcache)[c0] = o0;
-          ((float*)a.kcache)[c0 + half] = o1;
-        } else {
-          ((__half*)a.kcache)[c0] = __float2half_rn(o0);
-          ((__half*)a.kcache)[c0 + half] = __float2half_rn(o1);
-        }
-      }
-    } else {
-      for (int s = 0; s < n; s++) {
-        const uint32_t o = p + s - a.q_rows - a.kv_rows;
-        const uint32_t h = o / a.head_dim, dd = o % a.head_dim;
-        a.v_cur[o] = v[s];
-        const size_t c = ((size_t)h * a.max_seq + pos) * a.head_dim + dd;
-        if (a.kv_f32) ((float*)a.vcache)[c] = v[s];
-        else ((__half*)a.vcache)[c] = __float2half_rn(v[s]);
-      }
-    }
-  }
-  __device__ void flush() {}
-};
-
-struct EpiSwiGLU {
-  float* act;
-  // rows (2j, 2j+1) = (gate_j, up_j); silu(g) = g/(1+exp(-g)) then * up
-  // (compute.rs:337-350, model_executor.rs:229-230)
-  __device__ void operator()(int row0, const float* v, int n) {
-    if (n < 2) return;
-    const float g = v[0], u = v[1];
-    const float s = g / (1.0f + expf(-g));
-    act[row0 >> 1] = __fmul_rn(s, u);
-  }
-  __device__ void flush() {}
-};
-
-// Order-preserving 64-bit key: high word = float bits mapped to unsigned order,
-// low word = ~row so that equal values prefer the lower row (the reference's
-// strict '>' scan keeps the first maximum, sampling.rs:48-53).
-__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t row) {
-  uint32_t b = __float_as_uint(v);
-  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return ((unsigned long long)b << 32) | (unsigned long long)(~row);
-}
-
-struct EpiArgmax {
-  float* logits;
-  unsigned long long* key;
-  uint32_t row_offset;
-  unsigned long long best;
-  __device__ void operator()(int row0, const float* v, int n) {
-    for (int i = 0; i < n; i++) {
-      if (logits) logits[row0 + i] = v[i];
-      const unsigned long long k = argmax_key(v[i], row_offset + row0 + i);
-      best = k > best ? k : best;
-    }
-  }
-  // End of kernel, every lane of every warp: warp maximum, one atomic per warp.
-  __device__ void flush() {
-    unsigned long long b = best;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
-      b = t > b ? t : b;
-    }
-    if ((threadIdx.x & 31) == 0 && b) atomicMax(key, b);
-  }
-};
-
-// ---------------------------------------------------------------------------
-// quantized GEMV over the tiled layout
-// ---------------------------------------------------------------------------
-constexpr int QG_WARPS = 16;
-constexpr int QG_THREADS = QG_WARPS * 32;
-
-template <int FMT>
-struct QTraits;
-// Q4_K: a chunk is one super-block; piece c is sub-block pair c (byte l: element
-//       64c+l in the low nibble, 64c+32+l in the high one; quant.rs:235-248).
-template <>
-struct QTraits<T_Q4_K> {
-  static constexpr int CE = 256, SW = 4, XSF = 1;
-};
-// Q4_0: a chunk is 8 blocks; piece c is blocks 2c, 2c+1 (block byte j: element j
-//       low, 16+j high; value (q-8)*d, quant.rs:104-112).
-template <>
-struct QTraits<T_Q4_0> {
-  static constexpr int CE = 256, SW = 4, XSF = 8;
-};
-// Q8_0: a chunk is 4 blocks; piece c is block c (value q*d, quant.rs:176-180),
-//       bytes biased to q+128 on the fly.
-template <>
-struct QTraits<T_Q8_0> {
-  static constexpr int CE = 128, SW = 2, XSF = 128;
-};
-
-// Bit offset of the field holding element k (0..7) of a word pair (A, B) in
-// the decode below; high nibbles sit 4 bits above the low ones.
-//   k:   0  1  2  3  4  5  6  7
-//   off: 0  8 16  0  0  8 16  8
-__device__ __forceinline__ int pair_off(int k) { return (k & 3) == 3 ? (k >> 2) * 8 : (k & 3) * 8; }
-
-// Field offset of chunk element e.
-template <int FMT>
-__device__ __forceinline__ int qfield_off(int e) {
-  if (FMT == T_Q8_0) return pair_off(e & 7);
-  const int u = e & 63;
-  const bool hi = FMT == T_Q4_K ? (u >= 32) : ((u & 31) >= 16);
-  return pair_off(u & 7) + (hi ? 4 : 0);
-}
-
-// 16 nibbles of the word pair (A, B) = bytes 0..7: the low nibble of byte k
-// against xl[k], the high nibble against xh[k].  P gathers the top bytes of A
-// and B below bit 16.
-__device__ __forceinline__ void q4_pair(uint32_t A, uint32_t B, const float4& xl0, const float4& xl1,
-                                        const float4& xh0, const float4& xh1, float2& lo, float2& hi) {
-  const uint32_t P = __byte_perm(A, B, 0x0073);
-  lo = __ffma2_rn(ff2(as_f(A & 0xFu), as_f(A & 0xF00u)), ff2(xl0.x, xl0.y), lo);
-  lo = __ffma2_rn(ff2(as_f(A & 0xF0000u), as_f(P & 0xFu)), ff2(xl0.z, xl0.w), lo);
-  lo = __ffma2_rn(ff2(as_f(B & 0xFu), as_f(B & 0xF00u)), ff2(xl1.x, xl1.y), lo);
-  lo = __ffma2_rn(ff2(as_f(B & 0xF0000u), as_f(P & 0xF00u)), ff2(xl1.z, xl1.w), lo);
-  hi = __ffma2_rn(ff2(as_f(A & 0xF0u), as_f(A & 0xF000u)), ff2(xh0.x, xh0.y), hi);
-  hi = __ffma2_rn(ff2(as_f(A & 0xF00000u), as_f(P & 0xF0u)), ff2(xh0.z, xh0.w), hi);
-  hi = __ffma2_rn(ff2(as_f(B & 0xF0u), as_f(B & 0xF000u)), ff2(xh1.x, xh1.y), hi);
-  hi = __ffma2_rn(ff2(as_f(B & 0xF00000u), as_f(P & 0xF000u)), ff2(xh1.z, xh1.w), hi);
-}
-// 8 signed bytes of (A, B), biased to q+128, against x[k].
-__device__ __forceinline__ void q8_pair(uint32_t A, uint32_t B, const float4& x0, const float4& x1, float2& s) {
-  constexpr uint32_t M = 0x80808080u;
-  const uint32_t P = __byte_perm(A, B, 0x0073);
-  s = __ffma2_rn(ff2(as_f((A ^ M) & 0xFFu), as_f((A ^ M) & 0xFF00u)), ff2(x0.x, x0.y), s);
-  s = __ffma2_rn(ff2(as_f((A ^ M) & 0xFF0000u), as_f((P ^ M) & 0xFFu)), ff2(x0.z, x0.w), s);
-  s = __ffma2_rn(ff2(as_f((B ^ M) & 0xFFu), as_f((B ^ M) & 0xFF00u)), ff2(x1.x, x1.y), s);
-  s = __ffma2_rn(ff2(as_f((B ^ M) & 0xFF0000u), as_f((P ^ M) & 0xFF00u)), ff2(x1.z, x1.w), s);
-}
-
-// f16 block scale -> f32: hardware conversion, or the reference's decode when
-// the matrix holds subnormal scales.
-template <bool QUIRK>
-__device__ __forceinline__ float scale_f(uint32_t bits16) {
-  if constexpr (QUIRK) return h2f(bits16 & 0xFFFFu);
-  else return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
-}
-// Exact float of byte k of w.
-__device__ __forceinline__ float byte_f(uint32_t w, int k) {
-  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + k)) - 8388608.0f;
-}
-__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
-
-template <int FMT, bool QUIRK, class Epi>
-__device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __restrict__ x,
-                                           const float* __restrict__ nw, float eps, float* __restrict__ part,
-                                           unsigned* __restrict__ cnt, Epi& epi, float* smem) {
-  using T = QTraits<FMT>;
-  constexpr int CE = T::CE, SW = T::SW, NG = CE / 32, SB = SW * 4;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t nk = W.nk, ntiles = W.Mp / QT_ROWS;
-  const uint64_t N = (uint64_t)ntiles * nk;
-  const uint64_t Wt = (uint64_t)gridDim.x * QG_WARPS;
-  const uint64_t g0 = (uint64_t)blockIdx.x * QG_WARPS;
-  const uint64_t ia = N * (g0 + warp) / Wt, ib = N * (g0 + warp + 1) / Wt;  // this warp's items
-  const uint64_t ca = N * g0 / Wt, cb = N * (g0 + QG_WARPS) / Wt;           // this CTA's items
-  // chunks this CTA stages: all of them, or the (possibly wrapping) window it covers
-  uint32_t kc0 = 0, nst = nk;
-  if (cb - ca < nk) {
-    kc0 = (uint32_t)(ca % nk);
-    nst = (uint32_t)(cb - ca);
-  }
-  float* sx = smem;                               // [nst][CE] pre-scaled x
-  float* sxs = sx + (size_t)nst * CE;             // [nst][NG] XSF * (sum of each 32 elements)
-  float* sws = sxs + (size_t)nst * NG;            // [QG_WARPS][64] epilogue staging
-  float* sslot = sws + QG_WARPS * 64;             // [QG_WARPS*2][64] partial tile sums of each warp
-  int* stile = reinterpret_cast<int*>(sslot + QG_WARPS * 2 * 64);  // [QG_WARPS*2] their tiles (-1: none)
-  float* sred = reinterpret_cast<float*>(stile + QG_WARPS * 2);     // [40]
-  float* ws = sws + warp * 64;
-  if (lane < 2) stile[2 * warp + lane] = -1;
-
-  uint32_t w[2][4][8];  // [row r / r+32][piece][word] of the chunk in flight
-  uint32_t h[2][SW];    // its scale bytes
-  auto load_piece = [&](uint64_t i, int c) {
-    const uint8_t* q = W.qs + i * QT_ITEM_BYTES + c * (QT_ROWS * 32) + lane * 32;
-    ldg256(q, w[0][c]);
-    ldg256(q + 32 * 32, w[1][c]);
-  };
-  auto load_hdr = [&](uint64_t i) {
-    const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
-    if constexpr (SW == 4) {
-      ldg128(s, h[0]);
-      ldg128(s + 32 * SB, h[1]);
-    } else {
-      ldg64(s, h[0]);
-      ldg64(s + 32 * SB, h[1]);
-    }
-  };
-  if (ia < ib) {
-    load_hdr(ia);
-#pragma unroll
-    for (int c = 0; c < 4; c++) load_piece(ia, c);
-  }
-
-  griddep_wait();
-  float rms = 1.f;
-  if (nw) rms = rms_of(block_sumsq_v4<QG_THREADS>(x, (int)W.K, sred), (int)W.K, eps);
-  // stage: float4 q of the window = elements 4q..4q+3; 8 consecutive threads =
-  // one 32-element group (trip counts are warp-uniform: the window is a multiple
-  // of 128 elements).  SU float4s per thread are loaded before any is used.
-  constexpr int SU = 2;
-  const uint32_t nq = nst * CE / 4;
-  for (uint32_t q0 = (uint32_t)tid; q0 < nq; q0 += SU * QG_THREADS) {
-    float4 xv[SU], wv[SU];
-#pragma unroll
-    for (int u = 0; u < SU; u++) {
-      const uint32_t f = 4 * (q0 + u * QG_THREADS), s = f / CE, e = f % CE;
-      uint32_t kc = kc0 + s;
-      if (kc >= nk) kc -= nk;
-      const uint32_t gi = kc * CE + e;
-      const bool in = f < nst * CE && gi < W.K;  // K is a multiple of 32: a float4 is wholly in or out
-      xv[u] = in ? __ldg(reinterpret_cast<const float4*>(x + gi)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      wv[u] = in && nw ? __ldg(reinterpret_cast<const float4*>(nw + gi)) : make_float4(1.f, 1.f, 1.f, 1.f);
-    }
-#pragma unroll
-    for (int u = 0; u < SU; u++) {
-      const uint32_t f = 4 * (q0 + u * QG_THREADS), e = f % CE;
-      if (f >= nst * CE) break;
-      float4 v = xv[u];
-      if (nw) v = make_float4(v.x / rms * wv[u].x, v.y / rms * wv[u].y, v.z / rms * wv[u].z, v.w / rms * wv[u].w);
-      *reinterpret_cast<float4*>(sx + f) =
-          make_float4(v.x * prescale(qfield_off<FMT>(e)), v.y * prescale(qfield_off<FMT>(e + 1)),
-                      v.z * prescale(qfield_off<FMT>(e + 2)), v.w * prescale(qfield_off<FMT>(e + 3)));
-      float gs = ((v.x + v.y) + v.z) + v.w;
-      gs += __shfl_xor_sync(0xffffffffu, gs, 1);
-      gs += __shfl_xor_sync(0xffffffffu, gs, 2);
-      gs += __shfl_xor_sync(0xffffffffu, gs, 4);
-      if ((lane & 7) == 0) sxs[f / 32] = gs * (float)T::XSF;
-    }
-  }
-  __syncthreads();
-  griddep_launch();
-
-  // finished rows of a tile -> epilogue, two consecutive rows per lane
-  auto emit = [&](uint32_t tile, float v0, float v1) {
-    ws[lane] = v0;
-    ws[32 + lane] = v1;
-    __syncwarp();
-    const uint32_t r = tile * QT_ROWS + 2 * lane;
-    const float v[2] = {ws[2 * lane], ws[2 * lane + 1]};
-    if (r < W.M) epi((int)r, v, (int)min(2u, W.M - r));
-    __syncwarp();
-  };
-  // End of this warp's run of `len` chunks in `tile`: a whole tile goes to the
-  // epilogue, a part (at most two per warp: the ends of its range) waits in
-  // shared memory for the CTA-level merge.
-  int nslot = 0;
-  auto flush = [&](uint32_t tile, uint32_t len, float v0, float v1) {
-    if (len == nk) {
-      emit(tile, v0, v1);
-      return;
-    }
-    float* p = sslot + (2 * warp + nslot) * 64;
-    p[lane] = v0;
-    p[32 + lane] = v1;
-    if (lane == 0) stile[2 * warp + nslot] = (int)tile;
-    nslot++;
-  };
-
-  uint32_t tile = (uint32_t)(ia / nk), kc = (uint32_t)(ia % nk), len = 0;
-  float acc0 = 0.f, acc1 = 0.f;
-  for (uint64_t i = ia; i < ib; i++) {
-    uint32_t slot = kc + nk - kc0;
-    if (slot >= nk) slot -= nk;
-    const float* xc = sx + (size_t)slot * CE;
-    const float* xsc = sxs + (size_t)slot * NG;
-    uint32_t hc[2][SW];
-#pragma unroll
-    for (int s = 0; s < 2; s++)
-#pragma unroll
-      for (int k = 0; k < SW; k++) hc[s][k] = h[s][k];
-    const bool more = i + 1 < ib;
-    if (more) load_hdr(i + 1);
-    float acc[2] = {0.f, 0.f};
-
-    if constexpr (FMT == T_Q4_K) {
-      // header: d, dmin (f16) | scales[12] (get_scale_min_k4, quant.rs:216-226)
-      float d64[2], dmn[2];
-      uint32_t scl[2], sch[2], ml[2], mh[2];
-#pragma unroll
-      for (int s = 0; s < 2; s++) {
-        d64[s] = scale_f<QUIRK>(hc[s][0]) * kTwo64;
-        dmn[s] = scale_f<QUIRK>(hc[s][0] >> 16);
-        scl[s] = hc[s][1] & 0x3F3F3F3Fu;  // sc[0..3]
-        ml[s] = hc[s][2] & 0x3F3F3F3Fu;   // m[0..3]
-        sch[s] = (hc[s][3] & 0x0F0F0F0Fu) | ((hc[s][1] >> 2) & 0x30303030u);         // sc[4..7]
-        mh[s] = ((hc[s][3] >> 4) & 0x0F0F0F0Fu) | ((hc[s][2] >> 2) & 0x30303030u);  // m[4..7]
-      }
-      float aS[2] = {0.f, 0.f}, aM[2] = {0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        float2 lo[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)}, hi[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const float* xb = xc + 64 * c + 8 * j;
-          const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 32), xh1 = lds4(xb + 36);
-#pragma unroll
-          for (int s = 0; s < 2; s++) q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, lo[s], hi[s]);
-        }
-        if (more) load_piece(i + 1, c);
-        const float xsl = xsc[2 * c], xsh = xsc[2 * c + 1];
-#pragma unroll
-        for (int s = 0; s < 2; s++) {
-          const uint32_t scw = c < 2 ? scl[s] : sch[s], mw = c < 2 ? ml[s] : mh[s];
-          const int kb = (2 * c) & 3;
-          aS[s] = fmaf(byte_f(scw, kb), lo[s].x + lo[s].y, aS[s]);
-          aS[s] = fmaf(byte_f(scw, kb + 1), hi[s].x + hi[s].y, aS[s]);
-          aM[s] = fmaf(byte_f(mw, kb), xsl, aM[s]);
-          aM[s] = fmaf(byte_f(mw, kb + 1), xsh, aM[s]);
-        }
-      }
-#pragma unroll
-      for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dmn[s] * aM[s];
-    } else if constexpr (FMT == T_Q4_0) {
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        float2 sb[2][2];  // [row][block of the piece]: low and high nibbles of a block sum together
-#pragma unroll
-        for (int s = 0; s < 2; s++)
-#pragma unroll
-          for (int b = 0; b < 2; b++) sb[s][b] = ff2(0.f, 0.f);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int b = j >> 1;
-          const float* xb = xc + 64 * c + 32 * b + 8 * (j & 1);
-          const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 16), xh1 = lds4(xb + 20);
-#pragma unroll
-          for (int s = 0; s < 2; s++)
-            q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, sb[s][b], sb[s][b]);
-        }
-        if (more) load_piece(i + 1, c);
-#pragma unroll
-        for (int b = 0; b < 2; b++) {
-          const float xs8 = xsc[2 * c + b];
-#pragma unroll
-          for (int s = 0; s < 2; s++) {
-            const float d = scale_f<QUIRK>(hc[s][c] >> (16 * b));
-            acc[s] = fmaf(d, fmaf(sb[s][b].x + sb[s][b].y, kTwo64, -xs8), acc[s]);
-          }
-        }
-      }
-    } else {  // Q8_0
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        float2 sa[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const float* xb = xc + 32 * c + 8 * j;
-          const float4 x0 = lds4(xb), x1 = lds4(xb + 4);
-#pragma unroll
-          for (int s = 0; s < 2; s++) q8_pair(w[s][c][2 * j], w[s][c][2 * j + 1], x0, x1, sa[s]);
-        }
-        if (more) load_piece(i + 1, c);
-        const float xs128 = xsc[c];
-#pragma unroll
-        for (int s = 0; s < 2; s++) {
-          const float d = scale_f<QUIRK>(hc[s][c >> 1] >> (16 * (c & 1)));
-          acc[s] = fmaf(d, fmaf(sa[s].x + sa[s].y, kTwo64, -xs128), acc[s]);
-        }
-      }
-    }
-    acc0 += acc[0];
-    acc1 += acc[1];
-    len++;
-    if (++kc == nk || !more) {
-      flush(tile, len, acc0, acc1);
-      acc0 = acc1 = 0.f;
-      if (kc == nk) {
-        kc = 0;
-        tile++;
-      }
-      len = 0;
-    }
-  }
-
-  // CTA-level merge.  Slots 2w, 2w+1 are in chunk order, so the parts of a tile
-  // are consecutive non-empty slots; the warp holding the first one sums them.
-  __syncthreads();
-  for (int i = 2 * warp; i < 2 * warp + 2; i++) {
-    const int T = stile[i];
-    if (T < 0) continue;
-    int j = i - 1;
-    while (j >= 0 && stile[j] < 0) j--;
-    if (j >= 0 && stile[j] == T) continue;
-    float s0 = 0.f, s1 = 0.f;
-    for (int k = i; k < 2 * QG_WARPS; k++) {
-      const int tk = stile[k];
-      if (tk < 0) continue;
-      if (tk != T) break;
-      s0 += sslot[k * 64 + lane];
-      s1 += sslot[k * 64 + 32 + lane];
-    }
-    const uint64_t t0 = (uint64_t)T * nk;
-    const uint64_t a = ca > t0 ? ca : t0, b = cb < t0 + nk ? cb : t0 + nk;  // this CTA's chunks of T
-    if (a == t0 && b == t0 + nk) {
-      emit((uint32_t)T, s0, s1);
-      continue;
-    }
-    // Across CTAs: publish this CTA's part; the CTA completing the tile sums the
-    // parts in chunk order (they start at chunk 0 and at every CTA boundary).
-    const uint32_t len_c = (uint32_t)(b - a);
-    float* p = part + a * QT_ROWS;
-    __stcg(p + lane, s0);
-    __stcg(p + 32 + lane, s1);
-    __threadfence();
-    __syncwarp();
-    unsigned old = 0;
-    if (lane == 0) old = atomicAdd(cnt + T, len_c);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + len_c != nk) continue;
-    __threadfence();
-    const uint64_t G = gridDim.x;
-    float r0 = 0.f, r1 = 0.f;
-    for (uint32_t k = 0; k < nk;) {
-      uint32_t ks[8];
-      int m = 0;
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        if (k < nk) {
-          ks[u] = k;
-          m = u + 1;
-          const uint64_t g = ((t0 + k + 1) * G + N - 1) / N;  // first CTA starting after item t0+k
-          const uint64_t nb = N * g / G;
-          k = nb - t0 < nk ? (uint32_t)(nb - t0) : nk;
-        }
-      }
-      float a0[8], a1[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++)
-        if (u < m) {
-          a0[u] = __ldcg(part + (t0 + ks[u]) * QT_ROWS + lane);
-          a1[u] = __ldcg(part + (t0 + ks[u]) * QT_ROWS + 32 + lane);
-        }
-#pragma unroll
-      for (int u = 0; u < 8; u++)
-        if (u < m) {
-          r0 += a0[u];
-          r1 += a1[u];
-        }
-    }
-    if (lane == 0) cnt[T] = 0;
-    emit((uint32_t)T, r0, r1);
-  }
-}
 
 template <int FMT, bool QUIRK, class Epi>
 __global__ void __launch_bounds__(QG_THREADS, 1)
     qgemv_kernel(PackedMat W, const float* __restrict__ x, const float* __restrict__ nw, float eps,
                  float* __restrict__ part, unsigned* __restrict__ cnt, Epi epi) {
   extern __shared__ __align__(16) float qsm[];
-  qgemv_body<FMT, QUIRK>(W, x, nw, eps, part, cnt, epi, qsm);
+  qgemv_body<FMT, QUIRK>(W, x, nw, eps, part, cnt, epi, qsm, [] { griddep_wait(); });
   epi.flush();
 }
 
@@ -551,14 +21,9 @@ constexpr size_t kMaxSmem = 227 * 1024;
 template <int FMT, class Epi>
 static cudaError_t run_qgemv_t(const Launch& L, const PackedMat& W, const GemvScratch& ws, const float* x,
                                const float* nw, float eps, Epi epi) {
-  constexpr int CE = QTraits<FMT>::CE;
   auto k = W.sub_scales ? qgemv_kernel<FMT, true, Epi> : qgemv_kernel<FMT, false, Epi>;
   const int grid = num_sms();
-  const uint64_t N = (uint64_t)(W.Mp / QT_ROWS) * W.nk;
-  const uint64_t per_cta = (N + grid - 1) / grid;
-  const uint32_t nst = (uint32_t)std::min<uint64_t>(W.nk, std::max<uint64_t>(1, per_cta));
-  const size_t smem =
-      ((size_t)nst * CE + (size_t)nst * (CE / 32) + QG_WARPS * 64 + QG_WARPS * 2 * 65 + 40) * sizeof(float);
+  const size_t smem = qgemv_smem_bytes(W, grid);
   if (smem > kMaxSmem) return cudaErrorInvalidValue;
   if (ws.part_floats < (uint64_t)W.Mp * W.nk || ws.n_cnt < W.Mp / QT_ROWS) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -14,6 +14,7 @@
 
 #include <algorithm>
 
+#include "rf_attn.cuh"
 #include "rf_device.cuh"
 
 namespace rf {
@@ -128,50 +129,8 @@ cudaError_t launch_pack(const uint8_t* gguf, const int* src_row_of, PackedMat ds
 }
 
 // ---------------------------------------------------------------------------
-// element-exact dequantisation (embedding rows, parity dumps)
+// embedding rows, parity dumps (dequant_elem, rf_device.cuh)
 // ---------------------------------------------------------------------------
-__device__ float dequant_elem(const PackedMat& W, uint32_t row, uint32_t e) {
-  const uint8_t* q = W.qs;
-  const uint8_t* c = W.sc;
-  switch (W.type) {
-    case T_F32: return reinterpret_cast<const float*>(q + (uint64_t)row * W.qs_stride)[e];
-    case T_F16: return h2f(reinterpret_cast<const unsigned short*>(q + (uint64_t)row * W.qs_stride)[e]);
-    case T_Q8_0: {  // q*d (quant.rs:176-180)
-      const uint8_t* sp = c + sc_byte_off(W, row, 2ull * (e / 32));
-      const float d = h2f(sp[0] | (sp[1] << 8));
-      return __fmul_rn((float)(int8_t)q[qs_byte_off(W, row, e)], d);
-    }
-    case T_Q4_0: {  // (q-8)*d (quant.rs:104-112)
-      const uint32_t b = e / 32, j = e % 32;
-      const uint8_t byte = q[qs_byte_off(W, row, (uint64_t)b * 16 + (j & 15))];
-      const int v = (j < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
-      const uint8_t* sp = c + sc_byte_off(W, row, 2ull * b);
-      const float d = h2f(sp[0] | (sp[1] << 8));
-      return __fmul_rn((float)v, d);
-    }
-    case T_Q4_K: {  // d1*q - min1 (quant.rs:228-254)
-      const uint32_t sb = e / 256, r = e % 256, gi = r / 64, t = r % 64;
-      const uint8_t byte = q[qs_byte_off(W, row, (uint64_t)sb * 128 + gi * 32 + (t & 31))];
-      const uint32_t nq = t < 32 ? (byte & 0xF) : (byte >> 4);
-      const uint8_t* h = c + sc_byte_off(W, row, (uint64_t)sb * 16);
-      const float d = h2f(h[0] | (h[1] << 8)), dmin = h2f(h[2] | (h[3] << 8));
-      const uint8_t* s = h + 4;
-      const int j = (int)(2 * gi + (t >= 32));
-      uint32_t sc, m;
-      if (j < 4) {
-        sc = s[j] & 63;
-        m = s[j + 4] & 63;
-      } else {
-        sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
-        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-      }
-      const float d1 = __fmul_rn(d, (float)sc), mn = __fmul_rn(dmin, (float)m);
-      return __fsub_rn(__fmul_rn(d1, (float)nq), mn);
-    }
-  }
-  return 0.f;
-}
-
 __global__ void embed_kernel(PackedMat E, const uint32_t* __restrict__ d_token, float* __restrict__ hidden,
                              unsigned long long* key) {
   griddep_wait();
@@ -246,275 +205,18 @@ cudaError_t launch_kv_gather(const void* cache, int kv_f32, uint32_t kvh, uint32
 }
 
 // ---------------------------------------------------------------------------
-// decode attention: split-K over context, GQA group per CTA
+// decode attention: split-K over context, GQA group per CTA (rf_attn.cuh)
 // ---------------------------------------------------------------------------
-// attention_reference (compute.rs:461-547) for one query token: query head h
-// reads KV head h*KV/H (contiguous groups of G = H/KV heads), so one CTA loads
-// each K/V row once for its G heads.  A CTA covers a chunk of about 32+
-// positions; each warp takes ATT_UNROLL consecutive positions at a time and
-// issues all their row loads before using any (lane i holds dims
-// [i*DPL, i*DPL+DPL) of every row), so a CTA's pass over K and over V each cost
-// one memory round trip.  The last CTA of a head to finish merges the chunk
-// partials (max-rescaled sums); nothing waits on another CTA.
-constexpr int ATT_THREADS = 128;
-constexpr int ATT_WARPS = ATT_THREADS / 32;
-constexpr int ATT_MAX_CHUNK = 512;
-constexpr int ATT_MIN_CHUNK = 32;
-constexpr int ATT_UNROLL = 8;
-constexpr int ATT_MERGE_SPLITS = 64;  // merges of up to this many splits take the parallel path
-
-__host__ __device__ inline int attn_nsplit(int ctx, int max_splits) {
-  int s = (ctx + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK;
-  s = s < 1 ? 1 : s;
-  return s < max_splits ? s : max_splits;
-}
-
 size_t attn_part_floats(int batch, int n_kv_heads, int max_splits, int G, int hd) {
   return (size_t)batch * n_kv_heads * max_splits * G * (hd + 2);
 }
 
-// DPL consecutive elements of one K/V row into f32 registers (zero past hd).
-template <int DPL>
-__device__ __forceinline__ void load_row(const __half* p, int d0, int hd, float (&v)[DPL]) {
-  if (DPL == 4 && d0 + 4 <= hd) {
-    const uint2 r = __ldg(reinterpret_cast<const uint2*>(p + d0));
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
-    v[0] = a.x; v[1] = a.y; v[2 % DPL] = b.x; v[3 % DPL] = b.y;
-  } else if (DPL == 2 && d0 + 2 <= hd) {
-    const float2 a = __half22float2(__ldg(reinterpret_cast<const __half2*>(p + d0)));
-    v[0] = a.x; v[1 % DPL] = a.y;
-  } else {
-#pragma unroll
-    for (int i = 0; i < DPL; i++) v[i] = d0 + i < hd ? __half2float(p[d0 + i]) : 0.f;
-  }
-}
-template <int DPL>
-__device__ __forceinline__ void load_row(const float* p, int d0, int hd, float (&v)[DPL]) {
-#pragma unroll
-  for (int i = 0; i < DPL; i++) v[i] = d0 + i < hd ? p[d0 + i] : 0.f;
-}
-
+// One unit per CTA: grid (KV heads, max_splits, batch).
 template <int DPL, int G, typename KT>
 __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(AttnArgs a) {
-  __shared__ float ssc[G][ATT_MAX_CHUNK];
-  __shared__ float sred[ATT_WARPS][G][DPL * 32];
-  __shared__ float sm[G], sl[G];
-  __shared__ float s_w[ATT_MERGE_SPLITS][G];
-  __shared__ int s_last;
-  const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int hd = a.head_dim;
+  __shared__ __align__(16) float gsm[attn_group_floats<DPL, G>()];
   griddep_wait();
-  const int nhist = a.d_nhist ? *a.d_nhist : a.nhist;
-  const bool has_cur = a.k_cur != nullptr;
-  const int ctx = nhist + (has_cur ? 1 : 0);
-  const int nsplit = attn_nsplit(ctx, a.max_splits);
-  if (split >= nsplit || ctx <= 0) {
-    griddep_launch();
-    return;
-  }
-  const int chunk = (ctx + nsplit - 1) / nsplit;
-  const int h0 = kvh * G;
-  if (chunk > ATT_MAX_CHUNK) {  // host sizes max_splits >= ctx/ATT_MAX_CHUNK; never index past ssc
-    if (split == 0)
-      for (int t = threadIdx.x; t < G * hd; t += ATT_THREADS)
-        a.out[((size_t)b * a.n_heads + h0) * hd + t] = __int_as_float(0x7fc00000);
-    griddep_launch();
-    return;
-  }
-  const int p0 = split * chunk, p1 = min(ctx, p0 + chunk);
-  const int d0 = lane * DPL;
-  const float* qb = a.q + ((size_t)b * a.n_heads + h0) * hd;
-  float qr[G][DPL];
-#pragma unroll
-  for (int h = 0; h < G; h++)
-#pragma unroll
-    for (int i = 0; i < DPL; i++) qr[h][i] = d0 + i < hd ? qb[(size_t)h * hd + d0 + i] : 0.f;
-  const KT* kb = reinterpret_cast<const KT*>(a.kc) + (size_t)b * a.batch_stride + (size_t)kvh * a.head_stride;
-  const KT* vb = reinterpret_cast<const KT*>(a.vc) + (size_t)b * a.batch_stride + (size_t)kvh * a.head_stride;
-  const float* kcur = has_cur ? a.k_cur + (size_t)kvh * hd : nullptr;
-  const float* vcur = has_cur ? a.v_cur + (size_t)kvh * hd : nullptr;
-  const float div = sqrtf((float)hd);  // score = dot / sqrt(hd)  (compute.rs:530)
-
-  // pass 1: scores
-  for (int p = p0 + warp * ATT_UNROLL; p < p1; p += ATT_WARPS * ATT_UNROLL) {
-    float k[ATT_UNROLL][DPL];
-#pragma unroll
-    for (int t = 0; t < ATT_UNROLL; t++) {
-      const int pp = p + t;
-      if (pp < min(p1, nhist)) load_row<DPL>(kb + (size_t)pp * hd, d0, hd, k[t]);
-      else if (pp < p1) load_row<DPL>(kcur, d0, hd, k[t]);
-      else {
-#pragma unroll
-        for (int i = 0; i < DPL; i++) k[t][i] = 0.f;
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < ATT_UNROLL; t++) {
-#pragma unroll
-      for (int h = 0; h < G; h++) {
-        float s = 0.f;
-#pragma unroll
-        for (int i = 0; i < DPL; i++) s = fmaf(qr[h][i], k[t][i], s);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0 && p + t < p1) ssc[h][p + t - p0] = s / div;
-      }
-    }
-  }
-  __syncthreads();
-  // per-head max and exp-sum over the chunk (softmax_reference, compute.rs:363-384)
-  const int n = p1 - p0;
-  for (int h = warp; h < G; h += ATT_WARPS) {
-    float m = -INFINITY;
-    for (int i = lane; i < n; i += 32) m = fmaxf(m, ssc[h][i]);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int i = lane; i < n; i += 32) {
-      const float e = expf(ssc[h][i] - m);
-      ssc[h][i] = e;
-      l += e;
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) {
-      sm[h] = m;
-      sl[h] = l;
-    }
-  }
-  __syncthreads();
-  // pass 2: sum_p e_p * v_p
-  float acc[G][DPL];
-#pragma unroll
-  for (int h = 0; h < G; h++)
-#pragma unroll
-    for (int i = 0; i < DPL; i++) acc[h][i] = 0.f;
-  for (int p = p0 + warp * ATT_UNROLL; p < p1; p += ATT_WARPS * ATT_UNROLL) {
-    float v[ATT_UNROLL][DPL];
-#pragma unroll
-    for (int t = 0; t < ATT_UNROLL; t++) {
-      const int pp = p + t;
-      if (pp < min(p1, nhist)) load_row<DPL>(vb + (size_t)pp * hd, d0, hd, v[t]);
-      else if (pp < p1) load_row<DPL>(vcur, d0, hd, v[t]);
-      else {
-#pragma unroll
-        for (int i = 0; i < DPL; i++) v[t][i] = 0.f;
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < ATT_UNROLL; t++) {
-      if (p + t < p1) {
-#pragma unroll
-        for (int h = 0; h < G; h++) {
-          const float e = ssc[h][p + t - p0];
-#pragma unroll
-          for (int i = 0; i < DPL; i++) acc[h][i] = fmaf(e, v[t][i], acc[h][i]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < G; h++)
-#pragma unroll
-    for (int i = 0; i < DPL; i++) sred[warp][h][d0 + i] = acc[h][i];
-  __syncthreads();
-  float* out_b = a.out + ((size_t)b * a.n_heads + h0) * hd;
-  if (nsplit == 1) {
-    for (int t = threadIdx.x; t < G * hd; t += ATT_THREADS) {
-      const int h = t / hd, d = t % hd;
-      float s = 0.f;
-      for (int w = 0; w < ATT_WARPS; w++) s += sred[w][h][d];
-      out_b[(size_t)h * hd + d] = s / sl[h];
-    }
-    griddep_launch();
-    return;
-  }
-  // write this chunk's partial: [G][hd] sums then (m, l) per head
-  const size_t slot = ((size_t)b * a.n_kv_heads + kvh) * a.max_splits;
-  float* part = a.part + (slot + split) * (size_t)G * (hd + 2);
-  for (int t = threadIdx.x; t < G * hd; t += ATT_THREADS) {
-    const int h = t / hd, d = t % hd;
-    float s = 0.f;
-    for (int w = 0; w < ATT_WARPS; w++) s += sred[w][h][d];
-    part[(size_t)h * (hd + 2) + d] = s;
-  }
-  if (threadIdx.x < G) {
-    part[(size_t)threadIdx.x * (hd + 2) + hd] = sm[threadIdx.x];
-    part[(size_t)threadIdx.x * (hd + 2) + hd + 1] = sl[threadIdx.x];
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&a.counters[(size_t)b * a.n_kv_heads + kvh], 1u);
-    s_last = prev == (unsigned)(nsplit - 1);
-  }
-  __syncthreads();
-  if (!s_last) {
-    griddep_launch();
-    return;
-  }
-  __threadfence();
-  const float* pall = a.part + slot * (size_t)G * (hd + 2);
-  if (nsplit <= ATT_MERGE_SPLITS) {
-    // one warp per head: split weights exp(m_s - M) / sum_s exp(m_s - M) l_s in one load round
-    for (int h = warp; h < G; h += ATT_WARPS) {
-      float ms[ATT_MERGE_SPLITS / 32], ls[ATT_MERGE_SPLITS / 32];
-      float M = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) {
-        const int sp = lane + 32 * j;
-        const float* ps = pall + ((size_t)sp * G + h) * (hd + 2);
-        ms[j] = sp < nsplit ? __ldcg(ps + hd) : -INFINITY;
-        ls[j] = sp < nsplit ? __ldcg(ps + hd + 1) : 0.f;
-        M = fmaxf(M, ms[j]);
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      float L = 0.f;
-#pragma unroll
-      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) {
-        ms[j] = lane + 32 * j < nsplit ? expf(ms[j] - M) : 0.f;
-        L = fmaf(ms[j], ls[j], L);
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-#pragma unroll
-      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) s_w[lane + 32 * j][h] = ms[j] / L;
-    }
-    __syncthreads();
-    // every output element: sum_s w_s * O_s, eight independent loads at a time
-    for (int t = threadIdx.x; t < G * hd; t += ATT_THREADS) {
-      const int h = t / hd, d = t % hd;
-      float O = 0.f;
-      for (int s0 = 0; s0 < nsplit; s0 += 8) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-          v[j] = s0 + j < nsplit ? __ldcg(pall + ((size_t)(s0 + j) * G + h) * (hd + 2) + d) : 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-          if (s0 + j < nsplit) O = fmaf(s_w[s0 + j][h], v[j], O);
-      }
-      out_b[(size_t)h * hd + d] = O;
-    }
-  } else {
-    for (int t = threadIdx.x; t < G * hd; t += ATT_THREADS) {
-      const int h = t / hd, d = t % hd;
-      float M = -INFINITY;
-      for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(pall + ((size_t)s * G + h) * (hd + 2) + hd));
-      float L = 0.f, O = 0.f;
-      for (int s = 0; s < nsplit; s++) {
-        const float* ps = pall + ((size_t)s * G + h) * (hd + 2);
-        const float sc = expf(__ldcg(ps + hd) - M);
-        L = fmaf(sc, __ldcg(ps + hd + 1), L);
-        O = fmaf(sc, __ldcg(ps + d), O);
-      }
-      out_b[(size_t)h * hd + d] = O / L;
-    }
-  }
-  if (threadIdx.x == 0) a.counters[(size_t)b * a.n_kv_heads + kvh] = 0u;
+  attn_unit<DPL, G, KT>(a, blockIdx.x, blockIdx.y, blockIdx.z, gsm, 0);
   griddep_launch();
 }
 

@@ -155,6 +155,29 @@ class DecodeEngine:
         check(lib().rf_step_kernel_count(self._h, ctypes.byref(v)))
         return v.value
 
+    def set_step_kernel(self, enable: bool) -> None:
+        """Allow (default) or forbid the persistent one-launch-per-token step kernel."""
+        check(lib().rf_set_step_kernel(self._h, 1 if enable else 0))
+
+    @property
+    def step_kernel_active(self) -> bool:
+        v = ctypes.c_int()
+        check(lib().rf_step_kernel_active(self._h, ctypes.byref(v)))
+        return bool(v.value)
+
+    def step_profile(self, enable: bool) -> None:
+        """Record grid-barrier completion times in every step-kernel launch."""
+        check(lib().rf_step_profile(self._h, 1 if enable else 0))
+
+    def step_phase_times(self) -> np.ndarray:
+        """Phase durations (us) of the last profiled step: embedding, then per layer
+        [QKV, attention, Wo, gate/up, down], then LM head or final norm."""
+        n = 5 * self.config["n_layers"] + 8
+        out = np.zeros(n, np.float32)
+        k = ctypes.c_uint32()
+        check(lib().rf_step_phase_times(self._h, _fp(out), n, ctypes.byref(k)))
+        return out[:k.value]
+
     def decode_timed(self, token: int, n_steps: int):
         """n greedy decode steps timed on the device; returns (tokens, device_ms)."""
         out = np.zeros(max(1, n_steps), np.uint32)
