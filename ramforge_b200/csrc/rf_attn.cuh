@@ -105,6 +105,31 @@ __device__ __forceinline__ void cur_load(const float* p, int d0, int hd, float (
   for (int i = 0; i < DPL; i++) v[i] = p && d0 + i < hd ? __ldcg(p + d0 + i) : 0.f;
 }
 
+// Warp sums of CNT values at once (a transposing butterfly): at each level a lane
+// keeps half of the values it still holds, sends the other half to its partner
+// and adds what comes back, so CNT = 32 sums take 31 shuffles in chains five
+// deep (one sum at a time takes five dependent shuffles each).  Afterwards
+// v[0] of lane l is the full sum of value l >> (5 - log2 CNT).
+template <int CNT, int O>
+__device__ __forceinline__ void warp_transpose_sum(float* v, int lane) {
+  if constexpr (O >= 1) {
+    if constexpr (CNT > 1) {
+      constexpr int HALF = CNT / 2;
+      const bool up = (lane & O) != 0;
+#pragma unroll
+      for (int i = 0; i < HALF; i++) {
+        const float send = up ? v[i] : v[i + HALF];
+        const float keep = up ? v[i + HALF] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+      }
+      warp_transpose_sum<HALF, O / 2>(v, lane);
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], O);
+      warp_transpose_sum<1, O / 2>(v, lane);
+    }
+  }
+}
+
 // One (KV head, split, sequence) unit, run by the ATT_THREADS threads of group
 // `gid` (thread t = threadIdx.x % ATT_THREADS, barrier gid + 1).  The caller has
 // made a.q, a.k_cur, a.v_cur and the history length visible.
@@ -166,28 +191,37 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kvh, int split,
       if (pp < base + n && pp < nhist) {
         raw_load<DPL, RW>(kb + (size_t)pp * hd, d0, hd, kr[j]);
         raw_load<DPL, RW>(vb + (size_t)pp * hd, d0, hd, vr[j]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < RW; i++) kr[j][i] = vr[j][i] = 0u;
       }
     }
-    // scores of the pass
+    // scores of the pass: the PPW*G dot products (position j, head h) of this
+    // warp as value c = j*G + h, summed across the warp EC at a time
+    {
+      constexpr int E = PPW * G;
+      constexpr int EC = E > 16 ? 32 : (E > 8 ? 16 : 8);
+      constexpr int LSH = EC == 32 ? 0 : (EC == 16 ? 1 : 2);
 #pragma unroll
-    for (int j = 0; j < PPW; j++) {
-      const int pp = base + warp + ATT_WARPS * j;
-      if (pp < base + n) {
-        float k[DPL];
-        if (pp < nhist) raw_f32<DPL, RW, KT>(kr[j], k);
-        else {
+      for (int c0 = 0; c0 < E; c0 += EC) {
+        float v[EC];
 #pragma unroll
-          for (int i = 0; i < DPL; i++) k[i] = kcur[i];
-        }
-#pragma unroll
-        for (int h = 0; h < G; h++) {
+        for (int e = 0; e < EC; e++) {
+          const int c = c0 + e, j = c / G, h = c % G;
           float s = 0.f;
+          if (c < E) {
+            const bool cached = base + warp + ATT_WARPS * j < nhist;  // else the current step's row
+            float k[DPL];
+            raw_f32<DPL, RW, KT>(kr[j < PPW ? j : 0], k);
 #pragma unroll
-          for (int i = 0; i < DPL; i++) s = fmaf(qr[h][i], k[i], s);
-#pragma unroll
-          for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-          if (lane == 0) ssc[h][warp + ATT_WARPS * j] = s / div;
+            for (int i = 0; i < DPL; i++) s = fmaf(qr[h < G ? h : 0][i], cached ? k[i] : kcur[i], s);
+          }
+          v[e] = s;
         }
+        warp_transpose_sum<EC, 16>(v, lane);
+        const int c = c0 + (lane >> LSH), j = c / G, h = c % G;
+        if ((lane & ((1 << LSH) - 1)) == 0 && c < E && warp + ATT_WARPS * j < n)
+          ssc[h][warp + ATT_WARPS * j] = v[0] / div;
       }
     }
     group_sync(bar);
