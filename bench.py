@@ -22,9 +22,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
-import tempfile
 import threading
 import time
 
@@ -55,54 +53,81 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clocks, power and clock-event (throttle) reasons of this rank's GPU,
+    read through NVML every 5 ms by a thread while the timed region runs (the
+    same fields as nvidia-smi's clocks.sm / clocks_event_reasons.*)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_s: float = 0.005):
         self.dev = device_index
-        self.proc = None
-        self.tmp = None
+        self.period = period_s
+        self.rows = []
+        self.err = None
+        self.nvml = None
+        self.handle = None
+        self.thread = None
+        self.stop = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        self.nvml = pynvml
+        p = torch.cuda.get_device_properties(self.dev)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        try:
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+
+    def _sample(self):
+        n = self.nvml
+        sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+        mask = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        watts = n.nvmlDeviceGetPowerUsage(self.handle) / 1e3
+        self.rows.append((sm, mask, watts))
+
+    def _loop(self):
+        while not self.stop.is_set():
+            try:
+                self._sample()
+            except Exception as e:  # keep what was read; report the failure
+                self.err = str(e)
+                return
+            self.stop.wait(self.period)
 
     def __enter__(self):
         try:
-            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.dev), "-lms", "200"], stdout=self.tmp,
-                                         stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            self.handle = self._handle()
+            self.max_mhz = self.nvml.nvmlDeviceGetMaxClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+        except Exception as e:
+            self.err = f"nvml: {e}"
+            return self
+        self.stop = threading.Event()
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+        self.thread.start()
         return self
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
+        if self.thread:
+            self.stop.set()
+            self.thread.join(timeout=5)
+        if self.nvml and self.handle is not None:
             try:
-                self.proc.wait(timeout=5)
+                self._sample()  # one more at the end of the timed region
             except Exception:
-                self.proc.kill()
+                pass
 
     def summary(self):
-        if not self.proc or not self.tmp:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        self.tmp.flush()
-        rows = []
-        with open(self.tmp.name) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        os.unlink(self.tmp.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no samples"]}
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({name for _, mask, _ in self.rows for name, bit in self.REASONS if mask & bit})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(self.max_mhz), "reasons": reasons,
+                "samples": len(self.rows), "power_w_median": float(np.median([r[2] for r in self.rows])),
+                "source": "nvml, 5 ms period, during the timed region"}
 
 
 def algorithmic_bytes(spec, tp: int, ctx: float):

@@ -132,10 +132,13 @@ __device__ __forceinline__ void warp_transpose_sum(float* v, int lane) {
 
 // One (KV head, split, sequence) unit, run by the ATT_THREADS threads of group
 // `gid` (thread t = threadIdx.x % ATT_THREADS, barrier gid + 1).  The caller has
-// made a.q, a.k_cur, a.v_cur and the history length visible.
-template <int DPL, int G, typename KT>
+// made a.q, a.k_cur, a.v_cur and the history length visible.  PPW_CAP bounds
+// the positions per warp of a pass (fewer registers, for callers launched with
+// a tighter register budget).
+template <int DPL, int G, typename KT, int PPW_CAP = ATT_PASS_MAX>
 __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kvh, int split, int b, float* gsm, int gid) {
-  constexpr int PPW = attn_ppw<DPL, G, KT>(), PASS = ATT_WARPS * PPW, RW = RawW<KT, DPL>::RW;
+  constexpr int PPW = attn_ppw<DPL, G, KT>() < PPW_CAP ? attn_ppw<DPL, G, KT>() : PPW_CAP;
+  constexpr int PASS = ATT_WARPS * PPW, RW = RawW<KT, DPL>::RW;
   float(*ssc)[ATT_PASS_MAX] = reinterpret_cast<float(*)[ATT_PASS_MAX]>(gsm);
   float(*sred)[G][DPL * 32] = reinterpret_cast<float(*)[G][DPL * 32]>(gsm + G * ATT_PASS_MAX);
   float(*s_w)[G] = reinterpret_cast<float(*)[G]>(gsm + G * ATT_PASS_MAX + ATT_WARPS * G * DPL * 32);

@@ -284,7 +284,7 @@ int engine_init_device(rf_engine* e) {
   const uint32_t G = c.n_heads / c.n_kv_heads;
   const uint64_t part_f = attn_part_floats(1, e->kvh_local, e->max_splits, G, c.head_dim);
   // GEMV split-K scratch for any matrix this rank can hold, sized for the
-  // smallest chunk (128 elements, Q8_0)
+  // smallest chunk (128 elements, Q8_0): one 64-row partial per piece
   uint64_t gpart = 0;
   uint32_t gcnt = 0;
   const uint32_t shapes[5][2] = {{e->q_local + 2 * e->kv_local, c.n_embd},
@@ -294,7 +294,7 @@ int engine_init_device(rf_engine* e) {
                                  {e->vocab_local, c.n_embd}};
   for (auto& sh : shapes) {
     const uint64_t mp = (sh[0] + QT_ROWS - 1) / QT_ROWS * QT_ROWS;
-    gpart = std::max<uint64_t>(gpart, mp * ((sh[1] + 127) / 128));
+    gpart = std::max<uint64_t>(gpart, mp * ((sh[1] + 127) / 128) * QT_PIECES);
     gcnt = std::max<uint32_t>(gcnt, (uint32_t)(mp / QT_ROWS));
   }
   e->gws.part_floats = gpart;

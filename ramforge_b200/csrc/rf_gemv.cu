@@ -25,7 +25,7 @@ static cudaError_t run_qgemv_t(const Launch& L, const PackedMat& W, const GemvSc
   const int grid = num_sms();
   const size_t smem = qgemv_smem_bytes(W, grid);
   if (smem > kMaxSmem) return cudaErrorInvalidValue;
-  if (ws.part_floats < (uint64_t)W.Mp * W.nk || ws.n_cnt < W.Mp / QT_ROWS) return cudaErrorInvalidValue;
+  if (ws.part_floats < (uint64_t)W.Mp * W.nk * QT_PIECES || ws.n_cnt < W.Mp / QT_ROWS) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_k(L, k, dim3(grid), dim3(QG_THREADS), smem, W, x, nw, eps, ws.part, ws.cnt, epi);
@@ -33,7 +33,7 @@ static cudaError_t run_qgemv_t(const Launch& L, const PackedMat& W, const GemvSc
 
 void gemv_scratch_need(const PackedMat& W, uint64_t* part_floats, uint32_t* n_cnt) {
   if (is_tiled(W.type)) {
-    *part_floats = (uint64_t)W.Mp * W.nk;
+    *part_floats = (uint64_t)W.Mp * W.nk * QT_PIECES;
     *n_cnt = W.Mp / QT_ROWS;
   } else {
     *part_floats = 0;
@@ -124,7 +124,7 @@ cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const GemvScratch
 }
 cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
                           const float* nw, float eps, const RopeQKVArgs& a) {
-  return run_gemv(L, W, ws, x, nw, eps, EpiRope{a});
+  return run_gemv(L, W, ws, x, nw, eps, EpiRope{a, -1});
 }
 cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x, const float* nw,
                         float eps, float* act) {

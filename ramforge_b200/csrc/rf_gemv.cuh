@@ -21,14 +21,16 @@
 //    so every product is exactly q * x * 2^-64 and one packed fma.rn.f32x2 takes
 //    two elements.  The top byte of a word is brought down with one byte-permute
 //    shared by two words: 17 integer ops per 16 Q4 weights.
-//  * Work is split "stream-K": the (tile, chunk) items of the matrix are cut into
-//    equal contiguous ranges, one per warp of a persistent grid, so every SM gets
-//    the same number of bytes whatever the matrix shape.  A tile whose chunks span
+//  * Work is split "stream-K": the 32-byte pieces of the matrix's (tile, chunk)
+//    items are cut into equal contiguous ranges, one per warp of a persistent
+//    grid, so every SM gets the same number of bytes whatever the matrix shape
+//    and the warps' shares differ by at most one piece.  A tile whose pieces span
 //    several warps is finished by the last of them to arrive (arrival counter),
-//    which sums the partials in chunk order: results do not depend on timing, and
+//    which sums the partials in piece order: results do not depend on timing, and
 //    nothing waits on another warp or CTA.
 #pragma once
 #include <algorithm>
+#include <type_traits>
 
 #include "rf_device.cuh"
 
@@ -43,41 +45,75 @@ __device__ __forceinline__ float prescale(int off) { return __int_as_float((212 
 // ---------------------------------------------------------------------------
 // epilogues: called with the finished values of rows [row0, row0+n), n <= 2 and
 // row0 even, so RoPE and SwiGLU row pairs arrive together.
+//
+// An epilogue with kPre = true can have its per-row inputs fetched early: the
+// quantized GEMV calls pre_begin() once its inputs are visible and pre_load(row)
+// for every row of the tiles its CTA may finish, keeps the values in shared
+// memory while it multiplies, and passes them as `pre` (values of rows row0..);
+// `pre` is null when they were not fetched.
 // ---------------------------------------------------------------------------
 struct EpiStore {
+  static constexpr bool kPre = false;
   float* y;
-  __device__ void operator()(int row0, const float* v, int n) {
+  __device__ void operator()(int row0, const float* v, int n, const float* = nullptr) {
     for (int i = 0; i < n; i++) y[row0 + i] = v[i];
   }
+  __device__ void pre_begin() {}
+  __device__ float pre_load(uint32_t) { return 0.f; }
   __device__ void flush() {}
 };
 
-struct EpiResidual {
+struct EpiResidual {  // out = res + W.x (res may alias out: a row is read before it is written)
+  static constexpr bool kPre = true;
   const float* res;
   float* out;
-  __device__ void operator()(int row0, const float* v, int n) {
-    for (int i = 0; i < n; i++) out[row0 + i] = res ? __ldcg(res + row0 + i) + v[i] : v[i];
+  __device__ void operator()(int row0, const float* v, int n, const float* pre = nullptr) {
+    for (int i = 0; i < n; i++) {
+      const float r = pre ? pre[i] : (res ? __ldcg(res + row0 + i) : 0.f);
+      out[row0 + i] = res ? r + v[i] : v[i];
+    }
   }
+  __device__ void pre_begin() {}
+  __device__ float pre_load(uint32_t row) { return res ? __ldcg(res + row) : 0.f; }
   __device__ void flush() {}
 };
 
 // Q and K rows are packed as pairs (i, i+hd/2) of each head so that the
 // half-split rotation (compute.rs:440-456) happens in registers; V rows are in
-// natural order.
-__device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const float* v, int n);
+// natural order.  `pre`, when given, holds (cos, sin) of the pair and `pos` the
+// step's position.
+__device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const float* v, int n,
+                                           const float* pre = nullptr, int pos = -1);
+// (cos, sin) component (row & 1) of the rotation of Q/K row `row` at `pos`; 0 for V rows.
+__device__ __forceinline__ float rope_cs_of(const RopeQKVArgs& a, uint32_t row, int pos) {
+  if (row >= a.q_rows + a.kv_rows) return 0.f;
+  const uint32_t j = (row < a.q_rows ? row : row - a.q_rows) / 2, half = a.head_dim / 2;
+  const float* c = reinterpret_cast<const float*>(a.rope_cs + (size_t)pos * half + j % half);
+  return __ldg(c + (row & 1));
+}
 struct EpiRope {  // arguments held by value (a kernel parameter)
+  static constexpr bool kPre = true;
   RopeQKVArgs a;
-  __device__ void operator()(int row0, const float* v, int n) { rope_store(a, row0, v, n); }
+  int pos;
+  __device__ void operator()(int row0, const float* v, int n, const float* pre = nullptr) {
+    rope_store(a, row0, v, n, pre, pre ? pos : -1);
+  }
+  __device__ void pre_begin() { pos = __ldcg(a.d_pos); }
+  __device__ float pre_load(uint32_t row) { return rope_cs_of(a, row, pos); }
   __device__ void flush() {}
 };
 struct EpiRopeRef {  // arguments read from memory when a row pair finishes
+  static constexpr bool kPre = false;
   const RopeQKVArgs* a;
-  __device__ void operator()(int row0, const float* v, int n) { rope_store(*a, row0, v, n); }
+  __device__ void operator()(int row0, const float* v, int n, const float* = nullptr) { rope_store(*a, row0, v, n); }
+  __device__ void pre_begin() {}
+  __device__ float pre_load(uint32_t) { return 0.f; }
   __device__ void flush() {}
 };
-__device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const float* v, int n) {
+__device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const float* v, int n, const float* pre,
+                                           int pos) {
   {
-    const int pos = __ldcg(a.d_pos);
+    if (pos < 0) pos = __ldcg(a.d_pos);
     const uint32_t half = a.head_dim / 2;
     const uint32_t p = (uint32_t)row0;
     if (p < a.q_rows + a.kv_rows) {
@@ -85,7 +121,7 @@ __device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const
       const bool isq = p < a.q_rows;
       const uint32_t j = (isq ? p : p - a.q_rows) / 2;
       const uint32_t h = j / half, i = j % half;
-      const float2 cs = a.rope_cs[(size_t)pos * half + i];
+      const float2 cs = pre ? make_float2(pre[0], pre[1]) : a.rope_cs[(size_t)pos * half + i];
       const float x0 = v[0], x1 = v[1];
       // first*cos - second*sin ; first*sin + second*cos, one rounding per op
       const float o0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
@@ -120,10 +156,13 @@ __device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const
 }
 
 struct EpiSwiGLU {
+  static constexpr bool kPre = false;
   float* act;
+  __device__ void pre_begin() {}
+  __device__ float pre_load(uint32_t) { return 0.f; }
   // rows (2j, 2j+1) = (gate_j, up_j); silu(g) = g/(1+exp(-g)) then * up
   // (compute.rs:337-350, model_executor.rs:229-230)
-  __device__ void operator()(int row0, const float* v, int n) {
+  __device__ void operator()(int row0, const float* v, int n, const float* = nullptr) {
     if (n < 2) return;
     const float g = v[0], u = v[1];
     const float s = g / (1.0f + expf(-g));
@@ -142,11 +181,14 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t row) 
 }
 
 struct EpiArgmax {
+  static constexpr bool kPre = false;
   float* logits;
   unsigned long long* key;
   uint32_t row_offset;
   unsigned long long best;
-  __device__ void operator()(int row0, const float* v, int n) {
+  __device__ void pre_begin() {}
+  __device__ float pre_load(uint32_t) { return 0.f; }
+  __device__ void operator()(int row0, const float* v, int n, const float* = nullptr) {
     for (int i = 0; i < n; i++) {
       if (logits) logits[row0 + i] = v[i];
       const unsigned long long k = argmax_key(v[i], row_offset + row0 + i);
@@ -245,6 +287,32 @@ __device__ __forceinline__ float byte_f(uint32_t w, int k) {
 }
 __device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
+// floor(a * b / c); in 32-bit arithmetic when the product fits (`narrow`), as it
+// does for the piece splits of every matrix shape in use.
+__device__ __forceinline__ uint64_t muldiv(uint64_t a, uint64_t b, uint64_t c, bool narrow) {
+  return narrow ? (uint64_t)((uint32_t)(a * b) / (uint32_t)c) : a * b / c;
+}
+// a / b and a % b, likewise (a < 2^32 when narrow).
+__device__ __forceinline__ uint64_t div_n(uint64_t a, uint32_t b, bool narrow) {
+  return narrow ? (uint64_t)((uint32_t)a / b) : a / b;
+}
+__device__ __forceinline__ uint32_t mod_n(uint64_t a, uint32_t b, bool narrow) {
+  return narrow ? (uint32_t)a % b : (uint32_t)(a % b);
+}
+// ceil(a * b / c), likewise.
+__device__ __forceinline__ uint64_t muldiv_up(uint64_t a, uint64_t b, uint64_t c, bool narrow) {
+  return narrow ? (uint64_t)(((uint32_t)(a * b) + (uint32_t)c - 1) / (uint32_t)c) : (a * b + c - 1) / c;
+}
+// Arrival on a tile counter: release (the warp's partial stores, ordered before
+// this lane by a __syncwarp) and acquire (of the partials the other arrivals
+// released) in one round trip.
+__device__ __forceinline__ unsigned arrive_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+constexpr int EPI_ROWS = QG_THREADS;  // epilogue inputs prefetched per CTA (one per thread)
+
 // The quantized GEMV over every CTA of the grid.  `wait()` runs between the
 // first weight loads and the first read of x (the previous kernel's completion,
 // or a grid barrier of the persistent step kernel); x and the residual input are
@@ -256,16 +324,25 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   using T = QTraits<FMT>;
   constexpr int CE = T::CE, SW = T::SW, NG = CE / 32, SB = SW * 4;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t nk = W.nk, ntiles = W.Mp / QT_ROWS;
-  const uint64_t N = (uint64_t)ntiles * nk;
+  constexpr int NP = QT_PIECES;
+  const uint32_t nk = W.nk, ntiles = W.Mp / QT_ROWS, tp = nk * NP;  // tp: pieces per tile
+  // The work is split in pieces (item i = pieces NP*i .. NP*i+NP-1), so that the
+  // warps' shares differ by at most one piece; a warp loads and decodes whole
+  // items but only its pieces of the first and last one.
+  const uint64_t N = (uint64_t)ntiles * nk, P = N * NP;
   const uint64_t Wt = (uint64_t)gridDim.x * QG_WARPS;
   const uint64_t g0 = (uint64_t)blockIdx.x * QG_WARPS;
-  const uint64_t ia = N * (g0 + warp) / Wt, ib = N * (g0 + warp + 1) / Wt;  // this warp's items
-  const uint64_t ca = N * g0 / Wt, cb = N * (g0 + QG_WARPS) / Wt;           // this CTA's items
+  const bool narrow = P * Wt < (1ull << 32);
+  const uint64_t pa = muldiv(P, g0 + warp, Wt, narrow), pb = muldiv(P, g0 + warp + 1, Wt, narrow);  // this warp's
+  const uint64_t cpa = muldiv(P, g0, Wt, narrow), cpb = muldiv(P, g0 + QG_WARPS, Wt, narrow);         // this CTA's
+  const uint64_t ia = pa / NP, ib = pa < pb ? (pb + NP - 1) / NP : ia;      // items touched by the warp
+  const uint64_t ca = cpa / NP, cb = (cpb + NP - 1) / NP;                   // ... by the CTA
+  auto plo = [&](uint64_t i) { return i * NP < pa ? (int)(pa - i * NP) : 0; };         // first piece of item i
+  auto phi = [&](uint64_t i) { return (i + 1) * NP > pb ? (int)(pb - i * NP) : NP; };  // end piece of item i
   // chunks this CTA stages: all of them, or the (possibly wrapping) window it covers
   uint32_t kc0 = 0, nst = nk;
   if (cb - ca < nk) {
-    kc0 = (uint32_t)(ca % nk);
+    kc0 = mod_n(ca, nk, narrow);
     nst = (uint32_t)(cb - ca);
   }
   float* sx = smem;                               // [nst][CE] pre-scaled x
@@ -274,7 +351,15 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   float* sslot = sws + QG_WARPS * 64;             // [QG_WARPS*2][64] partial tile sums of each warp
   int* stile = reinterpret_cast<int*>(sslot + QG_WARPS * 2 * 64);  // [QG_WARPS*2] their tiles (-1: none)
   float* sred = reinterpret_cast<float*>(stile + QG_WARPS * 2);     // [40]
+  float* sepi = sred + 40;                                          // [EPI_ROWS] prefetched epilogue inputs
   float* ws = sws + warp * 64;
+  // Epilogue inputs of the rows of the tiles this CTA touches (the only tiles it
+  // can finish), when they fit: fetched after wait() and held in a register
+  // while the CTA multiplies.
+  const uint32_t etl = (uint32_t)div_n(cpa, tp, narrow);
+  const uint32_t eth = cpb > cpa ? (uint32_t)div_n(cpb - 1, tp, narrow) + 1 : etl;
+  const bool epre = Epi::kPre && (eth - etl) * QT_ROWS <= (uint32_t)EPI_ROWS;
+  float epf = 0.f;
 
   uint32_t w[2][4][8];  // [row r / r+32][piece][word] of the chunk in flight
   uint32_t h[2][SW];    // its scale bytes
@@ -295,14 +380,17 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   };
   if (ia < ib) {
     load_hdr(ia);
+    const int lo = plo(ia), hi = phi(ia);
 #pragma unroll
-    for (int c = 0; c < 4; c++) load_piece(ia, c);
+    for (int c = 0; c < NP; c++)
+      if (c >= lo && c < hi) load_piece(ia, c);
   }
 
   // Shared memory may still be in use by the CTA's previous phase until wait()
   // returns (the step kernel's barrier begins with a CTA barrier).
   wait();
   if (lane < 2) stile[2 * warp + lane] = -1;
+  if (epre) epi.pre_begin();
   // One pass over x.  The window is staged as x*nw: RMSNorm's 1/rms is applied
   // to every finished row instead (the product is linear in x), so with RMSNorm
   // the loads for the sum of squares (all of x, in the same per-thread order as
@@ -363,9 +451,14 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     rms = rms_of(t, (int)W.K, eps);
   }
   griddep_launch();
+  if (epre) {
+    const uint32_t r = etl * QT_ROWS + tid;
+    if (r < eth * QT_ROWS && r < W.M) epf = epi.pre_load(r);
+  }
 
   // finished rows of a tile -> epilogue, two consecutive rows per lane
-  auto emit = [&](uint32_t tile, float v0, float v1) {
+  // (`pre`: after the CTA barrier that publishes the prefetched inputs)
+  auto emit = [&](uint32_t tile, float v0, float v1, bool pre) {
     if (nw) {  // RMSNorm's division, once per row: W.(x*nw) / rms
       v0 = v0 / rms;
       v1 = v1 / rms;
@@ -375,16 +468,16 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     __syncwarp();
     const uint32_t r = tile * QT_ROWS + 2 * lane;
     const float v[2] = {ws[2 * lane], ws[2 * lane + 1]};
-    if (r < W.M) epi((int)r, v, (int)min(2u, W.M - r));
+    if (r < W.M) epi((int)r, v, (int)min(2u, W.M - r), pre && epre ? sepi + (r - etl * QT_ROWS) : nullptr);
     __syncwarp();
   };
-  // End of this warp's run of `len` chunks in `tile`: a whole tile goes to the
+  // End of this warp's run of `len` pieces in `tile`: a whole tile goes to the
   // epilogue, a part (at most two per warp: the ends of its range) waits in
   // shared memory for the CTA-level merge.
   int nslot = 0;
   auto flush = [&](uint32_t tile, uint32_t len, float v0, float v1) {
-    if (len == nk) {
-      emit(tile, v0, v1);
+    if (len == tp) {
+      emit(tile, v0, v1, false);
       return;
     }
     float* p = sslot + (2 * warp + nslot) * 64;
@@ -394,7 +487,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     nslot++;
   };
 
-  uint32_t tile = (uint32_t)(ia / nk), kc = (uint32_t)(ia % nk), len = 0;
+  uint32_t tile = (uint32_t)div_n(ia, nk, narrow), kc = mod_n(ia, nk, narrow), len = 0;
   float acc0 = 0.f, acc1 = 0.f;
   for (uint64_t i = ia; i < ib; i++) {
     uint32_t slot = kc + nk - kc0;
@@ -407,98 +500,119 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
 #pragma unroll
       for (int k = 0; k < SW; k++) hc[s][k] = h[s][k];
     const bool more = i + 1 < ib;
+    const int lo = plo(i), hi = phi(i), hi1 = more ? phi(i + 1) : 0;  // the next item starts at piece 0
     if (more) load_hdr(i + 1);
     float acc[2] = {0.f, 0.f};
-
-    if constexpr (FMT == T_Q4_K) {
-      // header: d, dmin (f16) | scales[12] (get_scale_min_k4, quant.rs:216-226)
-      float d64[2], dmn[2];
-      uint32_t scl[2], sch[2], ml[2], mh[2];
-#pragma unroll
-      for (int s = 0; s < 2; s++) {
-        d64[s] = scale_f<QUIRK>(hc[s][0]) * kTwo64;
-        dmn[s] = scale_f<QUIRK>(hc[s][0] >> 16);
-        scl[s] = hc[s][1] & 0x3F3F3F3Fu;  // sc[0..3]
-        ml[s] = hc[s][2] & 0x3F3F3F3Fu;   // m[0..3]
-        sch[s] = (hc[s][3] & 0x0F0F0F0Fu) | ((hc[s][1] >> 2) & 0x30303030u);         // sc[4..7]
-        mh[s] = ((hc[s][3] >> 4) & 0x0F0F0F0Fu) | ((hc[s][2] >> 2) & 0x30303030u);  // m[4..7]
-      }
-      float aS[2] = {0.f, 0.f}, aM[2] = {0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        float2 lo[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)}, hi[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const float* xb = xc + 64 * c + 8 * j;
-          const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 32), xh1 = lds4(xb + 36);
-#pragma unroll
-          for (int s = 0; s < 2; s++) q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, lo[s], hi[s]);
-        }
-        if (more) load_piece(i + 1, c);
-        const float xsl = xsc[2 * c], xsh = xsc[2 * c + 1];
+    // FULL: every piece of this item and of the next is the warp's (the hot
+    // path, without per-piece conditions); otherwise the first or last item.
+    auto decode = [&](auto full_tag) {
+      constexpr bool FULL = decltype(full_tag)::value;
+      if constexpr (FMT == T_Q4_K) {
+        // header: d, dmin (f16) | scales[12] (get_scale_min_k4, quant.rs:216-226)
+        float d64[2], dmn[2];
+        uint32_t scl[2], sch[2], ml[2], mh[2];
 #pragma unroll
         for (int s = 0; s < 2; s++) {
-          const uint32_t scw = c < 2 ? scl[s] : sch[s], mw = c < 2 ? ml[s] : mh[s];
-          const int kb = (2 * c) & 3;
-          aS[s] = fmaf(byte_f(scw, kb), lo[s].x + lo[s].y, aS[s]);
-          aS[s] = fmaf(byte_f(scw, kb + 1), hi[s].x + hi[s].y, aS[s]);
-          aM[s] = fmaf(byte_f(mw, kb), xsl, aM[s]);
-          aM[s] = fmaf(byte_f(mw, kb + 1), xsh, aM[s]);
+          d64[s] = scale_f<QUIRK>(hc[s][0]) * kTwo64;
+          dmn[s] = scale_f<QUIRK>(hc[s][0] >> 16);
+          scl[s] = hc[s][1] & 0x3F3F3F3Fu;  // sc[0..3]
+          ml[s] = hc[s][2] & 0x3F3F3F3Fu;   // m[0..3]
+          sch[s] = (hc[s][3] & 0x0F0F0F0Fu) | ((hc[s][1] >> 2) & 0x30303030u);         // sc[4..7]
+          mh[s] = ((hc[s][3] >> 4) & 0x0F0F0F0Fu) | ((hc[s][2] >> 2) & 0x30303030u);  // m[4..7]
         }
-      }
+        float aS[2] = {0.f, 0.f}, aM[2] = {0.f, 0.f};
 #pragma unroll
-      for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dmn[s] * aM[s];
-    } else if constexpr (FMT == T_Q4_0) {
+        for (int c = 0; c < NP; c++) {
+          const bool on = FULL || (c >= lo && c < hi);
+          float2 sl[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)}, sh[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
+          if (on) {
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        float2 sb[2][2];  // [row][block of the piece]: low and high nibbles of a block sum together
+            for (int j = 0; j < 4; j++) {
+              const float* xb = xc + 64 * c + 8 * j;
+              const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 32), xh1 = lds4(xb + 36);
 #pragma unroll
-        for (int s = 0; s < 2; s++)
+              for (int s = 0; s < 2; s++)
+                q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, sl[s], sh[s]);
+            }
+          }
+          if (FULL ? more : c < hi1) load_piece(i + 1, c);
+          if (on) {
+            const float xsl = xsc[2 * c], xsh = xsc[2 * c + 1];
 #pragma unroll
-          for (int b = 0; b < 2; b++) sb[s][b] = ff2(0.f, 0.f);
+            for (int s = 0; s < 2; s++) {
+              const uint32_t scw = c < 2 ? scl[s] : sch[s], mw = c < 2 ? ml[s] : mh[s];
+              const int kb = (2 * c) & 3;
+              aS[s] = fmaf(byte_f(scw, kb), sl[s].x + sl[s].y, aS[s]);
+              aS[s] = fmaf(byte_f(scw, kb + 1), sh[s].x + sh[s].y, aS[s]);
+              aM[s] = fmaf(byte_f(mw, kb), xsl, aM[s]);
+              aM[s] = fmaf(byte_f(mw, kb + 1), xsh, aM[s]);
+            }
+          }
+        }
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int b = j >> 1;
-          const float* xb = xc + 64 * c + 32 * b + 8 * (j & 1);
-          const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 16), xh1 = lds4(xb + 20);
+        for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dmn[s] * aM[s];
+      } else if constexpr (FMT == T_Q4_0) {
+#pragma unroll
+        for (int c = 0; c < NP; c++) {
+          const bool on = FULL || (c >= lo && c < hi);
+          float2 sb[2][2];  // [row][block of the piece]: low and high nibbles of a block sum together
 #pragma unroll
           for (int s = 0; s < 2; s++)
-            q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, sb[s][b], sb[s][b]);
-        }
-        if (more) load_piece(i + 1, c);
 #pragma unroll
-        for (int b = 0; b < 2; b++) {
-          const float xs8 = xsc[2 * c + b];
+            for (int b = 0; b < 2; b++) sb[s][b] = ff2(0.f, 0.f);
+          if (on) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const int b = j >> 1;
+              const float* xb = xc + 64 * c + 32 * b + 8 * (j & 1);
+              const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 16), xh1 = lds4(xb + 20);
+#pragma unroll
+              for (int s = 0; s < 2; s++)
+                q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, sb[s][b], sb[s][b]);
+            }
+          }
+          if (FULL ? more : c < hi1) load_piece(i + 1, c);
+          if (!on) continue;
+#pragma unroll
+          for (int b = 0; b < 2; b++) {
+            const float xs8 = xsc[2 * c + b];
+#pragma unroll
+            for (int s = 0; s < 2; s++) {
+              const float d = scale_f<QUIRK>(hc[s][c] >> (16 * b));
+              acc[s] = fmaf(d, fmaf(sb[s][b].x + sb[s][b].y, kTwo64, -xs8), acc[s]);
+            }
+          }
+        }
+      } else {  // Q8_0
+#pragma unroll
+        for (int c = 0; c < NP; c++) {
+          const bool on = FULL || (c >= lo && c < hi);
+          float2 sa[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
+          if (on) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const float* xb = xc + 32 * c + 8 * j;
+              const float4 x0 = lds4(xb), x1 = lds4(xb + 4);
+#pragma unroll
+              for (int s = 0; s < 2; s++) q8_pair(w[s][c][2 * j], w[s][c][2 * j + 1], x0, x1, sa[s]);
+            }
+          }
+          if (FULL ? more : c < hi1) load_piece(i + 1, c);
+          if (!on) continue;
+          const float xs128 = xsc[c];
 #pragma unroll
           for (int s = 0; s < 2; s++) {
-            const float d = scale_f<QUIRK>(hc[s][c] >> (16 * b));
-            acc[s] = fmaf(d, fmaf(sb[s][b].x + sb[s][b].y, kTwo64, -xs8), acc[s]);
+            const float d = scale_f<QUIRK>(hc[s][c >> 1] >> (16 * (c & 1)));
+            acc[s] = fmaf(d, fmaf(sa[s].x + sa[s].y, kTwo64, -xs128), acc[s]);
           }
         }
       }
-    } else {  // Q8_0
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        float2 sa[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const float* xb = xc + 32 * c + 8 * j;
-          const float4 x0 = lds4(xb), x1 = lds4(xb + 4);
-#pragma unroll
-          for (int s = 0; s < 2; s++) q8_pair(w[s][c][2 * j], w[s][c][2 * j + 1], x0, x1, sa[s]);
-        }
-        if (more) load_piece(i + 1, c);
-        const float xs128 = xsc[c];
-#pragma unroll
-        for (int s = 0; s < 2; s++) {
-          const float d = scale_f<QUIRK>(hc[s][c >> 1] >> (16 * (c & 1)));
-          acc[s] = fmaf(d, fmaf(sa[s].x + sa[s].y, kTwo64, -xs128), acc[s]);
-        }
-      }
-    }
+    };
+    if (lo == 0 && hi == NP && (!more || hi1 == NP)) decode(std::true_type{});
+    else decode(std::false_type{});
     acc0 += acc[0];
     acc1 += acc[1];
-    len++;
+    len += hi - lo;
     if (++kc == nk || !more) {
       flush(tile, len, acc0, acc1);
       acc0 = acc1 = 0.f;
@@ -512,6 +626,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
 
   // CTA-level merge.  Slots 2w, 2w+1 are in chunk order, so the parts of a tile
   // are consecutive non-empty slots; the warp holding the first one sums them.
+  if (epre) sepi[tid] = epf;
   __syncthreads();
   for (int i = 2 * warp; i < 2 * warp + 2; i++) {
     const int T = stile[i];
@@ -527,38 +642,37 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       s0 += sslot[k * 64 + lane];
       s1 += sslot[k * 64 + 32 + lane];
     }
-    const uint64_t t0 = (uint64_t)T * nk;
-    const uint64_t a = ca > t0 ? ca : t0, b = cb < t0 + nk ? cb : t0 + nk;  // this CTA's chunks of T
-    if (a == t0 && b == t0 + nk) {
-      emit((uint32_t)T, s0, s1);
+    const uint64_t t0 = (uint64_t)T * tp;  // first piece of tile T
+    const uint64_t a = cpa > t0 ? cpa : t0, b = cpb < t0 + tp ? cpb : t0 + tp;  // this CTA's pieces of T
+    if (a == t0 && b == t0 + tp) {
+      emit((uint32_t)T, s0, s1, true);
       continue;
     }
     // Across CTAs: publish this CTA's part; the CTA completing the tile sums the
-    // parts in chunk order (they start at chunk 0 and at every CTA boundary).
+    // parts in piece order (they start at piece 0 and at every CTA boundary).
     const uint32_t len_c = (uint32_t)(b - a);
     float* p = part + a * QT_ROWS;
     __stcg(p + lane, s0);
     __stcg(p + 32 + lane, s1);
-    __threadfence();
     __syncwarp();
     unsigned old = 0;
-    if (lane == 0) old = atomicAdd(cnt + T, len_c);
+    if (lane == 0) old = arrive_acq_rel(cnt + T, len_c);
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + len_c != nk) continue;
-    __threadfence();
+    if (old + len_c != tp) continue;
+    __syncwarp();  // lane 0's acquire before every lane's loads of the partials
     const uint64_t G = gridDim.x;
     float r0 = 0.f, r1 = 0.f;
-    for (uint32_t k = 0; k < nk;) {
+    for (uint32_t k = 0; k < tp;) {
       uint32_t ks[8];
       int m = 0;
 #pragma unroll
       for (int u = 0; u < 8; u++) {
-        if (k < nk) {
+        if (k < tp) {
           ks[u] = k;
           m = u + 1;
-          const uint64_t g = ((t0 + k + 1) * G + N - 1) / N;  // first CTA starting after item t0+k
-          const uint64_t nb = N * g / G;
-          k = nb - t0 < nk ? (uint32_t)(nb - t0) : nk;
+          const uint64_t g = muldiv_up(t0 + k + 1, G, P, narrow);  // first CTA starting after piece t0+k
+          const uint64_t nb = muldiv(P, g, G, narrow);               // and its first piece
+          k = nb - t0 < tp ? (uint32_t)(nb - t0) : tp;
         }
       }
       float a0[8], a1[8];
@@ -576,17 +690,19 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
         }
     }
     if (lane == 0) cnt[T] = 0;
-    emit((uint32_t)T, r0, r1);
+    emit((uint32_t)T, r0, r1, true);
   }
 }
 
 // Dynamic shared memory qgemv_body needs for W on a grid of `grid` CTAs.
 inline size_t qgemv_smem_bytes(const PackedMat& W, int grid) {
   const uint64_t CE = (uint64_t)chunk_elems(W.type);
-  const uint64_t N = (uint64_t)(W.Mp / QT_ROWS) * W.nk;
-  const uint64_t per_cta = (N + grid - 1) / grid;
-  const uint64_t nst = std::min<uint64_t>(W.nk, std::max<uint64_t>(1, per_cta));
-  return (size_t)(nst * CE + nst * (CE / 32) + QG_WARPS * 64 + QG_WARPS * 2 * 65 + 40) * sizeof(float);
+  // A CTA's pieces [cpa, cpb) number at most ceil(P/grid); the items they touch,
+  // floor(cpa/NP) .. ceil(cpb/NP), at most ceil(that/NP) + 1.
+  const uint64_t P = (uint64_t)(W.Mp / QT_ROWS) * W.nk * QT_PIECES;
+  const uint64_t per_cta = ((P + grid - 1) / grid + QT_PIECES - 1) / QT_PIECES + 1;
+  const uint64_t nst = std::min<uint64_t>(W.nk, per_cta);
+  return (size_t)(nst * CE + nst * (CE / 32) + QG_WARPS * 64 + QG_WARPS * 2 * 65 + 40 + EPI_ROWS) * sizeof(float);
 }
 
 }  // namespace rf

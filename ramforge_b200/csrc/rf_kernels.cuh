@@ -51,6 +51,7 @@ struct PackedMat {
 constexpr int QT_ROWS = 64;          // rows per tile
 constexpr int QT_CHUNK_BYTES = 128;  // quant bytes per row per chunk
 constexpr int QT_ITEM_BYTES = QT_ROWS * QT_CHUNK_BYTES;
+constexpr int QT_PIECES = 4;        // 32-byte pieces of a chunk row: the unit of the GEMV work split
 
 __host__ __device__ inline bool is_tiled(int type) { return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0; }
 __host__ __device__ inline int chunk_elems(int type) { return type == T_Q8_0 ? 128 : 256; }

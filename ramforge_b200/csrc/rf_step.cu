@@ -66,10 +66,13 @@ __device__ __forceinline__ void grid_barrier(unsigned* bar, unsigned* err, unsig
 // serves all four, which keeps the kernel's register allocation close to the
 // standalone GEMV's).
 struct EpiLayer {
+  static constexpr bool kPre = false;
   int kind;                 // 0: RoPE + K/V append, 1: residual add into out, 2: SwiGLU into out
   const RopeQKVArgs* rope;  // kind 0
   float* out;
-  __device__ void operator()(int row0, const float* v, int n) {
+  __device__ void pre_begin() {}
+  __device__ float pre_load(uint32_t) { return 0.f; }
+  __device__ void operator()(int row0, const float* v, int n, const float* = nullptr) {
     if (kind == 0) {
       rope_store(*rope, row0, v, n);
     } else if (kind == 1) {  // out = out + W.x  (model_executor.rs:213-215, 231-233)
@@ -90,7 +93,7 @@ __device__ __forceinline__ void attention_phase(const AttnArgs& aa, const StepAr
   // unit u runs on CTA u % grid first, so units spread over all SMs before any
   // SM takes a second one
   for (int u = gid * gridDim.x + blockIdx.x; u < units; u += gridDim.x * STEP_GROUPS)
-    attn_unit<DPL, G, __half>(aa, u / nsplit, u % nsplit, 0, gsm, gid);
+    attn_unit<DPL, G, __half, 8>(aa, u / nsplit, u % nsplit, 0, gsm, gid);  // 128 registers a thread
 }
 
 template <int FL, int FO, int DPL, int G>
