@@ -28,6 +28,29 @@ __device__ __forceinline__ void ldg128(const uint8_t* p, uint32_t (&w)[4]) {
 __device__ __forceinline__ void ldg64(const uint8_t* p, uint32_t (&w)[2]) {
   asm volatile("ld.global.nc.L1::no_allocate.v2.b32 {%0,%1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "l"(p));
 }
+// The same loads under a predicate (no branch): registers keep their values when
+// `on` is false, and nothing is read.
+__device__ __forceinline__ void ldg256_if(bool on, const uint8_t* p, uint32_t (&w)[8]) {
+  asm volatile(
+      "{ .reg .pred q; setp.ne.u32 q, %9, 0;\n"
+      "@q ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8]; }"
+      : "+r"(w[0]), "+r"(w[1]), "+r"(w[2]), "+r"(w[3]), "+r"(w[4]), "+r"(w[5]), "+r"(w[6]), "+r"(w[7])
+      : "l"(p), "r"((uint32_t)on));
+}
+__device__ __forceinline__ void ldg128_if(bool on, const uint8_t* p, uint32_t (&w)[4]) {
+  asm volatile(
+      "{ .reg .pred q; setp.ne.u32 q, %5, 0;\n"
+      "@q ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4]; }"
+      : "+r"(w[0]), "+r"(w[1]), "+r"(w[2]), "+r"(w[3])
+      : "l"(p), "r"((uint32_t)on));
+}
+__device__ __forceinline__ void ldg64_if(bool on, const uint8_t* p, uint32_t (&w)[2]) {
+  asm volatile(
+      "{ .reg .pred q; setp.ne.u32 q, %3, 0;\n"
+      "@q ld.global.nc.L1::no_allocate.v2.b32 {%0,%1}, [%2]; }"
+      : "+r"(w[0]), "+r"(w[1])
+      : "l"(p), "r"((uint32_t)on));
+}
 
 // f16 -> f32 as the reference decodes block scales and F16 tensors
 // (quant.rs:40-65, tensor.rs:1017-1041): IEEE for normal numbers, but a

@@ -30,7 +30,6 @@
 //    nothing waits on another warp or CTA.
 #pragma once
 #include <algorithm>
-#include <type_traits>
 
 #include "rf_device.cuh"
 
@@ -313,10 +312,10 @@ __device__ __forceinline__ unsigned arrive_acq_rel(unsigned* p, unsigned v) {
 }
 constexpr int EPI_ROWS = QG_THREADS;  // epilogue inputs prefetched per CTA (one per thread)
 
-// The quantized GEMV over every CTA of the grid.  `wait()` runs between the
-// first weight loads and the first read of x (the previous kernel's completion,
-// or a grid barrier of the persistent step kernel); x and the residual input are
-// read through L2, so they may come from earlier in the same kernel.
+// The quantized GEMV over every CTA of the grid.  `wait()` runs before the
+// first read of x (the previous kernel's completion, or a grid barrier of the
+// persistent step kernel); x and the residual input are read through L2, so
+// they may come from earlier in the same kernel.
 template <int FMT, bool QUIRK, class Epi, class Wait>
 __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __restrict__ x,
                                            const float* __restrict__ nw, float eps, float* __restrict__ part,
@@ -378,6 +377,25 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       ldg64(s + 32 * SB, h[1]);
     }
   };
+  // branch-free forms for the hot path (nothing is read when `on` is false)
+  auto load_piece_if = [&](bool on, uint64_t i, int c) {
+    const uint8_t* q = W.qs + i * QT_ITEM_BYTES + c * (QT_ROWS * 32) + lane * 32;
+    ldg256_if(on, q, w[0][c]);
+    ldg256_if(on, q + 32 * 32, w[1][c]);
+  };
+  auto load_hdr_if = [&](bool on, uint64_t i) {
+    const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
+    if constexpr (SW == 4) {
+      ldg128_if(on, s, h[0]);
+      ldg128_if(on, s + 32 * SB, h[1]);
+    } else {
+      ldg64_if(on, s, h[0]);
+      ldg64_if(on, s + 32 * SB, h[1]);
+    }
+  };
+
+  // The first item's weights, before wait(): with programmatic dependent launch
+  // they stream in while the previous kernel finishes.
   if (ia < ib) {
     load_hdr(ia);
     const int lo = plo(ia), hi = phi(ia);
@@ -501,115 +519,111 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       for (int k = 0; k < SW; k++) hc[s][k] = h[s][k];
     const bool more = i + 1 < ib;
     const int lo = plo(i), hi = phi(i), hi1 = more ? phi(i + 1) : 0;  // the next item starts at piece 0
-    if (more) load_hdr(i + 1);
+    load_hdr_if(more, i + 1);
     float acc[2] = {0.f, 0.f};
-    // FULL: every piece of this item and of the next is the warp's (the hot
-    // path, without per-piece conditions); otherwise the first or last item.
-    auto decode = [&](auto full_tag) {
-      constexpr bool FULL = decltype(full_tag)::value;
-      if constexpr (FMT == T_Q4_K) {
-        // header: d, dmin (f16) | scales[12] (get_scale_min_k4, quant.rs:216-226)
-        float d64[2], dmn[2];
-        uint32_t scl[2], sch[2], ml[2], mh[2];
+    // Pieces outside [lo, hi) (first and last item of the warp's range) are skipped
+    // with warp-uniform conditions; one copy of the code serves every item, which
+    // measured faster than a separate unconditional copy for whole items.
+    if constexpr (FMT == T_Q4_K) {
+      // header: d, dmin (f16) | scales[12] (get_scale_min_k4, quant.rs:216-226)
+      float d64[2], dmn[2];
+      uint32_t scl[2], sch[2], ml[2], mh[2];
 #pragma unroll
-        for (int s = 0; s < 2; s++) {
-          d64[s] = scale_f<QUIRK>(hc[s][0]) * kTwo64;
-          dmn[s] = scale_f<QUIRK>(hc[s][0] >> 16);
-          scl[s] = hc[s][1] & 0x3F3F3F3Fu;  // sc[0..3]
-          ml[s] = hc[s][2] & 0x3F3F3F3Fu;   // m[0..3]
-          sch[s] = (hc[s][3] & 0x0F0F0F0Fu) | ((hc[s][1] >> 2) & 0x30303030u);         // sc[4..7]
-          mh[s] = ((hc[s][3] >> 4) & 0x0F0F0F0Fu) | ((hc[s][2] >> 2) & 0x30303030u);  // m[4..7]
-        }
-        float aS[2] = {0.f, 0.f}, aM[2] = {0.f, 0.f};
+      for (int s = 0; s < 2; s++) {
+        d64[s] = scale_f<QUIRK>(hc[s][0]) * kTwo64;
+        dmn[s] = scale_f<QUIRK>(hc[s][0] >> 16);
+        scl[s] = hc[s][1] & 0x3F3F3F3Fu;  // sc[0..3]
+        ml[s] = hc[s][2] & 0x3F3F3F3Fu;   // m[0..3]
+        sch[s] = (hc[s][3] & 0x0F0F0F0Fu) | ((hc[s][1] >> 2) & 0x30303030u);         // sc[4..7]
+        mh[s] = ((hc[s][3] >> 4) & 0x0F0F0F0Fu) | ((hc[s][2] >> 2) & 0x30303030u);  // m[4..7]
+      }
+      float aS[2] = {0.f, 0.f}, aM[2] = {0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < NP; c++) {
-          const bool on = FULL || (c >= lo && c < hi);
-          float2 sl[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)}, sh[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
-          if (on) {
+      for (int c = 0; c < NP; c++) {
+        const bool on = c >= lo && c < hi;
+        float2 sl[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)}, sh[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
+        if (on) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-              const float* xb = xc + 64 * c + 8 * j;
-              const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 32), xh1 = lds4(xb + 36);
+          for (int j = 0; j < 4; j++) {
+            const float* xb = xc + 64 * c + 8 * j;
+            const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 32), xh1 = lds4(xb + 36);
 #pragma unroll
-              for (int s = 0; s < 2; s++)
-                q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, sl[s], sh[s]);
-            }
-          }
-          if (FULL ? more : c < hi1) load_piece(i + 1, c);
-          if (on) {
-            const float xsl = xsc[2 * c], xsh = xsc[2 * c + 1];
-#pragma unroll
-            for (int s = 0; s < 2; s++) {
-              const uint32_t scw = c < 2 ? scl[s] : sch[s], mw = c < 2 ? ml[s] : mh[s];
-              const int kb = (2 * c) & 3;
-              aS[s] = fmaf(byte_f(scw, kb), sl[s].x + sl[s].y, aS[s]);
-              aS[s] = fmaf(byte_f(scw, kb + 1), sh[s].x + sh[s].y, aS[s]);
-              aM[s] = fmaf(byte_f(mw, kb), xsl, aM[s]);
-              aM[s] = fmaf(byte_f(mw, kb + 1), xsh, aM[s]);
-            }
+            for (int s = 0; s < 2; s++)
+              q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, sl[s], sh[s]);
           }
         }
-#pragma unroll
-        for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dmn[s] * aM[s];
-      } else if constexpr (FMT == T_Q4_0) {
-#pragma unroll
-        for (int c = 0; c < NP; c++) {
-          const bool on = FULL || (c >= lo && c < hi);
-          float2 sb[2][2];  // [row][block of the piece]: low and high nibbles of a block sum together
-#pragma unroll
-          for (int s = 0; s < 2; s++)
-#pragma unroll
-            for (int b = 0; b < 2; b++) sb[s][b] = ff2(0.f, 0.f);
-          if (on) {
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-              const int b = j >> 1;
-              const float* xb = xc + 64 * c + 32 * b + 8 * (j & 1);
-              const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 16), xh1 = lds4(xb + 20);
-#pragma unroll
-              for (int s = 0; s < 2; s++)
-                q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, sb[s][b], sb[s][b]);
-            }
-          }
-          if (FULL ? more : c < hi1) load_piece(i + 1, c);
-          if (!on) continue;
-#pragma unroll
-          for (int b = 0; b < 2; b++) {
-            const float xs8 = xsc[2 * c + b];
-#pragma unroll
-            for (int s = 0; s < 2; s++) {
-              const float d = scale_f<QUIRK>(hc[s][c] >> (16 * b));
-              acc[s] = fmaf(d, fmaf(sb[s][b].x + sb[s][b].y, kTwo64, -xs8), acc[s]);
-            }
-          }
-        }
-      } else {  // Q8_0
-#pragma unroll
-        for (int c = 0; c < NP; c++) {
-          const bool on = FULL || (c >= lo && c < hi);
-          float2 sa[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
-          if (on) {
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-              const float* xb = xc + 32 * c + 8 * j;
-              const float4 x0 = lds4(xb), x1 = lds4(xb + 4);
-#pragma unroll
-              for (int s = 0; s < 2; s++) q8_pair(w[s][c][2 * j], w[s][c][2 * j + 1], x0, x1, sa[s]);
-            }
-          }
-          if (FULL ? more : c < hi1) load_piece(i + 1, c);
-          if (!on) continue;
-          const float xs128 = xsc[c];
+        load_piece_if(c < hi1, i + 1, c);
+        if (on) {
+          const float xsl = xsc[2 * c], xsh = xsc[2 * c + 1];
 #pragma unroll
           for (int s = 0; s < 2; s++) {
-            const float d = scale_f<QUIRK>(hc[s][c >> 1] >> (16 * (c & 1)));
-            acc[s] = fmaf(d, fmaf(sa[s].x + sa[s].y, kTwo64, -xs128), acc[s]);
+            const uint32_t scw = c < 2 ? scl[s] : sch[s], mw = c < 2 ? ml[s] : mh[s];
+            const int kb = (2 * c) & 3;
+            aS[s] = fmaf(byte_f(scw, kb), sl[s].x + sl[s].y, aS[s]);
+            aS[s] = fmaf(byte_f(scw, kb + 1), sh[s].x + sh[s].y, aS[s]);
+            aM[s] = fmaf(byte_f(mw, kb), xsl, aM[s]);
+            aM[s] = fmaf(byte_f(mw, kb + 1), xsh, aM[s]);
           }
         }
       }
-    };
-    if (lo == 0 && hi == NP && (!more || hi1 == NP)) decode(std::true_type{});
-    else decode(std::false_type{});
+#pragma unroll
+      for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dmn[s] * aM[s];
+    } else if constexpr (FMT == T_Q4_0) {
+#pragma unroll
+      for (int c = 0; c < NP; c++) {
+        const bool on = c >= lo && c < hi;
+        float2 sb[2][2];  // [row][block of the piece]: low and high nibbles of a block sum together
+#pragma unroll
+        for (int s = 0; s < 2; s++)
+#pragma unroll
+          for (int b = 0; b < 2; b++) sb[s][b] = ff2(0.f, 0.f);
+        if (on) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int b = j >> 1;
+            const float* xb = xc + 64 * c + 32 * b + 8 * (j & 1);
+            const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 16), xh1 = lds4(xb + 20);
+#pragma unroll
+            for (int s = 0; s < 2; s++)
+              q4_pair(w[s][c][2 * j], w[s][c][2 * j + 1], xl0, xl1, xh0, xh1, sb[s][b], sb[s][b]);
+          }
+        }
+        load_piece_if(c < hi1, i + 1, c);
+        if (!on) continue;
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+          const float xs8 = xsc[2 * c + b];
+#pragma unroll
+          for (int s = 0; s < 2; s++) {
+            const float d = scale_f<QUIRK>(hc[s][c] >> (16 * b));
+            acc[s] = fmaf(d, fmaf(sb[s][b].x + sb[s][b].y, kTwo64, -xs8), acc[s]);
+          }
+        }
+      }
+    } else {  // Q8_0
+#pragma unroll
+      for (int c = 0; c < NP; c++) {
+        const bool on = c >= lo && c < hi;
+        float2 sa[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
+        if (on) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const float* xb = xc + 32 * c + 8 * j;
+            const float4 x0 = lds4(xb), x1 = lds4(xb + 4);
+#pragma unroll
+            for (int s = 0; s < 2; s++) q8_pair(w[s][c][2 * j], w[s][c][2 * j + 1], x0, x1, sa[s]);
+          }
+        }
+        load_piece_if(c < hi1, i + 1, c);
+        if (!on) continue;
+        const float xs128 = xsc[c];
+#pragma unroll
+        for (int s = 0; s < 2; s++) {
+          const float d = scale_f<QUIRK>(hc[s][c >> 1] >> (16 * (c & 1)));
+          acc[s] = fmaf(d, fmaf(sa[s].x + sa[s].y, kTwo64, -xs128), acc[s]);
+        }
+      }
+    }
     acc0 += acc[0];
     acc1 += acc[1];
     len += hi - lo;
