@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define RF_ABI_VERSION 1
+#define RF_ABI_VERSION 2
 
 /* status codes */
 #define RF_OK 0
@@ -75,7 +75,8 @@ typedef struct rf_runtime_config {
   const uint8_t* nccl_id;     /* 128-byte id from rf_tp_unique_id (tp_size > 1) */
   uint32_t max_seq_len;       /* KV capacity in positions; 0 = context_length */
   uint64_t vram_budget_bytes; /* byte budget for everything the engine allocates; 0 = device free memory */
-  int ring_slots;             /* out-of-core VRAM ring depth; 0 = all layers resident */
+  int ring_slots;             /* out-of-core VRAM ring depth; 0 = all layers resident (non-resident
+                                 layers then load and release synchronously each step) */
   int kv_f32;                 /* 1 = f32 KV cache (reference format); 0 = f16 (default) */
   int disable_graphs;         /* 1 = launch kernels eagerly instead of replaying a CUDA graph */
 } rf_runtime_config;
@@ -93,6 +94,8 @@ typedef struct rf_tensor_view {
 typedef struct rf_residency_stats {
   uint64_t layer_loads, layer_releases, cache_hits, cache_misses, evictions;
   uint64_t peak_bytes, h2d_bytes;
+  uint64_t ring_copies;      /* layer images copied into ring slots */
+  uint64_t host_image_bytes; /* pinned host images of streamed layers (not charged to the VRAM budget) */
 } rf_residency_stats;
 
 /* One rank's slice of a tensor-parallel engine: Q/K/V and gate/up are split by
@@ -216,7 +219,14 @@ int rf_budget_total(const rf_engine* e, uint64_t* out);
 int rf_budget_used(const rf_engine* e, uint64_t* out);
 int rf_budget_available(const rf_engine* e, uint64_t* out);
 /* Choose which layers stay resident (mask[i] != 0) and the ring depth used for the
- * others; vram_weight_budget_bytes caps resident layer weights plus ring slots. */
+ * others; vram_weight_budget_bytes caps resident layer weights plus ring slots.
+ * With ring_slots > 0 (and a GGUF source) every step streams the non-resident
+ * layers: each is packed once into pinned host memory, then copied with
+ * cudaMemcpyAsync on a side stream into one of ring_slots device slots
+ * ("ring:slot:<i>" budget charges), overlapping the compute of the layers before
+ * it (StagingPlan's transfer/compute overlap, staging_plan.rs:46-77, which the
+ * reference leaves unsupported).  With ring_slots == 0 they load, compute and
+ * release in turn (load_layer/release_layer, streaming_model.rs:1081-1270). */
 int rf_set_residency_plan(rf_engine* e, const uint8_t* resident_mask, int ring_slots,
                           uint64_t vram_weight_budget_bytes);
 int rf_residency_stats_get(const rf_engine* e, rf_residency_stats* out);

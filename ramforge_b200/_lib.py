@@ -71,7 +71,8 @@ class TpShard(ctypes.Structure):
 
 class ResidencyStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("layer_loads", "layer_releases", "cache_hits", "cache_misses",
-                                               "evictions", "peak_bytes", "h2d_bytes")]
+                                               "evictions", "peak_bytes", "h2d_bytes", "ring_copies",
+                                               "host_image_bytes")]
 
 
 _lib = None

@@ -78,6 +78,21 @@ struct Layer {
   float* ffn_norm = nullptr;
 };
 
+// A layer's weights as one contiguous device image (packed Q/K/V, W_o, gate/up,
+// down, then the two norms; each part 256-byte aligned).  `tmpl` holds the
+// matrices' geometry with pointers as offsets from the image base, so the same
+// image can live in the layer's own allocation or in any ring slot.
+struct LayerImage {
+  std::vector<uint8_t> bytes;
+  Layer tmpl;
+};
+// A streamed layer's image in pinned host memory (the source of its ring copies).
+struct StreamImage {
+  uint8_t* host = nullptr;
+  uint64_t bytes = 0;
+  Layer tmpl;
+};
+
 struct StepIO {  // device words read by the step kernels
   uint32_t token;
   int pos;
@@ -120,6 +135,13 @@ struct rf_engine {
         *attn_part = nullptr;
   unsigned* attn_counters = nullptr;
   GemvScratch gws{};  // split-K partials + tile counters of the quantized GEMV
+  // out-of-core ring: pinned host images of streamed layers, device slots fed by
+  // a copy stream, and the events ordering copies against the layers' kernels
+  std::vector<StreamImage> simg;
+  cudaStream_t copy_stream = nullptr;
+  std::vector<void*> ring;
+  uint64_t ring_slot_bytes = 0;
+  std::vector<cudaEvent_t> ring_free, ring_ready;
   StepIO* d_io = nullptr;
   uint32_t* d_hist = nullptr;  // token produced at each position (device-side greedy history)
   unsigned long long* d_key = nullptr;
@@ -166,6 +188,14 @@ void dev_free(rf_engine* e, const std::string& charge, void** p) {
     *p = nullptr;
     e->budget.release(charge);
   }
+}
+
+// Host -> device copy ordered on the engine stream and finished on return (the
+// engine stream is non-blocking, so a legacy-stream copy would not order against
+// its kernels, and a copy from pageable memory may return before its DMA ends).
+cudaError_t h2d_sync(rf_engine* e, void* dst, const void* src, uint64_t bytes) {
+  cudaError_t ce = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, e->stream);
+  return ce == cudaSuccess ? cudaStreamSynchronize(e->stream) : ce;
 }
 
 void drop_graphs(rf_engine* e) {
@@ -270,6 +300,7 @@ int engine_init_device(rf_engine* e) {
   e->budget = Budget(e->rt.vram_budget_bytes ? e->rt.vram_budget_bytes : (uint64_t)free_b);
   e->layers.assign(c.n_layers, Layer{});
   e->plan_resident.assign(c.n_layers, 1);
+  e->simg.assign(c.n_layers, StreamImage{});
   // KV cache: per layer K and V, [kv_head_local][max_seq][head_dim]
   const uint64_t esz = e->rt.kv_f32 ? 4 : 2;
   const uint64_t per = align256((uint64_t)e->kvh_local * e->max_seq * c.head_dim * esz);
@@ -318,14 +349,17 @@ int engine_init_device(rf_engine* e) {
   uint64_t total = 0;
   for (auto& it : items) total += align256(it.bytes);
   RF_TRY(dev_alloc(e, "scratch:activations", total, &e->scratch));
-  RF_CUDA(cudaMemset(e->scratch, 0, total));
+  // zeroed on the engine stream: a legacy-stream memset is not ordered against
+  // the engine stream's copies and kernels
+  RF_CUDA(cudaMemsetAsync(e->scratch, 0, total, e->stream));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
   uint64_t off = 0;
   for (auto& it : items) {
     *it.p = (uint8_t*)e->scratch + off;
     off += align256(it.bytes);
   }
   auto tab = rope_table(e->max_seq, c.head_dim, c.rope_theta);
-  RF_CUDA(cudaMemcpy(e->rope_cs, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  RF_CUDA(h2d_sync(e, e->rope_cs, tab.data(), tab.size() * sizeof(float2)));
   // one pinned {token, pos} slot per position: asynchronous steps never share a source slot
   RF_CUDA(cudaMallocHost((void**)&e->h_io, sizeof(StepIO) * (e->max_seq + 1)));
   RF_CUDA(cudaMallocHost((void**)&e->h_tok, 4 * 4096));
@@ -400,21 +434,39 @@ std::vector<int> rope_pair_rows(uint32_t h0, uint32_t nh, uint32_t hd) {
   return r;
 }
 
-// Device image of a packed matrix: qs | sc (each 256-byte aligned).
-int upload_packed(const HostPacked& hp, uint8_t* base, uint64_t* off, PackedMat* dst) {
+// Place a packed matrix in a layer image at *off: qs | sc (each 256-byte aligned).
+void image_put(const HostPacked& hp, std::vector<uint8_t>* img, uint64_t* off, PackedMat* dst) {
   *dst = hp.geo;
-  dst->qs = base + *off;
-  RF_CUDA(cudaMemcpy(dst->qs, hp.qs.data(), hp.qs.size(), cudaMemcpyHostToDevice));
+  dst->qs = reinterpret_cast<uint8_t*>(*off);
+  memcpy(img->data() + *off, hp.qs.data(), hp.qs.size());
   *off += align256(hp.qs.size());
-  dst->sc = base + *off;
-  if (!hp.sc.empty()) RF_CUDA(cudaMemcpy(dst->sc, hp.sc.data(), hp.sc.size(), cudaMemcpyHostToDevice));
+  dst->sc = reinterpret_cast<uint8_t*>(*off);
+  if (!hp.sc.empty()) memcpy(img->data() + *off, hp.sc.data(), hp.sc.size());
   *off += align256(hp.sc.size() ? hp.sc.size() : 16);
   dst->sub_scales = has_subnormal_scales(hp.geo, hp.sc.data()) ? 1 : 0;
-  return RF_OK;
 }
 uint64_t packed_bytes(const HostPacked& hp) { return align256(hp.qs.size()) + align256(hp.sc.size() ? hp.sc.size() : 16); }
 
-int load_layer_views(rf_engine* e, int l, const View* v /*[9]*/) {
+// Image pointers (offsets) -> addresses inside the image at `base`.
+void bind_layer(Layer* L, const Layer& tmpl, uint8_t* base) {
+  auto rebase = [base](PackedMat m) {
+    m.qs = base + reinterpret_cast<uintptr_t>(m.qs);
+    m.sc = base + reinterpret_cast<uintptr_t>(m.sc);
+    return m;
+  };
+  L->qkv = rebase(tmpl.qkv);
+  L->wo = rebase(tmpl.wo);
+  L->gateup = rebase(tmpl.gateup);
+  L->down = rebase(tmpl.down);
+  L->attn_norm = reinterpret_cast<float*>(base + reinterpret_cast<uintptr_t>(tmpl.attn_norm));
+  L->ffn_norm = reinterpret_cast<float*>(base + reinterpret_cast<uintptr_t>(tmpl.ffn_norm));
+  L->bytes = tmpl.bytes;
+}
+
+// load_layer's packing (streaming_model.rs:581-847) into a host image: this
+// rank's rows of Q/K/V (RoPE pairs adjacent), W_o, interleaved gate/up and
+// down, in the tiled layout, plus the norms as f32.
+int build_layer_image(rf_engine* e, int l, const View* v /*[9]*/, LayerImage* out) {
   const rf_model_config& c = e->cfg;
   const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
   RF_TRY(check_view(v[0], "attn_norm", c.n_embd, 1));
@@ -450,31 +502,40 @@ int load_layer_views(rf_engine* e, int l, const View* v /*[9]*/) {
   RF_TRY(norm_to_f32(v[5], c.n_embd, &fn));
   const uint64_t total = packed_bytes(qkv) + packed_bytes(wo) + packed_bytes(gu) + packed_bytes(dn) +
                          2 * align256(4ull * c.n_embd);
+  out->bytes.assign(total, 0);
+  Layer& t = out->tmpl;
+  t = Layer{};
+  uint64_t off = 0;
+  image_put(qkv, &out->bytes, &off, &t.qkv);
+  image_put(wo, &out->bytes, &off, &t.wo);
+  image_put(gu, &out->bytes, &off, &t.gateup);
+  image_put(dn, &out->bytes, &off, &t.down);
+  t.attn_norm = reinterpret_cast<float*>(off);
+  memcpy(out->bytes.data() + off, an.data(), 4ull * c.n_embd);
+  off += align256(4ull * c.n_embd);
+  t.ffn_norm = reinterpret_cast<float*>(off);
+  memcpy(out->bytes.data() + off, fn.data(), 4ull * c.n_embd);
+  t.bytes = total;
+  return RF_OK;
+}
+
+int load_layer_views(rf_engine* e, int l, const View* v /*[9]*/) {
+  LayerImage img;
+  RF_TRY(build_layer_image(e, l, v, &img));
   Layer& L = e->layers[l];
   const std::string charge = "layer:" + std::to_string(l) + ":weights";
-  RF_TRY(dev_alloc(e, charge, total, &L.block));
-  uint8_t* base = (uint8_t*)L.block;
-  uint64_t off = 0;
-  int rc = upload_packed(qkv, base, &off, &L.qkv);
-  if (!rc) rc = upload_packed(wo, base, &off, &L.wo);
-  if (!rc) rc = upload_packed(gu, base, &off, &L.gateup);
-  if (!rc) rc = upload_packed(dn, base, &off, &L.down);
-  if (!rc) {
-    L.attn_norm = (float*)(base + off);
-    off += align256(4ull * c.n_embd);
-    L.ffn_norm = (float*)(base + off);
-    cudaError_t ce = cudaMemcpy(L.attn_norm, an.data(), 4ull * c.n_embd, cudaMemcpyHostToDevice);
-    if (ce == cudaSuccess) ce = cudaMemcpy(L.ffn_norm, fn.data(), 4ull * c.n_embd, cudaMemcpyHostToDevice);
-    if (ce != cudaSuccess) rc = set_error(RF_ECUDA, "norm upload failed: %s", cudaGetErrorString(ce));
-  }
-  if (rc) {  // release_layer on every error path (streaming_model.rs:1170-1270)
+  RF_TRY(dev_alloc(e, charge, img.tmpl.bytes, &L.block));
+  cudaError_t ce = h2d_sync(e, L.block, img.bytes.data(), img.tmpl.bytes);
+  if (ce != cudaSuccess) {  // release_layer on every error path (streaming_model.rs:1170-1270)
     dev_free(e, charge, &L.block);
-    return rc;
+    return set_error(RF_ECUDA, "layer %d upload failed: %s", l, cudaGetErrorString(ce));
   }
-  L.bytes = total;
+  void* block = L.block;
+  bind_layer(&L, img.tmpl, (uint8_t*)block);
+  L.block = block;
   L.resident = true;
   e->stats.layer_loads++;
-  e->stats.h2d_bytes += total;
+  e->stats.h2d_bytes += img.tmpl.bytes;
   e->stats.peak_bytes = e->budget.peak();
   drop_graphs(e);
   return RF_OK;
@@ -504,7 +565,7 @@ int load_persistent(rf_engine* e, int role, const View& v) {
       RF_TRY(dev_alloc(e, "persistent:output_norm", 4ull * c.n_embd, &p));
       e->out_norm = (float*)p;
     }
-    RF_CUDA(cudaMemcpy(e->out_norm, w.data(), 4ull * c.n_embd, cudaMemcpyHostToDevice));
+    RF_CUDA(h2d_sync(e, e->out_norm, w.data(), 4ull * c.n_embd));
     e->have_onorm = true;
   } else if (role == RF_ROLE_TOKEN_EMBD || role == RF_ROLE_OUTPUT) {
     const bool is_embd = role == RF_ROLE_TOKEN_EMBD;
@@ -519,8 +580,13 @@ int load_persistent(rf_engine* e, int role, const View& v) {
     void** blk = is_embd ? &e->embd_block : &e->out_block;
     dev_free(e, charge, blk);
     RF_TRY(dev_alloc(e, charge, packed_bytes(hp), blk));
+    std::vector<uint8_t> img(packed_bytes(hp));
     uint64_t off = 0;
-    RF_TRY(upload_packed(hp, (uint8_t*)*blk, &off, is_embd ? &e->embd : &e->out));
+    PackedMat* dst = is_embd ? &e->embd : &e->out;
+    image_put(hp, &img, &off, dst);
+    RF_CUDA(h2d_sync(e, *blk, img.data(), img.size()));
+    dst->qs = (uint8_t*)*blk + reinterpret_cast<uintptr_t>(dst->qs);
+    dst->sc = (uint8_t*)*blk + reinterpret_cast<uintptr_t>(dst->sc);
     if (is_embd) e->have_embd = true;
     else { e->have_out = true; e->tied = false; }
     e->stats.h2d_bytes += packed_bytes(hp);
@@ -720,6 +786,122 @@ int run_stepwise(rf_engine* e, bool decode) {
   return RF_OK;
 }
 
+// ---- out-of-core ring ---------------------------------------------------------------
+// Layers the residency plan leaves out stream through `ring_slots` device slots:
+// their packed images are built once into pinned host memory, and each step
+// copies them with cudaMemcpyAsync on a side stream.  A slot's copy waits for the
+// kernels of the layer that used it before (ring_free), a layer's kernels wait
+// for its copy (ring_ready), and the copy of the layer `ring_slots` ahead is
+// issued as soon as a layer's kernels are queued, so transfers overlap the
+// compute of the layers in between.  The slots are charged to the byte budget
+// ("ring:slot:<i>"), the pinned images are host memory and are not.
+int ensure_stream_image(rf_engine* e, int l) {
+  StreamImage& si = e->simg[l];
+  if (si.host) return RF_OK;
+  if (!e->src) return set_error(RF_ESTATE, "layer %d is not resident and the engine has no GGUF source", l);
+  View v[9];
+  for (int j = 0; j < 9; j++) {
+    const std::string name = "blk." + std::to_string(l) + "." + kRoleNames[j] + ".weight";
+    const GgufTensor* t = e->gguf.find(name);
+    if (!t || !t->data) return set_error(RF_EFORMAT, "missing tensor '%s'", name.c_str());
+    v[j] = view_from_gguf(t);
+  }
+  LayerImage img;
+  RF_TRY(build_layer_image(e, l, v, &img));
+  RF_CUDA(cudaHostAlloc((void**)&si.host, img.tmpl.bytes, cudaHostAllocDefault));
+  memcpy(si.host, img.bytes.data(), img.tmpl.bytes);
+  si.bytes = img.tmpl.bytes;
+  si.tmpl = img.tmpl;
+  e->stats.host_image_bytes += si.bytes;
+  return RF_OK;
+}
+
+void free_ring(rf_engine* e) {
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  if (e->copy_stream) cudaStreamSynchronize(e->copy_stream);
+  for (size_t i = 0; i < e->ring.size(); i++) dev_free(e, "ring:slot:" + std::to_string(i), &e->ring[i]);
+  for (auto ev : e->ring_free) cudaEventDestroy(ev);
+  for (auto ev : e->ring_ready) cudaEventDestroy(ev);
+  e->ring.clear();
+  e->ring_free.clear();
+  e->ring_ready.clear();
+  e->ring_slot_bytes = 0;
+}
+
+int ensure_ring(rf_engine* e, uint64_t slot_bytes) {
+  const int R = e->rt.ring_slots;
+  if ((int)e->ring.size() == R && e->ring_slot_bytes >= slot_bytes) return RF_OK;
+  free_ring(e);
+  if (!e->copy_stream) RF_CUDA(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking));
+  e->ring.assign(R, nullptr);
+  e->ring_free.assign(R, nullptr);
+  e->ring_ready.assign(R, nullptr);
+  for (int i = 0; i < R; i++) {
+    int rc = dev_alloc(e, "ring:slot:" + std::to_string(i), slot_bytes, &e->ring[i]);
+    if (rc) {
+      free_ring(e);
+      return rc;
+    }
+    RF_CUDA(cudaEventCreateWithFlags(&e->ring_free[i], cudaEventDisableTiming));
+    RF_CUDA(cudaEventCreateWithFlags(&e->ring_ready[i], cudaEventDisableTiming));
+    RF_CUDA(cudaEventRecord(e->ring_free[i], e->stream));
+  }
+  e->ring_slot_bytes = slot_bytes;
+  return RF_OK;
+}
+
+// One step with the non-resident layers streamed through the ring.
+int run_ring(rf_engine* e, bool decode) {
+  const int R = e->rt.ring_slots;
+  std::vector<int> S;  // streamed layers, in order
+  uint64_t maxb = 0;
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++)
+    if (!e->layers[l].resident) {
+      RF_TRY(ensure_stream_image(e, (int)l));
+      S.push_back((int)l);
+      maxb = std::max(maxb, e->simg[l].bytes);
+    }
+  RF_TRY(ensure_ring(e, maxb));
+  auto issue = [&](size_t j) -> int {
+    const int slot = (int)(j % R);
+    const StreamImage& si = e->simg[S[j]];
+    RF_CUDA(cudaStreamWaitEvent(e->copy_stream, e->ring_free[slot], 0));
+    RF_CUDA(cudaMemcpyAsync(e->ring[slot], si.host, si.bytes, cudaMemcpyHostToDevice, e->copy_stream));
+    RF_CUDA(cudaEventRecord(e->ring_ready[slot], e->copy_stream));
+    e->stats.ring_copies++;
+    e->stats.h2d_bytes += si.bytes;
+    return RF_OK;
+  };
+  const Launch La{e->stream, false};
+  RF_CUDA(launch_embed(La, e->embd, &e->d_io->token, e->hidden, e->d_key));
+  for (size_t j = 0; j < S.size() && j < (size_t)R; j++) RF_TRY(issue(j));
+  size_t j = 0;
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
+    Layer& L = e->layers[l];
+    if (L.resident) {
+      e->stats.cache_hits++;
+      RF_TRY(enqueue_layer(e, (int)l, false));
+      continue;
+    }
+    e->stats.cache_misses++;
+    const int slot = (int)(j % R);
+    RF_CUDA(cudaStreamWaitEvent(e->stream, e->ring_ready[slot], 0));
+    bind_layer(&L, e->simg[l].tmpl, (uint8_t*)e->ring[slot]);  // the layer stays non-resident
+    const int rc = enqueue_layer(e, (int)l, false);
+    L = Layer{};
+    RF_TRY(rc);
+    RF_CUDA(cudaEventRecord(e->ring_free[slot], e->stream));
+    if (j + R < S.size()) RF_TRY(issue(j + R));
+    j++;
+  }
+  RF_CUDA(launch_rmsnorm(La, e->hidden, e->out_norm, e->cfg.rms_eps, e->cfg.n_embd, e->final_hidden));
+  if (decode) {
+    RF_TRY(enqueue_logits(e, false, false));
+    RF_CUDA(launch_finalize(La, e->d_key, &e->d_io->token, &e->d_io->pos, e->d_hist, (int)e->max_seq));
+  }
+  return RF_OK;
+}
+
 int capture(rf_engine* e, bool decode, cudaGraphExec_t* out) {
   cudaGraph_t g = nullptr;
   RF_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
@@ -802,8 +984,7 @@ int prepare_step_kernel(rf_engine* e) {
     S.rope = rope_args(e, (int)l);
     S.attn = attn_args(e, (int)l);
   }
-  RF_CUDA(cudaMemcpy(e->d_step_layers, e->h_step_layers.data(), sizeof(StepLayer) * c.n_layers,
-                     cudaMemcpyHostToDevice));
+  RF_CUDA(h2d_sync(e, e->d_step_layers, e->h_step_layers.data(), sizeof(StepLayer) * c.n_layers));
   e->step_smem = step_kernel_smem(step_args(e, true), e->h_step_layers[0]);
   return RF_OK;
 }
@@ -817,7 +998,8 @@ int check_step_kernel(rf_engine* e) {
   unsigned err = 0;
   RF_CUDA(cudaMemcpy(&err, e->d_err, sizeof err, cudaMemcpyDeviceToHost));
   if (err) {
-    RF_CUDA(cudaMemset(e->d_err, 0, sizeof err));
+    RF_CUDA(cudaMemsetAsync(e->d_err, 0, sizeof err, e->stream));
+    RF_CUDA(cudaStreamSynchronize(e->stream));
     return set_error(RF_ETIMEOUT, "a grid barrier of the step kernel timed out (error word 0x%x)", err);
   }
   return RF_OK;
@@ -825,7 +1007,7 @@ int check_step_kernel(rf_engine* e) {
 
 // Launch one token step (forward, or decode = forward + logits + advance).
 int launch_step(rf_engine* e, bool decode) {
-  if (!all_resident(e)) return run_stepwise(e, decode);
+  if (!all_resident(e)) return e->rt.ring_slots > 0 && e->src ? run_ring(e, decode) : run_stepwise(e, decode);
   if (step_kernel_active(e)) {
     RF_CUDA(launch_step_kernel(e->stream, step_args(e, decode), e->h_step_layers[0], e->step_smem));
     e->step_used = true;
@@ -936,6 +1118,14 @@ void destroy(rf_engine* e) {
   if (e->out_norm) cudaFree(e->out_norm);
   if (e->kv_block) cudaFree(e->kv_block);
   if (e->scratch) cudaFree(e->scratch);
+  if (e->copy_stream) cudaStreamSynchronize(e->copy_stream);
+  for (auto p : e->ring)
+    if (p) cudaFree(p);
+  for (auto ev : e->ring_free) cudaEventDestroy(ev);
+  for (auto ev : e->ring_ready) cudaEventDestroy(ev);
+  if (e->copy_stream) cudaStreamDestroy(e->copy_stream);
+  for (auto& si : e->simg)
+    if (si.host) cudaFreeHost(si.host);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->h_tok) cudaFreeHost(e->h_tok);
   if (e->h_key) cudaFreeHost(e->h_key);
@@ -1107,7 +1297,7 @@ int rf_embed(rf_engine* e, uint32_t token) {
 int rf_hidden_write(rf_engine* e, const float* host, uint32_t n) {
   ENGINE_GUARD(e);
   if (!host || n != e->cfg.n_embd) return set_error(RF_EINVAL, "hidden size mismatch: expected %u", e->cfg.n_embd);
-  RF_CUDA(cudaMemcpy(e->hidden, host, 4ull * n, cudaMemcpyHostToDevice));
+  RF_CUDA(h2d_sync(e, e->hidden, host, 4ull * n));
   return RF_OK;
 }
 
@@ -1224,7 +1414,7 @@ int rf_set_step_kernel(rf_engine* e, int enable) {
 int rf_step_profile(rf_engine* e, int enable) {
   ENGINE_GUARD(e);
   e->step_profile = enable != 0;
-  if (e->step_profile) RF_CUDA(cudaMemset(e->d_stamps, 0, 8ull * (5 * e->cfg.n_layers + 8)));
+  if (e->step_profile) RF_CUDA(cudaMemsetAsync(e->d_stamps, 0, 8ull * (5 * e->cfg.n_layers + 8), e->stream));
   return RF_OK;
 }
 
@@ -1330,16 +1520,38 @@ int rf_budget_available(const rf_engine* e, uint64_t* out) {
   return RF_OK;
 }
 
+// Bytes of one layer's device image (build_layer_image's layout) for this rank,
+// from the GGUF tensor types of layer 0 (every layer has the same shapes).
+uint64_t layer_image_bytes(rf_engine* e) {
+  const rf_model_config& c = e->cfg;
+  auto type_of = [&](const char* role) -> int {
+    const GgufTensor* t = e->gguf.find(std::string("blk.0.") + role + ".weight");
+    return t ? (int)t->type : -1;
+  };
+  auto mat = [](int type, uint32_t M, uint32_t K) -> uint64_t {
+    PackedMat g{};
+    if (type < 0 || !packed_geometry(type, M, K, &g)) return 0;
+    const uint64_t sc = packed_sc_bytes(g);
+    return align256(packed_qs_bytes(g)) + align256(sc ? sc : 16);
+  };
+  return mat(type_of("attn_q"), e->q_local + 2 * e->kv_local, c.n_embd) + mat(type_of("attn_output"), c.n_embd, e->q_local) +
+         mat(type_of("ffn_gate"), 2 * e->ff_local, c.n_embd) + mat(type_of("ffn_down"), c.n_embd, e->ff_local) +
+         2 * align256(4ull * c.n_embd);
+}
+
 int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uint64_t vram_weight_budget_bytes) {
   ENGINE_GUARD(e);
   if (!mask) return set_error(RF_EINVAL, "null residency mask");
   if (ring_slots < 0) return set_error(RF_EINVAL, "ring_slots must be >= 0");
-  uint64_t resident_bytes = 0;
-  for (uint32_t l = 0; l < e->cfg.n_layers; l++)
+  uint64_t resident_bytes = 0, slot_bytes = 0;
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
     if (mask[l] && e->layers[l].resident) resident_bytes += e->layers[l].bytes;
-  if (vram_weight_budget_bytes && resident_bytes > vram_weight_budget_bytes)
-    return set_error(RF_ENOMEM, "resident layers need %llu bytes, weight budget is %llu",
-                     (unsigned long long)resident_bytes, (unsigned long long)vram_weight_budget_bytes);
+    if (!mask[l]) slot_bytes = std::max(slot_bytes, layer_image_bytes(e));
+  }
+  const uint64_t need = resident_bytes + (uint64_t)ring_slots * slot_bytes;
+  if (vram_weight_budget_bytes && need > vram_weight_budget_bytes)
+    return set_error(RF_ENOMEM, "resident layers and %d ring slots need %llu bytes, weight budget is %llu", ring_slots,
+                     (unsigned long long)need, (unsigned long long)vram_weight_budget_bytes);
   RF_CUDA(cudaStreamSynchronize(e->stream));
   for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
     e->plan_resident[l] = mask[l] ? 1 : 0;
@@ -1348,6 +1560,7 @@ int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uin
       e->stats.evictions++;
     }
   }
+  if (ring_slots != e->rt.ring_slots) free_ring(e);
   e->rt.ring_slots = ring_slots;
   return RF_OK;
 }

@@ -84,6 +84,7 @@ int gemv_workspace(int dev, const PackedMat& W, GemvScratch* out) {
     w.n_cnt = 0;
     RF_CUDA(cudaMalloc(&w.cnt, nc * sizeof(unsigned)));
     RF_CUDA(cudaMemset(w.cnt, 0, nc * sizeof(unsigned)));
+    RF_CUDA(cudaDeviceSynchronize());  // zero before any caller stream (possibly non-blocking) uses them
     w.n_cnt = nc;
   }
   *out = GemvScratch{w.part, w.cnt, w.part_floats, w.n_cnt};
@@ -106,6 +107,7 @@ int workspace(int dev, size_t part_floats, size_t n_counters, AttnWorkspace** ou
     w.n_counters = 0;
     RF_CUDA(cudaMalloc(&w.counters, n_counters * sizeof(unsigned)));
     RF_CUDA(cudaMemset(w.counters, 0, n_counters * sizeof(unsigned)));
+    RF_CUDA(cudaDeviceSynchronize());  // zero before any caller stream (possibly non-blocking) uses them
     w.n_counters = n_counters;
   }
   *out = &w;
@@ -159,6 +161,9 @@ int rf_matrix_create(int type, const void* bytes, uint64_t nbytes, int on_device
     }
     ce = cudaMemcpy(m->m.qs, hp.qs.data(), hp.qs.size(), cudaMemcpyHostToDevice);
     if (ce == cudaSuccess && !hp.sc.empty()) ce = cudaMemcpy(m->m.sc, hp.sc.data(), hp.sc.size(), cudaMemcpyHostToDevice);
+    // a copy from pageable memory may return before its DMA ends: finish it
+    // before the caller's streams (possibly non-blocking) read the matrix
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
     m->m.sub_scales = has_subnormal_scales(hp.geo, hp.sc.data()) ? 1 : 0;
   }
   if (ce != cudaSuccess) {
