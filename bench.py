@@ -130,6 +130,13 @@ class ClockSampler:
                 "source": "nvml, 5 ms period, during the timed region"}
 
 
+# DRAM bytes of one gate/up launch at TP1, from an ncu capture (dram__bytes_read.sum
+# 66,170,624 + dram__bytes_write.sum 577,024) of
+#   ncu --set full --clock-control none -k regex:EpiSwiGLU ... python bench.py --profile --layers 2
+# A rank of a TP-N run holds 1/N of the rows, so its launch moves 1/N of it.
+GATEUP_DRAM_BYTES_NCU = 66_747_648
+
+
 def algorithmic_bytes(spec, tp: int, ctx: float):
     """Weight + activation bytes one decode token must move (per rank), per SURVEY 8(d):
     matrices M*K*b (b = GGUF bytes/element), KV f16 at context ctx, vectors 4 bytes/elem."""
@@ -239,6 +246,50 @@ def run_profile(args, spec):
     eng.close()
 
 
+def run_ring(args, spec):
+    """--ring N: out-of-core decode (the residency ring).  The last N
+    layers of the same model are left out of the residency plan and stream every
+    step from pinned host images through 2 device ring slots; the line reports
+    tokens/s against the bound the measured pinned host-to-device bandwidth sets
+    (N layer images per token)."""
+    import torch
+    from ramforge_b200 import DecodeEngine
+    torch.cuda.set_device(0)
+    h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    d = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    d.copy_(h, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        d.copy_(h, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    h2d_gbs = 5 * (1 << 30) / (e0.elapsed_time(e1) / 1e3) / 1e9
+    del h, d
+    n = max(1, min(args.ring, spec.n_layers))
+    eng = DecodeEngine(make_model(spec, 1, 0), device=0, max_seq_len=PROMPT_LEN + args.warmup + args.steps + 16)
+    eng.set_residency_plan([i < spec.n_layers - n for i in range(spec.n_layers)], ring_slots=2)
+    prompt = np.random.default_rng(3).integers(0, spec.vocab_size, 8).tolist()
+    first = int(eng.generate(prompt, 1)[0])
+    toks, _ = eng.decode_timed(first, args.warmup)
+    toks, dev_ms = eng.decode_timed(int(toks[-1]), args.steps)
+    st = eng.residency_stats()
+    layer_bytes = st["host_image_bytes"] / n
+    value = args.steps / (dev_ms / 1e3)
+    bound = h2d_gbs * 1e9 / (n * layer_bytes)
+    print(json.dumps({
+        "metric": "out-of-core decode tokens/s (Llama-3-8B Q4_K shape, streamed layers)", "value": value,
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "data": "synthetic",
+        "config": {"workload": f"{n} of {spec.n_layers} layers streamed through 2 ring slots per token",
+                   "layer_image_bytes": layer_bytes, "prompt_tokens": len(prompt)},
+        "roofline": {"bound": "h2d", "achieved": n * layer_bytes * value / 1e9, "peak": h2d_gbs, "unit": "GB/s",
+                     "frac": value / bound, "peak_source": "pinned host-to-device copy measured in this run"},
+        "residency_stats": st}))
+    eng.close()
+
+
 def workload_config(spec, args, tp):
     return {"workload": "llama-3-8b-shape Q4_K batch-1 greedy decode (BASELINE configs[3])",
             "layers": spec.n_layers, "dim": spec.n_embd, "heads": f"{spec.n_heads}q/{spec.n_kv_heads}kv",
@@ -257,6 +308,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="small eager run for ncu captures")
     ap.add_argument("--layers", type=int, default=0, help="with --profile: layer count of the model")
+    ap.add_argument("--ring", type=int, default=0, help="out-of-core run: stream this many layers per step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -270,6 +322,9 @@ def main():
         return
     if args.profile:
         run_profile(args, spec)
+        return
+    if args.ring:
+        run_ring(args, spec)
         return
 
     import torch
@@ -344,10 +399,12 @@ def main():
     step_bytes, gateup_bytes = algorithmic_bytes(spec, world, ctx_mean)
     peak, peak_kind = measured_peaks()
     achieved = gateup_bytes / (kms[3] / 1e3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "gemv_kernel<Q4_K, EpiSwiGLU> (ffn gate/up + SwiGLU)",
+    roofline = {"bound": "hbm", "kernel": "qgemv_kernel<Q4_K, EpiSwiGLU> (ffn gate/up + SwiGLU)",
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": gateup_bytes,
-                "ms_per_launch": kms[3], "traffic": None}
+                "ms_per_launch": kms[3], "traffic": GATEUP_DRAM_BYTES_NCU / world,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one TP1 launch "
+                                  "(bench.py --profile --layers 2), divided by the ranks"}
     step_gbs = step_bytes / (dev_ms / args.steps / 1e3) / 1e9
 
     line = {
