@@ -234,6 +234,11 @@ int rf_residency_stats_get(const rf_engine* e, rf_residency_stats* out);
 /* ---- tensor parallelism -------------------------------------------------------- */
 /* 128-byte NCCL unique id for rank 0 to distribute (ncclGetUniqueId). */
 int rf_tp_unique_id(uint8_t* out128);
+/* *out = 1 when the row-parallel projections' sums run over NVLink peer memory
+ * (one kernel each, cudaIpc-mapped receive areas), 0 when they use NCCL
+ * all-reduce (single GPU, a peer mapping unavailable, or RF_PEER_SUM=0).  No
+ * counterpart in the reference (CPU only). */
+int rf_tp_peer_sum(const rf_engine* e, int* out);
 
 /* ---- standalone ops on device pointers (benchmark configs 2 and 3) ---------------
  * A packed matrix is the device form of one GGUF weight (quantized_matvec_dispatch,

@@ -32,7 +32,7 @@ EXPORTS = [
     "rf_budget_used", "rf_budget_available", "rf_set_residency_plan", "rf_residency_stats_get",
     "rf_step_kernel_count", "rf_set_step_kernel", "rf_step_kernel_active", "rf_step_profile", "rf_step_phase_times",
     "rf_selftest_barrier", "rf_decode_timed",
-    "rf_bench_layer_kernels", "rf_tp_unique_id", "rf_matrix_create", "rf_matrix_destroy", "rf_matrix_device_bytes",
+    "rf_bench_layer_kernels", "rf_tp_unique_id", "rf_tp_peer_sum", "rf_matrix_create", "rf_matrix_destroy", "rf_matrix_device_bytes",
     "rf_qmatvec", "rf_decode_attention", "rf_decode_attention_noalloc",
 ]
 
@@ -120,6 +120,7 @@ def lib():
             "rf_set_residency_plan": (c_int, [vp, ctypes.POINTER(ctypes.c_uint8), c_int, c_u64]),
             "rf_residency_stats_get": (c_int, [vp, ctypes.POINTER(ResidencyStats)]),
             "rf_tp_unique_id": (c_int, [ctypes.POINTER(ctypes.c_uint8)]),
+            "rf_tp_peer_sum": (c_int, [vp, ctypes.POINTER(c_int)]),
             "rf_step_kernel_count": (c_int, [vp, u32p]),
             "rf_set_step_kernel": (c_int, [vp, c_int]),
             "rf_step_kernel_active": (c_int, [vp, ctypes.POINTER(c_int)]),

@@ -1,0 +1,102 @@
+// rf_allreduce.cu - the tensor-parallel sum over NVLink peer memory (PeerSum in
+// rf_kernels.cuh): one kernel per row-parallel projection in place of a library
+// all-reduce.
+#include "rf_device.cuh"
+
+namespace rf {
+
+namespace {
+constexpr unsigned kSpinFast = 1u << 12;   // polls before a wait starts to back off
+constexpr unsigned kSpinLimit = 1u << 24;  // then ~1 s of 64 ns sleeps before it gives up
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(PS_THREADS) peer_sum_kernel(PeerSum P, const float* __restrict__ partial,
+                                                              float* __restrict__ out, int n, int site) {
+  griddep_wait();
+  // The next kernel may start now: it waits for this one's completion before it
+  // reads the sum, and meanwhile its weight prefetch overlaps the exchange.
+  griddep_launch();
+  const int b = blockIdx.x, par = site & 1;
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(P.epoch + site) + 1;  // this call's generation
+  const int i0 = b * PS_ELEMS + threadIdx.x * 4;
+  const bool in = i0 < n;
+  // 1. this rank's slice into every rank's receive area (row `rank`)
+  if (in) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(partial + i0));
+    for (int p = 0; p < P.n_ranks; p++)
+      __stcg(reinterpret_cast<float4*>(P.recv[p] + ((size_t)par * P.n_ranks + P.rank) * P.n_max + i0), v);
+  }
+  __syncthreads();  // the CTA's peer stores, then the flags' release (system scope) orders them
+  // 2. flag slice b on every rank, then wait for every rank's flag of slice b here
+  if (threadIdx.x < P.n_ranks) {
+    const int p = threadIdx.x;
+    st_release_sys(P.flags[p] + ((size_t)P.rank * P.sites + site) * P.max_ctas + b, e);
+    const unsigned* f = P.flags[P.rank] + ((size_t)p * P.sites + site) * P.max_ctas + b;
+    unsigned it = 0;
+    while (ld_acquire_sys(f) != e) {
+      if (++it > kSpinLimit) {
+        atomicOr(P.err, 1u);
+        break;
+      }
+      if (it > kSpinFast) __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  // 3. the ranks' partials in rank order
+  if (in) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < P.n_ranks; p++) {
+      const float4 t = __ldcv(reinterpret_cast<const float4*>(P.recv[P.rank] + ((size_t)par * P.n_ranks + p) * P.n_max + i0));
+      s.x += t.x;
+      s.y += t.y;
+      s.z += t.z;
+      s.w += t.w;
+    }
+    *reinterpret_cast<float4*>(out + i0) = s;
+  }
+  // 4. the last CTA moves the call site to the next generation
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(P.done + site, 1u) == gridDim.x - 1) {
+    P.epoch[site] = e;
+    P.done[site] = 0u;
+  }
+}
+}  // namespace
+
+static size_t recv_bytes(int n_ranks, int n_max) { return ((size_t)2 * n_ranks * n_max * sizeof(float) + 255) & ~size_t(255); }
+static int max_ctas_of(int n_max) { return (n_max + PS_ELEMS - 1) / PS_ELEMS; }
+static size_t flag_words(int n_ranks, int n_max, int sites) { return (size_t)n_ranks * sites * max_ctas_of(n_max); }
+
+size_t peer_sum_area_bytes(int n_ranks, int n_max, int sites) {
+  return recv_bytes(n_ranks, n_max) + 4 * (flag_words(n_ranks, n_max, sites) + 2 * (size_t)sites + 1);
+}
+
+void peer_sum_bind(PeerSum* P, int p, void* area, bool own) {
+  uint8_t* a = static_cast<uint8_t*>(area);
+  P->recv[p] = reinterpret_cast<float*>(a);
+  P->flags[p] = reinterpret_cast<unsigned*>(a + recv_bytes(P->n_ranks, P->n_max));
+  P->max_ctas = max_ctas_of(P->n_max);
+  if (own) {
+    unsigned* w = P->flags[p] + flag_words(P->n_ranks, P->n_max, P->sites);
+    P->epoch = w;
+    P->done = w + P->sites;
+    P->err = w + 2 * P->sites;
+  }
+}
+
+cudaError_t launch_peer_sum(const Launch& L, const PeerSum& P, const float* partial, float* out, int n, int site) {
+  if (n <= 0 || n % 4 || n > P.n_max || site < 0 || site >= P.sites || P.n_ranks > RF_MAX_TP)
+    return cudaErrorInvalidValue;
+  return launch_k(L, peer_sum_kernel, dim3((n + PS_ELEMS - 1) / PS_ELEMS), dim3(PS_THREADS), 0, P, partial, out, n,
+                  site);
+}
+
+}  // namespace rf

@@ -166,6 +166,11 @@ struct rf_engine {
   unsigned long long* d_stamps = nullptr;  // barrier completion times of the last profiled step
   // NCCL
   ncclComm_t comm = nullptr;
+  // tensor-parallel sums over NVLink peer memory (PeerSum); NCCL when unavailable
+  PeerSum ps{};
+  bool ps_ok = false;
+  void* ps_area = nullptr;
+  std::vector<void*> ps_peer;  // peer areas mapped through cudaIpc
   rf_residency_stats stats{};
 };
 
@@ -291,6 +296,72 @@ int setup_geometry(rf_engine* e) {
   return RF_OK;
 }
 
+// Peer-memory tensor-parallel sums (PeerSum): every rank exports one area through
+// cudaIpc, the handles travel by an NCCL all-gather, and every rank maps the
+// others'.  The ranks agree (an NCCL min) before using it, so either all ranks
+// sum over peer memory or all use NCCL all-reduce.  RF_PEER_SUM=0 forces NCCL.
+int setup_peer_sum(rf_engine* e) {
+  e->ps_ok = false;
+  const char* env = getenv("RF_PEER_SUM");
+  bool ok = !(env && env[0] == '0') && e->tp <= RF_MAX_TP && e->cfg.n_embd % 4 == 0;
+  PeerSum& P = e->ps;
+  P = PeerSum{};
+  P.rank = e->rank;
+  P.n_ranks = e->tp;
+  P.n_max = (int)e->cfg.n_embd;
+  P.sites = 2 * (int)e->cfg.n_layers;
+  const size_t bytes = peer_sum_area_bytes(P.n_ranks, P.n_max, P.sites);
+  uint8_t* d_x = nullptr;  // [tp][64] handle bytes, then one int for the agreement
+  RF_CUDA(cudaMalloc(&d_x, 64ull * e->tp + 64));
+  std::vector<cudaIpcMemHandle_t> h(e->tp);
+  memset(h.data(), 0, sizeof(cudaIpcMemHandle_t) * h.size());
+  if (ok && dev_alloc(e, "scratch:peer_sum", bytes, &e->ps_area) != RF_OK) ok = false;
+  if (ok)
+    ok = cudaMemsetAsync(e->ps_area, 0, bytes, e->stream) == cudaSuccess &&
+         cudaStreamSynchronize(e->stream) == cudaSuccess && cudaIpcGetMemHandle(&h[e->rank], e->ps_area) == cudaSuccess;
+  cudaGetLastError();
+  int rc = RF_OK;
+  cudaError_t ce = h2d_sync(e, d_x + 64ull * e->rank, &h[e->rank], sizeof(cudaIpcMemHandle_t));
+  if (ce == cudaSuccess) {
+    const ncclResult_t r = nccl()->allGather(d_x + 64ull * e->rank, d_x, 64, ncclUint8, e->comm, e->stream);
+    if (r != ncclSuccess) rc = set_error(RF_ENCCL, "peer-sum handle exchange failed: %s", nccl()->errStr(r));
+  }
+  if (!rc && ce == cudaSuccess) ce = cudaMemcpyAsync(h.data(), d_x, 64ull * e->tp, cudaMemcpyDeviceToHost, e->stream);
+  if (!rc && ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
+  e->ps_peer.assign(e->tp, nullptr);
+  for (int p = 0; !rc && ce == cudaSuccess && ok && p < e->tp; p++) {
+    if (p == e->rank) continue;
+    if (cudaIpcOpenMemHandle(&e->ps_peer[p], h[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      e->ps_peer[p] = nullptr;
+      ok = false;
+    }
+  }
+  // agreement: the minimum over ranks of ok
+  int flag = ok ? 1 : 0;
+  if (!rc && ce == cudaSuccess) ce = h2d_sync(e, d_x + 64ull * e->tp, &flag, sizeof flag);
+  if (!rc && ce == cudaSuccess) {
+    const ncclResult_t r =
+        nccl()->allReduce(d_x + 64ull * e->tp, d_x + 64ull * e->tp, 1, ncclInt32, ncclMin, e->comm, e->stream);
+    if (r != ncclSuccess) rc = set_error(RF_ENCCL, "peer-sum agreement failed: %s", nccl()->errStr(r));
+  }
+  if (!rc && ce == cudaSuccess)
+    ce = cudaMemcpyAsync(&flag, d_x + 64ull * e->tp, sizeof flag, cudaMemcpyDeviceToHost, e->stream);
+  if (!rc && ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
+  cudaFree(d_x);
+  if (!rc && ce != cudaSuccess) rc = set_error(RF_ECUDA, "peer-sum setup failed: %s", cudaGetErrorString(ce));
+  if (rc || flag != 1) {  // every rank falls back to NCCL
+    for (void* q : e->ps_peer)
+      if (q) cudaIpcCloseMemHandle(q);
+    e->ps_peer.clear();
+    if (e->ps_area) dev_free(e, "scratch:peer_sum", &e->ps_area);
+    return rc;
+  }
+  for (int p = 0; p < e->tp; p++) peer_sum_bind(&P, p, p == e->rank ? e->ps_area : e->ps_peer[p], p == e->rank);
+  e->ps_ok = true;
+  return RF_OK;
+}
+
 int engine_init_device(rf_engine* e) {
   const rf_model_config& c = e->cfg;
   RF_CUDA(cudaSetDevice(e->dev));
@@ -370,6 +441,7 @@ int engine_init_device(rf_engine* e) {
     ncclUniqueId id;
     memcpy(&id, e->rt.nccl_id, sizeof id);
     RF_NCCL(nccl()->commInitRank(&e->comm, e->tp, id, e->rank));
+    RF_TRY(setup_peer_sum(e));
   }
   return RF_OK;
 }
@@ -686,6 +758,17 @@ AttnArgs attn_args(rf_engine* e, int l) {
   return aa;
 }
 
+// hidden = the sum over ranks of e->partial (row-parallel projection at call site
+// `site` of the step): over peer memory, or an NCCL all-reduce.
+int tp_sum(rf_engine* e, const Launch& La, int site) {
+  if (e->ps_ok) {
+    RF_CUDA(launch_peer_sum(La, e->ps, e->partial, e->hidden, (int)e->cfg.n_embd, site));
+  } else {
+    RF_NCCL(nccl()->allReduce(e->partial, e->hidden, e->cfg.n_embd, ncclFloat32, ncclSum, e->comm, e->stream));
+  }
+  return RF_OK;
+}
+
 int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
   const rf_model_config& c = e->cfg;
   Layer& L = e->layers[l];
@@ -701,7 +784,7 @@ int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
       RF_CUDA(gemv_residual(La, W, &e->gws, x, e->hidden, e->hidden));
     } else {
       RF_CUDA(gemv_residual(La, W, &e->gws, x, e->rank == 0 ? e->hidden : nullptr, e->partial));
-      RF_NCCL(nccl()->allReduce(e->partial, e->hidden, c.n_embd, ncclFloat32, ncclSum, e->comm, e->stream));
+      RF_TRY(tp_sum(e, La, 2 * l + (k == 4 ? 1 : 0)));
     }
   } else {
     RF_CUDA(gemv_swiglu(La, L.gateup, &e->gws, e->hidden, L.ffn_norm, c.rms_eps, e->act));
@@ -991,8 +1074,19 @@ int prepare_step_kernel(rf_engine* e) {
 
 bool step_kernel_active(rf_engine* e) { return prepare_step_kernel(e) == RF_OK && e->step_smem > 0; }
 
-// After a synchronisation: a step-kernel barrier that gave up fails the call.
+// After a synchronisation: a step-kernel barrier or a peer-sum wait that gave up
+// fails the call.
 int check_step_kernel(rf_engine* e) {
+  if (e->ps_ok) {
+    unsigned perr = 0;
+    RF_CUDA(cudaMemcpyAsync(&perr, e->ps.err, sizeof perr, cudaMemcpyDeviceToHost, e->stream));
+    RF_CUDA(cudaStreamSynchronize(e->stream));
+    if (perr) {
+      RF_CUDA(cudaMemsetAsync(e->ps.err, 0, sizeof perr, e->stream));
+      RF_CUDA(cudaStreamSynchronize(e->stream));
+      return set_error(RF_ETIMEOUT, "a tensor-parallel peer sum waited too long for another rank (0x%x)", perr);
+    }
+  }
   if (!e->step_used) return RF_OK;
   e->step_used = false;
   unsigned err = 0;
@@ -1129,6 +1223,9 @@ void destroy(rf_engine* e) {
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->h_tok) cudaFreeHost(e->h_tok);
   if (e->h_key) cudaFreeHost(e->h_key);
+  for (void* q : e->ps_peer)
+    if (q) cudaIpcCloseMemHandle(q);
+  if (e->ps_area) cudaFree(e->ps_area);
   if (e->comm && nccl()) nccl()->commDestroy(e->comm);
   if (e->stream) cudaStreamDestroy(e->stream);
   if (e->map_addr) munmap(e->map_addr, e->map_len);
@@ -1569,6 +1666,12 @@ int rf_residency_stats_get(const rf_engine* e, rf_residency_stats* out) {
   if (!e || !out) return set_error(RF_EINVAL, "null argument");
   *out = e->stats;
   out->peak_bytes = e->budget.peak();
+  return RF_OK;
+}
+
+int rf_tp_peer_sum(const rf_engine* e, int* out) {
+  if (!e || !out) return set_error(RF_EINVAL, "null argument");
+  *out = e->ps_ok ? 1 : 0;
   return RF_OK;
 }
 

@@ -168,6 +168,31 @@ cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const GemvScratch* 
 cudaError_t gemv_batched(cudaStream_t s, const PackedMat& W, const GemvScratch* ws, const float* x, int batch,
                          float* y);
 
+// ---- tensor-parallel sum over NVLink peer memory ------------------------------
+// The sum of the ranks' partial vectors after a row-parallel projection, as one
+// kernel over peer memory instead of a library all-reduce: every rank stores its
+// partial straight into each rank's receive area (NVLink peer stores through
+// cudaIpc mappings), raises one flag per slice on each rank, waits for the other
+// ranks' flags of its slices and sums the ranks' partials in rank order (the same
+// result on every rank).  A flag holds the call site's generation, so flags of
+// earlier steps never match; waits are bounded and report through `err`.
+constexpr int RF_MAX_TP = 8;
+constexpr int PS_THREADS = 256, PS_ELEMS = 4 * PS_THREADS;  // elements a CTA sums
+struct PeerSum {
+  float* recv[RF_MAX_TP];      // rank p's receive area: [2 (site parity)][n_ranks][n_max]
+  unsigned* flags[RF_MAX_TP];  // rank p's flags: [n_ranks][sites][max_ctas]
+  unsigned* epoch;             // this rank: generation of each call site [sites]
+  unsigned* done;              // this rank: CTAs finished per call site [sites]
+  unsigned* err;               // this rank: bit 0 = a wait gave up
+  int rank, n_ranks, n_max, sites, max_ctas;
+};
+// Bytes of one rank's area (receive | flags | epoch | done | err), and its layout.
+size_t peer_sum_area_bytes(int n_ranks, int n_max, int sites);
+void peer_sum_bind(PeerSum* P, int p, void* area_of_p, bool own);
+// out[i] = sum over ranks of partial[i] (i < n, n a multiple of 4); call site
+// `site` < P.sites, consecutive sites of one step alternate parity.
+cudaError_t launch_peer_sum(const Launch& L, const PeerSum& P, const float* partial, float* out, int n, int site);
+
 // ---- attention -------------------------------------------------------------
 struct AttnArgs {
   const float* q;          // [batch][H][hd]

@@ -160,6 +160,13 @@ class DecodeEngine:
         check(lib().rf_set_step_kernel(self._h, 1 if enable else 0))
 
     @property
+    def tp_peer_sum(self) -> bool:
+        """True when tensor-parallel sums run over NVLink peer memory (else NCCL)."""
+        v = ctypes.c_int()
+        check(lib().rf_tp_peer_sum(self._h, ctypes.byref(v)))
+        return bool(v.value)
+
+    @property
     def step_kernel_active(self) -> bool:
         v = ctypes.c_int()
         check(lib().rf_step_kernel_active(self._h, ctypes.byref(v)))
