@@ -1,6 +1,7 @@
-"""Tensor parallelism on two GPUs (skipped with fewer): two ranks, one process
-per GPU, the row-parallel sums over NVLink peer memory (and, for comparison,
-NCCL all-reduce).  Both ranks must produce the oracle's greedy tokens.
+"""Tensor parallelism on several GPUs (skipped where the box has fewer): one
+process per GPU, the row-parallel sums over NVLink peer memory (and, at two
+ranks, NCCL all-reduce for comparison).  Every rank must produce the oracle's
+greedy tokens.
 """
 import multiprocessing as mp
 import os
@@ -14,8 +15,10 @@ from ramforge_b200 import synth
 pytestmark = pytest.mark.gpu
 THREADS = min(32, os.cpu_count() or 8)
 
-TP_MODEL = synth.scaled(synth.LLAMA3_8B, name="tp-q4k", vocab_size=1024, n_embd=1024, n_layers=3, n_ff=1536,
-                        n_heads=8, n_kv_heads=2, seed=51, context_length=128)
+# 8 KV heads of head_dim 128 and 4096 FFN rows: shards of up to 8 ranks fall on
+# Q4_K super-block boundaries.
+TP_MODEL = synth.scaled(synth.LLAMA3_8B, name="tp-q4k", vocab_size=1024, n_embd=2048, n_layers=2, n_ff=4096,
+                        n_heads=16, n_kv_heads=8, seed=51, context_length=128)
 
 
 def _gpu_count():
@@ -26,11 +29,11 @@ def _gpu_count():
         return 0
 
 
-def _rank(rank, path, nid, prompt, n_new, peer_sum, q):
+def _rank(rank, world, path, nid, prompt, n_new, peer_sum, q):
     try:
         os.environ["RF_PEER_SUM"] = "1" if peer_sum else "0"
         from ramforge_b200 import DecodeEngine
-        eng = DecodeEngine(path, device=rank, max_seq_len=64, tp_rank=rank, tp_size=2, nccl_id=nid)
+        eng = DecodeEngine(path, device=rank, max_seq_len=64, tp_rank=rank, tp_size=world, nccl_id=nid)
         toks = eng.generate(prompt, n_new).tolist()
         q.put((rank, toks, eng.tp_peer_sum, None))
         eng.close()
@@ -38,19 +41,26 @@ def _rank(rank, path, nid, prompt, n_new, peer_sum, q):
         q.put((rank, None, None, repr(ex)))
 
 
-@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("peer_sum", [True, False])
-def test_tp2_greedy_matches_oracle(tmp_path, peer_sum):
+@pytest.fixture(scope="module")
+def model(tmp_path_factory):
     g = synth.gguf_bytes(TP_MODEL)
-    path = str(tmp_path / "tp.gguf")
+    path = str(tmp_path_factory.mktemp("tp") / "tp.gguf")
     g.tofile(path)
     prompt = np.random.default_rng(6).integers(0, TP_MODEL.vocab_size, 7).tolist()
     want = orc.OracleModel(g, kv_f16=True, max_seq=64, threads=THREADS).generate(prompt, 16)[0].tolist()
+    return path, prompt, want
+
+
+@pytest.mark.parametrize("world,peer_sum", [(2, True), (2, False), (4, True), (8, True)])
+def test_tp_greedy_matches_oracle(model, world, peer_sum):
+    if _gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    path, prompt, want = model
     from ramforge_b200 import tp_unique_id
     nid = tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_rank, args=(r, path, nid, prompt, 16, peer_sum, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank, args=(r, world, path, nid, prompt, 16, peer_sum, q)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
@@ -59,7 +69,7 @@ def test_tp2_greedy_matches_oracle(tmp_path, peer_sum):
         res[r] = (toks, active, err)
     for p in ps:
         p.join(timeout=60)
-    for r in (0, 1):
+    for r in range(world):
         toks, active, err = res[r]
         assert err is None, err
         assert toks == want, (r, toks, want)
