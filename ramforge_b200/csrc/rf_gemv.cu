@@ -2,18 +2,29 @@
 // (quantized matrices: the routine of rf_gemv.cuh over one kernel launch;
 // F32/F16 matrices: a plain row-major kernel).
 #include <algorithm>
+#include <type_traits>
 
 #include "rf_gemv.cuh"
 
 namespace rf {
 
-template <int FMT, bool QUIRK, class Epi>
-__global__ void __launch_bounds__(QG_THREADS, 1)
+template <int FMT, bool QUIRK, class Epi, int NW>
+__global__ void __launch_bounds__(NW * 32, QG_WARPS / NW)
     qgemv_kernel(PackedMat W, const float* __restrict__ x, const float* __restrict__ nw, float eps,
                  float* __restrict__ part, unsigned* __restrict__ cnt, Epi epi) {
   extern __shared__ __align__(16) float qsm[];
-  qgemv_body<FMT, QUIRK>(W, x, nw, eps, part, cnt, epi, qsm, [] { griddep_wait(); });
+  qgemv_body<FMT, QUIRK, NW>(W, x, nw, eps, part, cnt, epi, qsm, [] { griddep_wait(); });
   epi.flush();
+}
+
+// Warps per CTA: the QKV, W_o and down products run as two 8-warp CTAs per SM
+// (the same warps a SM, half the warps behind each CTA barrier, and an SM frees
+// half its slots for the next kernel as soon as one CTA ends), which measured
+// faster in the decode step; gate/up and the LM head measured faster as one
+// 16-warp CTA per SM.
+template <class Epi>
+constexpr int qgemv_warps() {
+  return std::is_same<Epi, EpiSwiGLU>::value || std::is_same<Epi, EpiArgmax>::value ? QG_WARPS : QG_WARPS / 2;
 }
 
 constexpr size_t kMaxSmem = 227 * 1024;
@@ -21,14 +32,15 @@ constexpr size_t kMaxSmem = 227 * 1024;
 template <int FMT, class Epi>
 static cudaError_t run_qgemv_t(const Launch& L, const PackedMat& W, const GemvScratch& ws, const float* x,
                                const float* nw, float eps, Epi epi) {
-  auto k = W.sub_scales ? qgemv_kernel<FMT, true, Epi> : qgemv_kernel<FMT, false, Epi>;
-  const int grid = num_sms();
-  const size_t smem = qgemv_smem_bytes(W, grid);
+  constexpr int NW = qgemv_warps<Epi>();
+  auto k = W.sub_scales ? qgemv_kernel<FMT, true, Epi, NW> : qgemv_kernel<FMT, false, Epi, NW>;
+  const int grid = num_sms() * (QG_WARPS / NW);
+  const size_t smem = qgemv_smem_bytes(W, grid, NW);
   if (smem > kMaxSmem) return cudaErrorInvalidValue;
   if (ws.part_floats < (uint64_t)W.Mp * W.nk * QT_PIECES || ws.n_cnt < W.Mp / QT_ROWS) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_k(L, k, dim3(grid), dim3(QG_THREADS), smem, W, x, nw, eps, ws.part, ws.cnt, epi);
+  return launch_k(L, k, dim3(grid), dim3(NW * 32), smem, W, x, nw, eps, ws.part, ws.cnt, epi);
 }
 
 void gemv_scratch_need(const PackedMat& W, uint64_t* part_floats, uint32_t* n_cnt) {

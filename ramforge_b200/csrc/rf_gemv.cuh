@@ -310,13 +310,12 @@ __device__ __forceinline__ unsigned arrive_acq_rel(unsigned* p, unsigned v) {
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
 }
-constexpr int EPI_ROWS = QG_THREADS;  // epilogue inputs prefetched per CTA (one per thread)
 
 // The quantized GEMV over every CTA of the grid.  `wait()` runs before the
 // first read of x (the previous kernel's completion, or a grid barrier of the
 // persistent step kernel); x and the residual input are read through L2, so
 // they may come from earlier in the same kernel.
-template <int FMT, bool QUIRK, class Epi, class Wait>
+template <int FMT, bool QUIRK, int NW = QG_WARPS, class Epi, class Wait>
 __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __restrict__ x,
                                            const float* __restrict__ nw, float eps, float* __restrict__ part,
                                            unsigned* __restrict__ cnt, Epi& epi, float* smem, Wait&& wait) {
@@ -329,11 +328,11 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   // warps' shares differ by at most one piece; a warp loads and decodes whole
   // items but only its pieces of the first and last one.
   const uint64_t N = (uint64_t)ntiles * nk, P = N * NP;
-  const uint64_t Wt = (uint64_t)gridDim.x * QG_WARPS;
-  const uint64_t g0 = (uint64_t)blockIdx.x * QG_WARPS;
+  const uint64_t Wt = (uint64_t)gridDim.x * NW;
+  const uint64_t g0 = (uint64_t)blockIdx.x * NW;
   const bool narrow = P * Wt < (1ull << 32);
   const uint64_t pa = muldiv(P, g0 + warp, Wt, narrow), pb = muldiv(P, g0 + warp + 1, Wt, narrow);  // this warp's
-  const uint64_t cpa = muldiv(P, g0, Wt, narrow), cpb = muldiv(P, g0 + QG_WARPS, Wt, narrow);         // this CTA's
+  const uint64_t cpa = muldiv(P, g0, Wt, narrow), cpb = muldiv(P, g0 + NW, Wt, narrow);         // this CTA's
   const uint64_t ia = pa / NP, ib = pa < pb ? (pb + NP - 1) / NP : ia;      // items touched by the warp
   const uint64_t ca = cpa / NP, cb = (cpb + NP - 1) / NP;                   // ... by the CTA
   auto plo = [&](uint64_t i) { return i * NP < pa ? (int)(pa - i * NP) : 0; };         // first piece of item i
@@ -346,18 +345,18 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   }
   float* sx = smem;                               // [nst][CE] pre-scaled x
   float* sxs = sx + (size_t)nst * CE;             // [nst][NG] XSF * (sum of each 32 elements)
-  float* sws = sxs + (size_t)nst * NG;            // [QG_WARPS][64] epilogue staging
-  float* sslot = sws + QG_WARPS * 64;             // [QG_WARPS*2][64] partial tile sums of each warp
-  int* stile = reinterpret_cast<int*>(sslot + QG_WARPS * 2 * 64);  // [QG_WARPS*2] their tiles (-1: none)
-  float* sred = reinterpret_cast<float*>(stile + QG_WARPS * 2);     // [40]
-  float* sepi = sred + 40;                                          // [EPI_ROWS] prefetched epilogue inputs
+  float* sws = sxs + (size_t)nst * NG;            // [NW][64] epilogue staging
+  float* sslot = sws + NW * 64;             // [NW*2][64] partial tile sums of each warp
+  int* stile = reinterpret_cast<int*>(sslot + NW * 2 * 64);  // [NW*2] their tiles (-1: none)
+  float* sred = reinterpret_cast<float*>(stile + NW * 2);     // [40]
+  float* sepi = sred + 40;                                          // [NW * 32] prefetched epilogue inputs
   float* ws = sws + warp * 64;
   // Epilogue inputs of the rows of the tiles this CTA touches (the only tiles it
   // can finish), when they fit: fetched after wait() and held in a register
   // while the CTA multiplies.
   const uint32_t etl = (uint32_t)div_n(cpa, tp, narrow);
   const uint32_t eth = cpb > cpa ? (uint32_t)div_n(cpb - 1, tp, narrow) + 1 : etl;
-  const bool epre = Epi::kPre && (eth - etl) * QT_ROWS <= (uint32_t)EPI_ROWS;
+  const bool epre = Epi::kPre && (eth - etl) * QT_ROWS <= (uint32_t)(NW * 32);
   float epf = 0.f;
 
   uint32_t w[2][4][8];  // [row r / r+32][piece][word] of the chunk in flight
@@ -421,11 +420,11 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   const bool win_is_x = nst == nk;             // then kc0 == 0: window float4 q is x float4 q
   const uint32_t nloop = nq > KQ ? nq : KQ;
   float ss = 0.f;
-  for (uint32_t q0 = (uint32_t)tid; q0 < nloop; q0 += SU * QG_THREADS) {
+  for (uint32_t q0 = (uint32_t)tid; q0 < nloop; q0 += SU * (NW * 32)) {
     float4 xv[SU], wv[SU], sv[SU];
 #pragma unroll
     for (int u = 0; u < SU; u++) {
-      const uint32_t q = q0 + u * QG_THREADS, f = 4 * q, s = f / CE, e = f % CE;
+      const uint32_t q = q0 + u * (NW * 32), f = 4 * q, s = f / CE, e = f % CE;
       uint32_t kc = kc0 + s;
       if (kc >= nk) kc -= nk;
       const uint32_t gi = kc * CE + e;
@@ -436,7 +435,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     }
 #pragma unroll
     for (int u = 0; u < SU; u++) {
-      const uint32_t q = q0 + u * QG_THREADS, f = 4 * q, e = f % CE;
+      const uint32_t q = q0 + u * (NW * 32), f = 4 * q, e = f % CE;
       if (q < KQ) {
         const float4 t = win_is_x ? xv[u] : sv[u];
         ss = fmaf(t.x, t.x, ss);
@@ -465,7 +464,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   __syncthreads();
   if (nw) {
     float t = 0.f;
-    for (int w2 = 0; w2 < QG_WARPS; w2++) t += sred[w2];
+    for (int w2 = 0; w2 < NW; w2++) t += sred[w2];
     rms = rms_of(t, (int)W.K, eps);
   }
   griddep_launch();
@@ -649,7 +648,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     while (j >= 0 && stile[j] < 0) j--;
     if (j >= 0 && stile[j] == T) continue;
     float s0 = 0.f, s1 = 0.f;
-    for (int k = i; k < 2 * QG_WARPS; k++) {
+    for (int k = i; k < 2 * NW; k++) {
       const int tk = stile[k];
       if (tk < 0) continue;
       if (tk != T) break;
@@ -709,15 +708,15 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   }
 }
 
-// Dynamic shared memory qgemv_body needs for W on a grid of `grid` CTAs.
-inline size_t qgemv_smem_bytes(const PackedMat& W, int grid) {
+// Dynamic shared memory qgemv_body needs for W on a grid of `grid` CTAs of `nw` warps.
+inline size_t qgemv_smem_bytes(const PackedMat& W, int grid, int nw = QG_WARPS) {
   const uint64_t CE = (uint64_t)chunk_elems(W.type);
   // A CTA's pieces [cpa, cpb) number at most ceil(P/grid); the items they touch,
   // floor(cpa/NP) .. ceil(cpb/NP), at most ceil(that/NP) + 1.
   const uint64_t P = (uint64_t)(W.Mp / QT_ROWS) * W.nk * QT_PIECES;
   const uint64_t per_cta = ((P + grid - 1) / grid + QT_PIECES - 1) / QT_PIECES + 1;
   const uint64_t nst = std::min<uint64_t>(W.nk, per_cta);
-  return (size_t)(nst * CE + nst * (CE / 32) + QG_WARPS * 64 + QG_WARPS * 2 * 65 + 40 + EPI_ROWS) * sizeof(float);
+  return (size_t)(nst * CE + nst * (CE / 32) + nw * 64 + nw * 2 * 65 + 40 + nw * 32) * sizeof(float);
 }
 
 }  // namespace rf
