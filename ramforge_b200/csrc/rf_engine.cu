@@ -22,6 +22,7 @@
 #include <string>
 #include <vector>
 
+#include "rf_attn.cuh"
 #include "rf_common.h"
 
 using namespace rf;
@@ -292,7 +293,10 @@ int setup_geometry(rf_engine* e) {
   e->vocab_local = sh.vocab_rows;
   e->max_seq = e->rt.max_seq_len ? e->rt.max_seq_len : c.context_length;
   if (!e->max_seq) return set_error(RF_EINVAL, "max_seq_len is zero");
-  e->max_splits = std::max<int>(64, (int)((e->max_seq + 511) / 512));
+  // attention splits: one per 64 positions of the longest context this engine
+  // holds (so the attention grid has no more units than a step can use), at most
+  // 64 (512 positions a split past 32k)
+  e->max_splits = std::min<int>(attn_nsplit((int)e->max_seq, 1 << 30), std::max<int>(64, (int)((e->max_seq + 511) / 512)));
   return RF_OK;
 }
 
