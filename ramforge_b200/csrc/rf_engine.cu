@@ -776,7 +776,7 @@ int tp_sum(rf_engine* e, const Launch& La, int site) {
 int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
   const rf_model_config& c = e->cfg;
   Layer& L = e->layers[l];
-  const Launch La{e->stream, pdl};
+  const Launch La{e->stream, pdl, e->tp > 1};
   if (k == 0) {
     RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, rope_args(e, l)));
   } else if (k == 1) {

@@ -20,19 +20,19 @@ __global__ void __launch_bounds__(NW * 32, QG_WARPS / NW)
 // Warps per CTA: the QKV, W_o and down products run as two 8-warp CTAs per SM
 // (the same warps a SM, half the warps behind each CTA barrier, and an SM frees
 // half its slots for the next kernel as soon as one CTA ends), which measured
-// faster in the decode step; gate/up and the LM head measured faster as one
-// 16-warp CTA per SM.
+// faster in the single-GPU decode step; gate/up and the LM head measured faster
+// as one 16-warp CTA per SM, and so did every product of a tensor-parallel step
+// (Launch::wide), whose sums over ranks follow W_o and down.
 template <class Epi>
-constexpr int qgemv_warps() {
-  return std::is_same<Epi, EpiSwiGLU>::value || std::is_same<Epi, EpiArgmax>::value ? QG_WARPS : QG_WARPS / 2;
+constexpr bool qgemv_split_ctas() {
+  return !(std::is_same<Epi, EpiSwiGLU>::value || std::is_same<Epi, EpiArgmax>::value);
 }
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
-template <int FMT, class Epi>
-static cudaError_t run_qgemv_t(const Launch& L, const PackedMat& W, const GemvScratch& ws, const float* x,
+template <int FMT, class Epi, int NW>
+static cudaError_t run_qgemv_w(const Launch& L, const PackedMat& W, const GemvScratch& ws, const float* x,
                                const float* nw, float eps, Epi epi) {
-  constexpr int NW = qgemv_warps<Epi>();
   auto k = W.sub_scales ? qgemv_kernel<FMT, true, Epi, NW> : qgemv_kernel<FMT, false, Epi, NW>;
   const int grid = num_sms() * (QG_WARPS / NW);
   const size_t smem = qgemv_smem_bytes(W, grid, NW);
@@ -41,6 +41,14 @@ static cudaError_t run_qgemv_t(const Launch& L, const PackedMat& W, const GemvSc
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_k(L, k, dim3(grid), dim3(NW * 32), smem, W, x, nw, eps, ws.part, ws.cnt, epi);
+}
+
+template <int FMT, class Epi>
+static cudaError_t run_qgemv_t(const Launch& L, const PackedMat& W, const GemvScratch& ws, const float* x,
+                               const float* nw, float eps, Epi epi) {
+  if constexpr (qgemv_split_ctas<Epi>())
+    if (!L.wide) return run_qgemv_w<FMT, Epi, QG_WARPS / 2>(L, W, ws, x, nw, eps, epi);
+  return run_qgemv_w<FMT, Epi, QG_WARPS>(L, W, ws, x, nw, eps, epi);
 }
 
 void gemv_scratch_need(const PackedMat& W, uint64_t* part_floats, uint32_t* n_cnt) {

@@ -123,6 +123,7 @@ void gemv_scratch_need(const PackedMat& W, uint64_t* part_floats, uint32_t* n_cn
 struct Launch {
   cudaStream_t stream;
   bool pdl;
+  bool wide = false;  // quantized GEMVs as one 16-warp CTA per SM for every epilogue (tensor parallel)
 };
 
 // Repack GGUF rows (device bytes) into a PackedMat. src_row_of[dst] selects the
