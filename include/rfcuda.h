@@ -172,9 +172,10 @@ int rf_decode_step(rf_engine* e, uint32_t token, uint32_t* next_token);
 int rf_generate(rf_engine* e, const uint32_t* prompt, uint32_t n_prompt, uint32_t n_new, uint32_t* out);
 
 /* ---- measurement hooks (the Profiler's per-event timers, profile.rs:8-60) --------- */
-/* Kernels one decode step launches: 1 when the persistent step kernel runs the
- * step (see rf_step_kernel_active), else 5 per layer + embedding, output norm,
- * LM head with argmax, token advance. */
+/* Kernels of this library one decode step launches: 1 when the persistent step
+ * kernel runs the step (see rf_step_kernel_active), else 5 per layer + embedding,
+ * output norm, LM head with argmax, token advance, plus 2 per layer (the peer
+ * sums) under tensor parallelism over peer memory. */
 int rf_step_kernel_count(const rf_engine* e, uint32_t* out);
 /* The persistent step kernel: one cooperative launch per token runs every layer
  * and the LM head, with grid barriers between phases.  It is used when enabled

@@ -1501,7 +1501,9 @@ int rf_step_kernel_count(const rf_engine* ec, uint32_t* out) {
   if (!ec || !out) return set_error(RF_EINVAL, "null argument");
   rf_engine* e = const_cast<rf_engine*>(ec);
   if (all_resident(e) && step_kernel_active(e)) *out = 1u;  // the persistent step kernel
-  else *out = 5u * e->cfg.n_layers + 4u;  // embed, 5 per layer, output norm, LM head, advance
+  else *out = 5u * e->cfg.n_layers + 4u + (e->ps_ok ? 2u * e->cfg.n_layers : 0u);  // embed, 5 per layer,
+  // output norm, LM head, advance, and the two peer sums a layer under tensor parallelism (NCCL's own
+  // kernels are not counted)
   return RF_OK;
 }
 
