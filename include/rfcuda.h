@@ -44,6 +44,7 @@ extern "C" {
 #define RF_TYPE_Q4_0 2
 #define RF_TYPE_Q8_0 8
 #define RF_TYPE_Q4_K 12
+#define RF_TYPE_Q6_K 14
 
 /* per-layer tensor roles, the nine tensors of StreamingLayerWeights
  * (model_executor.rs:33-48; names blk.N.<role>.weight, model.rs:182-192) */
@@ -56,6 +57,12 @@ extern "C" {
 #define RF_ROLE_FFN_GATE 6
 #define RF_ROLE_FFN_UP 7
 #define RF_ROLE_FFN_DOWN 8
+/* optional qwen2 Q/K/V biases (StreamingLayerWeights::attn_{q,k,v}_bias,
+ * model_executor.rs:43-47): all three or none, vectors (ne1 = 0 or 1) in F32/F16 of
+ * n_heads*head_dim, n_kv_heads*head_dim, n_kv_heads*head_dim elements */
+#define RF_ROLE_ATTN_Q_BIAS 9
+#define RF_ROLE_ATTN_K_BIAS 10
+#define RF_ROLE_ATTN_V_BIAS 11
 /* persistent tensors (persistent.rs:20-80) */
 #define RF_ROLE_TOKEN_EMBD 16
 #define RF_ROLE_OUTPUT_NORM 17
@@ -136,7 +143,10 @@ int rf_engine_config(const rf_engine* e, rf_model_config* out);
 /* Persistent weight upload (PersistentWeight, persistent.rs:20-80). */
 int rf_persistent_load(rf_engine* e, const rf_tensor_view* view);
 /* load_layer (streaming_model.rs:581-847): copies and packs the nine tensors of one
- * layer into device memory, charging the byte budget "layer:<i>:weights". */
+ * layer (and its Q/K/V biases, when given) into device memory, charging the byte
+ * budget "layer:<i>:weights".  A partial bias set or a bias of the wrong shape is
+ * RF_EFORMAT (validate_qkv_bias, streaming_model.rs:1654-1696), with nothing charged.
+ * V may have another type than Q and K (it then runs as its own matrix). */
 int rf_layer_load(rf_engine* e, int layer, const rf_tensor_view* views, int n_views);
 /* load_layer from the engine's own GGUF source (engines created from a GGUF). */
 int rf_layer_load_gguf(rf_engine* e, int layer);

@@ -791,6 +791,35 @@ static int f32_view(const orc_tensor* t, size_t n, float* out) {
   return orc_dequant_row((int)t->type, t->data, t->nbytes, n, out);
 }
 
+/* validate_qkv_bias (ramforge-runtime/src/streaming_model.rs:1654-1696): layer l's
+ * qwen2 Q/K/V biases (load_layer's map, :829-831), all three or none, each 1-D of
+ * the projection's output size.  B[0..2] = NULL when the layer has none. */
+static int layer_biases(orc_model* m, uint32_t l, size_t qd, size_t kvd, const orc_tensor* B[3]) {
+  static const char* nm[3] = {"attn_q", "attn_k", "attn_v"};
+  int count = 0;
+  for (int i = 0; i < 3; i++) {
+    char name[128];
+    snprintf(name, sizeof name, "blk.%u.%s.bias", l, nm[i]);
+    B[i] = find_t(m, name);
+    if (B[i] && !B[i]->data) B[i] = NULL;
+    count += B[i] != NULL;
+  }
+  if (count == 0) return 0;
+  if (count != 3) {
+    set_err("layer %u has an incomplete Q/K/V bias set (q.bias: %s, k.bias: %s, v.bias: %s); refusing to run "
+            "inference with partial biases", l, B[0] ? "true" : "false", B[1] ? "true" : "false",
+            B[2] ? "true" : "false");
+    return -1;
+  }
+  const size_t want[3] = {qd, kvd, kvd};
+  for (int i = 0; i < 3; i++)
+    if (B[i]->ndims != 1 || B[i]->dims[0] != want[i]) {
+      set_err("invalid blk.%u.%s.bias shape: expected 1D [%zu]", l, nm[i], want[i]);
+      return -1;
+    }
+  return 0;
+}
+
 /* ModelExecutor::execute_layer (ramforge-runtime/src/model_executor.rs:102-236). */
 static int execute_layer(orc_model* m, uint32_t l, uint32_t pos, float* hidden, float* k_tmp, float* v_tmp) {
   const orc_config* c = &m->cfg;
@@ -807,6 +836,21 @@ static int execute_layer(orc_model* m, uint32_t l, uint32_t pos, float* hidden, 
   if (mv_tensor(m, T[1], tmp, d, qd, q)) goto out;                     /* :157 */
   if (mv_tensor(m, T[2], tmp, d, kvd, k_tmp)) goto out;                /* :158 */
   if (mv_tensor(m, T[3], tmp, d, kvd, v_tmp)) goto out;                /* :159 */
+  { /* :161-194 biases after the projections, before RoPE and the KV insert */
+    const orc_tensor* B[3];
+    if (layer_biases(m, l, qd, kvd, B)) goto out;
+    if (B[0]) {
+      float* b = malloc(4 * qd);
+      int bad = f32_view(B[0], qd, b);
+      for (size_t i = 0; !bad && i < qd; i++) q[i] += b[i];
+      bad = bad || f32_view(B[1], kvd, b);
+      for (size_t i = 0; !bad && i < kvd; i++) k_tmp[i] += b[i];
+      bad = bad || f32_view(B[2], kvd, b);
+      for (size_t i = 0; !bad && i < kvd; i++) v_tmp[i] += b[i];
+      free(b);
+      if (bad) goto out;
+    }
+  }
   if (orc_rope(q, k_tmp, pos, hd, c->n_heads, c->n_kv_heads, c->rope_theta)) goto out; /* :196 */
   /* :205-211 attention over kv[0, hist) + current K/V */
   kh = m->kcache + (size_t)l * m->max_seq * kvd;

@@ -18,8 +18,10 @@ ERROR_NAMES = {
     -6: "RF_EUNSUPPORTED", -7: "RF_ENCCL", -8: "RF_ETIMEOUT",
 }
 
-TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K = 0, 1, 2, 8, 12
+TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 2, 8, 12, 14
 ROLE_NAMES = ["attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"]
+# rf_layer_load roles 0-11: the nine weights, then the optional qwen2 Q/K/V biases
+LAYER_VIEW_NAMES = ROLE_NAMES + ["attn_q.bias", "attn_k.bias", "attn_v.bias"]
 ROLE_TOKEN_EMBD, ROLE_OUTPUT_NORM, ROLE_OUTPUT = 16, 17, 18
 
 # Every symbol include/rfcuda.h declares (checked by tests/test_abi.py).

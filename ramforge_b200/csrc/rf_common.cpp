@@ -263,6 +263,9 @@ int pack_rows(const uint8_t* src, uint64_t src_row_bytes, uint32_t src_blk_off, 
             for (int p = 0; p < 4; p++) memcpy(Q + qs_byte_off(g, dr, 128ull * k + 32 * p), s + 16 + 32 * p, 32);
           }
           break;
+        case T_Q6_K:
+          for (uint32_t k = 0; k < nblk; k++, s += 210) q6k_pack_block(g, Q, C, dr, k, s);
+          break;
       }
     }
   };

@@ -69,14 +69,22 @@ inline uint64_t align256(uint64_t x) { return (x + 255) & ~255ull; }
 
 const char* kRoleNames[9] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
                              "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+// A layer's tensor views: the nine weights (roles 0-8) and the optional qwen2
+// Q/K/V biases (roles 9-11, StreamingLayerWeights::attn_{q,k,v}_bias,
+// model_executor.rs:33-48).
+constexpr int kLayerViews = 12;
+const char* kBiasNames[3] = {"attn_q", "attn_k", "attn_v"};
 
 struct Layer {
   bool resident = false;
   void* block = nullptr;
   uint64_t bytes = 0;
   PackedMat qkv{}, wo{}, gateup{}, down{};
+  // V on its own when its type differs from Q/K's (then qkv holds [Q;K]); M = 0: V is in qkv
+  PackedMat vmat{};
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
+  float* qkv_bias = nullptr;  // [Q;K;V] biases in packed row order (qwen2), or null
 };
 
 // A layer's weights as one contiguous device image (packed Q/K/V, W_o, gate/up,
@@ -453,6 +461,7 @@ int engine_init_device(rf_engine* e) {
 // ---- weight packing ----------------------------------------------------------------
 struct View {
   int type = -1;
+  int ndims = 2;
   uint64_t ne0 = 0, ne1 = 0, bytes = 0;
   const uint8_t* host = nullptr;
 };
@@ -534,15 +543,43 @@ void bind_layer(Layer* L, const Layer& tmpl, uint8_t* base) {
   L->wo = rebase(tmpl.wo);
   L->gateup = rebase(tmpl.gateup);
   L->down = rebase(tmpl.down);
+  L->vmat = tmpl.vmat.M ? rebase(tmpl.vmat) : PackedMat{};
   L->attn_norm = reinterpret_cast<float*>(base + reinterpret_cast<uintptr_t>(tmpl.attn_norm));
   L->ffn_norm = reinterpret_cast<float*>(base + reinterpret_cast<uintptr_t>(tmpl.ffn_norm));
+  L->qkv_bias = tmpl.qkv_bias ? reinterpret_cast<float*>(base + reinterpret_cast<uintptr_t>(tmpl.qkv_bias)) : nullptr;
   L->bytes = tmpl.bytes;
+}
+
+// validate_qkv_bias (streaming_model.rs:1654-1696): the three biases come all or
+// none, each 1-D of the projection's output size.
+int validate_qkv_bias(const View* v, int l, uint64_t qd, uint64_t kvd) {
+  const bool p[3] = {v[9].host != nullptr, v[10].host != nullptr, v[11].host != nullptr};
+  const int count = (int)p[0] + (int)p[1] + (int)p[2];
+  if (count == 0) return RF_OK;
+  if (count != 3)
+    return set_error(RF_EFORMAT,
+                     "layer %d has an incomplete Q/K/V bias set (q.bias: %s, k.bias: %s, v.bias: %s); refusing to "
+                     "run inference with partial biases",
+                     l, p[0] ? "true" : "false", p[1] ? "true" : "false", p[2] ? "true" : "false");
+  const uint64_t want[3] = {qd, kvd, kvd};
+  for (int i = 0; i < 3; i++) {
+    const View& b = v[9 + i];
+    if (b.ndims != 1 || b.ne0 != want[i])
+      return set_error(RF_EFORMAT, "invalid blk.%d.%s.bias shape: expected 1D [%llu], got %s[%llu, %llu]", l,
+                       kBiasNames[i], (unsigned long long)want[i], b.ndims == 1 ? "1D " : "",
+                       (unsigned long long)b.ne0, (unsigned long long)b.ne1);
+    if (b.type != T_F32 && b.type != T_F16)
+      return set_error(RF_EUNSUPPORTED, "blk.%d.%s.bias: tensor type %d is not supported", l, kBiasNames[i], b.type);
+    if (b.bytes < want[i] * (b.type == T_F32 ? 4 : 2))
+      return set_error(RF_EINVAL, "blk.%d.%s.bias truncated", l, kBiasNames[i]);
+  }
+  return RF_OK;
 }
 
 // load_layer's packing (streaming_model.rs:581-847) into a host image: this
 // rank's rows of Q/K/V (RoPE pairs adjacent), W_o, interleaved gate/up and
 // down, in the tiled layout, plus the norms as f32.
-int build_layer_image(rf_engine* e, int l, const View* v /*[9]*/, LayerImage* out) {
+int build_layer_image(rf_engine* e, int l, const View* v /*[kLayerViews]*/, LayerImage* out) {
   const rf_model_config& c = e->cfg;
   const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
   RF_TRY(check_view(v[0], "attn_norm", c.n_embd, 1));
@@ -554,18 +591,43 @@ int build_layer_image(rf_engine* e, int l, const View* v /*[9]*/, LayerImage* ou
   RF_TRY(check_view(v[6], "ffn_gate", c.n_embd, c.n_ff));
   RF_TRY(check_view(v[7], "ffn_up", c.n_embd, c.n_ff));
   RF_TRY(check_view(v[8], "ffn_down", c.n_ff, c.n_embd));
-  if (v[1].type != v[2].type || v[1].type != v[3].type)
-    return set_error(RF_EUNSUPPORTED, "layer %d: Q/K/V of different types are not supported", l);
+  RF_TRY(validate_qkv_bias(v, l, qd, kvd));
+  if (v[1].type != v[2].type)
+    return set_error(RF_EUNSUPPORTED, "layer %d: Q and K of different types are not supported", l);
+  // V of another type (e.g. Q6_K beside Q4_K Q/K) is its own matrix, run as a
+  // second launch of the same epilogue
+  const bool split_v = v[3].type != v[1].type;
   if (v[6].type != v[7].type) return set_error(RF_EUNSUPPORTED, "layer %d: gate/up of different types", l);
   const uint32_t qk_o = block_elems(v[4].type), qk_d = block_elems(v[8].type);
   if ((e->qh_off * hd) % qk_o || e->q_local % qk_o || e->ff_off % qk_d || e->ff_local % qk_d)
     return set_error(RF_EINVAL, "tensor-parallel shard of layer %d does not fall on block boundaries", l);
-  HostPacked qkv, wo, gu, dn;
-  RF_TRY(host_packed_init(v[1].type, e->q_local + 2 * e->kv_local, c.n_embd, &qkv));
-  RF_TRY(pack_rows(v[1].host, row_bytes_of(v[1]), 0, rope_pair_rows(e->qh_off, e->qh_local, hd), &qkv, 0, 1));
-  RF_TRY(pack_rows(v[2].host, row_bytes_of(v[2]), 0, rope_pair_rows(e->kvh_off, e->kvh_local, hd), &qkv, e->q_local, 1));
-  RF_TRY(pack_rows(v[3].host, row_bytes_of(v[3]), 0, iota_rows(e->kvh_off * hd, e->kv_local), &qkv,
-                   e->q_local + e->kv_local, 1));
+  HostPacked qkv, vm, wo, gu, dn;
+  const std::vector<int> qrows = rope_pair_rows(e->qh_off, e->qh_local, hd),
+                         krows = rope_pair_rows(e->kvh_off, e->kvh_local, hd),
+                         vrows = iota_rows(e->kvh_off * hd, e->kv_local);
+  RF_TRY(host_packed_init(v[1].type, e->q_local + (split_v ? 1 : 2) * e->kv_local, c.n_embd, &qkv));
+  RF_TRY(pack_rows(v[1].host, row_bytes_of(v[1]), 0, qrows, &qkv, 0, 1));
+  RF_TRY(pack_rows(v[2].host, row_bytes_of(v[2]), 0, krows, &qkv, e->q_local, 1));
+  if (split_v) {
+    RF_TRY(host_packed_init(v[3].type, e->kv_local, c.n_embd, &vm));
+    RF_TRY(pack_rows(v[3].host, row_bytes_of(v[3]), 0, vrows, &vm, 0, 1));
+  } else {
+    RF_TRY(pack_rows(v[3].host, row_bytes_of(v[3]), 0, vrows, &qkv, e->q_local + e->kv_local, 1));
+  }
+  // biases in the packed row order of this rank's Q/K/V rows
+  const bool has_bias = v[9].host != nullptr;
+  const uint32_t nbias = e->q_local + 2 * e->kv_local;
+  std::vector<float> bias;
+  if (has_bias) {
+    std::vector<float> bq, bk, bv;
+    RF_TRY(norm_to_f32(v[9], qd, &bq));
+    RF_TRY(norm_to_f32(v[10], kvd, &bk));
+    RF_TRY(norm_to_f32(v[11], kvd, &bv));
+    bias.resize(nbias);
+    for (uint32_t i = 0; i < e->q_local; i++) bias[i] = bq[qrows[i]];
+    for (uint32_t i = 0; i < e->kv_local; i++) bias[e->q_local + i] = bk[krows[i]];
+    for (uint32_t i = 0; i < e->kv_local; i++) bias[e->q_local + e->kv_local + i] = bv[vrows[i]];
+  }
   RF_TRY(host_packed_init(v[4].type, c.n_embd, e->q_local, &wo));
   RF_TRY(pack_rows(v[4].host, row_bytes_of(v[4]), e->qh_off * hd / qk_o, iota_rows(0, c.n_embd), &wo, 0, 1));
   RF_TRY(host_packed_init(v[6].type, 2 * e->ff_local, c.n_embd, &gu));
@@ -576,13 +638,14 @@ int build_layer_image(rf_engine* e, int l, const View* v /*[9]*/, LayerImage* ou
   std::vector<float> an, fn;
   RF_TRY(norm_to_f32(v[0], c.n_embd, &an));
   RF_TRY(norm_to_f32(v[5], c.n_embd, &fn));
-  const uint64_t total = packed_bytes(qkv) + packed_bytes(wo) + packed_bytes(gu) + packed_bytes(dn) +
-                         2 * align256(4ull * c.n_embd);
+  const uint64_t total = packed_bytes(qkv) + (split_v ? packed_bytes(vm) : 0) + packed_bytes(wo) + packed_bytes(gu) +
+                         packed_bytes(dn) + 2 * align256(4ull * c.n_embd) + (has_bias ? align256(4ull * nbias) : 0);
   out->bytes.assign(total, 0);
   Layer& t = out->tmpl;
   t = Layer{};
   uint64_t off = 0;
   image_put(qkv, &out->bytes, &off, &t.qkv);
+  if (split_v) image_put(vm, &out->bytes, &off, &t.vmat);
   image_put(wo, &out->bytes, &off, &t.wo);
   image_put(gu, &out->bytes, &off, &t.gateup);
   image_put(dn, &out->bytes, &off, &t.down);
@@ -591,11 +654,16 @@ int build_layer_image(rf_engine* e, int l, const View* v /*[9]*/, LayerImage* ou
   off += align256(4ull * c.n_embd);
   t.ffn_norm = reinterpret_cast<float*>(off);
   memcpy(out->bytes.data() + off, fn.data(), 4ull * c.n_embd);
+  off += align256(4ull * c.n_embd);
+  if (has_bias) {
+    t.qkv_bias = reinterpret_cast<float*>(off);
+    memcpy(out->bytes.data() + off, bias.data(), 4ull * nbias);
+  }
   t.bytes = total;
   return RF_OK;
 }
 
-int load_layer_views(rf_engine* e, int l, const View* v /*[9]*/) {
+int load_layer_views(rf_engine* e, int l, const View* v /*[kLayerViews]*/) {
   LayerImage img;
   RF_TRY(build_layer_image(e, l, v, &img));
   Layer& L = e->layers[l];
@@ -621,6 +689,7 @@ View view_from_gguf(const GgufTensor* t) {
   View v;
   if (!t) return v;
   v.type = (int)t->type;
+  v.ndims = (int)t->dims.size();
   v.ne0 = t->dims.size() > 0 ? t->dims[0] : 1;
   v.ne1 = t->dims.size() > 1 ? t->dims[1] : 1;
   v.bytes = t->nbytes;
@@ -702,15 +771,26 @@ int release_layer_impl(rf_engine* e, int l) {
   return RF_OK;
 }
 
-int load_layer_gguf(rf_engine* e, int l) {
-  if (!e->src) return set_error(RF_ESTATE, "engine has no GGUF source");
-  View v[9];
+// Layer l's views from the GGUF: the nine weights (load_layer's map,
+// streaming_model.rs:581-847) and, when present, the Q/K/V biases (:829-831).
+int gguf_layer_views(rf_engine* e, int l, View* v /*[kLayerViews]*/) {
   for (int j = 0; j < 9; j++) {
     const std::string name = "blk." + std::to_string(l) + "." + kRoleNames[j] + ".weight";
     const GgufTensor* t = e->gguf.find(name);
     if (!t || !t->data) return set_error(RF_EFORMAT, "missing tensor '%s'", name.c_str());
     v[j] = view_from_gguf(t);
   }
+  for (int j = 0; j < 3; j++) {
+    const GgufTensor* t = e->gguf.find("blk." + std::to_string(l) + "." + kBiasNames[j] + ".bias");
+    v[9 + j] = t && t->data ? view_from_gguf(t) : View{};
+  }
+  return RF_OK;
+}
+
+int load_layer_gguf(rf_engine* e, int l) {
+  if (!e->src) return set_error(RF_ESTATE, "engine has no GGUF source");
+  View v[kLayerViews];
+  RF_TRY(gguf_layer_views(e, l, v));
   return load_layer_views(e, l, v);
 }
 
@@ -735,6 +815,8 @@ RopeQKVArgs rope_args(rf_engine* e, int l) {
   ra.kcache = e->kc[l];
   ra.vcache = e->vc[l];
   ra.kv_f32 = e->rt.kv_f32;
+  ra.row_base = 0;
+  ra.bias = e->layers[l].qkv_bias;
   return ra;
 }
 
@@ -778,7 +860,12 @@ int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
   Layer& L = e->layers[l];
   const Launch La{e->stream, pdl, e->tp > 1};
   if (k == 0) {
-    RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, rope_args(e, l)));
+    RopeQKVArgs ra = rope_args(e, l);
+    RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, ra));
+    if (L.vmat.M) {  // V of its own type: the same epilogue from the V rows on
+      ra.row_base = e->q_local + e->kv_local;
+      RF_CUDA(gemv_qkv_rope(La, L.vmat, &e->gws, e->hidden, L.attn_norm, c.rms_eps, ra));
+    }
   } else if (k == 1) {
     RF_CUDA(launch_attention(La, attn_args(e, l)));
   } else if (k == 2 || k == 4) {
@@ -886,13 +973,8 @@ int ensure_stream_image(rf_engine* e, int l) {
   StreamImage& si = e->simg[l];
   if (si.host) return RF_OK;
   if (!e->src) return set_error(RF_ESTATE, "layer %d is not resident and the engine has no GGUF source", l);
-  View v[9];
-  for (int j = 0; j < 9; j++) {
-    const std::string name = "blk." + std::to_string(l) + "." + kRoleNames[j] + ".weight";
-    const GgufTensor* t = e->gguf.find(name);
-    if (!t || !t->data) return set_error(RF_EFORMAT, "missing tensor '%s'", name.c_str());
-    v[j] = view_from_gguf(t);
-  }
+  View v[kLayerViews];
+  RF_TRY(gguf_layer_views(e, l, v));
   LayerImage img;
   RF_TRY(build_layer_image(e, l, v, &img));
   RF_CUDA(cudaHostAlloc((void**)&si.host, img.tmpl.bytes, cudaHostAllocDefault));
@@ -1058,6 +1140,8 @@ int prepare_step_kernel(rf_engine* e) {
   PackedMat lm;
   if (lm_head(e, &lm) != RF_OK) return RF_OK;
   const rf_model_config& c = e->cfg;
+  for (uint32_t l = 0; l < c.n_layers; l++)
+    if (e->layers[l].vmat.M) return RF_OK;  // a separate V matrix: per-kernel launches only
   e->h_step_layers.assign(c.n_layers, StepLayer{});
   for (uint32_t l = 0; l < c.n_layers; l++) {
     const Layer& L = e->layers[l];
@@ -1244,6 +1328,40 @@ void destroy(rf_engine* e) {
       return set_error(RF_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(_se)); \
   } while (0)
 
+// Bytes of layer l's device image (build_layer_image's layout) for this rank,
+// from its GGUF tensor types (layers of a mixed-format model differ).
+uint64_t layer_image_bytes(rf_engine* e, int l) {
+  const rf_model_config& c = e->cfg;
+  const std::string pre = "blk." + std::to_string(l) + ".";
+  auto type_of = [&](const char* role) -> int {
+    const GgufTensor* t = e->gguf.find(pre + role + ".weight");
+    return t ? (int)t->type : -1;
+  };
+  auto mat = [](int type, uint32_t M, uint32_t K) -> uint64_t {
+    PackedMat g{};
+    if (type < 0 || !packed_geometry(type, M, K, &g)) return 0;
+    const uint64_t sc = packed_sc_bytes(g);
+    return align256(packed_qs_bytes(g)) + align256(sc ? sc : 16);
+  };
+  const bool split_v = type_of("attn_v") != type_of("attn_q");
+  const bool bias = e->gguf.find(pre + "attn_q.bias") != nullptr;
+  return mat(type_of("attn_q"), e->q_local + (split_v ? 1 : 2) * e->kv_local, c.n_embd) +
+         (split_v ? mat(type_of("attn_v"), e->kv_local, c.n_embd) : 0) +
+         mat(type_of("attn_output"), c.n_embd, e->q_local) + mat(type_of("ffn_gate"), 2 * e->ff_local, c.n_embd) +
+         mat(type_of("ffn_down"), c.n_embd, e->ff_local) + 2 * align256(4ull * c.n_embd) +
+         (bias ? align256(4ull * (e->q_local + 2 * e->kv_local)) : 0);
+}
+
+// Whether layer l's V is a matrix of its own (its GGUF type differs from Q's);
+// false when the engine has no GGUF source (then only loaded layers tell).
+bool layer_v_split(rf_engine* e, int l) {
+  if (!e->src) return false;
+  const std::string pre = "blk." + std::to_string(l) + ".";
+  const GgufTensor* q = e->gguf.find(pre + "attn_q.weight");
+  const GgufTensor* v = e->gguf.find(pre + "attn_v.weight");
+  return q && v && q->type != v->type;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1338,11 +1456,13 @@ int rf_layer_load(rf_engine* e, int layer, const rf_tensor_view* views, int n_vi
   if (layer < 0 || layer >= (int)e->cfg.n_layers) return set_error(RF_EINVAL, "layer %d out of range", layer);
   if (!views || n_views <= 0) return set_error(RF_EINVAL, "no tensor views");
   if (e->layers[layer].resident) return set_error(RF_ESTATE, "layer %d is already loaded", layer);
-  View v[9];
+  View v[kLayerViews];
   for (int i = 0; i < n_views; i++) {
     const rf_tensor_view& t = views[i];
-    if (t.role < 0 || t.role > 8) return set_error(RF_EINVAL, "view %d has role %d (not a layer tensor)", i, t.role);
+    if (t.role < 0 || t.role >= kLayerViews)
+      return set_error(RF_EINVAL, "view %d has role %d (not a layer tensor)", i, t.role);
     v[t.role].type = t.ggml_type;
+    v[t.role].ndims = t.ne1 > 1 ? 2 : 1;  // ne1 = 0 or 1: a vector
     v[t.role].ne0 = t.ne0;
     v[t.role].ne1 = t.ne1 ? t.ne1 : 1;
     v[t.role].bytes = t.bytes;
@@ -1500,10 +1620,15 @@ int rf_decode_timed(rf_engine* e, uint32_t token, uint32_t n_steps, uint32_t* ou
 int rf_step_kernel_count(const rf_engine* ec, uint32_t* out) {
   if (!ec || !out) return set_error(RF_EINVAL, "null argument");
   rf_engine* e = const_cast<rf_engine*>(ec);
-  if (all_resident(e) && step_kernel_active(e)) *out = 1u;  // the persistent step kernel
-  else *out = 5u * e->cfg.n_layers + 4u + (e->ps_ok ? 2u * e->cfg.n_layers : 0u);  // embed, 5 per layer,
-  // output norm, LM head, advance, and the two peer sums a layer under tensor parallelism (NCCL's own
-  // kernels are not counted)
+  if (all_resident(e) && step_kernel_active(e)) {
+    *out = 1u;  // the persistent step kernel
+    return RF_OK;
+  }
+  // embed, 5 per layer (6 with a separate V matrix), output norm, LM head, advance, and the two peer sums
+  // a layer under tensor parallelism (NCCL's own kernels are not counted)
+  uint32_t n = 5u * e->cfg.n_layers + 4u + (e->ps_ok ? 2u * e->cfg.n_layers : 0u);
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++) n += e->layers[l].vmat.M || layer_v_split(e, (int)l) ? 1u : 0u;
+  *out = n;
   return RF_OK;
 }
 
@@ -1623,24 +1748,6 @@ int rf_budget_available(const rf_engine* e, uint64_t* out) {
   return RF_OK;
 }
 
-// Bytes of one layer's device image (build_layer_image's layout) for this rank,
-// from the GGUF tensor types of layer 0 (every layer has the same shapes).
-uint64_t layer_image_bytes(rf_engine* e) {
-  const rf_model_config& c = e->cfg;
-  auto type_of = [&](const char* role) -> int {
-    const GgufTensor* t = e->gguf.find(std::string("blk.0.") + role + ".weight");
-    return t ? (int)t->type : -1;
-  };
-  auto mat = [](int type, uint32_t M, uint32_t K) -> uint64_t {
-    PackedMat g{};
-    if (type < 0 || !packed_geometry(type, M, K, &g)) return 0;
-    const uint64_t sc = packed_sc_bytes(g);
-    return align256(packed_qs_bytes(g)) + align256(sc ? sc : 16);
-  };
-  return mat(type_of("attn_q"), e->q_local + 2 * e->kv_local, c.n_embd) + mat(type_of("attn_output"), c.n_embd, e->q_local) +
-         mat(type_of("ffn_gate"), 2 * e->ff_local, c.n_embd) + mat(type_of("ffn_down"), c.n_embd, e->ff_local) +
-         2 * align256(4ull * c.n_embd);
-}
 
 int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uint64_t vram_weight_budget_bytes) {
   ENGINE_GUARD(e);
@@ -1649,7 +1756,7 @@ int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uin
   uint64_t resident_bytes = 0, slot_bytes = 0;
   for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
     if (mask[l] && e->layers[l].resident) resident_bytes += e->layers[l].bytes;
-    if (!mask[l]) slot_bytes = std::max(slot_bytes, layer_image_bytes(e));
+    if (!mask[l]) slot_bytes = std::max(slot_bytes, layer_image_bytes(e, (int)l));
   }
   const uint64_t need = resident_bytes + (uint64_t)ring_slots * slot_bytes;
   if (vram_weight_budget_bytes && need > vram_weight_budget_bytes)

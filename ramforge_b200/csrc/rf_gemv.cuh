@@ -79,12 +79,14 @@ struct EpiResidual {  // out = res + W.x (res may alias out: a row is read befor
 
 // Q and K rows are packed as pairs (i, i+hd/2) of each head so that the
 // half-split rotation (compute.rs:440-456) happens in registers; V rows are in
-// natural order.  `pre`, when given, holds (cos, sin) of the pair and `pos` the
-// step's position.
+// natural order.  Q/K/V biases, when present, are added to the products first
+// (bias after projection, before RoPE and the KV append: model_executor.rs:161-196).
+// `pre`, when given, holds (cos, sin) of the pair and `pos` the step's position.
 __device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const float* v, int n,
                                            const float* pre = nullptr, int pos = -1);
 // (cos, sin) component (row & 1) of the rotation of Q/K row `row` at `pos`; 0 for V rows.
 __device__ __forceinline__ float rope_cs_of(const RopeQKVArgs& a, uint32_t row, int pos) {
+  row += a.row_base;
   if (row >= a.q_rows + a.kv_rows) return 0.f;
   const uint32_t j = (row < a.q_rows ? row : row - a.q_rows) / 2, half = a.head_dim / 2;
   const float* c = reinterpret_cast<const float*>(a.rope_cs + (size_t)pos * half + j % half);
@@ -114,14 +116,18 @@ __device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const
   {
     if (pos < 0) pos = __ldcg(a.d_pos);
     const uint32_t half = a.head_dim / 2;
-    const uint32_t p = (uint32_t)row0;
+    const uint32_t p = (uint32_t)row0 + a.row_base;
     if (p < a.q_rows + a.kv_rows) {
       if (n < 2) return;
       const bool isq = p < a.q_rows;
       const uint32_t j = (isq ? p : p - a.q_rows) / 2;
       const uint32_t h = j / half, i = j % half;
       const float2 cs = pre ? make_float2(pre[0], pre[1]) : a.rope_cs[(size_t)pos * half + i];
-      const float x0 = v[0], x1 = v[1];
+      float x0 = v[0], x1 = v[1];
+      if (a.bias) {
+        x0 = __fadd_rn(x0, __ldg(a.bias + p));
+        x1 = __fadd_rn(x1, __ldg(a.bias + p + 1));
+      }
       // first*cos - second*sin ; first*sin + second*cos, one rounding per op
       const float o0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
       const float o1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
@@ -145,10 +151,11 @@ __device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const
       for (int s = 0; s < n; s++) {
         const uint32_t o = p + s - a.q_rows - a.kv_rows;
         const uint32_t h = o / a.head_dim, dd = o % a.head_dim;
-        a.v_cur[o] = v[s];
+        const float x = a.bias ? __fadd_rn(v[s], __ldg(a.bias + p + s)) : v[s];
+        a.v_cur[o] = x;
         const size_t c = ((size_t)h * a.max_seq + pos) * a.head_dim + dd;
-        if (a.kv_f32) ((float*)a.vcache)[c] = v[s];
-        else ((__half*)a.vcache)[c] = __float2half_rn(v[s]);
+        if (a.kv_f32) ((float*)a.vcache)[c] = x;
+        else ((__half*)a.vcache)[c] = __float2half_rn(x);
       }
     }
   }
@@ -212,25 +219,36 @@ struct EpiArgmax {
 constexpr int QG_WARPS = 16;
 constexpr int QG_THREADS = QG_WARPS * 32;
 
+// Per format: CE elements per chunk, SW scale words per row and chunk, XSF the
+// factor on the per-group x sums, GE elements per group, PB bytes per piece of
+// the 64 rows, IB bytes per item.
 template <int FMT>
 struct QTraits;
 // Q4_K: a chunk is one super-block; piece c is sub-block pair c (byte l: element
 //       64c+l in the low nibble, 64c+32+l in the high one; quant.rs:235-248).
 template <>
 struct QTraits<T_Q4_K> {
-  static constexpr int CE = 256, SW = 4, XSF = 1;
+  static constexpr int CE = 256, SW = 4, XSF = 1, GE = 32, PB = QT_ROWS * 32, IB = QT_ITEM_BYTES;
 };
 // Q4_0: a chunk is 8 blocks; piece c is blocks 2c, 2c+1 (block byte j: element j
 //       low, 16+j high; value (q-8)*d, quant.rs:104-112).
 template <>
 struct QTraits<T_Q4_0> {
-  static constexpr int CE = 256, SW = 4, XSF = 8;
+  static constexpr int CE = 256, SW = 4, XSF = 8, GE = 32, PB = QT_ROWS * 32, IB = QT_ITEM_BYTES;
 };
 // Q8_0: a chunk is 4 blocks; piece c is block c (value q*d, quant.rs:176-180),
 //       bytes biased to q+128 on the fly.
 template <>
 struct QTraits<T_Q8_0> {
-  static constexpr int CE = 128, SW = 2, XSF = 128;
+  static constexpr int CE = 128, SW = 2, XSF = 128, GE = 32, PB = QT_ROWS * 32, IB = QT_ITEM_BYTES;
+};
+// Q6_K: a chunk is half a super-block; piece c is sub-blocks 2c, 2c+1 (three
+//       words each, q6k_sub_words; value (d*sc)*(u-32), quant.rs:376-406); the
+//       header is 8 int8 scales and the f16 d.
+template <>
+struct QTraits<T_Q6_K> {
+  static constexpr int CE = 128, SW = 3, XSF = 32, GE = 16, PB = QT_ROWS * Q6_PIECE_BYTES,
+                       IB = QT_ROWS * Q6_CHUNK_BYTES;
 };
 
 // Bit offset of the field holding element k (0..7) of a word pair (A, B) in
@@ -242,6 +260,7 @@ __device__ __forceinline__ int pair_off(int k) { return (k & 3) == 3 ? (k >> 2) 
 // Field offset of chunk element e.
 template <int FMT>
 __device__ __forceinline__ int qfield_off(int e) {
+  if (FMT == T_Q6_K) return 6 * (e & 3);  // element t of a sub-block: field t%4 of its word
   if (FMT == T_Q8_0) return pair_off(e & 7);
   const int u = e & 63;
   const bool hi = FMT == T_Q4_K ? (u >= 32) : ((u & 31) >= 16);
@@ -271,6 +290,41 @@ __device__ __forceinline__ void q8_pair(uint32_t A, uint32_t B, const float4& x0
   s = __ffma2_rn(ff2(as_f((A ^ M) & 0xFF0000u), as_f((P ^ M) & 0xFFu)), ff2(x0.z, x0.w), s);
   s = __ffma2_rn(ff2(as_f((B ^ M) & 0xFFu), as_f((B ^ M) & 0xFF00u)), ff2(x1.x, x1.y), s);
   s = __ffma2_rn(ff2(as_f((B ^ M) & 0xFF0000u), as_f((P ^ M) & 0xFF00u)), ff2(x1.z, x1.w), s);
+}
+
+// 16 six-bit fields of a Q6_K sub-block's words (A, B, C) against x[t]: P
+// gathers the top bytes of A, B and C below bit 24.
+__device__ __forceinline__ void q6_sub(uint32_t A, uint32_t B, uint32_t C, const float4& x0, const float4& x1,
+                                       const float4& x2, const float4& x3, float2& s) {
+  const uint32_t P = __byte_perm(__byte_perm(A, B, 0x0073), C, 0x0710);
+  s = __ffma2_rn(ff2(as_f(A & 0x3Fu), as_f(A & 0xFC0u)), ff2(x0.x, x0.y), s);
+  s = __ffma2_rn(ff2(as_f(A & 0x3F000u), as_f(A & 0xFC0000u)), ff2(x0.z, x0.w), s);
+  s = __ffma2_rn(ff2(as_f(B & 0x3Fu), as_f(B & 0xFC0u)), ff2(x1.x, x1.y), s);
+  s = __ffma2_rn(ff2(as_f(B & 0x3F000u), as_f(B & 0xFC0000u)), ff2(x1.z, x1.w), s);
+  s = __ffma2_rn(ff2(as_f(C & 0x3Fu), as_f(C & 0xFC0u)), ff2(x2.x, x2.y), s);
+  s = __ffma2_rn(ff2(as_f(C & 0x3F000u), as_f(C & 0xFC0000u)), ff2(x2.z, x2.w), s);
+  s = __ffma2_rn(ff2(as_f(P & 0x3Fu), as_f(P & 0xFC0u)), ff2(x3.x, x3.y), s);
+  s = __ffma2_rn(ff2(as_f(P & 0x3F000u), as_f(P & 0xFC0000u)), ff2(x3.z, x3.w), s);
+}
+// Signed byte k of w as a float (Q6_K sub-block scales).
+__device__ __forceinline__ float sbyte_f(uint32_t w, int k) { return (float)((int)(w << (24 - 8 * k)) >> 24); }
+// A Q6_K piece row (16-byte plane word 0-3 at pa, 8-byte plane words 4-5 at
+// pb) and a Q6_K header row (scales at pa, d at pb), under a predicate.
+__device__ __forceinline__ void ldg_q6_piece_if(bool on, const uint8_t* pa, const uint8_t* pb, uint32_t (&w)[8]) {
+  asm volatile(
+      "{ .reg .pred q; setp.ne.u32 q, %8, 0;\n"
+      "@q ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%6];\n"
+      "@q ld.global.nc.L1::no_allocate.v2.b32 {%4,%5}, [%7]; }"
+      : "+r"(w[0]), "+r"(w[1]), "+r"(w[2]), "+r"(w[3]), "+r"(w[4]), "+r"(w[5])
+      : "l"(pa), "l"(pb), "r"((uint32_t)on));
+}
+__device__ __forceinline__ void ldg_q6_hdr_if(bool on, const uint8_t* pa, const uint8_t* pb, uint32_t (&h)[3]) {
+  asm volatile(
+      "{ .reg .pred q; setp.ne.u32 q, %5, 0;\n"
+      "@q ld.global.nc.L1::no_allocate.v2.b32 {%0,%1}, [%3];\n"
+      "@q ld.global.nc.L1::no_allocate.b32 %2, [%4]; }"
+      : "+r"(h[0]), "+r"(h[1]), "+r"(h[2])
+      : "l"(pa), "l"(pb), "r"((uint32_t)on));
 }
 
 // f16 block scale -> f32: hardware conversion, or the reference's decode when
@@ -320,7 +374,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
                                            const float* __restrict__ nw, float eps, float* __restrict__ part,
                                            unsigned* __restrict__ cnt, Epi& epi, float* smem, Wait&& wait) {
   using T = QTraits<FMT>;
-  constexpr int CE = T::CE, SW = T::SW, NG = CE / 32, SB = SW * 4;
+  constexpr int CE = T::CE, SW = T::SW, GE = T::GE, NG = CE / GE, SB = SW * 4;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NP = QT_PIECES;
   const uint32_t nk = W.nk, ntiles = W.Mp / QT_ROWS, tp = nk * NP;  // tp: pieces per tile
@@ -344,7 +398,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     nst = (uint32_t)(cb - ca);
   }
   float* sx = smem;                               // [nst][CE] pre-scaled x
-  float* sxs = sx + (size_t)nst * CE;             // [nst][NG] XSF * (sum of each 32 elements)
+  float* sxs = sx + (size_t)nst * CE;             // [nst][NG] XSF * (sum of each GE elements)
   float* sws = sxs + (size_t)nst * NG;            // [NW][64] epilogue staging
   float* sslot = sws + NW * 64;             // [NW*2][64] partial tile sums of each warp
   int* stile = reinterpret_cast<int*>(sslot + NW * 2 * 64);  // [NW*2] their tiles (-1: none)
@@ -362,32 +416,54 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   uint32_t w[2][4][8];  // [row r / r+32][piece][word] of the chunk in flight
   uint32_t h[2][SW];    // its scale bytes
   auto load_piece = [&](uint64_t i, int c) {
-    const uint8_t* q = W.qs + i * QT_ITEM_BYTES + c * (QT_ROWS * 32) + lane * 32;
-    ldg256(q, w[0][c]);
-    ldg256(q + 32 * 32, w[1][c]);
+    if constexpr (FMT == T_Q6_K) {
+      const uint8_t* q = W.qs + i * T::IB + c * T::PB;
+      ldg_q6_piece_if(true, q + lane * 16, q + QT_ROWS * 16 + lane * 8, w[0][c]);
+      ldg_q6_piece_if(true, q + (lane + 32) * 16, q + QT_ROWS * 16 + (lane + 32) * 8, w[1][c]);
+    } else {
+      const uint8_t* q = W.qs + i * QT_ITEM_BYTES + c * (QT_ROWS * 32) + lane * 32;
+      ldg256(q, w[0][c]);
+      ldg256(q + 32 * 32, w[1][c]);
+    }
   };
   auto load_hdr = [&](uint64_t i) {
-    const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
-    if constexpr (SW == 4) {
+    if constexpr (FMT == T_Q6_K) {
+      const uint8_t* s = W.sc + i * (QT_ROWS * SB);
+      ldg_q6_hdr_if(true, s + lane * 8, s + QT_ROWS * 8 + lane * 4, h[0]);
+      ldg_q6_hdr_if(true, s + (lane + 32) * 8, s + QT_ROWS * 8 + (lane + 32) * 4, h[1]);
+    } else if constexpr (SW == 4) {
+      const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
       ldg128(s, h[0]);
       ldg128(s + 32 * SB, h[1]);
     } else {
+      const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
       ldg64(s, h[0]);
       ldg64(s + 32 * SB, h[1]);
     }
   };
   // branch-free forms for the hot path (nothing is read when `on` is false)
   auto load_piece_if = [&](bool on, uint64_t i, int c) {
-    const uint8_t* q = W.qs + i * QT_ITEM_BYTES + c * (QT_ROWS * 32) + lane * 32;
-    ldg256_if(on, q, w[0][c]);
-    ldg256_if(on, q + 32 * 32, w[1][c]);
+    if constexpr (FMT == T_Q6_K) {
+      const uint8_t* q = W.qs + i * T::IB + c * T::PB;
+      ldg_q6_piece_if(on, q + lane * 16, q + QT_ROWS * 16 + lane * 8, w[0][c]);
+      ldg_q6_piece_if(on, q + (lane + 32) * 16, q + QT_ROWS * 16 + (lane + 32) * 8, w[1][c]);
+    } else {
+      const uint8_t* q = W.qs + i * QT_ITEM_BYTES + c * (QT_ROWS * 32) + lane * 32;
+      ldg256_if(on, q, w[0][c]);
+      ldg256_if(on, q + 32 * 32, w[1][c]);
+    }
   };
   auto load_hdr_if = [&](bool on, uint64_t i) {
-    const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
-    if constexpr (SW == 4) {
+    if constexpr (FMT == T_Q6_K) {
+      const uint8_t* s = W.sc + i * (QT_ROWS * SB);
+      ldg_q6_hdr_if(on, s + lane * 8, s + QT_ROWS * 8 + lane * 4, h[0]);
+      ldg_q6_hdr_if(on, s + (lane + 32) * 8, s + QT_ROWS * 8 + (lane + 32) * 4, h[1]);
+    } else if constexpr (SW == 4) {
+      const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
       ldg128_if(on, s, h[0]);
       ldg128_if(on, s + 32 * SB, h[1]);
     } else {
+      const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
       ldg64_if(on, s, h[0]);
       ldg64_if(on, s + 32 * SB, h[1]);
     }
@@ -413,7 +489,8 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   // the loads for the sum of squares (all of x, in the same per-thread order as
   // block_sumsq_v4, so every CTA gets the same rms) are in flight together with
   // the window's.  float4 q of the window = elements 4q..4q+3; 8 consecutive
-  // threads = one 32-element group (warp-uniform: windows are multiples of 128).
+  // threads = one 32-element group, 4 one 16-element group (warp-uniform: windows
+  // are multiples of 128).
   constexpr int SU = 2;
   const uint32_t nq = nst * CE / 4;            // float4s of the window
   const uint32_t KQ = nw ? W.K / 4 : 0;        // float4s of x for the sum of squares
@@ -451,8 +528,8 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       float gs = ((v.x + v.y) + v.z) + v.w;
       gs += __shfl_xor_sync(0xffffffffu, gs, 1);
       gs += __shfl_xor_sync(0xffffffffu, gs, 2);
-      gs += __shfl_xor_sync(0xffffffffu, gs, 4);
-      if ((lane & 7) == 0) sxs[f / 32] = gs * (float)T::XSF;
+      if constexpr (GE == 32) gs += __shfl_xor_sync(0xffffffffu, gs, 4);
+      if ((lane & (GE / 4 - 1)) == 0) sxs[f / GE] = gs * (float)T::XSF;
     }
   }
   float rms = 1.f;  // rms = sqrt(sum/n + eps)  (compute.rs:312-317)
@@ -599,6 +676,50 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
           }
         }
       }
+    } else if constexpr (FMT == T_Q6_K) {
+      // d*sc_j*(sum_t u_t x_t - 32 sum_t x_t) per sub-block j; u_t x_t arrive
+      // scaled by 2^-64, the x sums (sxs) by 32
+      float d64[2], dd[2];
+#pragma unroll
+      for (int s = 0; s < 2; s++) {
+        dd[s] = scale_f<QUIRK>(hc[s][2]);
+        d64[s] = dd[s] * kTwo64;
+      }
+      float aS[2] = {0.f, 0.f}, aM[2] = {0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < NP; c++) {
+        const bool on = c >= lo && c < hi;
+        float2 sb[2][2];  // [row][sub-block of the piece]
+#pragma unroll
+        for (int s = 0; s < 2; s++)
+#pragma unroll
+          for (int b = 0; b < 2; b++) sb[s][b] = ff2(0.f, 0.f);
+        if (on) {
+#pragma unroll
+          for (int b = 0; b < 2; b++) {
+            const float* xb = xc + 32 * c + 16 * b;
+            const float4 x0 = lds4(xb), x1 = lds4(xb + 4), x2 = lds4(xb + 8), x3 = lds4(xb + 12);
+#pragma unroll
+            for (int s = 0; s < 2; s++)
+              q6_sub(w[s][c][3 * b], w[s][c][3 * b + 1], w[s][c][3 * b + 2], x0, x1, x2, x3, sb[s][b]);
+          }
+        }
+        load_piece_if(c < hi1, i + 1, c);
+        if (!on) continue;
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+          const int j = 2 * c + b;
+          const float xs32 = xsc[j];
+#pragma unroll
+          for (int s = 0; s < 2; s++) {
+            const float scf = sbyte_f(hc[s][j >> 2], j & 3);
+            aS[s] = fmaf(scf, sb[s][b].x + sb[s][b].y, aS[s]);
+            aM[s] = fmaf(scf, xs32, aM[s]);
+          }
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dd[s] * aM[s];
     } else {  // Q8_0
 #pragma unroll
       for (int c = 0; c < NP; c++) {
@@ -716,7 +837,8 @@ inline size_t qgemv_smem_bytes(const PackedMat& W, int grid, int nw = QG_WARPS) 
   const uint64_t P = (uint64_t)(W.Mp / QT_ROWS) * W.nk * QT_PIECES;
   const uint64_t per_cta = ((P + grid - 1) / grid + QT_PIECES - 1) / QT_PIECES + 1;
   const uint64_t nst = std::min<uint64_t>(W.nk, per_cta);
-  return (size_t)(nst * CE + nst * (CE / 32) + nw * 64 + nw * 2 * 65 + 40 + nw * 32) * sizeof(float);
+  return (size_t)(nst * CE + nst * (CE / chunk_group_elems(W.type)) + nw * 64 + nw * 2 * 65 + 40 + nw * 32) *
+         sizeof(float);
 }
 
 }  // namespace rf

@@ -34,6 +34,7 @@ bool packed_geometry(int type, uint32_t M, uint32_t K, PackedMat* p) {
     case T_Q8_0: p->qs_stride = p->Kp; break;
     case T_Q4_0:
     case T_Q4_K: p->qs_stride = p->Kp / 2; break;
+    case T_Q6_K: p->qs_stride = (uint64_t)p->Kp / 128 * Q6_CHUNK_BYTES; break;
   }
   if (is_tiled(type)) {
     p->Mp = (M + QT_ROWS - 1) / QT_ROWS * QT_ROWS;
@@ -55,6 +56,14 @@ __host__ __device__ inline bool subnormal_half(uint32_t lo, uint32_t hi) {
 
 bool has_subnormal_scales(const PackedMat& W, const uint8_t* sc) {
   if (!is_tiled(W.type)) return false;
+  if (W.type == T_Q6_K) {  // the f16 d at header bytes 8-9 of every row and chunk
+    for (uint32_t r = 0; r < W.Mp; r++)
+      for (uint32_t c = 0; c < W.nk; c++) {
+        const uint64_t o = sc_byte_off(W, r, (uint64_t)c * Q6_HDR_BYTES + 8);
+        if (subnormal_half(sc[o], sc[o + 1])) return true;
+      }
+    return false;
+  }
   const uint64_t n = packed_sc_bytes(W);
   // f16 scales: Q8_0/Q4_0 every pair of bytes; Q4_K the first two pairs (d, dmin)
   // of each 16-byte header
@@ -108,6 +117,11 @@ __global__ void pack_kernel(const uint8_t* __restrict__ src, const int* __restri
           uint8_t* q = d.qs + qs_byte_off(d, r, 128ull * b + 32 * p);
           for (int i = 0; i < 32; i++) q[i] = s[16 + 32 * p + i];
         }
+        break;
+      }
+      case T_Q6_K: {
+        q6k_pack_block(d, d.qs, d.sc, r, b, s);
+        sub = subnormal_half(s[208], s[209]);
         break;
       }
     }

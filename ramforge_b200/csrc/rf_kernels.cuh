@@ -7,7 +7,7 @@
 namespace rf {
 
 // ggml type ids (types.rs:238-270)
-enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12 };
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
 
 // Packed device form of one GGUF matrix (n_out rows of n_in elements).
 //
@@ -28,6 +28,15 @@ enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12 };
 // 1 KiB of consecutive bytes (piece `p` of 32 consecutive rows).  The scale
 // bytes of an item are contiguous too: sc[((tile*nk + chunk)*64 + row%64)*SB + b]
 // with SB = 16 (Q4_K header; Q4_0: eight f16) or 8 (Q8_0: four f16) bytes.
+//
+// Q6_K re-encodes its quants (the 6-bit values are kept, their bit positions
+// are not): a chunk is 128 elements, eight 16-element sub-blocks of three
+// 32-bit words each (q6k_sub_words), 96 bytes per row; piece p holds sub-blocks
+// 2p and 2p+1 (24 bytes), stored as a 16-byte plane (words 0-3 of the piece) of
+// the item's 64 rows followed by an 8-byte plane (words 4-5), so both warp-wide
+// loads stay contiguous.  The 12 header bytes of a row and chunk (the chunk's 8
+// int8 sub-block scales, then the super-block's f16 d and two zero bytes) are
+// split the same way: an 8-byte plane of the 64 rows, then a 4-byte plane.
 //
 // F32/F16 tensors stay row-major (qs_stride bytes per row, no sc).
 struct PackedMat {
@@ -53,20 +62,83 @@ constexpr int QT_CHUNK_BYTES = 128;  // quant bytes per row per chunk
 constexpr int QT_ITEM_BYTES = QT_ROWS * QT_CHUNK_BYTES;
 constexpr int QT_PIECES = 4;        // 32-byte pieces of a chunk row: the unit of the GEMV work split
 
-__host__ __device__ inline bool is_tiled(int type) { return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0; }
-__host__ __device__ inline int chunk_elems(int type) { return type == T_Q8_0 ? 128 : 256; }
-__host__ __device__ inline int chunk_scale_bytes(int type) { return type == T_Q8_0 ? 8 : 16; }
+constexpr int Q6_CHUNK_BYTES = 96;  // Q6_K quant bytes per row per chunk
+constexpr int Q6_PIECE_BYTES = 24;
+constexpr int Q6_HDR_BYTES = 12;
+
+__host__ __device__ inline bool is_tiled(int type) {
+  return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q6_K;
+}
+__host__ __device__ inline int chunk_elems(int type) { return type == T_Q8_0 || type == T_Q6_K ? 128 : 256; }
+__host__ __device__ inline int chunk_scale_bytes(int type) {
+  return type == T_Q8_0 ? 8 : type == T_Q6_K ? Q6_HDR_BYTES : 16;
+}
+__host__ __device__ inline int chunk_quant_bytes(int type) { return type == T_Q6_K ? Q6_CHUNK_BYTES : QT_CHUNK_BYTES; }
+// Elements per group of the GEMV's per-group x sums (one scale per group).
+__host__ __device__ inline int chunk_group_elems(int type) { return type == T_Q6_K ? 16 : 32; }
 
 // Byte b (0 <= b < qs_stride) of row r's quant bytes.
 __host__ __device__ inline uint64_t qs_byte_off(const PackedMat& W, uint32_t r, uint64_t b) {
   if (!is_tiled(W.type)) return (uint64_t)r * W.qs_stride + b;
+  if (W.type == T_Q6_K) {
+    const uint64_t item = (uint64_t)(r / QT_ROWS) * W.nk + b / Q6_CHUNK_BYTES;
+    const uint32_t o = (uint32_t)(b % Q6_CHUNK_BYTES), p = o / Q6_PIECE_BYTES, pb = o % Q6_PIECE_BYTES;
+    const uint64_t base = item * (QT_ROWS * Q6_CHUNK_BYTES) + (uint64_t)p * (QT_ROWS * Q6_PIECE_BYTES);
+    return pb < 16 ? base + (r % QT_ROWS) * 16 + pb : base + QT_ROWS * 16 + (r % QT_ROWS) * 8 + (pb - 16);
+  }
   const uint64_t item = (uint64_t)(r / QT_ROWS) * W.nk + b / QT_CHUNK_BYTES;
   return (item * 4 + (b / 32) % 4) * (QT_ROWS * 32) + (uint64_t)(r % QT_ROWS) * 32 + b % 32;
 }
 // Byte b (0 <= b < sc_stride) of row r's scale bytes.
 __host__ __device__ inline uint64_t sc_byte_off(const PackedMat& W, uint32_t r, uint64_t b) {
   const uint64_t item = (uint64_t)(r / QT_ROWS) * W.nk + b / W.sbytes;
+  if (W.type == T_Q6_K) {
+    const uint32_t o = (uint32_t)(b % Q6_HDR_BYTES);
+    const uint64_t base = item * (QT_ROWS * Q6_HDR_BYTES);
+    return o < 8 ? base + (r % QT_ROWS) * 8 + o : base + QT_ROWS * 8 + (r % QT_ROWS) * 4 + (o - 8);
+  }
   return (item * QT_ROWS + r % QT_ROWS) * W.sbytes + b % W.sbytes;
+}
+
+// 6-bit value q+32 of element e (0..255) of a GGUF Q6_K block (BlockQ6K::dequantize,
+// quant.rs:376-406: low nibble from ql, high bit pair from qh).
+__host__ __device__ inline uint32_t q6k_value(const uint8_t* blk, int e) {
+  const int h = e >> 7, l = e & 31, k = (e >> 5) & 3;
+  const uint8_t lq = blk[64 * h + l + 32 * (k & 1)];
+  const uint32_t lo = k < 2 ? (lq & 15u) : (uint32_t)(lq >> 4);
+  return lo | ((uint32_t)((blk[128 + 32 * h + l] >> (2 * k)) & 3) << 4);
+}
+// The three packed words of 16-element sub-block j (0..15) of a GGUF Q6_K block:
+// values u0..u15, A = u0..u3 at bits 0/6/12/18, B = u4..u7, C = u8..u11 likewise,
+// and the top bytes of A, B, C together hold u12..u15 at bits 0/6/12/18 of
+// A[31:24] | B[31:24] << 8 | C[31:24] << 16.  Every field then lies below bit 24.
+__host__ __device__ inline void q6k_sub_words(const uint8_t* blk, int j, uint32_t out[3]) {
+  uint32_t u[16];
+  for (int t = 0; t < 16; t++) u[t] = q6k_value(blk, 16 * j + t);
+  const uint32_t T = u[12] | (u[13] << 6) | (u[14] << 12) | (u[15] << 18);
+  for (int k = 0; k < 3; k++)
+    out[k] = u[4 * k] | (u[4 * k + 1] << 6) | (u[4 * k + 2] << 12) | (u[4 * k + 3] << 18) | (((T >> (8 * k)) & 0xFFu) << 24);
+}
+// Scatter GGUF Q6_K block k (256 elements at s) of a row into packed row r of g
+// (quant bytes into Q, header bytes into C; the zero padding is left as is).
+// Used by the device and the host packers alike.
+__host__ __device__ inline void q6k_pack_block(const PackedMat& g, uint8_t* Q, uint8_t* C, uint32_t r, uint32_t k,
+                                               const uint8_t* s) {
+  for (int j = 0; j < 16; j++) {
+    uint32_t w[3];
+    q6k_sub_words(s, j, w);
+    const uint64_t b = (uint64_t)(2 * k + j / 8) * Q6_CHUNK_BYTES + 12 * (j % 8);
+    for (int t = 0; t < 3; t++) {
+      uint8_t* p = Q + qs_byte_off(g, r, b + 4 * t);  // a word never straddles a plane
+      for (int i = 0; i < 4; i++) p[i] = (uint8_t)(w[t] >> (8 * i));
+    }
+  }
+  for (int h = 0; h < 2; h++) {
+    const uint64_t hb = (uint64_t)(2 * k + h) * Q6_HDR_BYTES;
+    for (int i = 0; i < 8; i++) C[sc_byte_off(g, r, hb + i)] = s[192 + 8 * h + i];
+    C[sc_byte_off(g, r, hb + 8)] = s[208];
+    C[sc_byte_off(g, r, hb + 9)] = s[209];
+  }
 }
 // Device bytes of the two streams.
 inline uint64_t packed_qs_bytes(const PackedMat& W) { return (uint64_t)W.Mp * W.qs_stride; }
@@ -84,7 +156,7 @@ __host__ __device__ inline int block_elems(int type) {
   switch (type) {
     case T_F32: case T_F16: return 1;
     case T_Q4_0: case T_Q8_0: return 32;
-    case T_Q4_K: return 256;
+    case T_Q4_K: case T_Q6_K: return 256;
     default: return 0;
   }
 }
@@ -95,6 +167,7 @@ __host__ __device__ inline int block_bytes(int type) {
     case T_Q4_0: return 18;
     case T_Q8_0: return 34;
     case T_Q4_K: return 144;
+    case T_Q6_K: return 210;
     default: return 0;
   }
 }
@@ -153,6 +226,11 @@ struct RopeQKVArgs {
   void* kcache;           // [kv_heads][max_seq][head_dim]
   void* vcache;
   int kv_f32;
+  // Packed [Q;K;V] row of the matrix's row 0: 0 for the fused matrix (or [Q;K]),
+  // q_rows + kv_rows for a separate V matrix.
+  uint32_t row_base;
+  // Q/K/V biases in packed [Q;K;V] row order, added before RoPE (null: none).
+  const float* bias;
 };
 // Fused: RMSNorm(attn_norm) -> packed [Q;K;V] matvec -> RoPE on Q/K pairs -> K/V append.
 cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,

@@ -6,8 +6,8 @@
 //   * GGUF v3 layout as parse_gguf_file reads it (crates/ramforge-core/src/gguf.rs:196-330):
 //     header, metadata KV, tensor infos, data section aligned to 32 bytes,
 //     every tensor offset aligned to 32 relative to the data start;
-//   * Q8_0 / Q4_0 / Q4_K encoders written from the block layouts the decoders
-//     read (crates/ramforge-core/src/quant.rs:84-255).  Encoder quality does
+//   * Q8_0 / Q4_0 / Q4_K / Q6_K encoders written from the block layouts the
+//     decoders read (crates/ramforge-core/src/quant.rs:84-255, 376-406).  Encoder quality does
 //     not matter for parity: the engine and the checker read the same bytes.
 // Weights are N(0, std) from a counter-based generator (splitmix64 + Box-Muller
 // in double precision), so any row of any tensor can be produced independently
@@ -164,11 +164,53 @@ void enc_q4_k(const float* x, uint8_t* b) {
     for (int l = 0; l < 32; l++) qs[32 * g + l] = (uint8_t)(q[64 * g + l] | (q[64 * g + 32 + l] << 4));
 }
 
+// Q6_K: per 16-element sub-block a symmetric scale amax/31, quantised to int8
+// against the f16 super-scale d = max scale/127; value (d*sc)*q with q in
+// [-32, 31] stored as q+32.  Bytes as BlockQ6K::dequantize reads them
+// (quant.rs:376-406): for half h and l < 32, element 128h+l+32k takes the
+// low (k < 2) or high nibble of ql[64h + l + 32(k&1)] and bits 2k..2k+1 of
+// qh[32h + l]; sub-block j of the super-block uses scales[j]; d at byte 208.
+void enc_q6_k(const float* x, uint8_t* b) {
+  float scale[16];
+  for (int j = 0; j < 16; j++) {
+    float amax = 0.f;
+    for (int l = 0; l < 16; l++) amax = std::max(amax, std::fabs(x[16 * j + l]));
+    scale[j] = amax / 31.f;
+  }
+  const float ms = *std::max_element(scale, scale + 16);
+  const uint16_t dh = f32_to_f16(ms / 127.f);
+  const float d = f16_to_f32(dh);
+  int8_t sc[16];
+  for (int j = 0; j < 16; j++) {
+    const int s = d > 0.f ? (int)std::lrint(scale[j] / d) : 0;
+    sc[j] = (int8_t)std::min(127, std::max(-128, s));
+  }
+  uint8_t u[256];
+  for (int j = 0; j < 16; j++) {
+    const float S = d * (float)sc[j], iS = S != 0.f ? 1.0f / S : 0.f;
+    for (int l = 0; l < 16; l++) {
+      const int q = (int)std::lrintf(x[16 * j + l] * iS);
+      u[16 * j + l] = (uint8_t)(std::min(31, std::max(-32, q)) + 32);
+    }
+  }
+  uint8_t* ql = b;
+  uint8_t* qh = b + 128;
+  for (int h = 0; h < 2; h++)
+    for (int l = 0; l < 32; l++) {
+      const uint8_t* v = u + 128 * h + l;  // v[32k]: element 128h + l + 32k
+      ql[64 * h + l] = (uint8_t)((v[0] & 15) | ((v[64] & 15) << 4));
+      ql[64 * h + 32 + l] = (uint8_t)((v[32] & 15) | ((v[96] & 15) << 4));
+      qh[32 * h + l] = (uint8_t)((v[0] >> 4) | ((v[32] >> 4) << 2) | ((v[64] >> 4) << 4) | ((v[96] >> 4) << 6));
+    }
+  for (int j = 0; j < 16; j++) b[192 + j] = (uint8_t)sc[j];
+  put16(b + 208, dh);
+}
+
 size_t block_elems(int type) {
   switch (type) {
     case RFS_F32: case RFS_F16: return 1;
     case RFS_Q4_0: case RFS_Q8_0: return 32;
-    case RFS_Q4_K: return 256;
+    case RFS_Q4_K: case RFS_Q6_K: return 256;
     default: return 0;
   }
 }
@@ -179,6 +221,7 @@ size_t block_bytes(int type) {
     case RFS_Q4_0: return 18;
     case RFS_Q8_0: return 34;
     case RFS_Q4_K: return 144;
+    case RFS_Q6_K: return 210;
     default: return 0;
   }
 }
@@ -194,6 +237,7 @@ void encode_row(int type, const float* x, size_t n, uint8_t* out) {
       case RFS_Q4_0: enc_q4_0(xb, ob); break;
       case RFS_Q8_0: enc_q8_0(xb, ob); break;
       case RFS_Q4_K: enc_q4_k(xb, ob); break;
+      case RFS_Q6_K: enc_q6_k(xb, ob); break;
     }
   }
 }
@@ -217,27 +261,34 @@ struct TensorPlan {
   int ndims, type;
   bool ones;          // norm weights: constant 1.0
   uint64_t offset, bytes, stream;
+  float stddev;       // 0: the spec's weight_std
 };
 
 std::vector<TensorPlan> plan_llama(const rfs_llama_spec* s) {
   std::vector<TensorPlan> t;
   uint64_t hd = s->n_embd / s->n_heads, qd = hd * s->n_heads, kvd = hd * s->n_kv_heads;
   uint64_t stream = 0;
-  auto add = [&](const std::string& n, uint64_t ne0, uint64_t ne1, int nd, int ty, bool ones) {
-    t.push_back({n, ne0, ne1, nd, ty, ones, 0, 0, stream++});
+  auto add = [&](const std::string& n, uint64_t ne0, uint64_t ne1, int nd, int ty, bool ones, float sd = 0.f) {
+    t.push_back({n, ne0, ne1, nd, ty, ones, 0, 0, stream++, sd});
   };
+  const int vt = s->v_type >= 0 ? s->v_type : s->layer_type, dt = s->down_type >= 0 ? s->down_type : s->layer_type;
   add("token_embd.weight", s->n_embd, s->vocab_size, 2, s->embd_type, false);
   for (uint32_t l = 0; l < s->n_layers; l++) {
     std::string p = "blk." + std::to_string(l) + ".";
     add(p + "attn_norm.weight", s->n_embd, 1, 1, RFS_F32, true);
     add(p + "attn_q.weight", s->n_embd, qd, 2, s->layer_type, false);
     add(p + "attn_k.weight", s->n_embd, kvd, 2, s->layer_type, false);
-    add(p + "attn_v.weight", s->n_embd, kvd, 2, s->layer_type, false);
+    add(p + "attn_v.weight", s->n_embd, kvd, 2, vt, false);
+    if (s->qkv_bias_std > 0.f) {
+      add(p + "attn_q.bias", qd, 1, 1, RFS_F32, false, s->qkv_bias_std);
+      add(p + "attn_k.bias", kvd, 1, 1, RFS_F32, false, s->qkv_bias_std);
+      add(p + "attn_v.bias", kvd, 1, 1, RFS_F32, false, s->qkv_bias_std);
+    }
     add(p + "attn_output.weight", qd, s->n_embd, 2, s->layer_type, false);
     add(p + "ffn_norm.weight", s->n_embd, 1, 1, RFS_F32, true);
     add(p + "ffn_gate.weight", s->n_embd, s->n_ff, 2, s->layer_type, false);
     add(p + "ffn_up.weight", s->n_embd, s->n_ff, 2, s->layer_type, false);
-    add(p + "ffn_down.weight", s->n_ff, s->n_embd, 2, s->layer_type, false);
+    add(p + "ffn_down.weight", s->n_ff, s->n_embd, 2, dt, false);
   }
   add("output_norm.weight", s->n_embd, 1, 1, RFS_F32, true);
   if (s->out_type >= 0) add("output.weight", s->n_embd, s->vocab_size, 2, s->out_type, false);
@@ -303,6 +354,8 @@ bool spec_ok(const rfs_llama_spec* s) {
     if (!qk || s->n_embd % qk || s->n_ff % qk || (hd * s->n_heads) % qk) return false;
   }
   if (s->out_type >= 0 && (!block_elems(s->out_type) || s->n_embd % block_elems(s->out_type))) return false;
+  if (s->v_type >= 0 && (!block_elems(s->v_type) || s->n_embd % block_elems(s->v_type))) return false;
+  if (s->down_type >= 0 && (!block_elems(s->down_type) || s->n_ff % block_elems(s->down_type))) return false;
   return true;
 }
 
@@ -370,7 +423,8 @@ int rfs_llama_gguf_write(const rfs_llama_spec* s, uint8_t* out, uint64_t cap, in
       std::vector<float> row(t.ne0);
       for (size_t r = a; r < b; r++) {
         if (t.ones) std::fill(row.begin(), row.end(), 1.0f);
-        else rfs_fill_normal(s->seed, key_stream, s->weight_std, (uint64_t)r * t.ne0, row.data(), t.ne0);
+        else rfs_fill_normal(s->seed, key_stream, t.stddev > 0.f ? t.stddev : s->weight_std, (uint64_t)r * t.ne0,
+                             row.data(), t.ne0);
         encode_row(t.type, row.data(), t.ne0, dst + r * rb);
       }
     });

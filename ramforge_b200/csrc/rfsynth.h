@@ -10,7 +10,7 @@
 extern "C" {
 #endif
 
-enum { RFS_F32 = 0, RFS_F16 = 1, RFS_Q4_0 = 2, RFS_Q8_0 = 8, RFS_Q4_K = 12 };
+enum { RFS_F32 = 0, RFS_F16 = 1, RFS_Q4_0 = 2, RFS_Q8_0 = 8, RFS_Q4_K = 12, RFS_Q6_K = 14 };
 
 typedef struct {
   const char* arch; /* "llama" (default) or "qwen2" */
@@ -21,6 +21,9 @@ typedef struct {
   int out_type;   /* output.weight; -1 = absent (tied to token_embd) */
   uint64_t seed;
   float weight_std;
+  int v_type;         /* attn_v.weight type; -1 = layer_type (Q4_K_M-style mixes use Q6_K) */
+  int down_type;      /* ffn_down.weight type; -1 = layer_type */
+  float qkv_bias_std; /* > 0: F32 blk.N.attn_{q,k,v}.bias of N(0, qkv_bias_std) (qwen2); 0 = none */
 } rfs_llama_spec;
 
 /* out[i] = N(0, stddev) sample #(start+i) of stream (seed, stream). */

@@ -92,13 +92,14 @@ class DecodeEngine:
         check(lib().rf_layer_load_gguf(self._h, layer))
 
     def load_layer_views(self, layer: int, tensors: dict):
-        """rf_layer_load with host tensors: {role_name: (ggml_type, ne0, ne1, uint8 array)}."""
+        """rf_layer_load with host tensors: {role_name: (ggml_type, ne0, ne1, uint8 array)}; role names
+        are the nine weights ("attn_q", ...) and the optional biases ("attn_q.bias", ...)."""
         views = (_lib.TensorView * len(tensors))()
         keep = []
         for i, (name, (gtype, ne0, ne1, data)) in enumerate(tensors.items()):
             arr = np.ascontiguousarray(data, np.uint8)
             keep.append(arr)
-            views[i] = _lib.TensorView(_lib.ROLE_NAMES.index(name), gtype, ne0, ne1, arr.ctypes.data, arr.size)
+            views[i] = _lib.TensorView(_lib.LAYER_VIEW_NAMES.index(name), gtype, ne0, ne1, arr.ctypes.data, arr.size)
         check(lib().rf_layer_load(self._h, layer, views, len(tensors)))
 
     def release_layer(self, layer: int):

@@ -17,8 +17,8 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 SYNTH_PATH = os.path.join(_HERE, "librfsynth.so")
 
-F32, F16, Q4_0, Q8_0, Q4_K = 0, 1, 2, 8, 12
-TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q8_0: "Q8_0", Q4_K: "Q4_K"}
+F32, F16, Q4_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 8, 12, 14
+TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
 
 
 class _Spec(ctypes.Structure):
@@ -26,7 +26,8 @@ class _Spec(ctypes.Structure):
         "vocab_size", "context_length", "n_embd", "n_layers", "n_ff", "n_heads", "n_kv_heads")] + [
         ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("layer_type", ctypes.c_int),
         ("embd_type", ctypes.c_int), ("out_type", ctypes.c_int), ("seed", ctypes.c_uint64),
-        ("weight_std", ctypes.c_float)]
+        ("weight_std", ctypes.c_float), ("v_type", ctypes.c_int), ("down_type", ctypes.c_int),
+        ("qkv_bias_std", ctypes.c_float)]
 
 
 _lib = None
@@ -73,6 +74,9 @@ class LlamaSpec:
     seed: int = 0
     weight_std: float = 0.02
     arch: str = "llama"
+    v_type: int = -1        # attn_v type; -1: layer_type (Q4_K_M-style mixes use Q6_K)
+    down_type: int = -1     # ffn_down type; -1: layer_type
+    qkv_bias_std: float = 0.0  # > 0: qwen2 Q/K/V biases of N(0, qkv_bias_std)
 
     @property
     def head_dim(self) -> int:
@@ -106,7 +110,7 @@ def gguf_bytes(spec: LlamaSpec, threads: int | None = None) -> np.ndarray:
     """Generate the GGUF image of `spec` in memory (uint8 array)."""
     s = _Spec(spec.arch.encode(), spec.vocab_size, spec.context_length, spec.n_embd, spec.n_layers, spec.n_ff,
               spec.n_heads, spec.n_kv_heads, spec.rms_eps, spec.rope_theta, spec.layer_type, spec.embd_type,
-              spec.out_type, spec.seed, spec.weight_std)
+              spec.out_type, spec.seed, spec.weight_std, spec.v_type, spec.down_type, spec.qkv_bias_std)
     n = lib().rfs_llama_gguf_size(ctypes.byref(s))
     if n == 0:
         raise ValueError(f"invalid synthetic spec {spec}")

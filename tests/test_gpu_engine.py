@@ -26,11 +26,15 @@ SMALL_Q8 = synth.scaled(synth.TINYLLAMA, name="small-q8", vocab_size=777, n_embd
 SMALL_Q40 = synth.scaled(synth.TINYLLAMA, name="small-q40", vocab_size=500, n_embd=256, n_layers=2, n_ff=640,
                          n_heads=4, n_kv_heads=4, seed=23, context_length=256, layer_type=synth.Q4_0,
                          embd_type=synth.Q4_0, out_type=-1)
+# Q6_K everywhere: every GEMV epilogue, the embedding row and the LM head in Q6_K
+SMALL_Q6K = synth.scaled(synth.LLAMA3_8B, name="small-q6k", vocab_size=700, n_embd=512, n_layers=2, n_ff=1536,
+                         n_heads=8, n_kv_heads=2, seed=24, context_length=256, layer_type=synth.Q6_K,
+                         embd_type=synth.Q6_K, out_type=synth.Q6_K)
 
 
 @pytest.fixture(scope="module")
 def models():
-    return {s.name: synth.gguf_bytes(s) for s in (SMALL_Q4K, SMALL_Q8, SMALL_Q40)}
+    return {s.name: synth.gguf_bytes(s) for s in (SMALL_Q4K, SMALL_Q8, SMALL_Q40, SMALL_Q6K)}
 
 
 def rel_err(a, b):
@@ -89,7 +93,7 @@ def test_gqa_fixture_greedy_generation():
     assert eng.generate([1, 3], 12).tolist() == ref.tolist()  # deterministic (inference.rs:2567-2571)
 
 
-@pytest.mark.parametrize("name", ["small-q4k", "small-q8", "small-q40"])
+@pytest.mark.parametrize("name", ["small-q4k", "small-q8", "small-q40", "small-q6k"])
 def test_small_models_stepwise_parity(models, name):
     g = models[name]
     rng = np.random.default_rng(5)
@@ -154,6 +158,24 @@ def test_layer_level_api_matches_oracle(models):
                 a = eng.kv_read(l, which, 0, pos + 1)
                 b = ref.kv_read(l, which, 0, pos + 1)
                 assert np.abs(a - b).max() <= 2e-3 * max(1.0, np.abs(b).max()), (pos, l, which)
+    eng.close()
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_q6_k_model_embedding_rows_and_greedy_generation(models, graphs):
+    g = models["small-q6k"]
+    eng = DecodeEngine(g, max_seq_len=64, disable_graphs=not graphs)
+    d = eng.config["n_embd"]
+    rb = orc.row_bytes(orc.Q6_K, d)
+    emb = _tensor_bytes(g, "token_embd.weight")
+    for tok in (0, 1, 345, eng.config["vocab_size"] - 1):
+        eng.embed(tok)
+        assert np.array_equal(eng.hidden(), orc.dequant_row(orc.Q6_K, emb[tok * rb:(tok + 1) * rb], d)), tok
+    eng.kv_reset()
+    prompt = [11, 402, 7, 650, 3]
+    want, _, margins = orc.OracleModel(g, kv_f16=True, max_seq=64, threads=THREADS).generate(prompt, 24)
+    got = eng.generate(prompt, 24)
+    assert got.tolist() == want.tolist(), (got, want, margins)
     eng.close()
 
 

@@ -44,7 +44,7 @@ def _run_qmv(gtype, M, K, batch=1, seed=1, raw=None):
     m.close()
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.F16, synth.F32])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, synth.F16, synth.F32])
 @pytest.mark.parametrize("M,K", [(1, 256), (7, 512), (33, 768), (130, 2304), (257, 4096)])
 def test_qmatvec_small_shapes(gtype, M, K):
     _run_qmv(gtype, M, K)
@@ -56,13 +56,13 @@ def test_qmatvec_ragged_rows_padded_to_units(gtype, M, K):
     _run_qmv(gtype, M, K)
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K])
 @pytest.mark.parametrize("M,K", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
 def test_qmatvec_config2_shapes(gtype, M, K):
     _run_qmv(gtype, M, K)
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K])
 @pytest.mark.parametrize("batch", [4, 8])
 def test_qmatvec_batched(gtype, batch):
     _run_qmv(gtype, 1024, 4096, batch=batch)
@@ -75,6 +75,40 @@ def test_qmatvec_subnormal_scales_follow_reference_decode():
     for r in range(4):
         raw[r * 68:r * 68 + 2] = (0x0155 + r).to_bytes(2, "little")
     _run_qmv(synth.Q8_0, 4, 64, raw=np.frombuffer(bytes(raw), np.uint8))
+
+
+def test_qmatvec_q6_k_subnormal_super_scale_follows_reference_decode():
+    # Q6_K's f16 d sits at bytes 208-209 of each 210-byte block; rows 1 and 3 get
+    # a subnormal one.
+    raw = bytearray(_weights(synth.Q6_K, 4, 512))
+    for r in (1, 3):
+        for b in range(2):
+            o = (r * 2 + b) * 210 + 208
+            raw[o:o + 2] = (0x0123 + b).to_bytes(2, "little")
+    _run_qmv(synth.Q6_K, 4, 512, raw=np.frombuffer(bytes(raw), np.uint8))
+
+
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, synth.F16])
+def test_device_packing_equals_host_packing(gtype):
+    # rf_matrix_create packs device-resident GGUF bytes with the pack kernel and
+    # host bytes on the CPU; both must give the same packed matrix, so the same
+    # products bit for bit.
+    torch = torch_mod()
+    M, K = 193, 1024
+    raw = _weights(gtype, M, K, seed=4)
+    x = torch.from_numpy(synth.normal(4, 7, K, std=1.0)).cuda()
+    draw = torch.from_numpy(np.ascontiguousarray(raw)).cuda()
+    a = QMatrix(gtype, raw, M, K)
+    b = QMatrix(gtype, None, M, K, on_device_ptr=draw.data_ptr(), nbytes=raw.size)
+    assert a.device_bytes == b.device_bytes
+    ya = torch.empty(M, device="cuda")
+    yb = torch.empty(M, device="cuda")
+    a.matvec(x.data_ptr(), ya.data_ptr())
+    b.matvec(x.data_ptr(), yb.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(ya, yb)
+    a.close()
+    b.close()
 
 
 @pytest.mark.parametrize("ctx", [1, 5, 512, 2048, 8192, 32768])

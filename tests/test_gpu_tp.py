@@ -19,6 +19,10 @@ THREADS = min(32, os.cpu_count() or 8)
 # Q4_K super-block boundaries.
 TP_MODEL = synth.scaled(synth.LLAMA3_8B, name="tp-q4k", vocab_size=1024, n_embd=2048, n_layers=2, n_ff=4096,
                         n_heads=16, n_kv_heads=8, seed=51, context_length=128)
+# A Q4_K_M-like qwen2 layout: Q6_K V (its own matrix), down and LM head, Q/K/V biases
+# sharded with their heads.
+TP_MIX = synth.scaled(TP_MODEL, name="tp-qwen2-mix", arch="qwen2", seed=52, v_type=synth.Q6_K, down_type=synth.Q6_K,
+                      out_type=synth.Q6_K, qkv_bias_std=0.5)
 
 
 def _gpu_count():
@@ -41,18 +45,36 @@ def _rank(rank, world, path, nid, prompt, n_new, peer_sum, q):
         q.put((rank, None, None, repr(ex)))
 
 
-@pytest.fixture(scope="module")
-def model(tmp_path_factory):
-    g = synth.gguf_bytes(TP_MODEL)
-    path = str(tmp_path_factory.mktemp("tp") / "tp.gguf")
+def _model(tmp_path_factory, spec):
+    g = synth.gguf_bytes(spec)
+    path = str(tmp_path_factory.mktemp("tp") / f"{spec.name}.gguf")
     g.tofile(path)
-    prompt = np.random.default_rng(6).integers(0, TP_MODEL.vocab_size, 7).tolist()
+    prompt = np.random.default_rng(6).integers(0, spec.vocab_size, 7).tolist()
     want = orc.OracleModel(g, kv_f16=True, max_seq=64, threads=THREADS).generate(prompt, 16)[0].tolist()
     return path, prompt, want
 
 
+@pytest.fixture(scope="module")
+def model(tmp_path_factory):
+    return _model(tmp_path_factory, TP_MODEL)
+
+
+@pytest.fixture(scope="module")
+def mixed_model(tmp_path_factory):
+    return _model(tmp_path_factory, TP_MIX)
+
+
 @pytest.mark.parametrize("world,peer_sum", [(2, True), (2, False), (4, True), (8, True)])
 def test_tp_greedy_matches_oracle(model, world, peer_sum):
+    _run_tp(model, world, peer_sum)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_mixed_format_biased_model_matches_oracle(mixed_model, world):
+    _run_tp(mixed_model, world, True)
+
+
+def _run_tp(model, world, peer_sum):
     if _gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")
     path, prompt, want = model

@@ -298,6 +298,41 @@ def test_gqa_forward_matches_scalar_reference():
         assert m.kv_read(0, False, 0, pos + 1).size == (pos + 1) * fx.GQA_N_KV_HEADS * fx.GQA_HEAD_DIM
 
 
+# ---- qwen2 Q/K/V biases (inference.rs:1995-2077, streaming_model.rs:3256-3330) ----
+def test_qwen2_biased_forward_matches_reference():
+    m = orc.OracleModel(fx.qwen2_bias_gguf(), kv_f16=False, max_seq=4)
+    assert (m.config["n_heads"], m.config["n_kv_heads"], m.config["head_dim"]) == (2, 2, 4)
+    w = fx.qwen2_bias_weights()
+    kh, vh = [], []
+    EPS = 2e-4
+    for tok, pos in [(1, 0), (5, 1)]:  # no history, then history + biases + RoPE at pos 1
+        hidden = m.forward(tok, pos)
+        ref_h = fx.qwen2_bias_reference_forward(w, tok, pos, kh, vh)
+        assert np.all(np.abs(hidden - ref_h) < EPS), (pos, hidden, ref_h)
+        ref_logits = w["embd"].reshape(fx.QB_VOCAB, fx.QB_N_EMBD) @ ref_h
+        assert np.all(np.abs(m.logits(hidden) - ref_logits) < EPS)
+    # the biases change the result: the fixture without them is measurably different
+    nb = {k: v for k, v in w.items() if not k.startswith("bias_")}
+    assert np.abs(fx.qwen2_bias_reference_forward(nb, 1, 0, [], []) -
+                  fx.qwen2_bias_reference_forward(w, 1, 0, [], [])).max() > 10 * EPS
+    g = fx.qwen2_bias_gguf()
+    t1 = orc.OracleModel(g, kv_f16=False, max_seq=16).generate([1, 3], 4)[0]
+    t2 = orc.OracleModel(g, kv_f16=False, max_seq=16).generate([1, 3], 4)[0]
+    assert len(t1) == 4 and t1.tolist() == t2.tolist()
+
+
+def test_qwen2_partial_bias_set_rejected():
+    m = orc.OracleModel(fx.qwen2_bias_gguf("only_q"), kv_f16=False, max_seq=4)
+    with pytest.raises(orc.OracleError, match="incomplete Q/K/V bias"):
+        m.forward(1, 0)
+
+
+def test_qwen2_bias_shape_mismatch_rejected():
+    m = orc.OracleModel(fx.qwen2_bias_gguf("wrong_dim"), kv_f16=False, max_seq=4)
+    with pytest.raises(orc.OracleError, match="attn_q.bias.*shape"):
+        m.forward(1, 0)
+
+
 def test_gqa_greedy_generation_is_deterministic():  # inference.rs:2567-2571
     g = fx.gqa_gguf()
     t1 = orc.OracleModel(g, kv_f16=False, max_seq=16).generate([1, 3], 5)[0]

@@ -41,7 +41,8 @@ def test_generated_gguf_parses_in_oracle_and_engine():
     assert c.as_dict() == cfg
 
 
-@pytest.mark.parametrize("gtype,tol", [(synth.Q8_0, 0.6 / 127), (synth.Q4_0, 0.6 / 7), (synth.Q4_K, 0.12)])
+@pytest.mark.parametrize("gtype,tol", [(synth.Q8_0, 0.6 / 127), (synth.Q4_0, 0.6 / 7), (synth.Q4_K, 0.12),
+                                      (synth.Q6_K, 0.6 / 31)])
 def test_encoders_round_trip_through_reference_decoder(gtype, tol):
     x = synth.normal(1, 7, 64 * 512, std=1.0).reshape(64, 512)
     raw = synth.quantize(gtype, x)
