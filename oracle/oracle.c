@@ -114,8 +114,12 @@ static int type_block(int type, size_t* qk, size_t* bsz) {
     case ORC_Q4_0: *qk = 32; *bsz = 18; return 1;
     case ORC_Q5_0: *qk = 32; *bsz = 22; return 1;
     case ORC_Q8_0: *qk = 32; *bsz = 34; return 1;
+    case ORC_Q2_K: *qk = 256; *bsz = 84; return 1;
+    case ORC_Q3_K: *qk = 256; *bsz = 110; return 1;
     case ORC_Q4_K: *qk = 256; *bsz = 144; return 1;
+    case ORC_Q5_K: *qk = 256; *bsz = 176; return 1;
     case ORC_Q6_K: *qk = 256; *bsz = 210; return 1;
+    case ORC_Q8_K: *qk = 256; *bsz = 292; return 1;
     default: return 0;
   }
 }
@@ -191,6 +195,108 @@ static void dq_q4_k(const uint8_t* b, float* out) {
   }
 }
 
+/* BlockQ5K::dequantize (quant.rs:303-343): per 64 elements d1 = d*sc, min1 = dmin*m
+ * (get_scale_min as Q4_K's, :288-299), value = d1*(q + 16*high) - min1.  The high
+ * bit of element l of group g is bit 2g (low nibbles) or 2g+1 (high nibbles) of
+ * qh[8g + l/8], the reference's own indexing. */
+static void dq_q5_k(const uint8_t* b, float* out) {
+  float d = rd_f16(b), dmin = rd_f16(b + 2);
+  const uint8_t* s = b + 4;
+  const uint8_t* qh = b + 16;
+  const uint8_t* qs = b + 48;
+  int y = 0, is = 0, qo = 0;
+  uint8_t u1 = 1, u2 = 2;
+  for (int g = 0; g < 4; g++) {
+    uint8_t sc0, m0, sc1, m1;
+    q4k_scale_min(s, is, &sc0, &m0);
+    q4k_scale_min(s, is + 1, &sc1, &m1);
+    float d1 = d * (float)sc0, min1 = dmin * (float)m0;
+    float d2 = d * (float)sc1, min2 = dmin * (float)m1;
+    for (int l = 0; l < 32; l++) {
+      int q = (qs[qo + l] & 0xF) + ((qh[qo / 4 + l / 8] & u1) ? 16 : 0);
+      out[y + l] = d1 * (float)q - min1;
+    }
+    y += 32;
+    for (int l = 0; l < 32; l++) {
+      int q = (qs[qo + l] >> 4) + ((qh[qo / 4 + l / 8] & u2) ? 16 : 0);
+      out[y + l] = d2 * (float)q - min2;
+    }
+    y += 32;
+    qo += 32;
+    is += 2;
+    u1 = (uint8_t)(u1 << 2);
+    u2 = (uint8_t)(u2 << 2);
+  }
+}
+
+/* BlockQ2K::dequantize (quant.rs:443-474): 16 scale bytes (low nibble scale, high
+ * nibble min), value = (d*sc)*q - dmin*m for 2-bit q. */
+static void dq_q2_k(const uint8_t* b, float* out) {
+  const uint8_t* sc = b;
+  const uint8_t* qs = b + 16;
+  float d = rd_f16(b + 80), dmin = rd_f16(b + 82);
+  int y = 0, is = 0, qo = 0;
+  for (int n = 0; n < 2; n++) {
+    int shift = 0;
+    for (int j = 0; j < 4; j++) {
+      for (int half = 0; half < 2; half++) {
+        uint8_t v = sc[is++];
+        float dl = d * (float)(v & 0xF), ml = dmin * (float)(v >> 4);
+        for (int l = 0; l < 16; l++) out[y + l] = dl * (float)((qs[qo + 16 * half + l] >> shift) & 3) - ml;
+        y += 16;
+      }
+      shift += 2;
+    }
+    qo += 32;
+  }
+}
+
+/* BlockQ3K::dequantize (quant.rs:506-574): the 12 scale bytes unpack to 16 six-bit
+ * scales (minus 32); q = 2 low bits - (hmask bit clear ? 4 : 0); value (d*sc)*q.
+ * As in the reference, both 128-element halves use scales 0-7 (j and j+4). */
+static void dq_q3_k(const uint8_t* b, float* out) {
+  const uint8_t* hm = b;
+  const uint8_t* qs = b + 32;
+  const uint8_t* sb = b + 96;
+  float d = rd_f16(b + 108);
+  uint32_t aux[4];
+  for (int i = 0; i < 3; i++) aux[i] = (uint32_t)sb[4 * i] | ((uint32_t)sb[4 * i + 1] << 8) |
+                                       ((uint32_t)sb[4 * i + 2] << 16) | ((uint32_t)sb[4 * i + 3] << 24);
+  const uint32_t k1 = 0x03030303u, k2 = 0x0F0F0F0Fu, tmp = aux[2], a0 = aux[0], a1 = aux[1];
+  aux[2] = ((a0 >> 4) & k2) | (((tmp >> 4) & k1) << 4);
+  aux[3] = ((a1 >> 4) & k2) | (((tmp >> 6) & k1) << 4);
+  aux[0] = (a0 & k2) | (((tmp >> 0) & k1) << 4);
+  aux[1] = (a1 & k2) | (((tmp >> 2) & k1) << 4);
+  int8_t s8[16];
+  for (int i = 0; i < 16; i++) s8[i] = (int8_t)(uint8_t)(aux[i / 4] >> (8 * (i % 4)));
+  int y = 0, qo = 0;
+  uint8_t m = 1;
+  for (int n = 0; n < 2; n++) {
+    int shift = 0;
+    for (int j = 0; j < 4; j++) {
+      for (int half = 0; half < 2; half++) {
+        float dl = d * (float)((int)s8[j + 4 * half] - 32);
+        for (int l = 0; l < 16; l++) {
+          int q = (qs[qo + 16 * half + l] >> shift) & 3;
+          q -= (hm[16 * half + l] & m) ? 0 : 4;
+          out[y + l] = dl * (float)q;
+        }
+        y += 16;
+      }
+      shift += 2;
+      m = (uint8_t)(m << 1);
+    }
+    qo += 32;
+  }
+}
+
+/* BlockQ8K::dequantize (quant.rs:605-609): f32 d, value d*q. */
+static void dq_q8_k(const uint8_t* b, float* out) {
+  float d;
+  memcpy(&d, b, 4);
+  for (int i = 0; i < 256; i++) out[i] = d * (float)(int8_t)b[4 + i];
+}
+
 /* BlockQ6K::dequantize (quant.rs:376-406): value = (d*sc)*q. */
 static void dq_q6_k(const uint8_t* b, float* out) {
   const uint8_t* ql = b;
@@ -236,6 +342,10 @@ int orc_dequant_row(int type, const uint8_t* bytes, size_t nbytes, size_t n, flo
       case ORC_Q8_0: dq_q8_0(b, o); break;
       case ORC_Q4_K: dq_q4_k(b, o); break;
       case ORC_Q6_K: dq_q6_k(b, o); break;
+      case ORC_Q2_K: dq_q2_k(b, o); break;
+      case ORC_Q3_K: dq_q3_k(b, o); break;
+      case ORC_Q5_K: dq_q5_k(b, o); break;
+      case ORC_Q8_K: dq_q8_k(b, o); break;
     }
   }
   return 0;
@@ -341,7 +451,10 @@ typedef struct {
 static void* mv_worker(void* arg) {
   mv_job* j = (mv_job*)arg;
   float* scratch = NULL;
-  int decoded = j->use_reference || j->type == ORC_F32 || j->type == ORC_F16 || j->type == ORC_Q5_0;
+  /* matvec_q5_0/_q5_k/_q2_k/_q3_k/_q8_k (quant.rs:1050-1490) decode each block then
+   * sum deq[j]*x[j] in order: the generic decode-then-dot */
+  int decoded = j->use_reference || j->type == ORC_F32 || j->type == ORC_F16 || j->type == ORC_Q5_0 ||
+                j->type == ORC_Q2_K || j->type == ORC_Q3_K || j->type == ORC_Q5_K || j->type == ORC_Q8_K;
   if (decoded) scratch = (float*)malloc(sizeof(float) * (j->in ? j->in : 1));
   for (size_t r = j->r0; r < j->r1; r++) {
     const uint8_t* row = j->w + r * j->rb;

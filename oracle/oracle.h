@@ -27,7 +27,7 @@ extern "C" {
 /* ggml type ids (crates/ramforge-core/src/types.rs:238-270). */
 enum {
   ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q5_0 = 6, ORC_Q8_0 = 8,
-  ORC_Q4_K = 12, ORC_Q6_K = 14
+  ORC_Q2_K = 10, ORC_Q3_K = 11, ORC_Q4_K = 12, ORC_Q5_K = 13, ORC_Q6_K = 14, ORC_Q8_K = 15
 };
 
 /* ---- block-level primitives ---------------------------------------- */

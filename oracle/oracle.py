@@ -18,6 +18,7 @@ _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 _lib = None
 
 F32, F16, Q4_0, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 6, 8, 12, 14
+Q2_K, Q3_K, Q5_K, Q8_K = 10, 11, 13, 15
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _u8p = ctypes.POINTER(ctypes.c_uint8)

@@ -5,6 +5,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cmath>
 #include <thread>
 
 namespace rf {
@@ -92,17 +93,13 @@ void read_scalar(Reader& r, uint32_t t, GgufMeta* m) {
   }
 }
 
+// GgmlType::type_info (types.rs:354-376) for the types the engine accepts: the
+// block table of rf_kernels.cuh (block_elems / block_bytes).
 bool type_info(uint32_t type, uint64_t* qk, uint64_t* bsz) {
-  switch (type) {  // GgmlType::type_info (types.rs:354-376) for the types the engine runs
-    case T_F32: *qk = 1; *bsz = 4; return true;
-    case T_F16: *qk = 1; *bsz = 2; return true;
-    case T_Q4_0: *qk = 32; *bsz = 18; return true;
-    case T_Q8_0: *qk = 32; *bsz = 34; return true;
-    case T_Q4_K: *qk = 256; *bsz = 144; return true;
-    case 6: *qk = 32; *bsz = 22; return true;    // Q5_0 (parsed, not executed)
-    case 14: *qk = 256; *bsz = 210; return true; // Q6_K (parsed, not executed)
-    default: return false;
-  }
+  if (type > 255 || !block_elems((int)type)) return false;
+  *qk = (uint64_t)block_elems((int)type);
+  *bsz = (uint64_t)block_bytes((int)type);
+  return true;
 }
 }  // namespace
 
@@ -264,7 +261,10 @@ int pack_rows(const uint8_t* src, uint64_t src_row_bytes, uint32_t src_blk_off, 
           }
           break;
         case T_Q6_K:
-          for (uint32_t k = 0; k < nblk; k++, s += 210) q6k_pack_block(g, Q, C, dr, k, s);
+          for (uint32_t k = 0; k < nblk; k++, s += 210) six_bit_pack_block(g, Q, C, dr, k, s);
+          break;
+        case T_Q5_K:
+          for (uint32_t k = 0; k < nblk; k++, s += 176) six_bit_pack_block(g, Q, C, dr, k, s);
           break;
       }
     }
@@ -277,6 +277,110 @@ int pack_rows(const uint8_t* src, uint64_t src_row_bytes, uint32_t src_blk_off, 
     const size_t per = (n + nt - 1) / nt;
     for (size_t t = 0; t < nt; t++) {
       const size_t a = t * per, b = std::min(n, a + per);
+      if (a < b) ts.emplace_back(work, a, b);
+    }
+    for (auto& t : ts) t.join();
+  }
+  return RF_OK;
+}
+
+
+// ---- formats stored as f32: the reference's block decodes --------------------------
+namespace {
+// f16 -> f32 as the reference reads block scales (quant.rs:40-65): IEEE, except that
+// a subnormal half comes out at half its IEEE value.
+float ref_f16(const uint8_t* p) {
+  const uint32_t h = (uint32_t)p[0] | ((uint32_t)p[1] << 8), e = (h >> 10) & 31, m = h & 1023;
+  float v;
+  if (e == 0) v = std::ldexp((float)m, -25);
+  else if (e == 31) v = m ? NAN : INFINITY;
+  else v = std::ldexp((float)(m | 1024), (int)e - 25);
+  return (h & 0x8000) ? -v : v;
+}
+uint32_t rd_u32(const uint8_t* p) {
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+// BlockQ5_0::dequantize (quant.rs:140-151): q = nibble | high bit << 4, value (q-16)*d.
+void dq_q5_0(const uint8_t* b, float* o) {
+  const float d = ref_f16(b);
+  const uint32_t qh = rd_u32(b + 2);
+  for (int j = 0; j < 16; j++) {
+    const int q0 = (int)((b[6 + j] & 0xFu) | (((qh >> j) << 4) & 0x10u)) - 16;
+    const int q1 = (int)((b[6 + j] >> 4) | ((qh >> (j + 12)) & 0x10u)) - 16;
+    o[j] = (float)q0 * d;
+    o[16 + j] = (float)q1 * d;
+  }
+}
+// BlockQ2K::dequantize (quant.rs:443-474): scale byte i = sc | m << 4 for 16 elements,
+// value (d*sc)*q - dmin*m for 2-bit q.
+void dq_q2_k(const uint8_t* b, float* o) {
+  const uint8_t *sc = b, *qs = b + 16;
+  const float d = ref_f16(b + 80), dmin = ref_f16(b + 82);
+  int y = 0, i = 0;
+  for (int n = 0; n < 2; n++)
+    for (int shift = 0; shift < 8; shift += 2)
+      for (int h = 0; h < 2; h++, i++, y += 16) {
+        const float dl = d * (float)(sc[i] & 0xF), ml = dmin * (float)(sc[i] >> 4);
+        for (int l = 0; l < 16; l++) o[y + l] = dl * (float)((qs[32 * n + 16 * h + l] >> shift) & 3) - ml;
+      }
+}
+// BlockQ3K::dequantize (quant.rs:506-574): 16 six-bit scales (minus 32) unpacked from
+// 12 bytes, q = 2 low bits - (hmask bit clear ? 4 : 0), value (d*sc)*q; as in the
+// reference, both 128-element halves use scales j and j+4 (j < 4).
+void dq_q3_k(const uint8_t* b, float* o) {
+  const uint8_t *hm = b, *qs = b + 32, *sb = b + 96;
+  const float d = ref_f16(b + 108);
+  const uint32_t k1 = 0x03030303u, k2 = 0x0F0F0F0Fu;
+  const uint32_t a0 = rd_u32(sb), a1 = rd_u32(sb + 4), t = rd_u32(sb + 8);
+  const uint32_t aux[4] = {(a0 & k2) | ((t & k1) << 4), (a1 & k2) | (((t >> 2) & k1) << 4),
+                           ((a0 >> 4) & k2) | (((t >> 4) & k1) << 4), ((a1 >> 4) & k2) | (((t >> 6) & k1) << 4)};
+  int y = 0;
+  uint32_t m = 1;
+  for (int n = 0; n < 2; n++)
+    for (int j = 0; j < 4; j++, m <<= 1)
+      for (int h = 0; h < 2; h++, y += 16) {
+        const int k = j + 4 * h;
+        const int sc = (int)(int8_t)(uint8_t)(aux[k / 4] >> (8 * (k % 4))) - 32;
+        const float dl = d * (float)sc;
+        for (int l = 0; l < 16; l++) {
+          const int q = ((qs[32 * n + 16 * h + l] >> (2 * j)) & 3) - ((hm[16 * h + l] & m) ? 0 : 4);
+          o[y + l] = dl * (float)q;
+        }
+      }
+}
+// BlockQ8K::dequantize (quant.rs:605-609): f32 d, value d*q.
+void dq_q8_k(const uint8_t* b, float* o) {
+  float d;
+  memcpy(&d, b, 4);
+  for (int i = 0; i < 256; i++) o[i] = d * (float)(int8_t)b[4 + i];
+}
+}  // namespace
+
+int expand_rows_f32(int type, const uint8_t* src, uint64_t src_row_bytes, uint64_t rows, uint32_t K, float* out) {
+  if (!expands_to_f32(type)) return set_error(RF_EINVAL, "type %d is not expanded to f32", type);
+  const uint32_t qk = block_elems(type), bsz = block_bytes(type);
+  if (K % qk || (uint64_t)(K / qk) * bsz > src_row_bytes) return set_error(RF_EINVAL, "bad row for type %d", type);
+  auto work = [&](uint64_t a, uint64_t b) {
+    for (uint64_t r = a; r < b; r++)
+      for (uint32_t k = 0; k < K / qk; k++) {
+        const uint8_t* blk = src + r * src_row_bytes + (uint64_t)k * bsz;
+        float* o = out + r * K + (uint64_t)k * qk;
+        switch (type) {
+          case T_Q5_0: dq_q5_0(blk, o); break;
+          case T_Q2_K: dq_q2_k(blk, o); break;
+          case T_Q3_K: dq_q3_k(blk, o); break;
+          case T_Q8_K: dq_q8_k(blk, o); break;
+        }
+      }
+  };
+  const uint64_t nt = std::min<uint64_t>(std::max(1u, std::thread::hardware_concurrency()), 32);
+  if (rows < 256 || nt <= 1) {
+    work(0, rows);
+  } else {
+    std::vector<std::thread> ts;
+    const uint64_t per = (rows + nt - 1) / nt;
+    for (uint64_t t = 0; t < nt; t++) {
+      const uint64_t a = t * per, b = std::min(rows, a + per);
       if (a < b) ts.emplace_back(work, a, b);
     }
     for (auto& t : ts) t.join();

@@ -95,5 +95,9 @@ int host_packed_init(int type, uint32_t M, uint32_t K, HostPacked* out);
 // (a column slice for row-parallel shards).  Multi-threaded, pure byte shuffle.
 int pack_rows(const uint8_t* src, uint64_t src_row_bytes, uint32_t src_blk_off, const std::vector<int>& src_rows,
               HostPacked* out, uint32_t dst_row0, uint32_t dst_row_step);
+// Decode `rows` GGUF rows of a format the engine stores as f32 (expands_to_f32),
+// K elements each (rows of src_row_bytes), into out[rows][K]: the reference's
+// block dequantize, value for value.  Multi-threaded.
+int expand_rows_f32(int type, const uint8_t* src, uint64_t src_row_bytes, uint64_t rows, uint32_t K, float* out);
 
 }  // namespace rf

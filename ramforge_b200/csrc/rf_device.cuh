@@ -101,7 +101,9 @@ __device__ __forceinline__ float dequant_elem(const PackedMat& W, uint32_t row, 
       const float d1 = __fmul_rn(d, (float)sc), mn = __fmul_rn(dmin, (float)m);
       return __fsub_rn(__fmul_rn(d1, (float)nq), mn);
     }
-    case T_Q6_K: {  // (d*sc)*q (quant.rs:376-406); words as q6k_sub_words packs them
+    case T_Q5_K:
+    case T_Q6_K: {  // Q6_K (d*sc)*q (quant.rs:376-406), Q5_K (d*sc)*u - dmin*m (:303-343); words as
+                    // six_bit_words packs them
       const uint32_t ch = e / 128, j = (e % 128) / 16, t = e % 16;
       const uint64_t wb = (uint64_t)ch * Q6_CHUNK_BYTES + 12 * j;
       auto word = [&](uint32_t k) {
@@ -109,8 +111,16 @@ __device__ __forceinline__ float dequant_elem(const PackedMat& W, uint32_t row, 
         return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
       };
       const uint32_t src = t < 12 ? word(t / 4) : (word(0) >> 24) | ((word(1) >> 24) << 8) | ((word(2) >> 24) << 16);
-      const int v = (int)((src >> (6 * (t % 4))) & 63u) - 32;
+      const uint32_t u = (src >> (6 * (t % 4))) & 63u;
       const uint64_t hb = (uint64_t)ch * Q6_HDR_BYTES;
+      if (W.type == T_Q5_K) {
+        const uint32_t sb = (e % 128) / 32;
+        const float sc = (float)c[sc_byte_off(W, row, hb + sb)], m = (float)c[sc_byte_off(W, row, hb + 4 + sb)];
+        const uint8_t* dp = c + sc_byte_off(W, row, hb + 8);
+        const float d = h2f(dp[0] | (dp[1] << 8)), dmin = h2f(dp[2] | (dp[3] << 8));
+        return __fsub_rn(__fmul_rn(__fmul_rn(d, sc), (float)u), __fmul_rn(dmin, m));
+      }
+      const int v = (int)u - 32;
       const float sc = (float)(int8_t)c[sc_byte_off(W, row, hb + j)];
       const uint8_t* dp = c + sc_byte_off(W, row, hb + 8);
       const float d = h2f(dp[0] | (dp[1] << 8));

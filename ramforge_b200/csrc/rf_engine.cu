@@ -484,6 +484,20 @@ int check_view(const View& v, const char* what, uint64_t ne0, uint64_t ne1) {
 
 uint64_t row_bytes_of(const View& v) { return v.ne0 / block_elems(v.type) * block_bytes(v.type); }
 
+// A matrix view of a format the engine stores as f32 (expands_to_f32) decoded into
+// `store` (the reference's dequantize, value for value) and described as F32; any
+// other view is passed through.
+int expand_view(const View& v, std::vector<float>* store, View* out) {
+  *out = v;
+  if (!v.host || !expands_to_f32(v.type)) return RF_OK;
+  store->resize(v.ne0 * v.ne1);
+  RF_TRY(expand_rows_f32(v.type, v.host, row_bytes_of(v), v.ne1, (uint32_t)v.ne0, store->data()));
+  out->type = T_F32;
+  out->host = reinterpret_cast<const uint8_t*>(store->data());
+  out->bytes = 4ull * v.ne0 * v.ne1;
+  return RF_OK;
+}
+
 // f32 copy of a norm vector (F32 or F16 storage; TensorData F16 rows are f32 after load)
 int norm_to_f32(const View& v, uint32_t n, std::vector<float>* out) {
   out->resize(n);
@@ -579,19 +593,23 @@ int validate_qkv_bias(const View* v, int l, uint64_t qd, uint64_t kvd) {
 // load_layer's packing (streaming_model.rs:581-847) into a host image: this
 // rank's rows of Q/K/V (RoPE pairs adjacent), W_o, interleaved gate/up and
 // down, in the tiled layout, plus the norms as f32.
-int build_layer_image(rf_engine* e, int l, const View* v /*[kLayerViews]*/, LayerImage* out) {
+int build_layer_image(rf_engine* e, int l, const View* vin /*[kLayerViews]*/, LayerImage* out) {
   const rf_model_config& c = e->cfg;
   const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
-  RF_TRY(check_view(v[0], "attn_norm", c.n_embd, 1));
-  RF_TRY(check_view(v[1], "attn_q", c.n_embd, qd));
-  RF_TRY(check_view(v[2], "attn_k", c.n_embd, kvd));
-  RF_TRY(check_view(v[3], "attn_v", c.n_embd, kvd));
-  RF_TRY(check_view(v[4], "attn_output", qd, c.n_embd));
-  RF_TRY(check_view(v[5], "ffn_norm", c.n_embd, 1));
-  RF_TRY(check_view(v[6], "ffn_gate", c.n_embd, c.n_ff));
-  RF_TRY(check_view(v[7], "ffn_up", c.n_embd, c.n_ff));
-  RF_TRY(check_view(v[8], "ffn_down", c.n_ff, c.n_embd));
-  RF_TRY(validate_qkv_bias(v, l, qd, kvd));
+  RF_TRY(check_view(vin[0], "attn_norm", c.n_embd, 1));
+  RF_TRY(check_view(vin[1], "attn_q", c.n_embd, qd));
+  RF_TRY(check_view(vin[2], "attn_k", c.n_embd, kvd));
+  RF_TRY(check_view(vin[3], "attn_v", c.n_embd, kvd));
+  RF_TRY(check_view(vin[4], "attn_output", qd, c.n_embd));
+  RF_TRY(check_view(vin[5], "ffn_norm", c.n_embd, 1));
+  RF_TRY(check_view(vin[6], "ffn_gate", c.n_embd, c.n_ff));
+  RF_TRY(check_view(vin[7], "ffn_up", c.n_embd, c.n_ff));
+  RF_TRY(check_view(vin[8], "ffn_down", c.n_ff, c.n_embd));
+  RF_TRY(validate_qkv_bias(vin, l, qd, kvd));
+  // matrices in formats stored as f32 are decoded here; from now on they are F32
+  std::vector<float> xs[kLayerViews];
+  View v[kLayerViews];
+  for (int j = 0; j < kLayerViews; j++) RF_TRY(expand_view(vin[j], &xs[j], &v[j]));
   if (v[1].type != v[2].type)
     return set_error(RF_EUNSUPPORTED, "layer %d: Q and K of different types are not supported", l);
   // V of another type (e.g. Q6_K beside Q4_K Q/K) is its own matrix, run as a
@@ -699,12 +717,12 @@ View view_from_gguf(const GgufTensor* t) {
 
 int lm_head(rf_engine* e, PackedMat* W);
 
-int load_persistent(rf_engine* e, int role, const View& v) {
+int load_persistent(rf_engine* e, int role, const View& v0) {
   const rf_model_config& c = e->cfg;
   if (role == RF_ROLE_OUTPUT_NORM) {
-    RF_TRY(check_view(v, "output_norm", c.n_embd, 1));
+    RF_TRY(check_view(v0, "output_norm", c.n_embd, 1));
     std::vector<float> w;
-    RF_TRY(norm_to_f32(v, c.n_embd, &w));
+    RF_TRY(norm_to_f32(v0, c.n_embd, &w));
     void* p = nullptr;
     if (!e->out_norm) {
       RF_TRY(dev_alloc(e, "persistent:output_norm", 4ull * c.n_embd, &p));
@@ -715,7 +733,10 @@ int load_persistent(rf_engine* e, int role, const View& v) {
   } else if (role == RF_ROLE_TOKEN_EMBD || role == RF_ROLE_OUTPUT) {
     const bool is_embd = role == RF_ROLE_TOKEN_EMBD;
     // get_embedding expects [n_embd, vocab] (tensor.rs:706-714)
-    RF_TRY(check_view(v, is_embd ? "token_embd" : "output", c.n_embd, c.vocab_size));
+    RF_TRY(check_view(v0, is_embd ? "token_embd" : "output", c.n_embd, c.vocab_size));
+    std::vector<float> xs;
+    View v;
+    RF_TRY(expand_view(v0, &xs, &v));
     HostPacked hp;
     const uint32_t rows = is_embd ? c.vocab_size : e->vocab_local;
     const uint32_t r0 = is_embd ? 0 : e->vocab_off;
@@ -1333,9 +1354,9 @@ void destroy(rf_engine* e) {
 uint64_t layer_image_bytes(rf_engine* e, int l) {
   const rf_model_config& c = e->cfg;
   const std::string pre = "blk." + std::to_string(l) + ".";
-  auto type_of = [&](const char* role) -> int {
+  auto type_of = [&](const char* role) -> int {  // the device storage type
     const GgufTensor* t = e->gguf.find(pre + role + ".weight");
-    return t ? (int)t->type : -1;
+    return t ? storage_type((int)t->type) : -1;
   };
   auto mat = [](int type, uint32_t M, uint32_t K) -> uint64_t {
     PackedMat g{};
@@ -1359,7 +1380,7 @@ bool layer_v_split(rf_engine* e, int l) {
   const std::string pre = "blk." + std::to_string(l) + ".";
   const GgufTensor* q = e->gguf.find(pre + "attn_q.weight");
   const GgufTensor* v = e->gguf.find(pre + "attn_v.weight");
-  return q && v && q->type != v->type;
+  return q && v && storage_type((int)q->type) != storage_type((int)v->type);
 }
 
 }  // namespace

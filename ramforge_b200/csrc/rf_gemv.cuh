@@ -243,11 +243,18 @@ struct QTraits<T_Q8_0> {
   static constexpr int CE = 128, SW = 2, XSF = 128, GE = 32, PB = QT_ROWS * 32, IB = QT_ITEM_BYTES;
 };
 // Q6_K: a chunk is half a super-block; piece c is sub-blocks 2c, 2c+1 (three
-//       words each, q6k_sub_words; value (d*sc)*(u-32), quant.rs:376-406); the
+//       words each, six_bit_words; value (d*sc)*(u-32), quant.rs:376-406); the
 //       header is 8 int8 scales and the f16 d.
 template <>
 struct QTraits<T_Q6_K> {
   static constexpr int CE = 128, SW = 3, XSF = 32, GE = 16, PB = QT_ROWS * Q6_PIECE_BYTES,
+                       IB = QT_ROWS * Q6_CHUNK_BYTES;
+};
+// Q5_K: the same words; piece c is 32-element sub-block c of the chunk (value
+//       d*sc*u - dmin*m, quant.rs:303-343); the header is 4 scales, 4 mins, d, dmin.
+template <>
+struct QTraits<T_Q5_K> {
+  static constexpr int CE = 128, SW = 3, XSF = 1, GE = 32, PB = QT_ROWS * Q6_PIECE_BYTES,
                        IB = QT_ROWS * Q6_CHUNK_BYTES;
 };
 
@@ -260,7 +267,7 @@ __device__ __forceinline__ int pair_off(int k) { return (k & 3) == 3 ? (k >> 2) 
 // Field offset of chunk element e.
 template <int FMT>
 __device__ __forceinline__ int qfield_off(int e) {
-  if (FMT == T_Q6_K) return 6 * (e & 3);  // element t of a sub-block: field t%4 of its word
+  if (FMT == T_Q6_K || FMT == T_Q5_K) return 6 * (e & 3);  // element t of a 16-group: field t%4 of its word
   if (FMT == T_Q8_0) return pair_off(e & 7);
   const int u = e & 63;
   const bool hi = FMT == T_Q4_K ? (u >= 32) : ((u & 31) >= 16);
@@ -416,7 +423,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   uint32_t w[2][4][8];  // [row r / r+32][piece][word] of the chunk in flight
   uint32_t h[2][SW];    // its scale bytes
   auto load_piece = [&](uint64_t i, int c) {
-    if constexpr (FMT == T_Q6_K) {
+    if constexpr (FMT == T_Q6_K || FMT == T_Q5_K) {
       const uint8_t* q = W.qs + i * T::IB + c * T::PB;
       ldg_q6_piece_if(true, q + lane * 16, q + QT_ROWS * 16 + lane * 8, w[0][c]);
       ldg_q6_piece_if(true, q + (lane + 32) * 16, q + QT_ROWS * 16 + (lane + 32) * 8, w[1][c]);
@@ -427,7 +434,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     }
   };
   auto load_hdr = [&](uint64_t i) {
-    if constexpr (FMT == T_Q6_K) {
+    if constexpr (FMT == T_Q6_K || FMT == T_Q5_K) {
       const uint8_t* s = W.sc + i * (QT_ROWS * SB);
       ldg_q6_hdr_if(true, s + lane * 8, s + QT_ROWS * 8 + lane * 4, h[0]);
       ldg_q6_hdr_if(true, s + (lane + 32) * 8, s + QT_ROWS * 8 + (lane + 32) * 4, h[1]);
@@ -443,7 +450,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   };
   // branch-free forms for the hot path (nothing is read when `on` is false)
   auto load_piece_if = [&](bool on, uint64_t i, int c) {
-    if constexpr (FMT == T_Q6_K) {
+    if constexpr (FMT == T_Q6_K || FMT == T_Q5_K) {
       const uint8_t* q = W.qs + i * T::IB + c * T::PB;
       ldg_q6_piece_if(on, q + lane * 16, q + QT_ROWS * 16 + lane * 8, w[0][c]);
       ldg_q6_piece_if(on, q + (lane + 32) * 16, q + QT_ROWS * 16 + (lane + 32) * 8, w[1][c]);
@@ -454,7 +461,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     }
   };
   auto load_hdr_if = [&](bool on, uint64_t i) {
-    if constexpr (FMT == T_Q6_K) {
+    if constexpr (FMT == T_Q6_K || FMT == T_Q5_K) {
       const uint8_t* s = W.sc + i * (QT_ROWS * SB);
       ldg_q6_hdr_if(on, s + lane * 8, s + QT_ROWS * 8 + lane * 4, h[0]);
       ldg_q6_hdr_if(on, s + (lane + 32) * 8, s + QT_ROWS * 8 + (lane + 32) * 4, h[1]);
@@ -720,6 +727,40 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       }
 #pragma unroll
       for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dd[s] * aM[s];
+    } else if constexpr (FMT == T_Q5_K) {
+      // sub-block c = piece c: d*sc_c*sum(u x) - dmin*m_c*sum(x); u x arrive scaled by 2^-64
+      float d64[2], dmn[2];
+#pragma unroll
+      for (int s = 0; s < 2; s++) {
+        d64[s] = scale_f<QUIRK>(hc[s][2]) * kTwo64;
+        dmn[s] = scale_f<QUIRK>(hc[s][2] >> 16);
+      }
+      float aS[2] = {0.f, 0.f}, aM[2] = {0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < NP; c++) {
+        const bool on = c >= lo && c < hi;
+        float2 sb[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
+        if (on) {
+#pragma unroll
+          for (int b = 0; b < 2; b++) {
+            const float* xb = xc + 32 * c + 16 * b;
+            const float4 x0 = lds4(xb), x1 = lds4(xb + 4), x2 = lds4(xb + 8), x3 = lds4(xb + 12);
+#pragma unroll
+            for (int s = 0; s < 2; s++)
+              q6_sub(w[s][c][3 * b], w[s][c][3 * b + 1], w[s][c][3 * b + 2], x0, x1, x2, x3, sb[s]);
+          }
+        }
+        load_piece_if(c < hi1, i + 1, c);
+        if (!on) continue;
+        const float xs = xsc[c];
+#pragma unroll
+        for (int s = 0; s < 2; s++) {
+          aS[s] = fmaf(byte_f(hc[s][0], c), sb[s].x + sb[s].y, aS[s]);
+          aM[s] = fmaf(byte_f(hc[s][1], c), xs, aM[s]);
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dmn[s] * aM[s];
     } else {  // Q8_0
 #pragma unroll
       for (int c = 0; c < NP; c++) {

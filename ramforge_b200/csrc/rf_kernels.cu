@@ -20,6 +20,7 @@
 namespace rf {
 
 bool packed_geometry(int type, uint32_t M, uint32_t K, PackedMat* p) {
+  if (expands_to_f32(type)) return false;  // stored as F32 (expand_rows_f32)
   if (!block_elems(type) || K == 0 || M == 0 || K % block_elems(type)) return false;
   p->type = type;
   p->M = M;
@@ -34,6 +35,7 @@ bool packed_geometry(int type, uint32_t M, uint32_t K, PackedMat* p) {
     case T_Q8_0: p->qs_stride = p->Kp; break;
     case T_Q4_0:
     case T_Q4_K: p->qs_stride = p->Kp / 2; break;
+    case T_Q5_K:
     case T_Q6_K: p->qs_stride = (uint64_t)p->Kp / 128 * Q6_CHUNK_BYTES; break;
   }
   if (is_tiled(type)) {
@@ -56,11 +58,12 @@ __host__ __device__ inline bool subnormal_half(uint32_t lo, uint32_t hi) {
 
 bool has_subnormal_scales(const PackedMat& W, const uint8_t* sc) {
   if (!is_tiled(W.type)) return false;
-  if (W.type == T_Q6_K) {  // the f16 d at header bytes 8-9 of every row and chunk
+  if (six_bit_fields(W.type)) {  // f16 d at header bytes 8-9 (and Q5_K's dmin at 10-11)
     for (uint32_t r = 0; r < W.Mp; r++)
       for (uint32_t c = 0; c < W.nk; c++) {
         const uint64_t o = sc_byte_off(W, r, (uint64_t)c * Q6_HDR_BYTES + 8);
         if (subnormal_half(sc[o], sc[o + 1])) return true;
+        if (W.type == T_Q5_K && subnormal_half(sc[o + 2], sc[o + 3])) return true;
       }
     return false;
   }
@@ -120,8 +123,13 @@ __global__ void pack_kernel(const uint8_t* __restrict__ src, const int* __restri
         break;
       }
       case T_Q6_K: {
-        q6k_pack_block(d, d.qs, d.sc, r, b, s);
+        six_bit_pack_block(d, d.qs, d.sc, r, b, s);
         sub = subnormal_half(s[208], s[209]);
+        break;
+      }
+      case T_Q5_K: {
+        six_bit_pack_block(d, d.qs, d.sc, r, b, s);
+        sub = subnormal_half(s[0], s[1]) || subnormal_half(s[2], s[3]);
         break;
       }
     }

@@ -7,7 +7,22 @@
 namespace rf {
 
 // ggml type ids (types.rs:238-270)
-enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+enum : int {
+  T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13,
+  T_Q6_K = 14, T_Q8_K = 15
+};
+// Formats the engine stores as f32, decoded at load exactly as the reference's
+// dequantize does (quant.rs:114-154, 408-612): matvec_q5_0/_q2_k/_q3_k/_q8_k
+// decode a block and sum deq[j]*x[j] (quant.rs:1050-1490), so the f32 rows give the
+// same products up to the order of the sum.
+__host__ __device__ inline bool expands_to_f32(int type) {
+  return type == T_Q5_0 || type == T_Q2_K || type == T_Q3_K || type == T_Q8_K;
+}
+// The type a matrix of GGUF `type` is stored in on the device.
+__host__ __device__ inline int storage_type(int type) { return expands_to_f32(type) ? T_F32 : type; }
+// Formats whose values the tiled layout holds as 6-bit fields (Q6_K: 6-bit values;
+// Q5_K: 5-bit values, one spare bit each, for the same cheap decode).
+__host__ __device__ inline bool six_bit_fields(int type) { return type == T_Q6_K || type == T_Q5_K; }
 
 // Packed device form of one GGUF matrix (n_out rows of n_in elements).
 //
@@ -29,14 +44,15 @@ enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K =
 // bytes of an item are contiguous too: sc[((tile*nk + chunk)*64 + row%64)*SB + b]
 // with SB = 16 (Q4_K header; Q4_0: eight f16) or 8 (Q8_0: four f16) bytes.
 //
-// Q6_K re-encodes its quants (the 6-bit values are kept, their bit positions
-// are not): a chunk is 128 elements, eight 16-element sub-blocks of three
-// 32-bit words each (q6k_sub_words), 96 bytes per row; piece p holds sub-blocks
-// 2p and 2p+1 (24 bytes), stored as a 16-byte plane (words 0-3 of the piece) of
-// the item's 64 rows followed by an 8-byte plane (words 4-5), so both warp-wide
-// loads stay contiguous.  The 12 header bytes of a row and chunk (the chunk's 8
-// int8 sub-block scales, then the super-block's f16 d and two zero bytes) are
-// split the same way: an 8-byte plane of the 64 rows, then a 4-byte plane.
+// Q6_K and Q5_K re-encode their quants (the values are kept, their bit positions
+// are not): a chunk is 128 elements, eight 16-element groups of three 32-bit
+// words each (six_bit_words), 96 bytes per row; piece p holds groups 2p and 2p+1
+// (24 bytes), stored as a 16-byte plane (words 0-3 of the piece) of the item's 64
+// rows followed by an 8-byte plane (words 4-5), so both warp-wide loads stay
+// contiguous.  The 12 header bytes of a row and chunk are split the same way: an
+// 8-byte plane of the 64 rows, then a 4-byte plane.  Q6_K: the chunk's 8 int8
+// scales | f16 d, 2 zero bytes.  Q5_K: the chunk's 4 six-bit scales, 4 mins | f16
+// d, f16 dmin.
 //
 // F32/F16 tensors stay row-major (qs_stride bytes per row, no sc).
 struct PackedMat {
@@ -67,20 +83,22 @@ constexpr int Q6_PIECE_BYTES = 24;
 constexpr int Q6_HDR_BYTES = 12;
 
 __host__ __device__ inline bool is_tiled(int type) {
-  return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q6_K;
+  return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || six_bit_fields(type);
 }
-__host__ __device__ inline int chunk_elems(int type) { return type == T_Q8_0 || type == T_Q6_K ? 128 : 256; }
+__host__ __device__ inline int chunk_elems(int type) { return type == T_Q8_0 || six_bit_fields(type) ? 128 : 256; }
 __host__ __device__ inline int chunk_scale_bytes(int type) {
-  return type == T_Q8_0 ? 8 : type == T_Q6_K ? Q6_HDR_BYTES : 16;
+  return type == T_Q8_0 ? 8 : six_bit_fields(type) ? Q6_HDR_BYTES : 16;
 }
-__host__ __device__ inline int chunk_quant_bytes(int type) { return type == T_Q6_K ? Q6_CHUNK_BYTES : QT_CHUNK_BYTES; }
+__host__ __device__ inline int chunk_quant_bytes(int type) {
+  return six_bit_fields(type) ? Q6_CHUNK_BYTES : QT_CHUNK_BYTES;
+}
 // Elements per group of the GEMV's per-group x sums (one scale per group).
 __host__ __device__ inline int chunk_group_elems(int type) { return type == T_Q6_K ? 16 : 32; }
 
 // Byte b (0 <= b < qs_stride) of row r's quant bytes.
 __host__ __device__ inline uint64_t qs_byte_off(const PackedMat& W, uint32_t r, uint64_t b) {
   if (!is_tiled(W.type)) return (uint64_t)r * W.qs_stride + b;
-  if (W.type == T_Q6_K) {
+  if (six_bit_fields(W.type)) {
     const uint64_t item = (uint64_t)(r / QT_ROWS) * W.nk + b / Q6_CHUNK_BYTES;
     const uint32_t o = (uint32_t)(b % Q6_CHUNK_BYTES), p = o / Q6_PIECE_BYTES, pb = o % Q6_PIECE_BYTES;
     const uint64_t base = item * (QT_ROWS * Q6_CHUNK_BYTES) + (uint64_t)p * (QT_ROWS * Q6_PIECE_BYTES);
@@ -92,7 +110,7 @@ __host__ __device__ inline uint64_t qs_byte_off(const PackedMat& W, uint32_t r, 
 // Byte b (0 <= b < sc_stride) of row r's scale bytes.
 __host__ __device__ inline uint64_t sc_byte_off(const PackedMat& W, uint32_t r, uint64_t b) {
   const uint64_t item = (uint64_t)(r / QT_ROWS) * W.nk + b / W.sbytes;
-  if (W.type == T_Q6_K) {
+  if (six_bit_fields(W.type)) {
     const uint32_t o = (uint32_t)(b % Q6_HDR_BYTES);
     const uint64_t base = item * (QT_ROWS * Q6_HDR_BYTES);
     return o < 8 ? base + (r % QT_ROWS) * 8 + o : base + QT_ROWS * 8 + (r % QT_ROWS) * 4 + (o - 8);
@@ -108,25 +126,44 @@ __host__ __device__ inline uint32_t q6k_value(const uint8_t* blk, int e) {
   const uint32_t lo = k < 2 ? (lq & 15u) : (uint32_t)(lq >> 4);
   return lo | ((uint32_t)((blk[128 + 32 * h + l] >> (2 * k)) & 3) << 4);
 }
-// The three packed words of 16-element sub-block j (0..15) of a GGUF Q6_K block:
-// values u0..u15, A = u0..u3 at bits 0/6/12/18, B = u4..u7, C = u8..u11 likewise,
-// and the top bytes of A, B, C together hold u12..u15 at bits 0/6/12/18 of
-// A[31:24] | B[31:24] << 8 | C[31:24] << 16.  Every field then lies below bit 24.
-__host__ __device__ inline void q6k_sub_words(const uint8_t* blk, int j, uint32_t out[3]) {
-  uint32_t u[16];
-  for (int t = 0; t < 16; t++) u[t] = q6k_value(blk, 16 * j + t);
+// 5-bit value q + 16*high of element e (0..255) of a GGUF Q5_K block
+// (BlockQ5K::dequantize, quant.rs:303-343): nibble of qs[32g + l] (low for the
+// first 32 elements of group g = e/64, high for the next 32), high bit 2g or 2g+1
+// of qh[8g + l/8] (the reference's indexing).
+__host__ __device__ inline uint32_t q5k_value(const uint8_t* blk, int e) {
+  const int g = e >> 6, hi = (e >> 5) & 1, l = e & 31;
+  const uint32_t nib = (blk[48 + 32 * g + l] >> (4 * hi)) & 15u;
+  return nib | ((uint32_t)((blk[16 + 8 * g + l / 8] >> (2 * g + hi)) & 1) << 4);
+}
+// get_scale_min of Q4_K/Q5_K (quant.rs:288-299): 6-bit scale and min of sub-block j.
+__host__ __device__ inline void k4_scale_min(const uint8_t* s, int j, uint32_t* sc, uint32_t* m) {
+  if (j < 4) {
+    *sc = s[j] & 63u;
+    *m = s[j + 4] & 63u;
+  } else {
+    *sc = (s[j + 4] & 0xFu) | ((uint32_t)(s[j - 4] >> 6) << 4);
+    *m = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+  }
+}
+// The three packed words of 16 values u0..u15 (< 64): A = u0..u3 at bits 0/6/12/18,
+// B = u4..u7, C = u8..u11 likewise, and the top bytes of A, B, C together hold
+// u12..u15 at bits 0/6/12/18 of A[31:24] | B[31:24] << 8 | C[31:24] << 16.  Every
+// field then lies below bit 24.
+__host__ __device__ inline void six_bit_words(const uint32_t u[16], uint32_t out[3]) {
   const uint32_t T = u[12] | (u[13] << 6) | (u[14] << 12) | (u[15] << 18);
   for (int k = 0; k < 3; k++)
     out[k] = u[4 * k] | (u[4 * k + 1] << 6) | (u[4 * k + 2] << 12) | (u[4 * k + 3] << 18) | (((T >> (8 * k)) & 0xFFu) << 24);
 }
-// Scatter GGUF Q6_K block k (256 elements at s) of a row into packed row r of g
-// (quant bytes into Q, header bytes into C; the zero padding is left as is).
+// Scatter GGUF Q6_K or Q5_K block k (256 elements at s) of a row into packed row r
+// of g (quant bytes into Q, header bytes into C; the zero padding is left as is).
 // Used by the device and the host packers alike.
-__host__ __device__ inline void q6k_pack_block(const PackedMat& g, uint8_t* Q, uint8_t* C, uint32_t r, uint32_t k,
-                                               const uint8_t* s) {
+__host__ __device__ inline void six_bit_pack_block(const PackedMat& g, uint8_t* Q, uint8_t* C, uint32_t r, uint32_t k,
+                                                   const uint8_t* s) {
+  const bool q5 = g.type == T_Q5_K;
   for (int j = 0; j < 16; j++) {
-    uint32_t w[3];
-    q6k_sub_words(s, j, w);
+    uint32_t u[16], w[3];
+    for (int t = 0; t < 16; t++) u[t] = q5 ? q5k_value(s, 16 * j + t) : q6k_value(s, 16 * j + t);
+    six_bit_words(u, w);
     const uint64_t b = (uint64_t)(2 * k + j / 8) * Q6_CHUNK_BYTES + 12 * (j % 8);
     for (int t = 0; t < 3; t++) {
       uint8_t* p = Q + qs_byte_off(g, r, b + 4 * t);  // a word never straddles a plane
@@ -135,9 +172,19 @@ __host__ __device__ inline void q6k_pack_block(const PackedMat& g, uint8_t* Q, u
   }
   for (int h = 0; h < 2; h++) {
     const uint64_t hb = (uint64_t)(2 * k + h) * Q6_HDR_BYTES;
-    for (int i = 0; i < 8; i++) C[sc_byte_off(g, r, hb + i)] = s[192 + 8 * h + i];
-    C[sc_byte_off(g, r, hb + 8)] = s[208];
-    C[sc_byte_off(g, r, hb + 9)] = s[209];
+    if (q5) {  // sub-blocks 4h..4h+3: scales, mins, then d and dmin as stored
+      for (int i = 0; i < 4; i++) {
+        uint32_t sc, m;
+        k4_scale_min(s + 4, 4 * h + i, &sc, &m);
+        C[sc_byte_off(g, r, hb + i)] = (uint8_t)sc;
+        C[sc_byte_off(g, r, hb + 4 + i)] = (uint8_t)m;
+      }
+      for (int i = 0; i < 4; i++) C[sc_byte_off(g, r, hb + 8 + i)] = s[i];
+    } else {
+      for (int i = 0; i < 8; i++) C[sc_byte_off(g, r, hb + i)] = s[192 + 8 * h + i];
+      C[sc_byte_off(g, r, hb + 8)] = s[208];
+      C[sc_byte_off(g, r, hb + 9)] = s[209];
+    }
   }
 }
 // Device bytes of the two streams.
@@ -155,8 +202,8 @@ __host__ __device__ inline int elems_per_unit(int type) {
 __host__ __device__ inline int block_elems(int type) {
   switch (type) {
     case T_F32: case T_F16: return 1;
-    case T_Q4_0: case T_Q8_0: return 32;
-    case T_Q4_K: case T_Q6_K: return 256;
+    case T_Q4_0: case T_Q5_0: case T_Q8_0: return 32;
+    case T_Q2_K: case T_Q3_K: case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_Q8_K: return 256;
     default: return 0;
   }
 }
@@ -166,8 +213,13 @@ __host__ __device__ inline int block_bytes(int type) {
     case T_F16: return 2;
     case T_Q4_0: return 18;
     case T_Q8_0: return 34;
+    case T_Q5_0: return 22;
+    case T_Q2_K: return 84;
+    case T_Q3_K: return 110;
     case T_Q4_K: return 144;
+    case T_Q5_K: return 176;
     case T_Q6_K: return 210;
+    case T_Q8_K: return 292;
     default: return 0;
   }
 }

@@ -121,6 +121,25 @@ int rf_matrix_create(int type, const void* bytes, uint64_t nbytes, int on_device
                      rf_matrix** out) {
   if (!bytes || !out) return set_error(RF_EINVAL, "null argument");
   *out = nullptr;
+  if (expands_to_f32(type)) {  // stored as f32: decode on the host, then an F32 matrix
+    const uint32_t qk = block_elems(type);
+    if (n_out == 0 || n_in == 0 || n_in % qk)
+      return set_error(RF_EINVAL, "type %d cannot hold a %u x %u matrix", type, n_out, n_in);
+    const uint64_t rb = (uint64_t)(n_in / qk) * block_bytes(type);
+    if (nbytes < rb * n_out)
+      return set_error(RF_EINVAL, "weight truncated: expected %llu bytes, got %llu", (unsigned long long)(rb * n_out),
+                       (unsigned long long)nbytes);
+    std::vector<uint8_t> staged;
+    const uint8_t* src = (const uint8_t*)bytes;
+    if (on_device) {
+      staged.resize(rb * n_out);
+      RF_CUDA(cudaMemcpy(staged.data(), bytes, staged.size(), cudaMemcpyDeviceToHost));
+      src = staged.data();
+    }
+    std::vector<float> f((size_t)n_in * n_out);
+    RF_TRY(expand_rows_f32(type, src, rb, n_out, n_in, f.data()));
+    return rf_matrix_create(T_F32, f.data(), 4ull * f.size(), 0, n_out, n_in, out);
+  }
   PackedMat g;
   if (!packed_geometry(type, n_out, n_in, &g))
     return set_error(RF_EINVAL, "type %d cannot hold a %u x %u matrix", type, n_out, n_in);

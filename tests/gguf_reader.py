@@ -7,7 +7,8 @@ import struct
 import numpy as np
 
 _SCALAR = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<B", 10: "<Q", 11: "<q", 12: "<d"}
-_BLOCK = {0: (1, 4), 1: (1, 2), 2: (32, 18), 6: (32, 22), 8: (32, 34), 12: (256, 144), 14: (256, 210)}
+_BLOCK = {0: (1, 4), 1: (1, 2), 2: (32, 18), 6: (32, 22), 8: (32, 34), 10: (256, 84), 11: (256, 110),
+          12: (256, 144), 13: (256, 176), 14: (256, 210), 15: (256, 292)}
 
 
 def read_tensors(img) -> dict:

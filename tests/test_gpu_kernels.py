@@ -12,6 +12,7 @@ import pytest
 
 from oracle import oracle as orc
 from ramforge_b200 import QMatrix, decode_attention, synth
+from tests import fixtures as fx
 
 pytestmark = pytest.mark.gpu
 THREADS = min(32, os.cpu_count() or 8)
@@ -22,7 +23,12 @@ def torch_mod():
     return torch
 
 
+Q5_K = orc.Q5_K  # no synthetic encoder: random blocks (tests/fixtures.py)
+
+
 def _weights(gtype, M, K, seed=1):
+    if gtype == Q5_K:
+        return fx.random_blocks(Q5_K, M, K, seed)
     w = synth.normal(seed, 100 + gtype, M * K, std=0.02).reshape(M, K)
     return synth.quantize(gtype, w)
 
@@ -44,7 +50,7 @@ def _run_qmv(gtype, M, K, batch=1, seed=1, raw=None):
     m.close()
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, synth.F16, synth.F32])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K, synth.F16, synth.F32])
 @pytest.mark.parametrize("M,K", [(1, 256), (7, 512), (33, 768), (130, 2304), (257, 4096)])
 def test_qmatvec_small_shapes(gtype, M, K):
     _run_qmv(gtype, M, K)
@@ -56,13 +62,13 @@ def test_qmatvec_ragged_rows_padded_to_units(gtype, M, K):
     _run_qmv(gtype, M, K)
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K])
 @pytest.mark.parametrize("M,K", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
 def test_qmatvec_config2_shapes(gtype, M, K):
     _run_qmv(gtype, M, K)
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K])
 @pytest.mark.parametrize("batch", [4, 8])
 def test_qmatvec_batched(gtype, batch):
     _run_qmv(gtype, 1024, 4096, batch=batch)
@@ -88,7 +94,18 @@ def test_qmatvec_q6_k_subnormal_super_scale_follows_reference_decode():
     _run_qmv(synth.Q6_K, 4, 512, raw=np.frombuffer(bytes(raw), np.uint8))
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, synth.F16])
+def test_qmatvec_q5_k_subnormal_scales_follow_reference_decode():
+    # Q5_K's f16 d and dmin sit at bytes 0-3 of each 176-byte block; rows 1 and 2
+    # get a subnormal dmin, row 3 a subnormal d.
+    raw = bytearray(_weights(Q5_K, 4, 512))
+    for r, o in ((1, 2), (2, 2), (3, 0)):
+        for b in range(2):
+            p = (r * 2 + b) * 176 + o
+            raw[p:p + 2] = (0x0155 + b).to_bytes(2, "little")
+    _run_qmv(Q5_K, 4, 512, raw=np.frombuffer(bytes(raw), np.uint8))
+
+
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K, synth.F16])
 def test_device_packing_equals_host_packing(gtype):
     # rf_matrix_create packs device-resident GGUF bytes with the pack kernel and
     # host bytes on the CPU; both must give the same packed matrix, so the same

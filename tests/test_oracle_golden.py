@@ -127,8 +127,104 @@ def test_q6_k_decode_runs():  # quant.rs:1852-1866
     assert orc.dequant_row(orc.Q6_K, raw, 256).shape == (256,)
 
 
+# ---- the other K-quants (quant.rs:257-612) ---------------------------------------
+def test_k_quant_block_sizes():  # quant.rs:1626-1649
+    for t, n in ((orc.Q2_K, 84), (orc.Q3_K, 110), (orc.Q5_K, 176), (orc.Q6_K, 210), (orc.Q8_K, 292)):
+        assert orc.row_bytes(t, 256) == n
+
+
+def test_q5_k_decode_all_ones():  # quant.rs:1826-1841
+    raw = struct.pack("<HH", 0x3C00, 0x0000) + bytes([1] * 12) + bytes(32) + bytes([0x11] * 128)
+    assert np.allclose(orc.dequant_row(orc.Q5_K, raw, 256), 1.0, atol=1e-5)
+
+
+def test_q8_k_decode_all_ones():  # quant.rs:1888-1900
+    raw = struct.pack("<f", 1.0) + bytes([1] * 256) + bytes(32)
+    assert np.allclose(orc.dequant_row(orc.Q8_K, raw, 256), 1.0, atol=1e-5)
+
+
+def test_q2_k_and_q3_k_decode_run():  # quant.rs:1859-1886
+    q2 = bytes([0x11] * 16) + bytes([0x11] * 64) + struct.pack("<HH", 0x3C00, 0x0000)
+    q3 = bytes([0x11] * 32) + bytes([0x11] * 64) + bytes([1] * 12) + struct.pack("<H", 0x3C00)
+    assert np.isfinite(orc.dequant_row(orc.Q2_K, q2, 256)).all()
+    assert np.isfinite(orc.dequant_row(orc.Q3_K, q3, 256)).all()
+
+
+def _f16(b, o):
+    return np.frombuffer(bytes(b[o:o + 2]), np.float16)[0].astype(np.float32)
+
+
+def _py_dequant(t, b):
+    """A second, independent transcription of BlockQ{2,3,5,8}K::dequantize
+    (quant.rs:303-343, 443-474, 506-574, 605-609), in float32 numpy scalars."""
+    f = np.float32
+    out = np.zeros(256, np.float32)
+    if t == orc.Q8_K:
+        d = np.frombuffer(bytes(b[0:4]), np.float32)[0]
+        return (d * np.frombuffer(bytes(b[4:260]), np.int8).astype(np.float32)).astype(np.float32)
+    if t == orc.Q5_K:
+        d, dmin, sc, qh, qs = _f16(b, 0), _f16(b, 2), b[4:16], b[16:48], b[48:176]
+
+        def sm(j):
+            if j < 4:
+                return sc[j] & 63, sc[j + 4] & 63
+            return (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4), (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4)
+        y = 0
+        for g in range(4):
+            (s0, m0), (s1, m1) = sm(2 * g), sm(2 * g + 1)
+            u1, u2 = 1 << (2 * g), 2 << (2 * g)
+            for l in range(32):
+                hb = qh[32 * g // 4 + l // 8]
+                out[y + l] = f(d * f(s0)) * f((qs[32 * g + l] & 0xF) + (16 if hb & u1 else 0)) - f(dmin * f(m0))
+                out[y + 32 + l] = f(d * f(s1)) * f((qs[32 * g + l] >> 4) + (16 if hb & u2 else 0)) - f(dmin * f(m1))
+            y += 64
+        return out
+    if t == orc.Q2_K:
+        sc, qs, d, dmin = b[0:16], b[16:80], _f16(b, 80), _f16(b, 82)
+        y, i = 0, 0
+        for n in range(2):
+            for shift in (0, 2, 4, 6):
+                for h in range(2):
+                    dl, ml = f(d * f(sc[i] & 0xF)), f(dmin * f(sc[i] >> 4))
+                    i += 1
+                    for l in range(16):
+                        out[y + l] = dl * f((qs[32 * n + 16 * h + l] >> shift) & 3) - ml
+                    y += 16
+        return out
+    hm, qs, sb, d = b[0:32], b[32:96], b[96:108], _f16(b, 108)  # Q3_K
+    a = [int.from_bytes(bytes(sb[4 * i:4 * i + 4]), "little") for i in range(3)]
+    k1, k2 = 0x03030303, 0x0F0F0F0F
+    aux = [(a[0] & k2) | (((a[2] >> 0) & k1) << 4), (a[1] & k2) | (((a[2] >> 2) & k1) << 4),
+           ((a[0] >> 4) & k2) | (((a[2] >> 4) & k1) << 4), ((a[1] >> 4) & k2) | (((a[2] >> 6) & k1) << 4)]
+    s8 = np.frombuffer(b"".join(v.to_bytes(4, "little") for v in aux), np.int8)
+    y, m = 0, 1
+    for n in range(2):
+        for j, shift in enumerate((0, 2, 4, 6)):
+            for h in range(2):
+                dl = f(d * f(int(s8[j + 4 * h]) - 32))
+                for l in range(16):
+                    q = ((qs[32 * n + 16 * h + l] >> shift) & 3) - (0 if hm[16 * h + l] & m else 4)
+                    out[y + l] = dl * f(q)
+                y += 16
+            m <<= 1
+    return out
+
+
+@pytest.mark.parametrize("gtype,size,dpos", [(orc.Q5_K, 176, (0, 2)), (orc.Q2_K, 84, (80, 82)),
+                                            (orc.Q3_K, 110, (108,)), (orc.Q8_K, 292, ())])
+def test_k_quant_decoders_match_an_independent_transcription(gtype, size, dpos):
+    rng = np.random.default_rng(gtype)
+    for _ in range(8):
+        b = bytearray(rng.integers(0, 256, size, dtype=np.uint8).tobytes())
+        for o in dpos:  # finite, normal f16 super-scales
+            b[o:o + 2] = int(rng.integers(0x2000, 0x3C00)).to_bytes(2, "little")
+        if gtype == orc.Q8_K:
+            b[0:4] = struct.pack("<f", float(rng.uniform(0.001, 0.1)))
+        assert np.array_equal(orc.dequant_row(gtype, bytes(b), 256), _py_dequant(gtype, b))
+
+
 def test_truncated_block_rejection():  # quant.rs:1911-1921
-    for t in (orc.Q4_0, orc.Q8_0, orc.Q4_K, orc.Q6_K):
+    for t in (orc.Q4_0, orc.Q8_0, orc.Q4_K, orc.Q6_K, orc.Q2_K, orc.Q3_K, orc.Q5_K, orc.Q8_K):
         with pytest.raises(orc.OracleError):
             orc.dequant_row(t, bytes(5), {orc.Q4_0: 32, orc.Q8_0: 32}.get(t, 256))
 
