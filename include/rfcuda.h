@@ -43,14 +43,14 @@ extern "C" {
 #define RF_TYPE_F16 1
 #define RF_TYPE_Q4_0 2
 #define RF_TYPE_Q8_0 8
+#define RF_TYPE_Q2_K 10
+#define RF_TYPE_Q3_K 11
 #define RF_TYPE_Q4_K 12
 #define RF_TYPE_Q5_K 13
 #define RF_TYPE_Q6_K 14
 /* accepted and stored as f32, decoded at load exactly as the reference's dequantize
- * (quant.rs:114-154, 408-612): its matvec for these decodes then sums in f32 */
+ * (quant.rs:114-154, 579-612): its matvec for these decodes then sums in f32 */
 #define RF_TYPE_Q5_0 6
-#define RF_TYPE_Q2_K 10
-#define RF_TYPE_Q3_K 11
 #define RF_TYPE_Q8_K 15
 
 /* per-layer tensor roles, the nine tensors of StreamingLayerWeights

@@ -19,7 +19,8 @@ ERROR_NAMES = {
 }
 
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 0, 1, 2, 8, 12, 13, 14
-TYPE_Q5_0, TYPE_Q2_K, TYPE_Q3_K, TYPE_Q8_K = 6, 10, 11, 15  # stored as f32
+TYPE_Q2_K, TYPE_Q3_K = 10, 11
+TYPE_Q5_0, TYPE_Q8_K = 6, 15  # stored as f32
 ROLE_NAMES = ["attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"]
 # rf_layer_load roles 0-11: the nine weights, then the optional qwen2 Q/K/V biases
 LAYER_VIEW_NAMES = ROLE_NAMES + ["attn_q.bias", "attn_k.bias", "attn_v.bias"]

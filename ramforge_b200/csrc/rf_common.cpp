@@ -266,6 +266,12 @@ int pack_rows(const uint8_t* src, uint64_t src_row_bytes, uint32_t src_blk_off, 
         case T_Q5_K:
           for (uint32_t k = 0; k < nblk; k++, s += 176) six_bit_pack_block(g, Q, C, dr, k, s);
           break;
+        case T_Q3_K:
+          for (uint32_t k = 0; k < nblk; k++, s += 110) nibble_group_pack_block(g, Q, C, dr, k, s);
+          break;
+        case T_Q2_K:
+          for (uint32_t k = 0; k < nblk; k++, s += 84) nibble_group_pack_block(g, Q, C, dr, k, s);
+          break;
       }
     }
   };
@@ -311,43 +317,6 @@ void dq_q5_0(const uint8_t* b, float* o) {
     o[16 + j] = (float)q1 * d;
   }
 }
-// BlockQ2K::dequantize (quant.rs:443-474): scale byte i = sc | m << 4 for 16 elements,
-// value (d*sc)*q - dmin*m for 2-bit q.
-void dq_q2_k(const uint8_t* b, float* o) {
-  const uint8_t *sc = b, *qs = b + 16;
-  const float d = ref_f16(b + 80), dmin = ref_f16(b + 82);
-  int y = 0, i = 0;
-  for (int n = 0; n < 2; n++)
-    for (int shift = 0; shift < 8; shift += 2)
-      for (int h = 0; h < 2; h++, i++, y += 16) {
-        const float dl = d * (float)(sc[i] & 0xF), ml = dmin * (float)(sc[i] >> 4);
-        for (int l = 0; l < 16; l++) o[y + l] = dl * (float)((qs[32 * n + 16 * h + l] >> shift) & 3) - ml;
-      }
-}
-// BlockQ3K::dequantize (quant.rs:506-574): 16 six-bit scales (minus 32) unpacked from
-// 12 bytes, q = 2 low bits - (hmask bit clear ? 4 : 0), value (d*sc)*q; as in the
-// reference, both 128-element halves use scales j and j+4 (j < 4).
-void dq_q3_k(const uint8_t* b, float* o) {
-  const uint8_t *hm = b, *qs = b + 32, *sb = b + 96;
-  const float d = ref_f16(b + 108);
-  const uint32_t k1 = 0x03030303u, k2 = 0x0F0F0F0Fu;
-  const uint32_t a0 = rd_u32(sb), a1 = rd_u32(sb + 4), t = rd_u32(sb + 8);
-  const uint32_t aux[4] = {(a0 & k2) | ((t & k1) << 4), (a1 & k2) | (((t >> 2) & k1) << 4),
-                           ((a0 >> 4) & k2) | (((t >> 4) & k1) << 4), ((a1 >> 4) & k2) | (((t >> 6) & k1) << 4)};
-  int y = 0;
-  uint32_t m = 1;
-  for (int n = 0; n < 2; n++)
-    for (int j = 0; j < 4; j++, m <<= 1)
-      for (int h = 0; h < 2; h++, y += 16) {
-        const int k = j + 4 * h;
-        const int sc = (int)(int8_t)(uint8_t)(aux[k / 4] >> (8 * (k % 4))) - 32;
-        const float dl = d * (float)sc;
-        for (int l = 0; l < 16; l++) {
-          const int q = ((qs[32 * n + 16 * h + l] >> (2 * j)) & 3) - ((hm[16 * h + l] & m) ? 0 : 4);
-          o[y + l] = dl * (float)q;
-        }
-      }
-}
 // BlockQ8K::dequantize (quant.rs:605-609): f32 d, value d*q.
 void dq_q8_k(const uint8_t* b, float* o) {
   float d;
@@ -367,8 +336,6 @@ int expand_rows_f32(int type, const uint8_t* src, uint64_t src_row_bytes, uint64
         float* o = out + r * K + (uint64_t)k * qk;
         switch (type) {
           case T_Q5_0: dq_q5_0(blk, o); break;
-          case T_Q2_K: dq_q2_k(blk, o); break;
-          case T_Q3_K: dq_q3_k(blk, o); break;
           case T_Q8_K: dq_q8_k(blk, o); break;
         }
       }

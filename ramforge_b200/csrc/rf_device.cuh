@@ -101,6 +101,19 @@ __device__ __forceinline__ float dequant_elem(const PackedMat& W, uint32_t row, 
       const float d1 = __fmul_rn(d, (float)sc), mn = __fmul_rn(dmin, (float)m);
       return __fsub_rn(__fmul_rn(d1, (float)nq), mn);
     }
+    case T_Q3_K:
+    case T_Q2_K: {  // Q3_K (d*sc)*(u-4) (quant.rs:506-574), Q2_K (d*sc)*u - dmin*m (:443-474)
+      const uint32_t ch = e / 256, G = (e % 256) / 16, t = e % 16;
+      const uint8_t byte = q[qs_byte_off(W, row, (uint64_t)ch * QT_CHUNK_BYTES + 32 * (G / 4) + 8 * (G % 4) + t % 8)];
+      const uint32_t u = t < 8 ? (byte & 15u) : (uint32_t)(byte >> 4);
+      const uint64_t hb = (uint64_t)ch * NG_HDR_BYTES;
+      const uint8_t sbyte = c[sc_byte_off(W, row, hb + G)];
+      const uint8_t* dp = c + sc_byte_off(W, row, hb + 16);
+      const float d = h2f(dp[0] | (dp[1] << 8));
+      if (W.type == T_Q3_K) return __fmul_rn(__fmul_rn(d, (float)(int8_t)sbyte), (float)((int)u - 4));
+      const float dmin = h2f(dp[2] | (dp[3] << 8));
+      return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)(sbyte & 15)), (float)u), __fmul_rn(dmin, (float)(sbyte >> 4)));
+    }
     case T_Q5_K:
     case T_Q6_K: {  // Q6_K (d*sc)*q (quant.rs:376-406), Q5_K (d*sc)*u - dmin*m (:303-343); words as
                     // six_bit_words packs them

@@ -130,6 +130,8 @@ static cudaError_t run_gemv(const Launch& L, const PackedMat& W, const GemvScrat
     case T_Q8_0: return run_qgemv_t<T_Q8_0>(L, W, *ws, x, nw, eps, epi);
     case T_Q6_K: return run_qgemv_t<T_Q6_K>(L, W, *ws, x, nw, eps, epi);
     case T_Q5_K: return run_qgemv_t<T_Q5_K>(L, W, *ws, x, nw, eps, epi);
+    case T_Q3_K: return run_qgemv_t<T_Q3_K>(L, W, *ws, x, nw, eps, epi);
+    case T_Q2_K: return run_qgemv_t<T_Q2_K>(L, W, *ws, x, nw, eps, epi);
     case T_F16: return run_fgemv_t<T_F16>(L, W, x, nw, eps, epi);
     case T_F32: return run_fgemv_t<T_F32>(L, W, x, nw, eps, epi);
     default: return cudaErrorInvalidValue;

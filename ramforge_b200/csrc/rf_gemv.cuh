@@ -250,6 +250,18 @@ struct QTraits<T_Q6_K> {
   static constexpr int CE = 128, SW = 3, XSF = 32, GE = 16, PB = QT_ROWS * Q6_PIECE_BYTES,
                        IB = QT_ROWS * Q6_CHUNK_BYTES;
 };
+// Q3_K, Q2_K: a chunk is one super-block; piece c is groups 4c..4c+3, word pair p
+//       of the piece group 4c+p (elements 0-7 low nibbles, 8-15 high); values
+//       d*sc*(u-4) (Q3_K, quant.rs:506-574) and d*sc*u - dmin*m (Q2_K, :443-474);
+//       the header is 16 group scale bytes and d (Q2_K: d, dmin).
+template <>
+struct QTraits<T_Q3_K> {
+  static constexpr int CE = 256, SW = 5, XSF = 4, GE = 16, PB = QT_ROWS * 32, IB = QT_ITEM_BYTES;
+};
+template <>
+struct QTraits<T_Q2_K> {
+  static constexpr int CE = 256, SW = 5, XSF = 1, GE = 16, PB = QT_ROWS * 32, IB = QT_ITEM_BYTES;
+};
 // Q5_K: the same words; piece c is 32-element sub-block c of the chunk (value
 //       d*sc*u - dmin*m, quant.rs:303-343); the header is 4 scales, 4 mins, d, dmin.
 template <>
@@ -269,6 +281,7 @@ template <int FMT>
 __device__ __forceinline__ int qfield_off(int e) {
   if (FMT == T_Q6_K || FMT == T_Q5_K) return 6 * (e & 3);  // element t of a 16-group: field t%4 of its word
   if (FMT == T_Q8_0) return pair_off(e & 7);
+  if (FMT == T_Q3_K || FMT == T_Q2_K) return pair_off(e & 7) + ((e & 15) >= 8 ? 4 : 0);  // element t of a group
   const int u = e & 63;
   const bool hi = FMT == T_Q4_K ? (u >= 32) : ((u & 31) >= 16);
   return pair_off(u & 7) + (hi ? 4 : 0);
@@ -331,6 +344,16 @@ __device__ __forceinline__ void ldg_q6_hdr_if(bool on, const uint8_t* pa, const 
       "@q ld.global.nc.L1::no_allocate.v2.b32 {%0,%1}, [%3];\n"
       "@q ld.global.nc.L1::no_allocate.b32 %2, [%4]; }"
       : "+r"(h[0]), "+r"(h[1]), "+r"(h[2])
+      : "l"(pa), "l"(pb), "r"((uint32_t)on));
+}
+
+// A 20-byte header row (16 bytes at pa, 4 at pb) under a predicate.
+__device__ __forceinline__ void ldg_hdr20_if(bool on, const uint8_t* pa, const uint8_t* pb, uint32_t (&h)[5]) {
+  asm volatile(
+      "{ .reg .pred q; setp.ne.u32 q, %7, 0;\n"
+      "@q ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%5];\n"
+      "@q ld.global.nc.L1::no_allocate.b32 %4, [%6]; }"
+      : "+r"(h[0]), "+r"(h[1]), "+r"(h[2]), "+r"(h[3]), "+r"(h[4])
       : "l"(pa), "l"(pb), "r"((uint32_t)on));
 }
 
@@ -438,6 +461,10 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       const uint8_t* s = W.sc + i * (QT_ROWS * SB);
       ldg_q6_hdr_if(true, s + lane * 8, s + QT_ROWS * 8 + lane * 4, h[0]);
       ldg_q6_hdr_if(true, s + (lane + 32) * 8, s + QT_ROWS * 8 + (lane + 32) * 4, h[1]);
+    } else if constexpr (FMT == T_Q3_K || FMT == T_Q2_K) {
+      const uint8_t* s = W.sc + i * (QT_ROWS * SB);
+      ldg_hdr20_if(true, s + lane * 16, s + QT_ROWS * 16 + lane * 4, h[0]);
+      ldg_hdr20_if(true, s + (lane + 32) * 16, s + QT_ROWS * 16 + (lane + 32) * 4, h[1]);
     } else if constexpr (SW == 4) {
       const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
       ldg128(s, h[0]);
@@ -465,6 +492,10 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       const uint8_t* s = W.sc + i * (QT_ROWS * SB);
       ldg_q6_hdr_if(on, s + lane * 8, s + QT_ROWS * 8 + lane * 4, h[0]);
       ldg_q6_hdr_if(on, s + (lane + 32) * 8, s + QT_ROWS * 8 + (lane + 32) * 4, h[1]);
+    } else if constexpr (FMT == T_Q3_K || FMT == T_Q2_K) {
+      const uint8_t* s = W.sc + i * (QT_ROWS * SB);
+      ldg_hdr20_if(on, s + lane * 16, s + QT_ROWS * 16 + lane * 4, h[0]);
+      ldg_hdr20_if(on, s + (lane + 32) * 16, s + QT_ROWS * 16 + (lane + 32) * 4, h[1]);
     } else if constexpr (SW == 4) {
       const uint8_t* s = W.sc + (i * QT_ROWS + lane) * SB;
       ldg128_if(on, s, h[0]);
@@ -727,6 +758,47 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       }
 #pragma unroll
       for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dd[s] * aM[s];
+    } else if constexpr (FMT == T_Q3_K || FMT == T_Q2_K) {
+      // group G: sum of u x (scaled by 2^-64) with its scale byte; Q3_K subtracts 4*sc*sum(x)
+      // with d (x sums staged as 4x), Q2_K m*sum(x) with dmin
+      float d64[2], dm[2];
+#pragma unroll
+      for (int s = 0; s < 2; s++) {
+        d64[s] = scale_f<QUIRK>(hc[s][4]) * kTwo64;
+        dm[s] = scale_f<QUIRK>(FMT == T_Q3_K ? hc[s][4] : hc[s][4] >> 16);
+      }
+      float aS[2] = {0.f, 0.f}, aM[2] = {0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < NP; c++) {
+        const bool on = c >= lo && c < hi;
+        if (on) {
+#pragma unroll
+          for (int p = 0; p < 4; p++) {
+            const int G = 4 * c + p;
+            const float* xb = xc + 16 * G;
+            const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 8), xh1 = lds4(xb + 12);
+            const float xs = xsc[G];
+#pragma unroll
+            for (int s = 0; s < 2; s++) {
+              float2 sl = ff2(0.f, 0.f), sh = ff2(0.f, 0.f);
+              q4_pair(w[s][c][2 * p], w[s][c][2 * p + 1], xl0, xl1, xh0, xh1, sl, sh);
+              const float S = (sl.x + sl.y) + (sh.x + sh.y);
+              if constexpr (FMT == T_Q3_K) {
+                const float scf = sbyte_f(hc[s][G >> 2], G & 3);
+                aS[s] = fmaf(scf, S, aS[s]);
+                aM[s] = fmaf(scf, xs, aM[s]);
+              } else {
+                const uint32_t sb = (hc[s][G >> 2] >> (8 * (G & 3))) & 0xFFu;
+                aS[s] = fmaf((float)(sb & 15u), S, aS[s]);
+                aM[s] = fmaf((float)(sb >> 4), xs, aM[s]);
+              }
+            }
+          }
+        }
+        load_piece_if(c < hi1, i + 1, c);
+      }
+#pragma unroll
+      for (int s = 0; s < 2; s++) acc[s] = d64[s] * aS[s] - dm[s] * aM[s];
     } else if constexpr (FMT == T_Q5_K) {
       // sub-block c = piece c: d*sc_c*sum(u x) - dmin*m_c*sum(x); u x arrive scaled by 2^-64
       float d64[2], dmn[2];

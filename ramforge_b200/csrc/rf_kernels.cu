@@ -34,7 +34,9 @@ bool packed_geometry(int type, uint32_t M, uint32_t K, PackedMat* p) {
     case T_F16: p->qs_stride = (uint64_t)p->Kp * 2; p->sc_stride = 0; break;
     case T_Q8_0: p->qs_stride = p->Kp; break;
     case T_Q4_0:
-    case T_Q4_K: p->qs_stride = p->Kp / 2; break;
+    case T_Q4_K:
+    case T_Q3_K:
+    case T_Q2_K: p->qs_stride = p->Kp / 2; break;
     case T_Q5_K:
     case T_Q6_K: p->qs_stride = (uint64_t)p->Kp / 128 * Q6_CHUNK_BYTES; break;
   }
@@ -58,12 +60,14 @@ __host__ __device__ inline bool subnormal_half(uint32_t lo, uint32_t hi) {
 
 bool has_subnormal_scales(const PackedMat& W, const uint8_t* sc) {
   if (!is_tiled(W.type)) return false;
-  if (six_bit_fields(W.type)) {  // f16 d at header bytes 8-9 (and Q5_K's dmin at 10-11)
+  if (six_bit_fields(W.type) || nibble_group_fields(W.type)) {
+    // f16 d in the first two bytes of the 4-byte header plane (and Q5_K's or Q2_K's dmin after it)
+    const bool two = W.type == T_Q5_K || W.type == T_Q2_K;
     for (uint32_t r = 0; r < W.Mp; r++)
       for (uint32_t c = 0; c < W.nk; c++) {
-        const uint64_t o = sc_byte_off(W, r, (uint64_t)c * Q6_HDR_BYTES + 8);
+        const uint64_t o = sc_byte_off(W, r, (uint64_t)c * W.sbytes + (W.sbytes - 4));
         if (subnormal_half(sc[o], sc[o + 1])) return true;
-        if (W.type == T_Q5_K && subnormal_half(sc[o + 2], sc[o + 3])) return true;
+        if (two && subnormal_half(sc[o + 2], sc[o + 3])) return true;
       }
     return false;
   }
@@ -130,6 +134,16 @@ __global__ void pack_kernel(const uint8_t* __restrict__ src, const int* __restri
       case T_Q5_K: {
         six_bit_pack_block(d, d.qs, d.sc, r, b, s);
         sub = subnormal_half(s[0], s[1]) || subnormal_half(s[2], s[3]);
+        break;
+      }
+      case T_Q3_K: {
+        nibble_group_pack_block(d, d.qs, d.sc, r, b, s);
+        sub = subnormal_half(s[108], s[109]);
+        break;
+      }
+      case T_Q2_K: {
+        nibble_group_pack_block(d, d.qs, d.sc, r, b, s);
+        sub = subnormal_half(s[80], s[81]) || subnormal_half(s[82], s[83]);
         break;
       }
     }

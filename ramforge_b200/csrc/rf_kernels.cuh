@@ -12,12 +12,13 @@ enum : int {
   T_Q6_K = 14, T_Q8_K = 15
 };
 // Formats the engine stores as f32, decoded at load exactly as the reference's
-// dequantize does (quant.rs:114-154, 408-612): matvec_q5_0/_q2_k/_q3_k/_q8_k
-// decode a block and sum deq[j]*x[j] (quant.rs:1050-1490), so the f32 rows give the
-// same products up to the order of the sum.
-__host__ __device__ inline bool expands_to_f32(int type) {
-  return type == T_Q5_0 || type == T_Q2_K || type == T_Q3_K || type == T_Q8_K;
-}
+// dequantize does (quant.rs:114-154, 579-612): matvec_q5_0/_q8_k decode a block
+// and sum deq[j]*x[j] (quant.rs:1050-1490), so the f32 rows give the same products
+// up to the order of the sum.
+__host__ __device__ inline bool expands_to_f32(int type) { return type == T_Q5_0 || type == T_Q8_K; }
+// Q3_K and Q2_K: 2- and 3-bit values held one per nibble, 16-element groups
+// (each with its own scale) in one 8-byte word pair, and a 20-byte header.
+__host__ __device__ inline bool nibble_group_fields(int type) { return type == T_Q3_K || type == T_Q2_K; }
 // The type a matrix of GGUF `type` is stored in on the device.
 __host__ __device__ inline int storage_type(int type) { return expands_to_f32(type) ? T_F32 : type; }
 // Formats whose values the tiled layout holds as 6-bit fields (Q6_K: 6-bit values;
@@ -44,6 +45,16 @@ __host__ __device__ inline bool six_bit_fields(int type) { return type == T_Q6_K
 // bytes of an item are contiguous too: sc[((tile*nk + chunk)*64 + row%64)*SB + b]
 // with SB = 16 (Q4_K header; Q4_0: eight f16) or 8 (Q8_0: four f16) bytes.
 //
+// Q3_K and Q2_K re-encode their quants as nibbles (the values are kept): a chunk
+// is one super-block (256 elements, 128 bytes a row, the Q4 piece layout above);
+// group G (16 elements) is bytes 8(G%4)..8(G%4)+7 of piece G/4, element t of the
+// group in the low (t < 8) or high nibble of byte t%8.  Q3_K holds u = q + 4
+// (0..7), Q2_K the 2-bit q.  The 20 header bytes of a row and chunk are a 16-byte
+// plane (one scale byte per group: Q3_K the signed scale sc-32, Q2_K the stored
+// sc | m << 4) of the item's 64 rows, then a 4-byte plane (f16 d, and Q2_K's f16
+// dmin; Q3_K two zero bytes).
+constexpr int NG_HDR_BYTES = 20;
+
 // Q6_K and Q5_K re-encode their quants (the values are kept, their bit positions
 // are not): a chunk is 128 elements, eight 16-element groups of three 32-bit
 // words each (six_bit_words), 96 bytes per row; piece p holds groups 2p and 2p+1
@@ -83,17 +94,19 @@ constexpr int Q6_PIECE_BYTES = 24;
 constexpr int Q6_HDR_BYTES = 12;
 
 __host__ __device__ inline bool is_tiled(int type) {
-  return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || six_bit_fields(type);
+  return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || six_bit_fields(type) || nibble_group_fields(type);
 }
 __host__ __device__ inline int chunk_elems(int type) { return type == T_Q8_0 || six_bit_fields(type) ? 128 : 256; }
 __host__ __device__ inline int chunk_scale_bytes(int type) {
-  return type == T_Q8_0 ? 8 : six_bit_fields(type) ? Q6_HDR_BYTES : 16;
+  return type == T_Q8_0 ? 8 : six_bit_fields(type) ? Q6_HDR_BYTES : nibble_group_fields(type) ? NG_HDR_BYTES : 16;
 }
 __host__ __device__ inline int chunk_quant_bytes(int type) {
   return six_bit_fields(type) ? Q6_CHUNK_BYTES : QT_CHUNK_BYTES;
 }
 // Elements per group of the GEMV's per-group x sums (one scale per group).
-__host__ __device__ inline int chunk_group_elems(int type) { return type == T_Q6_K ? 16 : 32; }
+__host__ __device__ inline int chunk_group_elems(int type) {
+  return type == T_Q6_K || nibble_group_fields(type) ? 16 : 32;
+}
 
 // Byte b (0 <= b < qs_stride) of row r's quant bytes.
 __host__ __device__ inline uint64_t qs_byte_off(const PackedMat& W, uint32_t r, uint64_t b) {
@@ -110,10 +123,10 @@ __host__ __device__ inline uint64_t qs_byte_off(const PackedMat& W, uint32_t r, 
 // Byte b (0 <= b < sc_stride) of row r's scale bytes.
 __host__ __device__ inline uint64_t sc_byte_off(const PackedMat& W, uint32_t r, uint64_t b) {
   const uint64_t item = (uint64_t)(r / QT_ROWS) * W.nk + b / W.sbytes;
-  if (six_bit_fields(W.type)) {
-    const uint32_t o = (uint32_t)(b % Q6_HDR_BYTES);
-    const uint64_t base = item * (QT_ROWS * Q6_HDR_BYTES);
-    return o < 8 ? base + (r % QT_ROWS) * 8 + o : base + QT_ROWS * 8 + (r % QT_ROWS) * 4 + (o - 8);
+  if (six_bit_fields(W.type) || nibble_group_fields(W.type)) {  // an A-byte plane, then a 4-byte plane
+    const uint32_t A = W.sbytes - 4, o = (uint32_t)(b % W.sbytes);
+    const uint64_t base = item * (QT_ROWS * (uint64_t)W.sbytes);
+    return o < A ? base + (r % QT_ROWS) * A + o : base + QT_ROWS * A + (r % QT_ROWS) * 4 + (o - A);
   }
   return (item * QT_ROWS + r % QT_ROWS) * W.sbytes + b % W.sbytes;
 }
@@ -154,6 +167,56 @@ __host__ __device__ inline void six_bit_words(const uint32_t u[16], uint32_t out
   for (int k = 0; k < 3; k++)
     out[k] = u[4 * k] | (u[4 * k + 1] << 6) | (u[4 * k + 2] << 12) | (u[4 * k + 3] << 18) | (((T >> (8 * k)) & 0xFFu) << 24);
 }
+// Nibble u of element e (0..255) of a GGUF Q3_K block (BlockQ3K::dequantize,
+// quant.rs:506-574): q = 2 bits of qs[32n + 16h + l] at 2j, minus 4 when hmask bit
+// 4n + j of hmask[16h + l] is clear, for group 8n + 2j + h; u = q + 4.
+__host__ __device__ inline uint32_t q3k_nibble(const uint8_t* blk, int e) {
+  const int n = e >> 7, j = (e >> 5) & 3, h = (e >> 4) & 1, l = e & 15;
+  const uint32_t low = (blk[32 + 32 * n + 16 * h + l] >> (2 * j)) & 3u;
+  return low + ((blk[16 * h + l] >> (4 * n + j)) & 1u) * 4u;
+}
+// Signed scale sc - 32 of group G (0..15) of a Q3_K block: the 12 scale bytes
+// unpack to 16 six-bit values, of which group 8n + 2j + h uses value j + 4h (the
+// reference uses the first eight in both halves).
+__host__ __device__ inline int q3k_group_scale(const uint8_t* blk, int G) {
+  const uint8_t* sb = blk + 96;
+  auto rd = [&](int o) {
+    return (uint32_t)sb[o] | ((uint32_t)sb[o + 1] << 8) | ((uint32_t)sb[o + 2] << 16) | ((uint32_t)sb[o + 3] << 24);
+  };
+  const uint32_t k1 = 0x03030303u, k2 = 0x0F0F0F0Fu, a0 = rd(0), a1 = rd(4), t = rd(8);
+  const uint32_t aux[4] = {(a0 & k2) | ((t & k1) << 4), (a1 & k2) | (((t >> 2) & k1) << 4),
+                           ((a0 >> 4) & k2) | (((t >> 4) & k1) << 4), ((a1 >> 4) & k2) | (((t >> 6) & k1) << 4)};
+  const int k = ((G >> 1) & 3) + 4 * (G & 1);
+  return (int)(int8_t)(uint8_t)(aux[k >> 2] >> (8 * (k & 3))) - 32;
+}
+// 2-bit q of element e of a GGUF Q2_K block (BlockQ2K::dequantize, quant.rs:443-474):
+// bits 2j of qs[32n + 16h + l] for group 8n + 2j + h (scale byte of that group).
+__host__ __device__ inline uint32_t q2k_nibble(const uint8_t* blk, int e) {
+  const int n = e >> 7, j = (e >> 5) & 3, h = (e >> 4) & 1, l = e & 15;
+  return (blk[16 + 32 * n + 16 * h + l] >> (2 * j)) & 3u;
+}
+// Scatter GGUF Q3_K or Q2_K block k (one chunk) of a row into packed row r of g.
+// Used by the device and the host packers alike.
+__host__ __device__ inline void nibble_group_pack_block(const PackedMat& g, uint8_t* Q, uint8_t* C, uint32_t r,
+                                                        uint32_t k, const uint8_t* s) {
+  const bool q3 = g.type == T_Q3_K;
+  for (int G = 0; G < 16; G++) {
+    for (int t = 0; t < 8; t++) {
+      const int e = 16 * G + t;
+      const uint32_t lo = q3 ? q3k_nibble(s, e) : q2k_nibble(s, e), hi = q3 ? q3k_nibble(s, e + 8) : q2k_nibble(s, e + 8);
+      Q[qs_byte_off(g, r, (uint64_t)k * QT_CHUNK_BYTES + 32 * (G / 4) + 8 * (G % 4) + t)] = (uint8_t)(lo | (hi << 4));
+    }
+    C[sc_byte_off(g, r, (uint64_t)k * NG_HDR_BYTES + G)] = q3 ? (uint8_t)(int8_t)q3k_group_scale(s, G) : s[G];
+  }
+  const uint64_t hb = (uint64_t)k * NG_HDR_BYTES + 16;
+  if (q3) {
+    C[sc_byte_off(g, r, hb)] = s[108];
+    C[sc_byte_off(g, r, hb + 1)] = s[109];
+  } else {
+    for (int i = 0; i < 4; i++) C[sc_byte_off(g, r, hb + i)] = s[80 + i];
+  }
+}
+
 // Scatter GGUF Q6_K or Q5_K block k (256 elements at s) of a row into packed row r
 // of g (quant bytes into Q, header bytes into C; the zero padding is left as is).
 // Used by the device and the host packers alike.

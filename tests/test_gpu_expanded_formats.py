@@ -1,12 +1,13 @@
-"""Q5_0, Q2_K, Q3_K and Q8_K: formats the engine decodes to f32 at load.
+"""Q5_0 and Q8_K, formats the engine decodes to f32 at load, and a model mixing
+every supported format.
 
-The reference decodes each block of these formats and sums deq[j]*x[j]
-(matvec_q5_0/_q2_k/_q3_k/_q8_k, quant.rs:1050-1490), so the engine keeps the
-decoded rows (the reference's dequantize, value for value, on the host) and runs
-its F32 GEMV.  Bars: matvec within 2e-4*max|y| of the oracle (f32 reassociation
-only); embedding rows bit-exact (the host decode against the oracle's); a model
-mixing these with the tiled formats (Q5_K among them) gives the oracle's greedy
-tokens and logits within 1e-3.
+The reference decodes each block of Q5_0 and Q8_K and sums deq[j]*x[j]
+(matvec_q5_0/_q8_k, quant.rs:1050-1490), so the engine keeps the decoded rows
+(the reference's dequantize, value for value, on the host) and runs its F32 GEMV.
+Bars: matvec within 2e-4*max|y| of the oracle (f32 reassociation only);
+embedding rows bit-exact (the host decode against the oracle's); a model mixing
+these with the tiled formats (Q5_K, Q3_K, Q2_K among them, a V of its own type,
+a Q2_K LM head) gives the oracle's greedy tokens and logits within 1e-3.
 """
 import os
 
@@ -20,7 +21,8 @@ from tests.gguf_writer import F32, STR, U32, f32_bytes, write_gguf
 
 pytestmark = pytest.mark.gpu
 THREADS = min(32, os.cpu_count() or 8)
-EXPANDED = [orc.Q5_0, orc.Q2_K, orc.Q3_K, orc.Q8_K]
+EXPANDED = [orc.Q5_0, orc.Q8_K]
+RANDOM = EXPANDED + [orc.Q5_K, orc.Q3_K, orc.Q2_K]  # formats without a synthetic encoder
 
 
 def _y(m, x, M):
@@ -61,14 +63,14 @@ def test_device_bytes_equal_host_bytes(gtype):
 
 D, H, KV, FF, V, L = 256, 4, 2, 512, 300, 2
 HD = D // H
-# per layer: the ggml type of q, k, v, o, gate, up, down (layer 0: Q5_K Q/K beside an
-# f32-stored V; layer 1: the tiled formats with a Q6_K V of its own and a Q5_K down)
+# per layer: the ggml type of q, k, v, o, gate, up, down (layer 0: Q5_K Q/K beside a
+# Q3_K V, f32-stored gate/up and down; layer 1: Q4_K Q/K, a Q6_K V, Q5_K down)
 LAYER_TYPES = [(orc.Q5_K, orc.Q5_K, orc.Q3_K, orc.Q2_K, orc.Q8_K, orc.Q8_K, orc.Q5_0),
                (orc.Q4_K, orc.Q4_K, orc.Q6_K, orc.Q8_0, orc.Q4_0, orc.Q4_0, orc.Q5_K)]
 
 
 def _matrix(gtype, rows, k, seed):
-    if gtype in EXPANDED or gtype == orc.Q5_K:
+    if gtype in RANDOM:
         return fx.random_blocks(gtype, rows, k, seed)
     return synth.quantize(gtype, synth.normal(seed, 1, rows * k, std=0.05).reshape(rows, k))
 

@@ -23,11 +23,12 @@ def torch_mod():
     return torch
 
 
-Q5_K = orc.Q5_K  # no synthetic encoder: random blocks (tests/fixtures.py)
+Q5_K, Q3_K, Q2_K = orc.Q5_K, orc.Q3_K, orc.Q2_K  # no synthetic encoders: random blocks (tests/fixtures.py)
+RANDOM_BLOCK_TYPES = (Q5_K, Q3_K, Q2_K)
 
 
 def _weights(gtype, M, K, seed=1):
-    if gtype == Q5_K:
+    if gtype in RANDOM_BLOCK_TYPES:
         return fx.random_blocks(Q5_K, M, K, seed)
     w = synth.normal(seed, 100 + gtype, M * K, std=0.02).reshape(M, K)
     return synth.quantize(gtype, w)
@@ -50,7 +51,8 @@ def _run_qmv(gtype, M, K, batch=1, seed=1, raw=None):
     m.close()
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K, synth.F16, synth.F32])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K, Q3_K, Q2_K, synth.F16,
+                                   synth.F32])
 @pytest.mark.parametrize("M,K", [(1, 256), (7, 512), (33, 768), (130, 2304), (257, 4096)])
 def test_qmatvec_small_shapes(gtype, M, K):
     _run_qmv(gtype, M, K)
@@ -62,13 +64,13 @@ def test_qmatvec_ragged_rows_padded_to_units(gtype, M, K):
     _run_qmv(gtype, M, K)
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K, Q3_K, Q2_K])
 @pytest.mark.parametrize("M,K", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
 def test_qmatvec_config2_shapes(gtype, M, K):
     _run_qmv(gtype, M, K)
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K])
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K, Q3_K, Q2_K])
 @pytest.mark.parametrize("batch", [4, 8])
 def test_qmatvec_batched(gtype, batch):
     _run_qmv(gtype, 1024, 4096, batch=batch)
@@ -105,7 +107,18 @@ def test_qmatvec_q5_k_subnormal_scales_follow_reference_decode():
     _run_qmv(Q5_K, 4, 512, raw=np.frombuffer(bytes(raw), np.uint8))
 
 
-@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K, synth.F16])
+@pytest.mark.parametrize("gtype,size,offs", [(Q3_K, 110, (108,)), (Q2_K, 84, (80, 82))])
+def test_qmatvec_low_bit_k_quants_subnormal_scales_follow_reference_decode(gtype, size, offs):
+    # each row gets a subnormal f16 d (Q3_K) or d and dmin (Q2_K) in one of its blocks
+    raw = bytearray(_weights(gtype, 4, 512))
+    for r in range(4):
+        for o in offs:
+            p = (2 * r + r % 2) * size + o
+            raw[p:p + 2] = (0x0101 + r).to_bytes(2, "little")
+    _run_qmv(gtype, 4, 512, raw=np.frombuffer(bytes(raw), np.uint8))
+
+
+@pytest.mark.parametrize("gtype", [synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q6_K, Q5_K, Q3_K, Q2_K, synth.F16])
 def test_device_packing_equals_host_packing(gtype):
     # rf_matrix_create packs device-resident GGUF bytes with the pack kernel and
     # host bytes on the CPU; both must give the same packed matrix, so the same
