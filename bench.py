@@ -225,7 +225,7 @@ def run_reference(args, spec):
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "model_generation_s": gen_s,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_profile(args, spec):
@@ -242,7 +242,7 @@ def run_profile(args, spec):
     first = int(eng.generate([11, 22, 33, 44], 1)[0])
     toks, ms = eng.decode_timed(first, 2)
     torch.cuda.synchronize()
-    print(json.dumps({"profile_run": spec.name, "layers": spec.n_layers, "tokens": toks.tolist(), "ms": ms}))
+    emit({"profile_run": spec.name, "layers": spec.n_layers, "tokens": toks.tolist(), "ms": ms})
     eng.close()
 
 
@@ -278,7 +278,7 @@ def run_ring(args, spec):
     layer_bytes = st["host_image_bytes"] / n
     value = args.steps / (dev_ms / 1e3)
     bound = h2d_gbs * 1e9 / (n * layer_bytes)
-    print(json.dumps({
+    emit({
         "metric": "out-of-core decode tokens/s (Llama-3-8B Q4_K shape, streamed layers)", "value": value,
         "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "data": "synthetic",
@@ -286,7 +286,7 @@ def run_ring(args, spec):
                    "layer_image_bytes": layer_bytes, "prompt_tokens": len(prompt)},
         "roofline": {"bound": "h2d", "achieved": n * layer_bytes * value / 1e9, "peak": h2d_gbs, "unit": "GB/s",
                      "frac": value / bound, "peak_source": "pinned host-to-device copy measured in this run"},
-        "residency_stats": st}))
+        "residency_stats": st})
     eng.close()
 
 
@@ -299,7 +299,27 @@ def workload_config(spec, args, tp):
             "l2": "no flush: every step streams 4.5 GB of weights (> 126 MB L2)"}
 
 
+_RESULT_FD = None
+
+
+def emit(obj):
+    """Write one result line (JSON) to the process's real stdout."""
+    sys.stdout.flush()
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(obj) + "\n").encode())
+
+
+def json_only_stdout():
+    """Point file descriptor 1 at stderr for the rest of the run, so that nothing
+    but the result line reaches stdout: libraries print there at the C level (NCCL's
+    version banner when the environment sets NCCL_DEBUG, for one)."""
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
 def main():
+    json_only_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
@@ -425,7 +445,7 @@ def main():
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(gguf, spec)
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 if __name__ == "__main__":

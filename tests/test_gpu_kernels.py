@@ -29,7 +29,7 @@ RANDOM_BLOCK_TYPES = (Q5_K, Q3_K, Q2_K)
 
 def _weights(gtype, M, K, seed=1):
     if gtype in RANDOM_BLOCK_TYPES:
-        return fx.random_blocks(Q5_K, M, K, seed)
+        return fx.random_blocks(gtype, M, K, seed)
     w = synth.normal(seed, 100 + gtype, M * K, std=0.02).reshape(M, K)
     return synth.quantize(gtype, w)
 
