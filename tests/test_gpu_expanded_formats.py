@@ -75,14 +75,13 @@ def _matrix(gtype, rows, k, seed):
     return synth.quantize(gtype, synth.normal(seed, 1, rows * k, std=0.05).reshape(rows, k))
 
 
-@pytest.fixture(scope="module")
-def mixed_model():
+def _mixed_gguf(embd_type=orc.Q5_0):
     meta = [("general.architecture", STR, "llama"), ("llama.vocab_size", U32, V), ("llama.context_length", U32, 128),
             ("llama.embedding_length", U32, D), ("llama.block_count", U32, L), ("llama.feed_forward_length", U32, FF),
             ("llama.attention.head_count", U32, H), ("llama.attention.head_count_kv", U32, KV),
             ("llama.attention.layer_norm_rms_epsilon", F32, 1e-5), ("llama.rope.freq_base", F32, 10000.0)]
     ones = f32_bytes(np.ones(D, np.float32))
-    ts = [("token_embd.weight", [D, V], orc.Q5_0, fx.random_blocks(orc.Q5_0, V, D, 1).tobytes())]
+    ts = [("token_embd.weight", [D, V], embd_type, _matrix(embd_type, V, D, 1).tobytes())]
     shapes = [(D, H * HD), (D, KV * HD), (D, KV * HD), (H * HD, D), (D, FF), (D, FF), (FF, D)]
     names = ["attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"]
     for l in range(L):
@@ -93,6 +92,11 @@ def mixed_model():
     ts.append(("output_norm.weight", [D], 0, ones))
     ts.append(("output.weight", [D, V], orc.Q2_K, fx.random_blocks(orc.Q2_K, V, D, 2).tobytes()))
     return write_gguf(meta, ts)
+
+
+@pytest.fixture(scope="module")
+def mixed_model():
+    return _mixed_gguf()
 
 
 def test_mixed_model_embedding_rows_are_exact(mixed_model):
@@ -122,4 +126,26 @@ def test_mixed_model_stepwise_parity_and_generation(mixed_model):
     want, _, margins = orc.OracleModel(mixed_model, kv_f16=True, max_seq=64, threads=THREADS).generate(prompt, 20)
     eng = DecodeEngine(mixed_model, max_seq_len=64)
     assert eng.generate(prompt, 20).tolist() == want.tolist(), margins
+    eng.close()
+
+
+@pytest.mark.parametrize("embd_type", [orc.Q2_K, orc.Q3_K, orc.Q5_K, orc.Q6_K, orc.Q8_K])
+def test_embedding_rows_of_every_format_are_exact(embd_type):
+    # token_embd in each format: the row the engine decodes on the device (tiled
+    # formats) or on the host (f32-held ones) equals the reference's dequantize
+    from tests.gguf_reader import tensor_bytes
+    g = _mixed_gguf(embd_type)
+    eng = DecodeEngine(g, max_seq_len=16)
+    rb = orc.row_bytes(embd_type, D)
+    emb = tensor_bytes(g, "token_embd.weight")
+    for tok in (0, 64, 199, V - 1):
+        eng.embed(tok)
+        assert np.array_equal(eng.hidden(), orc.dequant_row(embd_type, emb[tok * rb:(tok + 1) * rb], D)), tok
+    eng.kv_reset()
+    ref = orc.OracleModel(g, kv_f16=True, max_seq=16, threads=THREADS)
+    h, hr = eng.forward_single_streaming(42, 0), ref.forward(42, 0)
+    assert np.abs(h - hr).max() <= 1e-3 * np.abs(hr).max()
+    lg, am = eng.compute_logits()
+    lr = ref.logits(hr)
+    assert np.abs(lg - lr).max() <= 1e-3 * np.abs(lr).max() and am == orc.argmax(lr)
     eng.close()
