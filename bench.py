@@ -290,6 +290,58 @@ def run_ring(args, spec):
     eng.close()
 
 
+# GGUF bytes per 256 weights (quant.rs block sizes)
+GGUF_BYTES_PER_256 = {"Q8_0": 272, "Q4_0": 144, "Q4_K": 144, "Q5_K": 176, "Q6_K": 210, "Q3_K": 110, "Q2_K": 84}
+
+
+def run_gemv_sweep(args):
+    """--gemv-sweep: benchmark configuration 2, the standalone quantized GEMV
+    (rf_qmatvec) of every tiled format on the four config-2 shapes at batch 1, one
+    JSON line each.  Time: CUDA events on the launching stream around 100 calls
+    after 3 warm-up calls, rotating over distinct copies of the matrix that
+    together exceed 4x the 126 MB L2.  `gbs` is algorithmic bytes (GGUF bytes
+    M*K*b plus 4K + 4M) over that time; `moved_bytes` is the packed matrix."""
+    import torch
+    from ramforge_b200 import QMatrix, synth
+    peak, peak_kind = measured_peaks()
+    names = {synth.Q8_0: "Q8_0", synth.Q4_0: "Q4_0", synth.Q4_K: "Q4_K", synth.Q5_K: "Q5_K", synth.Q6_K: "Q6_K",
+             synth.Q3_K: "Q3_K", synth.Q2_K: "Q2_K"}
+    shapes = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+    stream = torch.cuda.current_stream()
+    for gtype, name in names.items():
+        for M, K in shapes:
+            if gtype in (synth.Q5_K, synth.Q3_K, synth.Q2_K):
+                raw = synth.random_blocks(gtype, M, K, seed=M)
+            else:
+                raw = synth.quantize(gtype, synth.normal(1, 100 + gtype, M * K, std=0.02).reshape(M, K))
+            first = QMatrix(gtype, raw, M, K)
+            copies = [first] + [QMatrix(gtype, raw, M, K)
+                                for _ in range(min(63, -(-4 * 126_000_000 // first.device_bytes) - 1))]
+            del raw
+            x = torch.randn(K, device="cuda")
+            y = torch.empty(M, device="cuda")
+            for i in range(3):
+                copies[i % len(copies)].matvec(x.data_ptr(), y.data_ptr(), 1, stream.cuda_stream)
+            n = 100
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for i in range(n):
+                copies[i % len(copies)].matvec(x.data_ptr(), y.data_ptr(), 1, stream.cuda_stream)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / n
+            alg = M * K * GGUF_BYTES_PER_256[name] / 256 + 4 * K + 4 * M
+            emit({"metric": "standalone GEMV GB/s (benchmark configuration 2)", "format": name, "M": M, "K": K,
+                  "batch": 1, "us_per_call": us, "gbs": alg / us / 1e3, "unit": "GB/s",
+                  "frac": alg / us / 1e3 / peak, "peak": peak, "peak_source": f"{peak_kind} hbm_gbs",
+                  "algorithmic_bytes": alg, "moved_bytes": first.device_bytes, "copies": len(copies), "calls": n})
+            for m in copies:
+                m.close()
+            del copies
+            torch.cuda.empty_cache()
+
+
 def workload_config(spec, args, tp):
     return {"workload": "llama-3-8b-shape Q4_K batch-1 greedy decode (BASELINE configs[3])",
             "layers": spec.n_layers, "dim": spec.n_embd, "heads": f"{spec.n_heads}q/{spec.n_kv_heads}kv",
@@ -329,6 +381,7 @@ def main():
     ap.add_argument("--profile", action="store_true", help="small eager run for ncu captures")
     ap.add_argument("--layers", type=int, default=0, help="with --profile: layer count of the model")
     ap.add_argument("--ring", type=int, default=0, help="out-of-core run: stream this many layers per step")
+    ap.add_argument("--gemv-sweep", action="store_true", help="benchmark configuration 2: GEMV per format and shape")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -345,6 +398,9 @@ def main():
         return
     if args.ring:
         run_ring(args, spec)
+        return
+    if args.gemv_sweep:
+        run_gemv_sweep(args)
         return
 
     import torch

@@ -18,6 +18,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 SYNTH_PATH = os.path.join(_HERE, "librfsynth.so")
 
 F32, F16, Q4_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 8, 12, 14
+Q5_0, Q2_K, Q3_K, Q5_K, Q8_K = 6, 10, 11, 13, 15  # no encoder here: random_blocks
 TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
 
 
@@ -146,3 +147,25 @@ def quantize(gtype: int, x: np.ndarray, threads: int | None = None) -> np.ndarra
 
 def row_bytes(gtype: int, n: int) -> int:
     return lib().rfs_row_bytes(gtype, n)
+
+
+# Block layouts of the formats without an encoder here: (elements, bytes, offsets of
+# the f16 super-scales that must be finite).
+_RANDOM_BLOCKS = {Q5_0: (32, 22, (0,)), Q2_K: (256, 84, (80, 82)), Q3_K: (256, 110, (108,)),
+                  Q5_K: (256, 176, (0, 2)), Q8_K: (256, 292, ())}
+
+
+def random_blocks(gtype: int, rows: int, k: int, seed: int) -> np.ndarray:
+    """rows x k weights of ggml type gtype (Q5_0, Q2_K, Q3_K, Q5_K, Q8_K) as GGUF blocks of
+    random quant and scale bytes, with normal f16 super-scales in [2^-12, 2^-10)
+    (Q8_K: an f32 d in [1e-3, 3e-3)).  Every byte pattern of the other fields is a
+    valid block, so these are well-formed weights of the format's full value range."""
+    qk, bs, dpos = _RANDOM_BLOCKS[gtype]
+    rng = np.random.default_rng(seed)
+    nb = rows * k // qk
+    b = rng.integers(0, 256, (nb, bs), dtype=np.uint8)
+    for o in dpos:
+        b[:, o:o + 2] = rng.integers(0x0C00, 0x1400, nb).astype("<u2").view(np.uint8).reshape(nb, 2)
+    if gtype == Q8_K:
+        b[:, 0:4] = rng.uniform(1e-3, 3e-3, nb).astype("<f4").view(np.uint8).reshape(nb, 4)
+    return b.reshape(-1)

@@ -235,22 +235,8 @@ def qwen2_bias_reference_forward(w, token, pos, k_hist: list, v_hist: list, eps=
                              QB_FFN)
 
 
-# Block layouts of formats without a synthetic encoder, for random test weights:
-# (elements, bytes, offsets of the f16 super-scales that must be finite).
-_RANDOM_BLOCKS = {6: (32, 22, (0,)), 10: (256, 84, (80, 82)), 11: (256, 110, (108,)), 13: (256, 176, (0, 2)),
-                  15: (256, 292, ())}
-
-
 def random_blocks(gtype: int, rows: int, k: int, seed: int) -> np.ndarray:
-    """rows x k weights of ggml type gtype (Q5_0, Q2_K, Q3_K, Q5_K, Q8_K) as GGUF blocks of
-    random quant and scale bytes, with normal f16 super-scales in [2^-12, 2^-10)
-    (Q8_K: an f32 d in [1e-3, 3e-3))."""
-    qk, bs, dpos = _RANDOM_BLOCKS[gtype]
-    rng = np.random.default_rng(seed)
-    nb = rows * k // qk
-    b = rng.integers(0, 256, (nb, bs), dtype=np.uint8)
-    for o in dpos:
-        b[:, o:o + 2] = rng.integers(0x0C00, 0x1400, nb).astype("<u2").view(np.uint8).reshape(nb, 2)
-    if gtype == 15:
-        b[:, 0:4] = rng.uniform(1e-3, 3e-3, nb).astype("<f4").view(np.uint8).reshape(nb, 4)
-    return b.reshape(-1)
+    """Random well-formed GGUF blocks of a format without a synthetic encoder
+    (ramforge_b200.synth.random_blocks)."""
+    from ramforge_b200 import synth
+    return synth.random_blocks(gtype, rows, k, seed)
