@@ -1,0 +1,37 @@
+"""bench.py's output contract, checked on CPU: the run prints exactly one JSON
+line on stdout with the keys the driver reads, whatever else the process or its
+libraries write to file descriptor 1 (NCCL's version banner under NCCL_DEBUG,
+for one).  The reference arm runs here without a GPU; the same routing serves
+every mode of bench.py.
+"""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_arm_prints_one_json_line():
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = r.stdout.splitlines()
+    assert len(lines) == 1, lines
+    d = json.loads(lines[0])
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "e2e", "cpu_baseline"):
+        assert k in d, k
+    assert d["impl"] == "reference" and d["warmup"] >= 3 and d["value"] > 0
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
+    assert "workload" in d["config"]
+
+
+def test_only_the_result_line_reaches_stdout():
+    code = ("import os, sys; sys.path.insert(0, %r); import bench; bench.json_only_stdout(); "
+            "os.write(1, b'banner from a library\\n'); print('a stray print'); bench.emit({'value': 1})" % ROOT)
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.splitlines() == ['{"value": 1}']
+    assert "banner from a library" in r.stderr and "a stray print" in r.stderr
