@@ -35,3 +35,17 @@ def test_only_the_result_line_reaches_stdout():
     assert r.returncode == 0, r.stderr
     assert r.stdout.splitlines() == ['{"value": 1}']
     assert "banner from a library" in r.stderr and "a stray print" in r.stderr
+
+
+def test_reference_arm_under_torchrun_prints_from_rank_0_only():
+    # two ranks as the driver launches them: rank 0 runs the bounded CPU sample and
+    # prints the line, rank 1 exits 0 without work
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", "29617", "bench.py", "--impl", "reference",
+                        "--gpus", "2", "--steps", "1", "--warmup", "0"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2
