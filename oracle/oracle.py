@@ -120,6 +120,8 @@ def matvec(gtype: int, raw, n_in: int, n_out: int, x: np.ndarray, threads: int =
     b = np.ascontiguousarray(np.frombuffer(bytes(raw), np.uint8) if not isinstance(raw, np.ndarray) else raw,
                              dtype=np.uint8)
     x = np.ascontiguousarray(x, np.float32)
+    if x.size != n_in:  # TensorData::matvec refuses, never reinterprets (tensor.rs:1205-1218)
+        raise OracleError(f"matvec arity mismatch: x has {x.size} elements, the matrix takes {n_in}")
     y = np.empty(n_out, np.float32)
     if reference:
         _check(lib().orc_matvec_reference(gtype, b.ctypes.data_as(_u8p), b.size, n_in, n_out, _fp(x), _fp(y)))

@@ -84,6 +84,22 @@ def test_gqa_fixture_matches_oracle_and_reference_forward():
     eng.close()
 
 
+def test_kv_invariants_across_prompt_and_decode():  # inference.rs:2879-3003
+    eng = DecodeEngine(fx.gqa_gguf(), max_seq_len=16)
+    kvd = eng.config["n_kv_heads"] * eng.config["head_dim"]
+    seq, pos = [1, 3, 5, 7], 0
+    for _ in range(len(seq) + 3):
+        assert eng.kv_seq_len == pos
+        eng.forward_single_streaming(seq[pos], pos)
+        assert eng.kv_seq_len == pos + 1
+        for which in (False, True):
+            assert eng.kv_read(0, which, 0, pos + 1).shape == (pos + 1, kvd)
+        if pos >= len(seq) - 1:
+            seq.append(eng.compute_logits()[1])
+        pos += 1
+    eng.close()
+
+
 def test_gqa_fixture_greedy_generation():
     g = fx.gqa_gguf()
     ref = orc.OracleModel(g, kv_f16=True, max_seq=32).generate([1, 3], 12)[0]

@@ -141,6 +141,44 @@ def test_device_packing_equals_host_packing(gtype):
     b.close()
 
 
+def _qmv_once(gtype, raw, M, K, x):
+    torch = torch_mod()
+    m = QMatrix(gtype, np.frombuffer(bytes(raw), np.uint8), M, K)
+    dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    dy = torch.empty(M, device="cuda")
+    m.matvec(dx.data_ptr(), dy.data_ptr())
+    torch.cuda.synchronize()
+    m.close()
+    return dy.cpu().numpy()
+
+
+def test_qmatvec_nonsquare_layout_anchors():
+    # the ggml [in, out] anchors of tensor.rs:1161-1306 through rf_qmatvec
+    import struct
+    f32 = np.array([1, 2, 3, 4, 5, 6], np.float32).tobytes()
+    assert _qmv_once(synth.F32, f32, 3, 2, [10, 20]).tolist() == [50.0, 110.0, 170.0]
+    assert _qmv_once(synth.F32, f32, 2, 3, [1, 0, -1]).tolist() == [-2.0, -2.0]
+    f16 = struct.pack("<4H", 0x3C00, 0x4000, 0x4200, 0x4400)
+    assert np.allclose(_qmv_once(synth.F16, f16, 2, 2, [1, 1]), [3.0, 7.0], atol=1e-3)
+    blk = lambda fill: struct.pack("<H", 0x3C00) + bytes([fill] * 16)
+    q40 = b"".join(blk(fill) * 2 for fill in (0x11, 0x23, 0xF8))
+    assert np.allclose(_qmv_once(synth.Q4_0, q40, 3, 64, [1.0] * 32 + [2.0] * 32), [-672.0, -528.0, 336.0], atol=1e-3)
+    q4k = b"".join(struct.pack("<HH", 0x3C00, 0) + bytes([1] * 12) + bytes([fill] * 128) for fill in (0x11, 0x22))
+    assert np.allclose(_qmv_once(synth.Q4_K, q4k, 2, 256, [1.0] * 256), [256.0, 512.0], atol=1e-3)
+
+
+def test_qmatvec_q4_0_lcg_rows_at_qwen2_5_q_shape():
+    # the pseudorandom Q4_0 matrix of streaming_model.rs:3332-3411 against the oracle
+    from tests.test_oracle_golden import lcg_q4_0_rows
+    n = 1536
+    raw = lcg_q4_0_rows(n, n)
+    x = (np.sin(np.arange(n, dtype=np.float32) * np.float32(0.0137) - np.float32(0.5)) * np.float32(0.7)).astype(
+        np.float32)
+    _run_qmv(synth.Q4_0, n, n, raw=np.frombuffer(raw, np.uint8))
+    ref = orc.matvec(orc.Q4_0, raw, n, n, x, reference=True)
+    assert np.abs(_qmv_once(synth.Q4_0, raw, n, n, x) - ref).max() < 1e-2
+
+
 @pytest.mark.parametrize("ctx", [1, 5, 512, 2048, 8192, 32768])
 @pytest.mark.parametrize("batch", [1, 8])
 def test_decode_attention_config3(ctx, batch):

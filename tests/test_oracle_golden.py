@@ -370,6 +370,67 @@ def test_quantized_reference_covers_every_format(gtype, qk, block):  # compute.r
     assert np.all(np.abs(a - b) <= 1e-2 + 1e-5 * np.maximum(np.abs(a), np.abs(b)))
 
 
+# ---- ggml [in, out] layout anchors (tensor.rs:1161-1306) -------------------------
+def test_matvec_nonsquare_layout_anchors():
+    f32 = np.array([1, 2, 3, 4, 5, 6], np.float32).tobytes()
+    assert orc.matvec(orc.F32, f32, 2, 3, np.array([10, 20], np.float32)).tolist() == [50.0, 110.0, 170.0]
+    assert orc.matvec(orc.F32, f32, 3, 2, np.array([1, 0, -1], np.float32)).tolist() == [-2.0, -2.0]
+    f16 = struct.pack("<4H", 0x3C00, 0x4000, 0x4200, 0x4400)  # 1, 2, 3, 4
+    assert np.allclose(orc.matvec(orc.F16, f16, 2, 2, np.ones(2, np.float32)), [3.0, 7.0], atol=1e-3)
+    with pytest.raises(orc.OracleError, match="arity mismatch"):  # x of 3 for a 2-input matrix
+        orc.matvec(orc.F32, f32, 2, 3, np.ones(3, np.float32))
+    q40 = b"".join(q4_0_block(0x3C00, [fill] * 16) * 2 for fill in (0x11, 0x23, 0xF8))
+    x = np.array([1.0] * 32 + [2.0] * 32, np.float32)
+    y = orc.matvec(orc.Q4_0, q40, 64, 3, x)
+    assert np.allclose(y, [-672.0, -528.0, 336.0], atol=1e-3)
+    assert np.allclose(y, orc.matvec(orc.Q4_0, q40, 64, 3, x, reference=True), atol=1e-3)
+    q4k = b"".join(struct.pack("<HH", 0x3C00, 0) + bytes([1] * 12) + bytes([fill] * 128) for fill in (0x11, 0x22))
+    assert np.allclose(orc.matvec(orc.Q4_K, q4k, 256, 2, np.ones(256, np.float32)), [256.0, 512.0], atol=1e-3)
+
+
+def lcg_q4_0_rows(in_dim, out_dim, seed=0xC0FFEE):
+    """The pseudorandom Q4_0 rows of streaming_model.rs:3344-3362: a u32 LCG (1664525,
+    1013904223) per row, d = f16 of 0.05 + 0.45 * (s >> 8) / 2^24, nibbles from s."""
+    M = 0xFFFFFFFF
+    step = lambda v: (v * 1664525 + 1013904223) & M
+    out = bytearray()
+    for _ in range(out_dim):
+        s, seed = seed, step(seed)
+        for _ in range(in_dim // 32):
+            s = step(s)
+            d = np.float32(0.05) + np.float32((s >> 8) / float(1 << 24)) * np.float32(0.45)
+            out += np.float16(d).tobytes()
+            for _ in range(16):
+                s = step(s)
+                out.append((s & 0x0F) | (((s >> 4) & 0x0F) << 4))
+    return bytes(out)
+
+
+def test_q4_0_parallel_matvec_matches_scalar_at_qwen2_5_q_shape():  # streaming_model.rs:3332-3411
+    n = 1536
+    raw = lcg_q4_0_rows(n, n)
+    x = (np.sin(np.arange(n, dtype=np.float32) * np.float32(0.0137) - np.float32(0.5)) * np.float32(0.7)).astype(
+        np.float32)
+    ref = orc.matvec(orc.Q4_0, raw, n, n, x, reference=True)
+    got = orc.matvec(orc.Q4_0, raw, n, n, x, threads=4)
+    assert np.abs(got - ref).max() < 1e-2
+
+
+def test_kv_invariants_across_prompt_and_decode():  # inference.rs:2879-3003
+    m = orc.OracleModel(fx.gqa_gguf(), kv_f16=False, max_seq=16)
+    kvd = fx.GQA_N_KV_HEADS * fx.GQA_HEAD_DIM
+    seq, pos = [1, 3, 5, 7], 0
+    for step in range(len(seq) + 3):
+        assert m.kv_len == pos
+        h = m.forward(seq[pos], pos)
+        assert m.kv_len == pos + 1
+        for which in (False, True):
+            assert m.kv_read(0, which, 0, pos + 1).size == (pos + 1) * kvd
+        if pos >= len(seq) - 1:
+            seq.append(orc.argmax(m.logits(h)))
+        pos += 1
+
+
 def test_greedy_argmax_first_max_wins():  # sampling.rs:45-56
     assert orc.argmax([1.0, 3.0, 3.0, 2.0]) == 1
     assert orc.argmax([5.0]) == 0
