@@ -138,8 +138,8 @@ GATEUP_DRAM_BYTES_NCU = 66_747_648
 
 
 def algorithmic_bytes(spec, tp: int, ctx: float):
-    """Weight + activation bytes one decode token must move (per rank), per SURVEY 8(d):
-    matrices M*K*b (b = GGUF bytes/element), KV f16 at context ctx, vectors 4 bytes/elem."""
+    """Weight + activation bytes one decode token must move (per rank): matrices
+    M*K*b (b = GGUF bytes/element), KV f16 at context ctx, vectors 4 bytes/elem."""
     from ramforge_b200 import synth
     bpe = {synth.Q4_K: 144 / 256, synth.Q8_0: 34 / 32, synth.Q4_0: 18 / 32}
     d, ff, hd = spec.n_embd, spec.n_ff, spec.head_dim
@@ -247,7 +247,7 @@ def run_profile(args, spec):
 
 
 def run_ring(args, spec):
-    """--ring N: out-of-core decode (the residency ring).  The last N
+    """--ring N: out-of-core decode through the residency ring.  The last N
     layers of the same model are left out of the residency plan and stream every
     step from pinned host images through 2 device ring slots; the line reports
     tokens/s against the bound the measured pinned host-to-device bandwidth sets
