@@ -308,7 +308,10 @@ def run_gemv_sweep(args):
              synth.Q3_K: "Q3_K", synth.Q2_K: "Q2_K"}
     shapes = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
     stream = torch.cuda.current_stream()
+    want = set(f for f in args.formats.split(",") if f) or set(names.values())
     for gtype, name in names.items():
+        if name not in want:
+            continue
         for M, K in shapes:
             if gtype in (synth.Q5_K, synth.Q3_K, synth.Q2_K):
                 raw = synth.random_blocks(gtype, M, K, seed=M)
@@ -382,6 +385,7 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="with --profile: layer count of the model")
     ap.add_argument("--ring", type=int, default=0, help="out-of-core run: stream this many layers per step")
     ap.add_argument("--gemv-sweep", action="store_true", help="benchmark configuration 2: GEMV per format and shape")
+    ap.add_argument("--formats", default="", help="with --gemv-sweep: comma-separated subset, e.g. Q4_K,Q6_K")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()

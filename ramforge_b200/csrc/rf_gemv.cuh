@@ -302,6 +302,17 @@ __device__ __forceinline__ void q4_pair(uint32_t A, uint32_t B, const float4& xl
   hi = __ffma2_rn(ff2(as_f(B & 0xF0u), as_f(B & 0xF000u)), ff2(xh1.x, xh1.y), hi);
   hi = __ffma2_rn(ff2(as_f(B & 0xF00000u), as_f(P & 0xF000u)), ff2(xh1.z, xh1.w), hi);
 }
+// Half of q4_pair: the low (HI = false) or the high nibbles of bytes 0..7 of
+// (A, B) against x0 (bytes 0-3) and x1 (bytes 4-7), into acc; P = byte_perm(A, B, 0x0073).
+template <bool HI>
+__device__ __forceinline__ void q4_half(uint32_t A, uint32_t B, uint32_t P, const float4& x0, const float4& x1,
+                                        float2& acc) {
+  constexpr uint32_t s = HI ? 4 : 0;
+  acc = __ffma2_rn(ff2(as_f(A & (0xFu << s)), as_f(A & (0xF00u << s))), ff2(x0.x, x0.y), acc);
+  acc = __ffma2_rn(ff2(as_f(A & (0xF0000u << s)), as_f(P & (0xFu << s))), ff2(x0.z, x0.w), acc);
+  acc = __ffma2_rn(ff2(as_f(B & (0xFu << s)), as_f(B & (0xF00u << s))), ff2(x1.x, x1.y), acc);
+  acc = __ffma2_rn(ff2(as_f(B & (0xF0000u << s)), as_f(P & (0xF00u << s))), ff2(x1.z, x1.w), acc);
+}
 // 8 signed bytes of (A, B), biased to q+128, against x[k].
 __device__ __forceinline__ void q8_pair(uint32_t A, uint32_t B, const float4& x0, const float4& x1, float2& s) {
   constexpr uint32_t M = 0x80808080u;
@@ -776,13 +787,28 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
           for (int p = 0; p < 4; p++) {
             const int G = 4 * c + p;
             const float* xb = xc + 16 * G;
-            const float4 xl0 = lds4(xb), xl1 = lds4(xb + 4), xh0 = lds4(xb + 8), xh1 = lds4(xb + 12);
             const float xs = xsc[G];
+            // low nibbles (elements 0-7) then high ones (8-15): 8 activations live at a time
+            float2 sa[2] = {ff2(0.f, 0.f), ff2(0.f, 0.f)};
+            {
+              const float4 x0 = lds4(xb), x1 = lds4(xb + 4);
+#pragma unroll
+              for (int s = 0; s < 2; s++) {
+                const uint32_t A = w[s][c][2 * p], B = w[s][c][2 * p + 1];
+                q4_half<false>(A, B, __byte_perm(A, B, 0x0073), x0, x1, sa[s]);
+              }
+            }
+            {
+              const float4 x0 = lds4(xb + 8), x1 = lds4(xb + 12);
+#pragma unroll
+              for (int s = 0; s < 2; s++) {
+                const uint32_t A = w[s][c][2 * p], B = w[s][c][2 * p + 1];
+                q4_half<true>(A, B, __byte_perm(A, B, 0x0073), x0, x1, sa[s]);
+              }
+            }
 #pragma unroll
             for (int s = 0; s < 2; s++) {
-              float2 sl = ff2(0.f, 0.f), sh = ff2(0.f, 0.f);
-              q4_pair(w[s][c][2 * p], w[s][c][2 * p + 1], xl0, xl1, xh0, xh1, sl, sh);
-              const float S = (sl.x + sl.y) + (sh.x + sh.y);
+              const float S = sa[s].x + sa[s].y;
               if constexpr (FMT == T_Q3_K) {
                 const float scf = sbyte_f(hc[s][G >> 2], G & 3);
                 aS[s] = fmaf(scf, S, aS[s]);
