@@ -75,6 +75,28 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(L, name), name
 
 
+def _header_defines(prefix):
+    hdr = open(os.path.join(ROOT, "include", "rfcuda.h")).read()
+    return {m.group(1): int(m.group(2)) for m in re.finditer(r"#define (%s\w+) \(?(-?\d+)\)?" % prefix, hdr)}
+
+
+def test_type_and_role_ids_agree_across_header_bindings_and_oracle():
+    types = _header_defines("RF_TYPE_")
+    assert set(types) == {"RF_TYPE_" + n for n in ("F32", "F16", "Q4_0", "Q5_0", "Q8_0", "Q2_K", "Q3_K", "Q4_K",
+                                                    "Q5_K", "Q6_K", "Q8_K")}
+    for name, v in types.items():
+        short = name[len("RF_TYPE_"):]
+        assert getattr(_lib, "TYPE_" + short) == v, name
+        assert getattr(orc, short) == v, name
+        if hasattr(synth, short):
+            assert getattr(synth, short) == v, name
+    roles = _header_defines("RF_ROLE_")
+    for i, n in enumerate(_lib.LAYER_VIEW_NAMES):
+        assert roles["RF_ROLE_" + n.replace(".", "_").upper()] == i, n
+    assert (roles["RF_ROLE_TOKEN_EMBD"], roles["RF_ROLE_OUTPUT_NORM"], roles["RF_ROLE_OUTPUT"]) == (
+        _lib.ROLE_TOKEN_EMBD, _lib.ROLE_OUTPUT_NORM, _lib.ROLE_OUTPUT)
+
+
 def test_abi_version_matches_header():
     src = open(os.path.join(ROOT, "include", "rfcuda.h")).read()
     v = int(re.search(r"#define RF_ABI_VERSION (\d+)", src).group(1))
