@@ -191,6 +191,11 @@ def test_shard_plan_rejects_uneven_or_block_cutting_splits():
     cfg = _spec_cfg(synth.scaled(synth.LLAMA3_8B, n_embd=1024, n_heads=8, n_kv_heads=8))
     assert shard(cfg, 8, 0, synth.Q4_K)[0] == _lib.RF_EINVAL
     assert shard(cfg, 8, 0, synth.Q8_0)[0] == 0
+    # every 256-element K-quant has Q4_K's constraint; the 32-element formats have Q8_0's
+    for t in (synth.Q2_K, synth.Q3_K, synth.Q5_K, synth.Q6_K, synth.Q8_K):
+        assert shard(cfg, 8, 0, t)[0] == _lib.RF_EINVAL, t
+        assert shard(cfg, 4, 0, t)[0] == 0, t
+    assert shard(cfg, 8, 0, synth.Q5_0)[0] == 0
 
 
 def test_engine_creation_fails_cleanly_without_gpu():
