@@ -1,6 +1,7 @@
 #!/usr/bin/env python3
 """Decode benchmark: batch-1 greedy decode tokens/s of the Llama-3-8B-shaped
-Q4_K model on 1..8 B200s (tensor parallel).
+Q4_K model (32 layers, dim 4096, 32/8 heads, FFN 14336, vocab 128256, Q8_0
+embedding/output) on 1..8 B200s (tensor parallel).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -169,62 +170,82 @@ def make_model(spec, world, rank):
     return path
 
 
-def cpu_baseline(gguf, spec):
-    """Reference CPU path (oracle port): one full decode token (32 layers + LM head)
-    at position 0 with the reference's dispatch (Q4_K/Q8_0 matvecs single-threaded,
-    compute_dispatch.rs:219-254)."""
+def cpu_baseline(gguf, spec, ctx: int, threads: int = 1):
+    """Reference CPU path (oracle port): one full decode token (32 layers + LM head +
+    argmax) at position `ctx`, the context the GPU arm decodes at, over a seeded
+    synthetic KV history of that length.  threads=1 is the reference's own
+    dispatch (Q4_K/Q8_0 matvecs single-threaded, compute_dispatch.rs:219-254);
+    more threads split every matvec's rows over host cores (not the reference's
+    dispatch for these formats; the rows' arithmetic is unchanged)."""
     from oracle import oracle as orc
-    m = orc.OracleModel(gguf, kv_f16=True, max_seq=8, threads=1)
+    m = orc.OracleModel(gguf, kv_f16=True, max_seq=ctx + 2, threads=threads)
+    m.kv_fill_synthetic(ctx)
     t0 = time.perf_counter()
-    fh = m.forward(1, 0)
+    fh = m.forward(1, ctx)
     orc.argmax(m.logits(fh))
     dt = time.perf_counter() - t0
     m.close()
-    return {"value": 1.0 / dt, "unit": UNIT, "cores": 1, "kind": "port",
-            "sample": "1 greedy decode token of the same model (32 layers + LM head, position 0), oracle port "
-                      "with the reference's threading (Q4_K/Q8_0 matvecs single-threaded)",
+    what = ("the reference's threading (Q4_K/Q8_0 matvecs single-threaded)" if threads == 1 else
+            f"every matvec's rows split over {threads} host threads (all cores, row-parallel; the reference "
+            "itself runs Q4_K/Q8_0 single-threaded)")
+    return {"value": 1.0 / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"1 greedy decode token of the same model (32 layers + LM head + argmax) at position {ctx} "
+                      f"over a synthetic KV history, oracle port with {what}",
             "seconds": dt}
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
 
 
 def run_reference(args, spec):
     """--impl reference: the reference's CPU implementation (oracle port, its own
-    threading) on this workload.  A step is a bounded sample: one layer of a token
-    forward (layer i mod 32, no commit) plus 1/32 of the LM head rows, so
-    tokens/s = 1 / (32 * mean step time)."""
+    threading: Q4_K/Q8_0 matvecs single-threaded, compute_dispatch.rs:219-254) on
+    this workload, at the contexts the GPU arm decodes at (step i attends over
+    PROMPT_LEN + warmup + i positions of a seeded synthetic KV history).  A step is
+    a bounded sample: one layer of a decode token (layer i mod 32, no commit) plus
+    1/32 of the LM-head rows, so tokens/s = 1 / (32 * mean step time)."""
     from oracle import oracle as orc
     from ramforge_b200 import synth
     t_gen = time.perf_counter()
     g = synth.gguf_bytes(spec)
     gen_s = time.perf_counter() - t_gen
-    m = orc.OracleModel(g, kv_f16=True, max_seq=8, threads=1)
+    ctx0 = PROMPT_LEN + args.warmup
+    m = orc.OracleModel(g, kv_f16=True, max_seq=ctx0 + args.steps + 2, threads=1)
+    m.kv_fill_synthetic(ctx0 + args.steps)
     L, V = spec.n_layers, spec.vocab_size
     hidden = np.asarray(synth.normal(9, 9, spec.n_embd), np.float32)
 
-    def step(i):
+    def step(i, pos):
         layer = i % L
-        m.layer_step(layer, 0, hidden)
+        m.layer_step(layer, pos, hidden)
         r0 = layer * V // L
         m.logits_rows(hidden, r0, (layer + 1) * V // L)
 
     for i in range(args.warmup):
-        step(i)
+        step(i, PROMPT_LEN + i)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        step(args.warmup + i)
+        step(args.warmup + i, ctx0 + i)
     dt = time.perf_counter() - t0
     per_step = dt / args.steps
     value = 1.0 / (per_step * L)
+    sample = (f"per step: one layer of a decode token (layer i mod 32) at context {ctx0}+i over a synthetic KV "
+              "history + 1/32 of the LM-head rows; reference threading (Q4_K/Q8_0 single-threaded)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(spec, args, 1),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "port",
-                         "sample": "per step: one layer of a decode token (layer i mod 32) + 1/32 of the LM-head "
-                                   "rows; reference threading (Q4_K/Q8_0 single-threaded)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "port", "sample": sample,
+                         "host_cores": host_cores()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "model_generation_s": gen_s,
     }
+    m.close()
     emit(line)
 
 
@@ -345,8 +366,74 @@ def run_gemv_sweep(args):
             torch.cuda.empty_cache()
 
 
+ATTN_SHAPES = [(b, c) for b in (1, 8) for c in (512, 2048, 8192, 32768)]
+
+
+def attention_sweep(peak: float, peak_kind: str, iters: int = 50):
+    """Benchmark configuration 3: rf_decode_attention (32 query heads over 8 KV
+    heads of head_dim 128, f16 K/V, one query token per sequence) at batch 1/8 x
+    context 512/2048/8192/32768.  Time: CUDA events on the launching stream around
+    `iters` calls after 3 warm-up calls, rotating over distinct K/V buffers that
+    together exceed 4x the 126 MB L2 (one buffer when a single one already does).
+    Algorithmic bytes per call: batch*ctx*KV*hd*2*2 (K and V f16) + batch*H*hd*4*2
+    (query in, output out)."""
+    import torch
+    from ramforge_b200 import decode_attention
+    H, KV, hd = 32, 8, 128
+    stream = torch.cuda.current_stream()
+    rows = []
+    for batch, ctx in ATTN_SHAPES:
+        kv_elems = batch * KV * ctx * hd
+        per_copy = kv_elems * 2 * 2
+        copies = max(1, min(256, -(-4 * 126_000_000 // per_copy)))
+        k = torch.empty(copies, kv_elems, dtype=torch.float16, device="cuda").normal_()
+        v = torch.empty(copies, kv_elems, dtype=torch.float16, device="cuda").normal_()
+        q = torch.randn(batch, H, hd, device="cuda")
+        o = torch.empty(batch, H, hd, device="cuda")
+
+        def call(i):
+            j = i % copies
+            decode_attention(q.data_ptr(), k[j].data_ptr(), v[j].data_ptr(), ctx, H, KV, hd, batch, o.data_ptr(),
+                             stream.cuda_stream)
+
+        for i in range(3):
+            call(i)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(iters):
+            call(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / iters
+        alg = per_copy + batch * H * hd * 4 * 2
+        rows.append({"batch": batch, "ctx": ctx, "us_per_call": us, "gbs": alg / us / 1e3,
+                     "frac": alg / us / 1e3 / peak, "algorithmic_bytes": alg, "copies": copies})
+        del k, v, q, o
+        torch.cuda.empty_cache()
+    return {"kernel": "attn_kernel (rf_decode_attention)", "peak": peak, "peak_source": f"{peak_kind} hbm_gbs",
+            "unit": "GB/s", "rows": rows}
+
+
+def run_attn_sweep(args):
+    """--attn-sweep: benchmark configuration 3 on its own, one JSON line per shape."""
+    import torch
+    torch.cuda.set_device(0)
+    peak, peak_kind = measured_peaks()
+    res = attention_sweep(peak, peak_kind)
+    for r in res["rows"]:
+        emit({"metric": "decode attention GB/s (benchmark configuration 3)", "unit": "GB/s", "value": r["gbs"],
+              "heads": "32q/8kv", "head_dim": 128, "kv": "f16", "peak": peak,
+              "peak_source": res["peak_source"], **r})
+
+
+def token_digest(tokens) -> str:
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(tokens, np.uint32).tobytes()).hexdigest()[:16]
+
+
 def workload_config(spec, args, tp):
-    return {"workload": "llama-3-8b-shape Q4_K batch-1 greedy decode (BASELINE configs[3])",
+    return {"workload": "llama-3-8b-shape Q4_K batch-1 greedy decode after a 512-token prompt",
             "layers": spec.n_layers, "dim": spec.n_embd, "heads": f"{spec.n_heads}q/{spec.n_kv_heads}kv",
             "ffn": spec.n_ff, "vocab": spec.vocab_size, "weights": "Q4_K layers, Q8_0 token_embd/output",
             "kv_cache": "f16", "prompt_tokens": PROMPT_LEN, "decode_context": f"{PROMPT_LEN + args.warmup}.."
@@ -386,6 +473,8 @@ def main():
     ap.add_argument("--ring", type=int, default=0, help="out-of-core run: stream this many layers per step")
     ap.add_argument("--gemv-sweep", action="store_true", help="benchmark configuration 2: GEMV per format and shape")
     ap.add_argument("--formats", default="", help="with --gemv-sweep: comma-separated subset, e.g. Q4_K,Q6_K")
+    ap.add_argument("--attn-sweep", action="store_true", help="benchmark configuration 3: decode attention GB/s")
+    ap.add_argument("--no-attn-sweep", action="store_true", help="leave the attention sweep off the main line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -405,6 +494,9 @@ def main():
         return
     if args.gemv_sweep:
         run_gemv_sweep(args)
+        return
+    if args.attn_sweep:
+        run_attn_sweep(args)
         return
 
     import torch
@@ -455,6 +547,7 @@ def main():
         barrier()
     dev_ms = max_over_ranks(dev_ms)
     clocks = clk.summary()
+    timed_tokens = toks.copy()
     value = args.steps / (dev_ms / 1e3)
 
     # e2e: same positions again through rf_decode_step (pinned H2D token+pos, D2H token, sync)
@@ -464,13 +557,20 @@ def main():
     for _ in range(args.warmup):
         tok = eng.decode_step(tok)
     barrier()
+    e2e_tokens = np.zeros(e2e_steps, np.uint32)
     t0 = time.perf_counter()
-    for _ in range(e2e_steps):
+    for i in range(e2e_steps):
         tok = eng.decode_step(tok)
+        e2e_tokens[i] = tok
     barrier()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e = {"value": e2e_steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
            "api": "rf_decode_step (token + position in, next token out)"}
+    # Greedy tokens of both runs: identical on every rank count when the
+    # tensor-parallel decode reproduces the single-GPU one (same prompt, positions).
+    tokens = {"timed_sha256_16": token_digest(timed_tokens), "e2e_sha256_16": token_digest(e2e_tokens),
+              "timed_first8": timed_tokens[:8].tolist(), "first_after_prompt": first,
+              "timed_equals_e2e": bool(np.array_equal(timed_tokens, e2e_tokens))}
 
     # dominant kernel: gate/up + SwiGLU GEMV, timed over every layer (weights >> L2)
     kms = eng.bench_layer_kernels(iters=3)
@@ -495,6 +595,7 @@ def main():
         "gpu_launches": args.steps * eng.step_kernel_count, "roofline": roofline,
         "step_roofline": {"bytes_per_token_per_gpu": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak},
         "kernel_ms": dict(zip(["qkv_rope", "attention", "wo_residual", "gateup_swiglu", "down_residual"], kms)),
+        "tokens": tokens, "tp_peer_sum": eng.tp_peer_sum if world > 1 else None,
         "setup_s": {"model_generation": gen_s, "engine_load": load_s},
     }
     eng.close()
@@ -503,8 +604,12 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
+        if world == 1 and not args.no_attn_sweep:
+            line["attention_sweep"] = attention_sweep(peak, peak_kind)
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(gguf, spec)
+            ctx = PROMPT_LEN + args.warmup
+            line["cpu_baseline"] = cpu_baseline(gguf, spec, ctx, threads=1)
+            line["cpu_baseline_all_cores"] = cpu_baseline(gguf, spec, ctx, threads=host_cores())
         emit(line)
 
 

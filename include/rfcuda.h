@@ -284,10 +284,15 @@ int rf_decode_attention(const float* dQ, const uint16_t* dK, const uint16_t* dV,
  * latency-critical loops that cannot afford the device synchronisation
  * cudaMalloc/cudaFree may imply.  The split-K scratch is a fixed 16 MiB
  * array in the library, held on every GPU that loads it until exit; shapes
- * that need more return RF_EINVAL.  The first call on a device looks the array
- * up, so make it before any stream capture.  All calls share the array: calls
- * that overlap on the GPU race.  Same arguments and results as
- * rf_decode_attention. */
+ * that need more return RF_EINVAL.  Every call looks the array's address up in
+ * the current context (so it stays valid across a cudaDeviceReset); the first
+ * call on a device may load the library's device code, so make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * race.  Same arguments as rf_decode_attention; results equal its results
+ * within the attention tolerance (max|o - o_ref| <= 1e-4 * max|o_ref|), and
+ * exactly when the fixed scratch holds the split count rf_decode_attention
+ * uses; for larger shapes the scratch forces fewer context splits, which
+ * changes the f32 summation order. */
 int rf_decode_attention_noalloc(const float* dQ, const uint16_t* dK, const uint16_t* dV, int ctx, int n_heads,
                                 int n_kv_heads, int head_dim, int batch, float* dOut, void* stream);
 

@@ -876,6 +876,27 @@ int orc_model_config(const orc_model* m, orc_config* cfg) { *cfg = m->cfg; retur
 uint32_t orc_kv_len(const orc_model* m) { return m->seq_len; }
 void orc_kv_reset(orc_model* m) { m->seq_len = 0; }
 
+/* Timing support for the CPU baseline, not a reference function: set the history
+ * length to n and fill positions [0, n) of every layer with seeded values in
+ * [-1, 1) (f16-exact when the cache is f16), so a layer step can be timed at the
+ * context a long decode reaches without running n forwards first.  Attention
+ * cost depends on the length only, not on the values. */
+int orc_kv_fill_synthetic(orc_model* m, uint32_t n, uint32_t seed) {
+  if (n > m->max_seq) { set_err("KV fill beyond max_seq"); return -1; }
+  size_t kvd = (size_t)m->cfg.n_kv_heads * m->cfg.head_dim;
+  uint64_t st = 0x9E3779B97F4A7C15ull * (seed + 1);
+  for (uint32_t l = 0; l < m->cfg.n_layers; l++)
+    for (int w = 0; w < 2; w++) {
+      float* base = (w ? m->vcache : m->kcache) + (size_t)l * m->max_seq * kvd;
+      for (size_t i = 0; i < (size_t)n * kvd; i++) {
+        st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+        base[i] = (float)((int)(st >> 40 & 0x7FF) - 1024) / 1024.0f;
+      }
+    }
+  m->seq_len = n;
+  return 0;
+}
+
 int orc_kv_read(const orc_model* m, uint32_t layer, int which_v, uint32_t start, uint32_t end, float* out) {
   if (layer >= m->cfg.n_layers || start > end || end > m->seq_len) { set_err("KV read out of range"); return -1; }
   size_t kvd = (size_t)m->cfg.n_kv_heads * m->cfg.head_dim;

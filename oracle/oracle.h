@@ -89,6 +89,7 @@ int orc_layer_step(orc_model* m, uint32_t layer, uint32_t pos, float* hidden);
 int orc_logits_rows(orc_model* m, const float* final_hidden, uint32_t r0, uint32_t r1, float* out);
 uint32_t orc_kv_len(const orc_model* m);
 void orc_kv_reset(orc_model* m);
+int orc_kv_fill_synthetic(orc_model* m, uint32_t n, uint32_t seed);
 /* K or V history of one layer, reference layout [pos][kv_head][head_dim], f32. */
 int orc_kv_read(const orc_model* m, uint32_t layer, int which_v, uint32_t start, uint32_t end,
                 float* out);

@@ -78,6 +78,7 @@ def lib():
         L.orc_kv_len.restype = ctypes.c_uint32
         L.orc_kv_len.argtypes = [ctypes.c_void_p]
         L.orc_kv_reset.argtypes = [ctypes.c_void_p]
+        L.orc_kv_fill_synthetic.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32]
         L.orc_kv_read.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_uint32,
                                   ctypes.c_uint32, _f32p]
         L.orc_generate.argtypes = [ctypes.c_void_p, _u32p, ctypes.c_uint32, ctypes.c_uint32, _u32p,
@@ -212,6 +213,11 @@ class OracleModel:
 
     def reset(self):
         lib().orc_kv_reset(self._h)
+
+    def kv_fill_synthetic(self, n: int, seed: int = 0) -> None:
+        """Timing support only: history length n with seeded values, so a layer
+        step can be timed at a long decode's context without n forwards."""
+        _check(lib().orc_kv_fill_synthetic(self._h, n, seed))
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         out = np.empty(self.config["n_embd"], np.float32)

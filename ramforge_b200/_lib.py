@@ -26,7 +26,7 @@ ROLE_NAMES = ["attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_nor
 LAYER_VIEW_NAMES = ROLE_NAMES + ["attn_q.bias", "attn_k.bias", "attn_v.bias"]
 ROLE_TOKEN_EMBD, ROLE_OUTPUT_NORM, ROLE_OUTPUT = 16, 17, 18
 
-# Every symbol include/rfcuda.h declares (checked by tests/test_abi.py).
+# Every symbol include/rfcuda.h declares (checked by tests/test_synth_and_abi.py).
 EXPORTS = [
     "rf_last_error", "rf_abi_version", "rf_gguf_read_config", "rf_tp_shard_plan", "rf_engine_create", "rf_engine_create_from_gguf",
     "rf_engine_create_from_file", "rf_engine_destroy", "rf_engine_config", "rf_persistent_load",

@@ -35,23 +35,18 @@ std::unordered_map<int, AttnWorkspace> g_ws;
 constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;  // 16 MiB
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-float* g_noalloc_addr[kMaxDevices] = {};
-
-// Device address of g_noalloc_scratch on the current device (looked up once
-// per device, with that device current).
-int noalloc_scratch(int dev, float** out) {
-  if (dev < 0 || dev >= kMaxDevices) return set_error(RF_EINVAL, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* p = nullptr;
-    cudaError_t ce = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (ce != cudaSuccess || !p)
-      return set_error(RF_ECUDA, "cudaGetSymbolAddress(no-allocation scratch) failed: %s", cudaGetErrorString(ce));
-    g_noalloc_addr[dev] = (float*)p;
-  }
-  *out = g_noalloc_addr[dev];
+// Device address of g_noalloc_scratch in the current device's current context.
+// Looked up on every call rather than cached: after a cudaDeviceReset the
+// library's device code is loaded again into the new context and the array gets
+// a new address, which a cached pointer would miss.  The lookup allocates
+// nothing; the first one in a context may load the device code, which is why the
+// first call should come before any stream capture.
+int noalloc_scratch(float** out) {
+  void* p = nullptr;
+  cudaError_t ce = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (ce != cudaSuccess || !p)
+    return set_error(RF_ECUDA, "cudaGetSymbolAddress(no-allocation scratch) failed: %s", cudaGetErrorString(ce));
+  *out = (float*)p;
   return RF_OK;
 }
 
@@ -257,9 +252,9 @@ int rf_decode_attention(const float* dQ, const uint16_t* dK, const uint16_t* dV,
 
 // rf_decode_attention for callers that cannot allocate device memory: the
 // split-K partials and counters live in g_noalloc_scratch instead of a
-// workspace grown with cudaMalloc.  The first call on a device looks up the
-// array's device address (cudaGetSymbolAddress, with that device current);
-// make that first call before any stream capture.  Calls share the array: the
+// workspace grown with cudaMalloc.  Every call looks up the array's device
+// address in the current context (cudaGetSymbolAddress); make the first call on
+// a device before any stream capture.  Calls share the array: the
 // counters are cleared (cudaMemsetAsync, no allocation) before every launch,
 // and calls that overlap on the GPU race on the scratch.  Shapes whose scratch
 // exceeds kNoAllocScratchFloats are rejected with RF_EINVAL.
@@ -270,10 +265,8 @@ int rf_decode_attention_noalloc(const float* dQ, const uint16_t* dK, const uint1
     return set_error(RF_EINVAL, "invalid attention shape");
   const int G = n_heads / n_kv_heads;
   if (G != 1 && G != 2 && G != 4 && G != 8) return set_error(RF_EUNSUPPORTED, "GQA group %d unsupported", G);
-  int dev = 0;
-  RF_CUDA(cudaGetDevice(&dev));
   float* scratch = nullptr;
-  RF_TRY(noalloc_scratch(dev, &scratch));
+  RF_TRY(noalloc_scratch(&scratch));
   const size_t n_counters = (size_t)batch * n_kv_heads;
   const size_t per_split = attn_part_floats(batch, n_kv_heads, 1, G, head_dim);
   const int min_splits = (ctx + 511) / 512;  // every split covers at most 512 positions

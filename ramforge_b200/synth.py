@@ -1,6 +1,6 @@
 """Seeded synthetic Llama GGUF models for the benchmark configurations.
 
-BASELINE.json's configs name synthetic models (weights N(0, 0.02) from a seed,
+The benchmark configurations are synthetic models (weights N(0, 0.02) from a seed,
 quantised to GGUF block formats, f32 ones for norms); there is no public
 checkpoint or dataset on this path.  The images are produced by
 librfsynth.so (counter-based normal generator + the build's own GGUF writer
@@ -84,17 +84,17 @@ class LlamaSpec:
         return self.n_embd // self.n_heads
 
 
-# TinyLlama-1.1B shape, Q8_0 everywhere, seed 0.  The
-# reference derives head_dim = n_embd / n_heads = 64 (runtime/src/model.rs:148),
-# so the config's "head_dim 128" cannot run on its CPU executor; 64 is used.
+# TinyLlama-1.1B shape, Q8_0 everywhere, seed 0.  The reference derives
+# head_dim = n_embd / n_heads = 64 (runtime/src/model.rs:148), so a head_dim of
+# 128 at this width cannot run on its CPU executor; 64 is used.
 TINYLLAMA = LlamaSpec("tinyllama-1.1b-q8_0", vocab_size=32000, n_embd=2048, n_layers=22, n_ff=5632, n_heads=32,
                       n_kv_heads=4, rope_theta=10000.0, context_length=2048, layer_type=Q8_0, embd_type=Q8_0,
                       out_type=Q8_0, seed=0)
-# configs[3]: Llama-3-8B shape, Q4_K layers, Q8_0 embedding/output, seed 3.
+# Llama-3-8B shape, Q4_K layers, Q8_0 embedding/output, seed 3.
 LLAMA3_8B = LlamaSpec("llama-3-8b-q4_k", vocab_size=128256, n_embd=4096, n_layers=32, n_ff=14336, n_heads=32,
                       n_kv_heads=8, rope_theta=500000.0, context_length=8192, layer_type=Q4_K, embd_type=Q8_0,
                       out_type=Q8_0, seed=3)
-# configs[4]: Llama-3-70B shape, Q4_K everywhere, seed 4 (out-of-core workload).
+# Llama-3-70B shape, Q4_K everywhere, seed 4 (out-of-core workload).
 LLAMA3_70B = LlamaSpec("llama-3-70b-q4_k", vocab_size=128256, n_embd=8192, n_layers=80, n_ff=28672, n_heads=64,
                        n_kv_heads=8, rope_theta=500000.0, context_length=8192, layer_type=Q4_K, embd_type=Q4_K,
                        out_type=Q4_K, seed=4)

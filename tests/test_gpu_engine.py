@@ -1,7 +1,7 @@
 """GPU parity of the decode engine against the CPU oracle (the reference's
 executor restated), through the C ABI.
 
-Bars (BASELINE north_star): final logits within 1e-3 max relative error,
+Bars: final logits within 1e-3 max relative error,
 measured as max|l - l_ref| / max|l_ref| per step; greedy token sequences
 identical; embedding rows bit-exact; KV entries within f16 rounding of the
 oracle's (K/V come out of differently-ordered f32 sums before rounding).
@@ -279,7 +279,7 @@ def test_residency_plan_streams_nonresident_layers(models):
 
 
 def test_tinyllama_config1_greedy_parity():
-    """TinyLlama shape Q8_0, 32 seeded prompt tokens + 128 greedy tokens."""
+    """TinyLlama shape, Q8_0 everywhere: 32 seeded prompt tokens + 128 greedy tokens."""
     g = synth.gguf_bytes(synth.TINYLLAMA)
     prompt = np.random.default_rng(0).integers(0, 32000, 32).tolist()
     ref = orc.OracleModel(g, kv_f16=True, max_seq=256, threads=THREADS)
@@ -300,7 +300,7 @@ def test_tinyllama_config1_greedy_parity():
 
 
 def test_llama3_8b_config4_short_parity():
-    """BASELINE configs[3] shape (Q4_K layers, Q8_0 embedding/output): 12 prompt + 8 greedy tokens."""
+    """Llama-3-8B shape (Q4_K layers, Q8_0 embedding/output): 12 prompt + 8 greedy tokens."""
     g = synth.gguf_bytes(synth.LLAMA3_8B)
     prompt = np.random.default_rng(3).integers(0, 128256, 12).tolist()
     ref = orc.OracleModel(g, kv_f16=True, max_seq=64, threads=THREADS)
@@ -313,4 +313,37 @@ def test_llama3_8b_config4_short_parity():
         eng.forward_single_streaming(t, p, want_hidden=False)
     lg, am = eng.compute_logits()
     assert rel_err(lg, want_logits[0]) <= LOGIT_RTOL and am == want[0]
+    eng.close()
+
+
+def test_llama3_8b_width_bench_context_parity():
+    """The benchmark's decode context: Llama-3-8B width (dim 4096, 32/8 heads, FFN
+    14336, vocab 128256, Q4_K layers, Q8_0 embedding/output, seed 3) with 4 of its
+    layers, the benchmark's 512-token prompt, then 64 greedy tokens, out to context
+    576.  Attention there runs ~9 context splits with the current position's K/V
+    taken from the step, the path the timed decode uses.  Tokens from rf_generate
+    (the decode graph) must equal the oracle's; logits of every generated step,
+    through the stepwise API, within 1e-3."""
+    spec = synth.scaled(synth.LLAMA3_8B, name="llama-3-8b-4l", n_layers=4)
+    g = synth.gguf_bytes(spec)
+    prompt = np.random.default_rng(3).integers(0, spec.vocab_size, 512).tolist()
+    n_new = 64
+    ref = orc.OracleModel(g, kv_f16=True, max_seq=600, threads=os.cpu_count() or 8)
+    want, want_logits, margins = ref.generate(prompt, n_new, want_logits=True)
+    ref.close()
+    eng = DecodeEngine(g, max_seq_len=600)
+    got = eng.generate(prompt, n_new)
+    assert got.tolist() == want.tolist(), (np.nonzero(got != want)[0][:3], float(margins.min()))
+    eng.kv_reset()
+    for p, t in enumerate(prompt):
+        eng.forward_single_streaming(t, p, want_hidden=False)
+    worst = 0.0
+    for i in range(n_new):
+        lg, am = eng.compute_logits()
+        e = rel_err(lg, want_logits[i])
+        worst = max(worst, e)
+        assert e <= LOGIT_RTOL, (i, e)
+        assert am == want[i], (i, am, want[i])
+        eng.forward_single_streaming(int(want[i]), len(prompt) + i, want_hidden=False)
+    assert eng.kv_seq_len == len(prompt) + n_new
     eng.close()
