@@ -189,31 +189,16 @@ int rf_decode_step(rf_engine* e, uint32_t token, uint32_t* next_token);
 int rf_generate(rf_engine* e, const uint32_t* prompt, uint32_t n_prompt, uint32_t n_new, uint32_t* out);
 
 /* ---- measurement hooks (the Profiler's per-event timers, profile.rs:8-60) --------- */
-/* Kernels of this library one decode step launches: 1 when the persistent step
- * kernel runs the step (see rf_step_kernel_active), else 5 per layer + embedding,
+/* Kernels of this library one decode step launches: 5 per layer + embedding,
  * output norm, LM head with argmax, token advance, plus 2 per layer (the peer
  * sums) under tensor parallelism over peer memory. */
 int rf_step_kernel_count(const rf_engine* e, uint32_t* out);
-/* The persistent step kernel: one cooperative launch per token runs every layer
- * and the LM head, with grid barriers between phases.  It is used when enabled
- * (off by default), tp_size == 1, every layer is resident, the KV cache is f16 and
- * the model shape has an instance; otherwise steps run as separate kernels.
- * No counterpart in the reference (its executor is CPU code). */
-int rf_set_step_kernel(rf_engine* e, int enable);
-int rf_step_kernel_active(rf_engine* e, int* out);
-/* Phase timers of the step kernel (the Profiler's per-event timers, profile.rs:8-60):
- * while enabled, each step-kernel launch records when every grid barrier
- * completes.  rf_step_phase_times writes the last step's phase durations in
- * microseconds: [embedding, then per layer QKV, attention, Wo, gate/up, down,
- * then LM head (decode) or final norm], at most n entries, count in *n_out. */
-int rf_step_profile(rf_engine* e, int enable);
-int rf_step_phase_times(rf_engine* e, float* us, uint32_t n, uint32_t* n_out);
-/* Failure-detection check of the step kernel's grid barrier: one cooperative
- * launch on `device` waits at a barrier that also expects `phantom_arrivals`
- * CTAs which never arrive.  Every wait is bounded (about a second): *err_word is
- * 1 when the wait gave up, 0 when the barrier completed (phantom_arrivals == 0).
- * No counterpart in the reference. */
-int rf_selftest_barrier(int device, uint32_t phantom_arrivals, uint32_t* err_word);
+/* Failure-detection check of the bounded wait of the tensor-parallel peer sum,
+ * on one GPU: a two-rank sum whose second rank is a local area that never
+ * raises its flag.  The wait gives up after about a second and *err_word is 1
+ * (0 would mean the phantom rank's flag arrived).  No counterpart in the
+ * reference (its executor is CPU code). */
+int rf_selftest_wait(int device, uint32_t* err_word);
 /* n_steps greedy decode steps from `token` at pos = KV length, token fed back on
  * the device (rf_generate's loop), bracketed by CUDA events on the engine stream:
  * *device_ms = their elapsed device time.  out_tokens (n_steps) may be NULL. */

@@ -34,8 +34,7 @@ EXPORTS = [
     "rf_embed", "rf_hidden_write", "rf_hidden_read", "rf_kv_commit", "rf_forward_token", "rf_compute_logits",
     "rf_decode_step", "rf_generate", "rf_kv_reset", "rf_kv_seq_len", "rf_kv_read", "rf_budget_total",
     "rf_budget_used", "rf_budget_available", "rf_set_residency_plan", "rf_residency_stats_get",
-    "rf_step_kernel_count", "rf_set_step_kernel", "rf_step_kernel_active", "rf_step_profile", "rf_step_phase_times",
-    "rf_selftest_barrier", "rf_decode_timed",
+    "rf_step_kernel_count", "rf_selftest_wait", "rf_decode_timed",
     "rf_bench_layer_kernels", "rf_tp_unique_id", "rf_tp_peer_sum", "rf_matrix_create", "rf_matrix_destroy", "rf_matrix_device_bytes",
     "rf_qmatvec", "rf_decode_attention", "rf_decode_attention_noalloc",
 ]
@@ -126,11 +125,7 @@ def lib():
             "rf_tp_unique_id": (c_int, [ctypes.POINTER(ctypes.c_uint8)]),
             "rf_tp_peer_sum": (c_int, [vp, ctypes.POINTER(c_int)]),
             "rf_step_kernel_count": (c_int, [vp, u32p]),
-            "rf_set_step_kernel": (c_int, [vp, c_int]),
-            "rf_step_kernel_active": (c_int, [vp, ctypes.POINTER(c_int)]),
-            "rf_selftest_barrier": (c_int, [c_int, c_u32, u32p]),
-            "rf_step_profile": (c_int, [vp, c_int]),
-            "rf_step_phase_times": (c_int, [vp, f32p, c_u32, u32p]),
+            "rf_selftest_wait": (c_int, [c_int, u32p]),
             "rf_decode_timed": (c_int, [vp, c_u32, c_u32, u32p, f32p]),
             "rf_bench_layer_kernels": (c_int, [vp, c_u32, f32p]),
             "rf_matrix_create": (c_int, [c_int, vp, c_u64, c_int, c_u32, c_u32, ctypes.POINTER(vp)]),

@@ -99,4 +99,34 @@ cudaError_t launch_peer_sum(const Launch& L, const PeerSum& P, const float* part
                   site);
 }
 
+// Check of the peer sum's bounded wait on one GPU: a two-rank sum whose second
+// rank is a second local area that no kernel ever flags.  The wait for that
+// rank's flag gives up after about a second, sets bit 0 of the error word and
+// the kernel finishes; *err_out gets the word.
+cudaError_t peer_sum_selftest(unsigned* err_out) {
+  const int n_max = PS_ELEMS, sites = 2;
+  // each area and the vectors start on a 256-byte boundary (float4 accesses)
+  const size_t bytes = (peer_sum_area_bytes(2, n_max, sites) + 255) & ~size_t(255);
+  uint8_t* mem = nullptr;
+  cudaError_t e = cudaMalloc(&mem, 2 * bytes + 2 * n_max * sizeof(float));
+  if (e != cudaSuccess) return e;
+  e = cudaMemset(mem, 0, 2 * bytes + 2 * n_max * sizeof(float));
+  PeerSum P{};
+  P.rank = 0;
+  P.n_ranks = 2;
+  P.n_max = n_max;
+  P.sites = sites;
+  peer_sum_bind(&P, 0, mem, true);
+  peer_sum_bind(&P, 1, mem + bytes, false);
+  float* partial = reinterpret_cast<float*>(mem + 2 * bytes);
+  float* out = partial + n_max;
+  if (e == cudaSuccess) e = launch_peer_sum(Launch{nullptr, false}, P, partial, out, n_max, 0);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  unsigned w = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&w, P.err, sizeof w, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) *err_out = w;
+  cudaFree(mem);
+  return e;
+}
+
 }  // namespace rf

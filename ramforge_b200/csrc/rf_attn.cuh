@@ -1,7 +1,6 @@
 // rf_attn.cuh - split-K GQA decode attention (one query token per sequence),
-// written as a routine for a group of ATT_THREADS threads so that the same code
-// runs as a standalone kernel (one group per CTA) and as a phase of the
-// persistent decode-step kernel (several groups per CTA).
+// written as a routine for a group of ATT_THREADS threads (one group per CTA of
+// attn_kernel).
 //
 // attention_reference (compute.rs:461-547) for one query token: query head h
 // reads KV head h*KV/H (contiguous groups of G = H/KV heads), so one unit loads

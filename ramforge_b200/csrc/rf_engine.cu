@@ -161,18 +161,7 @@ struct rf_engine {
   unsigned long long* h_key = nullptr;
   // graphs
   cudaGraphExec_t g_forward = nullptr, g_decode = nullptr;
-  // persistent step kernel: per-layer matrix table (host copy + device copy),
-  // its shared memory (0 = not applicable), barrier word and error word
-  bool step_enabled = false;  // opt-in (rf_set_step_kernel): the per-kernel graph is faster today
-  bool step_dirty = true;
-  size_t step_smem = 0;
-  std::vector<StepLayer> h_step_layers;
-  StepLayer* d_step_layers = nullptr;
-  unsigned* d_bar = nullptr;
-  unsigned* d_err = nullptr;
-  bool step_used = false;  // the step kernel ran since the last error check
-  bool step_profile = false;
-  unsigned long long* d_stamps = nullptr;  // barrier completion times of the last profiled step
+  unsigned* h_err = nullptr;  // pinned copy of the peer-sum error word, read after each synchronisation
   // NCCL
   ncclComm_t comm = nullptr;
   // tensor-parallel sums over NVLink peer memory (PeerSum); NCCL when unavailable
@@ -216,7 +205,6 @@ void drop_graphs(rf_engine* e) {
   if (e->g_forward) cudaGraphExecDestroy(e->g_forward);
   if (e->g_decode) cudaGraphExecDestroy(e->g_decode);
   e->g_forward = e->g_decode = nullptr;
-  e->step_dirty = true;
 }
 
 // Build the RoPE (cos, sin) table on the host with the reference's f32
@@ -423,9 +411,6 @@ int engine_init_device(rf_engine* e) {
       {(void**)&e->logits, 4ull * vl_pad},          {(void**)&e->logits_all, 4ull * vl_pad * e->tp},
       {(void**)&e->attn_part, 4ull * part_f},       {(void**)&e->attn_counters, 4ull * e->kvh_local},
       {(void**)&e->gws.part, 4ull * gpart},         {(void**)&e->gws.cnt, 4ull * gcnt},
-      {(void**)&e->d_bar, 4},                       {(void**)&e->d_err, 4},
-      {(void**)&e->d_stamps, 8ull * (5 * c.n_layers + 8)},
-      {(void**)&e->d_step_layers, sizeof(StepLayer) * c.n_layers},
       {(void**)&e->d_io, sizeof(StepIO)},           {(void**)&e->d_key, 8},
       {(void**)&e->d_hist, 4ull * e->max_seq},
       {(void**)&e->rope_cs, 8ull * e->max_seq * (c.head_dim / 2)}};
@@ -447,6 +432,8 @@ int engine_init_device(rf_engine* e) {
   RF_CUDA(cudaMallocHost((void**)&e->h_io, sizeof(StepIO) * (e->max_seq + 1)));
   RF_CUDA(cudaMallocHost((void**)&e->h_tok, 4 * 4096));
   RF_CUDA(cudaMallocHost((void**)&e->h_key, 8));
+  RF_CUDA(cudaMallocHost((void**)&e->h_err, 8));
+  e->h_err[0] = 0;
   if (e->tp > 1) {
     if (!nccl()) return set_error(RF_ENCCL, "tensor parallelism needs libnccl.so.2, which could not be loaded");
     if (!e->rt.nccl_id) return set_error(RF_EINVAL, "tp_size > 1 requires nccl_id");
@@ -1108,115 +1095,24 @@ int capture(rf_engine* e, bool decode, cudaGraphExec_t* out) {
   return RF_OK;
 }
 
-StepArgs step_args(rf_engine* e, bool decode) {
-  const rf_model_config& c = e->cfg;
-  StepArgs a{};
-  a.layers = e->d_step_layers;
-  a.n_layers = (int)c.n_layers;
-  a.decode = decode ? 1 : 0;
-  a.embd = e->embd;
-  lm_head(e, &a.lm);
-  a.out_norm = e->out_norm;
-  a.eps = c.rms_eps;
-  a.n_embd = c.n_embd;
-  a.q_rows = e->q_local;
-  a.kv_rows = e->kv_local;
-  a.head_dim = c.head_dim;
-  a.max_seq = e->max_seq;
-  a.n_heads = e->qh_local;
-  a.n_kv_heads = e->kvh_local;
-  a.rope_cs = e->rope_cs;
-  a.hidden = e->hidden;
-  a.final_hidden = e->final_hidden;
-  a.q = e->q;
-  a.k_cur = e->k_cur;
-  a.v_cur = e->v_cur;
-  a.att = e->att;
-  a.act = e->act;
-  a.logits = nullptr;
-  a.d_token = &e->d_io->token;
-  a.d_pos = &e->d_io->pos;
-  a.hist = e->d_hist;
-  a.hist_len = (int)e->max_seq;
-  a.key = e->d_key;
-  a.vocab_off = e->vocab_off;
-  a.gws = e->gws;
-  a.attn_part = e->attn_part;
-  a.attn_counters = e->attn_counters;
-  a.max_splits = e->max_splits;
-  a.bar = e->d_bar;
-  a.err = e->d_err;
-  a.stamps = e->step_profile ? e->d_stamps : nullptr;
-  return a;
-}
-
-// Decide whether the persistent step kernel runs the step (one GPU, every layer
-// resident, f16 KV cache, an instantiated shape) and refresh its layer table.
-int prepare_step_kernel(rf_engine* e) {
-  if (!e->step_dirty) return RF_OK;
-  e->step_smem = 0;
-  e->step_dirty = false;
-  if (!e->step_enabled || e->tp > 1 || e->rt.kv_f32 || !all_resident(e) || !e->have_embd || !e->have_onorm)
-    return RF_OK;
-  PackedMat lm;
-  if (lm_head(e, &lm) != RF_OK) return RF_OK;
-  const rf_model_config& c = e->cfg;
-  for (uint32_t l = 0; l < c.n_layers; l++)
-    if (e->layers[l].vmat.M) return RF_OK;  // a separate V matrix: per-kernel launches only
-  e->h_step_layers.assign(c.n_layers, StepLayer{});
-  for (uint32_t l = 0; l < c.n_layers; l++) {
-    const Layer& L = e->layers[l];
-    StepLayer& S = e->h_step_layers[l];
-    S.qkv = L.qkv;
-    S.wo = L.wo;
-    S.gateup = L.gateup;
-    S.down = L.down;
-    S.attn_norm = L.attn_norm;
-    S.ffn_norm = L.ffn_norm;
-    S.rope = rope_args(e, (int)l);
-    S.attn = attn_args(e, (int)l);
-  }
-  RF_CUDA(h2d_sync(e, e->d_step_layers, e->h_step_layers.data(), sizeof(StepLayer) * c.n_layers));
-  e->step_smem = step_kernel_smem(step_args(e, true), e->h_step_layers[0]);
-  return RF_OK;
-}
-
-bool step_kernel_active(rf_engine* e) { return prepare_step_kernel(e) == RF_OK && e->step_smem > 0; }
-
-// After a synchronisation: a step-kernel barrier or a peer-sum wait that gave up
-// fails the call.
-int check_step_kernel(rf_engine* e) {
-  if (e->ps_ok) {
-    unsigned perr = 0;
-    RF_CUDA(cudaMemcpyAsync(&perr, e->ps.err, sizeof perr, cudaMemcpyDeviceToHost, e->stream));
-    RF_CUDA(cudaStreamSynchronize(e->stream));
-    if (perr) {
-      RF_CUDA(cudaMemsetAsync(e->ps.err, 0, sizeof perr, e->stream));
-      RF_CUDA(cudaStreamSynchronize(e->stream));
-      return set_error(RF_ETIMEOUT, "a tensor-parallel peer sum waited too long for another rank (0x%x)", perr);
-    }
-  }
-  if (!e->step_used) return RF_OK;
-  e->step_used = false;
-  unsigned err = 0;
-  RF_CUDA(cudaMemcpy(&err, e->d_err, sizeof err, cudaMemcpyDeviceToHost));
-  if (err) {
-    RF_CUDA(cudaMemsetAsync(e->d_err, 0, sizeof err, e->stream));
-    RF_CUDA(cudaStreamSynchronize(e->stream));
-    return set_error(RF_ETIMEOUT, "a grid barrier of the step kernel timed out (error word 0x%x)", err);
-  }
-  return RF_OK;
+// After a synchronisation of the engine stream: a tensor-parallel peer-sum wait
+// that gave up fails the call.  The error word is copied into pinned host memory
+// on the stream and read after it drains.
+int check_async_errors(rf_engine* e) {
+  if (!e->ps_ok) return RF_OK;
+  RF_CUDA(cudaMemcpyAsync(e->h_err, e->ps.err, 4, cudaMemcpyDeviceToHost, e->stream));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  const unsigned perr = e->h_err[0];
+  if (!perr) return RF_OK;
+  RF_CUDA(cudaMemsetAsync(e->ps.err, 0, 4, e->stream));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  e->h_err[0] = 0;
+  return set_error(RF_ETIMEOUT, "a tensor-parallel peer sum waited too long for another rank (0x%x)", perr);
 }
 
 // Launch one token step (forward, or decode = forward + logits + advance).
 int launch_step(rf_engine* e, bool decode) {
   if (!all_resident(e)) return e->rt.ring_slots > 0 && e->src ? run_ring(e, decode) : run_stepwise(e, decode);
-  if (step_kernel_active(e)) {
-    RF_CUDA(launch_step_kernel(e->stream, step_args(e, decode), e->h_step_layers[0], e->step_smem));
-    e->step_used = true;
-    e->stats.cache_hits += e->cfg.n_layers;
-    return RF_OK;
-  }
   if (e->rt.disable_graphs) return decode ? enqueue_decode(e, true) : enqueue_forward(e, true);
   cudaGraphExec_t* g = decode ? &e->g_decode : &e->g_forward;
   if (!*g) RF_TRY(capture(e, decode, g));
@@ -1280,7 +1176,7 @@ int decode_loop(rf_engine* e, uint32_t token, uint32_t n, uint32_t* out, float* 
   if (rc) return rc;
   if (out) RF_CUDA(cudaMemcpyAsync(out, e->d_hist + p0, 4ull * n, cudaMemcpyDeviceToHost, e->stream));
   RF_CUDA(cudaStreamSynchronize(e->stream));
-  return check_step_kernel(e);
+  return check_async_errors(e);
 }
 
 int engine_finish_create(rf_engine* e) {
@@ -1332,6 +1228,7 @@ void destroy(rf_engine* e) {
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->h_tok) cudaFreeHost(e->h_tok);
   if (e->h_key) cudaFreeHost(e->h_key);
+  if (e->h_err) cudaFreeHost(e->h_err);
   for (void* q : e->ps_peer)
     if (q) cudaIpcCloseMemHandle(q);
   if (e->ps_area) cudaFree(e->ps_area);
@@ -1568,7 +1465,7 @@ int rf_forward_token(rf_engine* e, uint32_t token, uint32_t pos, float* final_hi
     RF_CUDA(cudaMemcpyAsync(final_hidden, e->final_hidden, 4ull * e->cfg.n_embd, cudaMemcpyDeviceToHost, e->stream));
   }
   RF_CUDA(cudaStreamSynchronize(e->stream));
-  return check_step_kernel(e);
+  return check_async_errors(e);
 }
 
 int rf_compute_logits(rf_engine* e, float* logits, uint32_t* argmax) {
@@ -1596,7 +1493,7 @@ int rf_decode_step(rf_engine* e, uint32_t token, uint32_t* next_token) {
   e->seq_len++;
   RF_CUDA(cudaMemcpyAsync(e->h_tok, &e->d_io->token, 4, cudaMemcpyDeviceToHost, e->stream));
   RF_CUDA(cudaStreamSynchronize(e->stream));
-  RF_TRY(check_step_kernel(e));
+  RF_TRY(check_async_errors(e));
   if (next_token) *next_token = e->h_tok[0];
   return RF_OK;
 }
@@ -1621,7 +1518,7 @@ int rf_generate(rf_engine* e, const uint32_t* prompt, uint32_t n_prompt, uint32_
     RF_TRY(launch_step(e, false));
     e->seq_len++;
     RF_CUDA(cudaStreamSynchronize(e->stream));
-    return check_step_kernel(e);
+    return check_async_errors(e);
   }
   // The last prompt token and every generated token but the last go through
   // decode steps whose argmax feeds the next step on the device (the reference
@@ -1641,10 +1538,6 @@ int rf_decode_timed(rf_engine* e, uint32_t token, uint32_t n_steps, uint32_t* ou
 int rf_step_kernel_count(const rf_engine* ec, uint32_t* out) {
   if (!ec || !out) return set_error(RF_EINVAL, "null argument");
   rf_engine* e = const_cast<rf_engine*>(ec);
-  if (all_resident(e) && step_kernel_active(e)) {
-    *out = 1u;  // the persistent step kernel
-    return RF_OK;
-  }
   // embed, 5 per layer (6 with a separate V matrix), output norm, LM head, advance, and the two peer sums
   // a layer under tensor parallelism (NCCL's own kernels are not counted)
   uint32_t n = 5u * e->cfg.n_layers + 4u + (e->ps_ok ? 2u * e->cfg.n_layers : 0u);
@@ -1653,46 +1546,12 @@ int rf_step_kernel_count(const rf_engine* ec, uint32_t* out) {
   return RF_OK;
 }
 
-int rf_set_step_kernel(rf_engine* e, int enable) {
-  ENGINE_GUARD(e);
-  e->step_enabled = enable != 0;
-  e->step_dirty = true;
-  return RF_OK;
-}
-
-int rf_step_profile(rf_engine* e, int enable) {
-  ENGINE_GUARD(e);
-  e->step_profile = enable != 0;
-  if (e->step_profile) RF_CUDA(cudaMemsetAsync(e->d_stamps, 0, 8ull * (5 * e->cfg.n_layers + 8), e->stream));
-  return RF_OK;
-}
-
-int rf_step_phase_times(rf_engine* e, float* us, uint32_t n, uint32_t* n_out) {
-  ENGINE_GUARD(e);
-  if (!us || !n_out) return set_error(RF_EINVAL, "null argument");
-  const uint32_t nb = 5 * e->cfg.n_layers + 8;
-  std::vector<unsigned long long> t(nb);
-  RF_CUDA(cudaStreamSynchronize(e->stream));
-  RF_CUDA(cudaMemcpy(t.data(), e->d_stamps, 8ull * nb, cudaMemcpyDeviceToHost));
-  uint32_t k = 0;
-  for (uint32_t i = 1; i < nb && t[i] >= t[i - 1] && t[i] && k < n; i++) us[k++] = (float)(t[i] - t[i - 1]) * 1e-3f;
-  *n_out = k;
-  return RF_OK;
-}
-
-int rf_selftest_barrier(int device, uint32_t phantom_arrivals, uint32_t* err_word) {
+int rf_selftest_wait(int device, uint32_t* err_word) {
   if (!err_word) return set_error(RF_EINVAL, "null argument");
   RF_CUDA(cudaSetDevice(device));
   unsigned w = 0;
-  RF_CUDA(barrier_selftest(phantom_arrivals, &w));
+  RF_CUDA(peer_sum_selftest(&w));
   *err_word = w;
-  return RF_OK;
-}
-
-int rf_step_kernel_active(rf_engine* e, int* out) {
-  ENGINE_GUARD(e);
-  if (!out) return set_error(RF_EINVAL, "null argument");
-  *out = all_resident(e) && step_kernel_active(e) ? 1 : 0;
   return RF_OK;
 }
 

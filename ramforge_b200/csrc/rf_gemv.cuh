@@ -407,9 +407,8 @@ __device__ __forceinline__ unsigned arrive_acq_rel(unsigned* p, unsigned v) {
 }
 
 // The quantized GEMV over every CTA of the grid.  `wait()` runs before the
-// first read of x (the previous kernel's completion, or a grid barrier of the
-// persistent step kernel); x and the residual input are read through L2, so
-// they may come from earlier in the same kernel.
+// first read of x (griddepcontrol.wait: the previous kernel's completion); x and
+// the residual input are read through L2.
 template <int FMT, bool QUIRK, int NW = QG_WARPS, class Epi, class Wait>
 __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __restrict__ x,
                                            const float* __restrict__ nw, float eps, float* __restrict__ part,
@@ -528,8 +527,6 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       if (c >= lo && c < hi) load_piece(ia, c);
   }
 
-  // Shared memory may still be in use by the CTA's previous phase until wait()
-  // returns (the step kernel's barrier begins with a CTA barrier).
   wait();
   if (lane < 2) stile[2 * warp + lane] = -1;
   if (epre) epi.pre_begin();

@@ -386,6 +386,9 @@ void peer_sum_bind(PeerSum* P, int p, void* area_of_p, bool own);
 // out[i] = sum over ranks of partial[i] (i < n, n a multiple of 4); call site
 // `site` < P.sites, consecutive sites of one step alternate parity.
 cudaError_t launch_peer_sum(const Launch& L, const PeerSum& P, const float* partial, float* out, int n, int site);
+// One peer sum whose second rank never arrives (a local phantom area): its
+// bounded wait gives up and sets bit 0 of *err_out.
+cudaError_t peer_sum_selftest(unsigned* err_out);
 
 // ---- attention -------------------------------------------------------------
 struct AttnArgs {
@@ -417,53 +420,6 @@ cudaError_t launch_finalize(const Launch& L, const unsigned long long* key, uint
                             uint32_t* hist, int hist_len);
 // Dequantize rows [r0, r0+n) of a packed matrix into f32 (debug / parity dumps).
 cudaError_t launch_dequant_rows(const PackedMat& W, uint32_t r0, uint32_t n, float* out, cudaStream_t s);
-// ---- the persistent decode-step kernel (rf_step.cu) ------------------------------
-// One cooperative launch runs a whole token step: embedding row, every layer
-// (QKV+RoPE+KV append | attention | Wo+residual | gate/up+SwiGLU | down+residual),
-// then either the LM head + greedy argmax + advance (decode) or the final
-// RMSNorm into final_hidden (forward).  Phases are separated by grid barriers
-// whose waits are bounded (err bit 0 on expiry); each GEMV phase issues its
-// first weight loads before its barrier.
-struct StepLayer {
-  PackedMat qkv, wo, gateup, down;
-  const float* attn_norm;
-  const float* ffn_norm;
-  RopeQKVArgs rope;  // the QKV epilogue of this layer (its K/V cache, shapes, buffers)
-  AttnArgs attn;     // the attention of this layer
-};
-struct StepArgs {
-  const StepLayer* layers;  // device array [n_layers]
-  int n_layers;
-  int decode;
-  PackedMat embd, lm;
-  const float* out_norm;
-  float eps;
-  uint32_t n_embd, q_rows, kv_rows, head_dim, max_seq, n_heads, n_kv_heads;
-  const float2* rope_cs;
-  float *hidden, *final_hidden, *q, *k_cur, *v_cur, *att, *act, *logits;  // logits may be NULL
-  uint32_t* d_token;
-  int* d_pos;
-  uint32_t* hist;
-  int hist_len;
-  unsigned long long* key;
-  uint32_t vocab_off;
-  GemvScratch gws;
-  float* attn_part;
-  unsigned* attn_counters;
-  int max_splits;
-  unsigned* bar;  // arrival counter (zeroed by launch_step_kernel)
-  unsigned* err;  // bit 0: a barrier wait gave up
-  unsigned long long* stamps;  // NULL, or [barriers + 1] globaltimer ns: kernel start, then each barrier's end
-};
-// Dynamic shared memory of the step kernel for these shapes, or 0 when the
-// kernel has no instance for them (layer / LM-head types, head_dim, GQA group,
-// f16 KV cache, no subnormal scales) or they do not fit one CTA per SM.
-size_t step_kernel_smem(const StepArgs& a, const StepLayer& layer0);
-cudaError_t launch_step_kernel(cudaStream_t s, const StepArgs& a, const StepLayer& layer0, size_t smem);
-// Runs one step-kernel barrier on the current device with `phantom` extra
-// expected arrivals (none of which come) and returns the error word.
-cudaError_t barrier_selftest(unsigned phantom, unsigned* err_out);
-
 // f16/f32 KV read in reference layout: out[p][h][d] for p in [start,end).
 cudaError_t launch_kv_gather(const void* cache, int kv_f32, uint32_t kv_heads, uint32_t max_seq, uint32_t hd,
                              uint32_t start, uint32_t end, float* out, cudaStream_t s);

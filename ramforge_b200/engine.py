@@ -156,35 +156,12 @@ class DecodeEngine:
         check(lib().rf_step_kernel_count(self._h, ctypes.byref(v)))
         return v.value
 
-    def set_step_kernel(self, enable: bool) -> None:
-        """Allow (default) or forbid the persistent one-launch-per-token step kernel."""
-        check(lib().rf_set_step_kernel(self._h, 1 if enable else 0))
-
     @property
     def tp_peer_sum(self) -> bool:
         """True when tensor-parallel sums run over NVLink peer memory (else NCCL)."""
         v = ctypes.c_int()
         check(lib().rf_tp_peer_sum(self._h, ctypes.byref(v)))
         return bool(v.value)
-
-    @property
-    def step_kernel_active(self) -> bool:
-        v = ctypes.c_int()
-        check(lib().rf_step_kernel_active(self._h, ctypes.byref(v)))
-        return bool(v.value)
-
-    def step_profile(self, enable: bool) -> None:
-        """Record grid-barrier completion times in every step-kernel launch."""
-        check(lib().rf_step_profile(self._h, 1 if enable else 0))
-
-    def step_phase_times(self) -> np.ndarray:
-        """Phase durations (us) of the last profiled step: embedding, then per layer
-        [QKV, attention, Wo, gate/up, down], then LM head or final norm."""
-        n = 5 * self.config["n_layers"] + 8
-        out = np.zeros(n, np.float32)
-        k = ctypes.c_uint32()
-        check(lib().rf_step_phase_times(self._h, _fp(out), n, ctypes.byref(k)))
-        return out[:k.value]
 
     def decode_timed(self, token: int, n_steps: int):
         """n greedy decode steps timed on the device; returns (tokens, device_ms)."""
@@ -277,10 +254,18 @@ class QMatrix:
             pass
 
 
+def selftest_wait(device: int = 0) -> int:
+    """Runs one peer sum whose second rank never arrives (rf_selftest_wait);
+    returns its error word (1: the bounded wait gave up, as it must)."""
+    w = ctypes.c_uint32()
+    check(lib().rf_selftest_wait(device, ctypes.byref(w)))
+    return w.value
+
+
 def decode_attention(q_ptr: int, k_ptr: int, v_ptr: int, ctx: int, n_heads: int, n_kv_heads: int, head_dim: int,
                      batch: int, out_ptr: int, stream: int = 0):
     """GQA decode attention on device pointers (rf_decode_attention)."""
     check(lib().rf_decode_attention(q_ptr, k_ptr, v_ptr, ctx, n_heads, n_kv_heads, head_dim, batch, out_ptr, stream))
 
 
-__all__ = ["DecodeEngine", "QMatrix", "decode_attention", "tp_unique_id", "RfError"]
+__all__ = ["DecodeEngine", "QMatrix", "decode_attention", "selftest_wait", "tp_unique_id", "RfError"]

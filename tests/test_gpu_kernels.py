@@ -226,3 +226,12 @@ def test_decode_attention_repeated_calls_reuse_workspace():
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
     ref = torch.softmax((q.view(1, KV, 4, hd) @ k.float().transpose(-1, -2)) / hd ** 0.5, -1) @ v.float()
     assert torch.allclose(outs[0], ref.view(1, H, hd), atol=1e-4, rtol=1e-4)
+
+
+def test_bounded_peer_sum_wait_gives_up_and_reports():
+    """The tensor-parallel peer sum's wait is bounded: a rank whose flag never
+    comes makes it give up after about a second, set the error bit and return,
+    and the device stays usable (a matvec right after it is correct)."""
+    from ramforge_b200 import selftest_wait
+    assert selftest_wait(0) == 1
+    _run_qmv(synth.Q4_K, 512, 1024)
