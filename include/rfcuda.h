@@ -256,6 +256,18 @@ uint64_t rf_matrix_device_bytes(const rf_matrix* m);
 /* y[b][out] = W . x[b][in] for b < batch (1..8); dX, dY device pointers; stream
  * is a cudaStream_t (NULL = legacy default stream). */
 int rf_qmatvec(const rf_matrix* m, const float* dX, float* dY, int batch, void* stream);
+/* Y[t][out] = W . X[t] for t < n_tokens (any positive count): the batched form
+ * of quantized_matvec_dispatch (compute_dispatch.rs:90-254) on the tensor cores,
+ * for prompt batches.  dX [n_tokens][in] f32, dY [n_tokens][out] f32, device
+ * pointers; Q4_K and Q8_0 matrices (RF_EUNSUPPORTED otherwise).  Each weight and
+ * activation is split into bf16 hi + lo and multiplied as hi*hi + hi*lo + lo*hi
+ * with f32 accumulation (relative error near 2^-16 against the f32 reference).
+ * The split activations live in a per-device workspace the library grows. */
+int rf_qgemm(const rf_matrix* m, const float* dX, float* dY, int n_tokens, void* stream);
+/* Error word of rf_qgemm on the current device (synchronises it, reads, clears):
+ * bit 0 = a bounded wait of the GEMM gave up, so some output since the last read
+ * is unspecified.  No counterpart in the reference. */
+int rf_qgemm_error_word(uint32_t* word);
 /* Single-token GQA decode attention (attention_reference compute.rs:461-547)
  * for `batch` sequences: dQ [batch][H][hd] f32, dK/dV [batch][KV][ctx][hd] f16,
  * dOut [batch][H][hd] f32; softmax over all ctx positions with scale 1/sqrt(hd).

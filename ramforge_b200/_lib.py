@@ -36,7 +36,7 @@ EXPORTS = [
     "rf_budget_used", "rf_budget_available", "rf_set_residency_plan", "rf_residency_stats_get",
     "rf_step_kernel_count", "rf_selftest_wait", "rf_decode_timed",
     "rf_bench_layer_kernels", "rf_tp_unique_id", "rf_tp_peer_sum", "rf_matrix_create", "rf_matrix_destroy", "rf_matrix_device_bytes",
-    "rf_qmatvec", "rf_decode_attention", "rf_decode_attention_noalloc",
+    "rf_qmatvec", "rf_qgemm", "rf_qgemm_error_word", "rf_decode_attention", "rf_decode_attention_noalloc",
 ]
 
 
@@ -132,6 +132,8 @@ def lib():
             "rf_matrix_destroy": (None, [vp]),
             "rf_matrix_device_bytes": (c_u64, [vp]),
             "rf_qmatvec": (c_int, [vp, vp, vp, c_int, vp]),
+            "rf_qgemm": (c_int, [vp, vp, vp, c_int, vp]),
+            "rf_qgemm_error_word": (c_int, [u32p]),
             "rf_decode_attention": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp, vp]),
             "rf_decode_attention_noalloc": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp, vp]),
         }

@@ -22,7 +22,8 @@ NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2,-ffp-contract=off", "--expt-relaxed-constexpr",
                      "-I" + os.path.join(ROOT, "include")]
-CUDA_SOURCES = ["rf_kernels.cu", "rf_gemv.cu", "rf_allreduce.cu", "rf_engine.cu", "rf_ops.cu", "rf_common.cpp"]
+CUDA_SOURCES = ["rf_kernels.cu", "rf_gemv.cu", "rf_prefill.cu", "rf_allreduce.cu", "rf_engine.cu", "rf_ops.cu",
+                "rf_common.cpp"]
 
 
 def _run(cmd):

@@ -362,6 +362,23 @@ cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const GemvScratch* 
 cudaError_t gemv_batched(cudaStream_t s, const PackedMat& W, const GemvScratch* ws, const float* x, int batch,
                          float* y);
 
+// ---- batched prompt GEMM on the tensor cores (rf_prefill.cu) ---------------------
+// Formats the tensor-core GEMM dequantizes (Q4_K, Q8_0); other matrices keep the
+// token-by-token path.
+bool prefill_supported(int type);
+// Bytes of the split activation buffer for T tokens of padded row length Kp.
+size_t prefill_xt_bytes(uint32_t T, uint32_t Kp);
+// X [T][K] f32 (row stride ldx), RMS-normalised per token with nw/eps when nw is
+// set, split into bf16 hi/lo in the GEMM's tiled operand layout (Kp >= K, a
+// multiple of 64; the padding is zero).
+cudaError_t prefill_split(const Launch& L, const float* X, uint32_t ldx, uint32_t T, uint32_t K, uint32_t Kp,
+                          const float* nw, float eps, void* Xt);
+// y[t][row] = (W . x_t)[row] for t < T on the tensor cores (3 bf16 products per
+// element pair: hi*hi + hi*lo + lo*hi, f32 accumulation); err (may be null) gets
+// bit 0 when a bounded wait gave up.
+cudaError_t prefill_gemm_store(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
+                               float* y, uint32_t ldy);
+
 // ---- tensor-parallel sum over NVLink peer memory ------------------------------
 // The sum of the ranks' partial vectors after a row-parallel projection, as one
 // kernel over peer memory instead of a library all-reduce: every rank stores its

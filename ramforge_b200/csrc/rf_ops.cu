@@ -214,6 +214,71 @@ int rf_qmatvec(const rf_matrix* m, const float* dX, float* dY, int batch, void* 
   return RF_OK;
 }
 
+// rf_qgemm's per-device workspace: the split activations and an error word.
+struct QgemmWorkspace {
+  void* xt = nullptr;
+  size_t xt_bytes = 0;
+  unsigned* err = nullptr;
+};
+std::mutex g_qg_mu;
+std::unordered_map<int, QgemmWorkspace> g_qg;
+
+int rf_qgemm(const rf_matrix* m, const float* dX, float* dY, int n_tokens, void* stream) {
+  if (!m || !dX || !dY) return set_error(RF_EINVAL, "null argument");
+  if (n_tokens < 1) return set_error(RF_EINVAL, "n_tokens %d must be positive", n_tokens);
+  if (!prefill_supported(m->m.type))
+    return set_error(RF_EUNSUPPORTED, "the tensor-core GEMM covers Q4_K and Q8_0 matrices, not type %d", m->m.type);
+  cudaStream_t s = (cudaStream_t)stream;
+  int cur = 0;
+  RF_CUDA(cudaGetDevice(&cur));
+  if (cur != m->device) return set_error(RF_EINVAL, "matrix lives on device %d, current device is %d", m->device, cur);
+  const size_t need = prefill_xt_bytes((uint32_t)n_tokens, m->m.Kp);
+  void* xt = nullptr;
+  unsigned* err = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_qg_mu);
+    QgemmWorkspace& w = g_qg[cur];
+    if (!w.err) {
+      RF_CUDA(cudaMalloc(&w.err, sizeof(unsigned)));
+      RF_CUDA(cudaMemset(w.err, 0, sizeof(unsigned)));
+      RF_CUDA(cudaDeviceSynchronize());
+    }
+    if (w.xt_bytes < need) {
+      if (w.xt) cudaFree(w.xt);
+      w.xt = nullptr;
+      w.xt_bytes = 0;
+      RF_CUDA(cudaMalloc(&w.xt, need));
+      w.xt_bytes = need;
+    }
+    xt = w.xt;
+    err = w.err;
+  }
+  RF_CUDA(prefill_split(Launch{s, false}, dX, m->m.K, (uint32_t)n_tokens, m->m.K, m->m.Kp, nullptr, 0.f, xt));
+  RF_CUDA(prefill_gemm_store(Launch{s, false}, m->m, xt, (uint32_t)n_tokens, err, dY, m->m.M));
+  return RF_OK;
+}
+
+int rf_qgemm_error_word(uint32_t* word) {
+  if (!word) return set_error(RF_EINVAL, "null argument");
+  int dev = 0;
+  RF_CUDA(cudaGetDevice(&dev));
+  unsigned* err = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_qg_mu);
+    auto it = g_qg.find(dev);
+    if (it != g_qg.end()) err = it->second.err;
+  }
+  *word = 0;
+  if (!err) return RF_OK;
+  RF_CUDA(cudaDeviceSynchronize());
+  unsigned w = 0;
+  RF_CUDA(cudaMemcpy(&w, err, sizeof w, cudaMemcpyDeviceToHost));
+  if (w) RF_CUDA(cudaMemset(err, 0, sizeof w));
+  RF_CUDA(cudaDeviceSynchronize());
+  *word = w;
+  return RF_OK;
+}
+
 int rf_decode_attention(const float* dQ, const uint16_t* dK, const uint16_t* dV, int ctx, int n_heads, int n_kv_heads,
                         int head_dim, int batch, float* dOut, void* stream) {
   if (!dQ || !dK || !dV || !dOut) return set_error(RF_EINVAL, "null argument");

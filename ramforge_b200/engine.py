@@ -242,6 +242,10 @@ class QMatrix:
         """y[b] = W x[b] on device pointers (e.g. torch tensor .data_ptr())."""
         check(lib().rf_qmatvec(self._h, x_ptr, y_ptr, batch, stream))
 
+    def gemm(self, x_ptr: int, y_ptr: int, n_tokens: int, stream: int = 0):
+        """Y[t] = W X[t] for n_tokens rows on the tensor cores (rf_qgemm); device pointers."""
+        check(lib().rf_qgemm(self._h, x_ptr, y_ptr, n_tokens, stream))
+
     def close(self):
         if self._h:
             lib().rf_matrix_destroy(self._h)
