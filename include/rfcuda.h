@@ -205,8 +205,9 @@ int rf_selftest_wait(int device, uint32_t* err_word);
 int rf_decode_timed(rf_engine* e, uint32_t token, uint32_t n_steps, uint32_t* out_tokens, float* device_ms);
 /* Average device time per launch of each per-layer kernel class
  * (0 QKV+RoPE, 1 attention, 2 Wo+residual, 3 gate/up+SwiGLU, 4 down+residual),
- * each class launched over every resident layer in turn, `iters` rounds, with
- * events on the engine stream.  Runs at pos = KV length without committing. */
+ * each class launched over every resident layer in turn, `iters` rounds, captured
+ * into one CUDA graph and replayed between events on the engine stream (device
+ * time, no host launch time).  Runs at pos = KV length without committing. */
 int rf_bench_layer_kernels(rf_engine* e, uint32_t iters, float* avg_ms5);
 
 /* ---- KV cache (KvCache, kv_cache.rs:20-510) ------------------------------------ */

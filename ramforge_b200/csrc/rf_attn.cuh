@@ -129,6 +129,106 @@ __device__ __forceinline__ void warp_transpose_sum(float* v, int lane) {
   }
 }
 
+// End of a split unit that has written its partial ([G][hd] sums, then (m, l)
+// per head) to a.part: the last unit of (sequence b, KV head kvh) to arrive
+// merges the nsplit partials (max-rescaled sums) into out_b; the others return.
+// Run by ATT_THREADS threads (t = thread index, warp/lane of t); `sync` is their
+// barrier, s_w [ATT_MERGE_SPLITS][G] and s_last shared scratch.
+template <int DPL, int G, class Sync>
+__device__ __forceinline__ void attn_merge_tail(const AttnArgs& a, int b, int kvh, int nsplit, float* out_b,
+                                                float (*s_w)[G], int* s_last, int t, Sync&& sync) {
+  const int lane = t & 31, warp = t >> 5, hd = a.head_dim;
+  const size_t slot = ((size_t)b * a.n_kv_heads + kvh) * a.max_splits;
+  __threadfence();
+  sync();
+  if (t == 0) {
+    const unsigned prev = atomicAdd(&a.counters[(size_t)b * a.n_kv_heads + kvh], 1u);
+    *s_last = prev == (unsigned)(nsplit - 1);
+  }
+  sync();
+  if (!*s_last) {
+    sync();
+    return;
+  }
+  __threadfence();
+  const float* pall = a.part + slot * (size_t)G * (hd + 2);
+  if (nsplit <= ATT_MERGE_SPLITS) {
+    // one warp per head: split weights exp(m_s - M) / sum_s exp(m_s - M) l_s in one load round
+    for (int h = warp; h < G; h += ATT_WARPS) {
+      float ms[ATT_MERGE_SPLITS / 32], ls[ATT_MERGE_SPLITS / 32];
+      float M = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) {
+        const int sp = lane + 32 * j;
+        const float* ps = pall + ((size_t)sp * G + h) * (hd + 2);
+        ms[j] = sp < nsplit ? __ldcg(ps + hd) : -INFINITY;
+        ls[j] = sp < nsplit ? __ldcg(ps + hd + 1) : 0.f;
+        M = fmaxf(M, ms[j]);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float L = 0.f;
+#pragma unroll
+      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) {
+        ms[j] = lane + 32 * j < nsplit ? expf(ms[j] - M) : 0.f;
+        L = fmaf(ms[j], ls[j], L);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+#pragma unroll
+      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) s_w[lane + 32 * j][h] = ms[j] / L;
+    }
+    sync();
+    // every output element: sum_s w_s * O_s.  A thread owns EPT elements and
+    // loads four splits of all of them per round, every load of a round in
+    // flight together.
+    constexpr int EPT = (G * DPL * 32 + ATT_THREADS - 1) / ATT_THREADS;  // hd <= 32*DPL
+    float O[EPT];
+#pragma unroll
+    for (int k = 0; k < EPT; k++) O[k] = 0.f;
+    for (int s0 = 0; s0 < nsplit; s0 += 4) {
+      float v[EPT][4];
+#pragma unroll
+      for (int k = 0; k < EPT; k++) {
+        const int i = t + k * ATT_THREADS, h = i / hd, d = i % hd;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          v[k][j] = i < G * hd && s0 + j < nsplit ? __ldcg(pall + ((size_t)(s0 + j) * G + h) * (hd + 2) + d) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < EPT; k++) {
+        const int i = t + k * ATT_THREADS, h = i / hd;
+        if (i < G * hd) {
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+            if (s0 + j < nsplit) O[k] = fmaf(s_w[s0 + j][h], v[k][j], O[k]);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < EPT; k++) {
+      const int i = t + k * ATT_THREADS, h = i / hd, d = i % hd;
+      if (i < G * hd) out_b[(size_t)h * hd + d] = O[k];
+    }
+  } else {
+    for (int i = t; i < G * hd; i += ATT_THREADS) {
+      const int h = i / hd, d = i % hd;
+      float M = -INFINITY;
+      for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(pall + ((size_t)s * G + h) * (hd + 2) + hd));
+      float L = 0.f, O = 0.f;
+      for (int s = 0; s < nsplit; s++) {
+        const float* ps = pall + ((size_t)s * G + h) * (hd + 2);
+        const float sc = expf(__ldcg(ps + hd) - M);
+        L = fmaf(sc, __ldcg(ps + hd + 1), L);
+        O = fmaf(sc, __ldcg(ps + d), O);
+      }
+      out_b[(size_t)h * hd + d] = O / L;
+    }
+  }
+  if (t == 0) a.counters[(size_t)b * a.n_kv_heads + kvh] = 0u;
+  sync();  // shared memory may be reused after this
+}
+
 // One (KV head, split, sequence) unit, run by the ATT_THREADS threads of group
 // `gid` (thread t = threadIdx.x % ATT_THREADS, barrier gid + 1).  The caller has
 // made a.q, a.k_cur, a.v_cur and the history length visible.  PPW_CAP bounds
@@ -307,94 +407,7 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kvh, int split,
     __stcg(part + (size_t)t * (hd + 2) + hd, sm[t]);
     __stcg(part + (size_t)t * (hd + 2) + hd + 1, sl[t]);
   }
-  __threadfence();
-  group_sync(bar);
-  if (t == 0) {
-    const unsigned prev = atomicAdd(&a.counters[(size_t)b * a.n_kv_heads + kvh], 1u);
-    *s_last = prev == (unsigned)(nsplit - 1);
-  }
-  group_sync(bar);
-  if (!*s_last) {
-    group_sync(bar);
-    return;
-  }
-  __threadfence();
-  const float* pall = a.part + slot * (size_t)G * (hd + 2);
-  if (nsplit <= ATT_MERGE_SPLITS) {
-    // one warp per head: split weights exp(m_s - M) / sum_s exp(m_s - M) l_s in one load round
-    for (int h = warp; h < G; h += ATT_WARPS) {
-      float ms[ATT_MERGE_SPLITS / 32], ls[ATT_MERGE_SPLITS / 32];
-      float M = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) {
-        const int sp = lane + 32 * j;
-        const float* ps = pall + ((size_t)sp * G + h) * (hd + 2);
-        ms[j] = sp < nsplit ? __ldcg(ps + hd) : -INFINITY;
-        ls[j] = sp < nsplit ? __ldcg(ps + hd + 1) : 0.f;
-        M = fmaxf(M, ms[j]);
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      float L = 0.f;
-#pragma unroll
-      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) {
-        ms[j] = lane + 32 * j < nsplit ? expf(ms[j] - M) : 0.f;
-        L = fmaf(ms[j], ls[j], L);
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-#pragma unroll
-      for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) s_w[lane + 32 * j][h] = ms[j] / L;
-    }
-    group_sync(bar);
-    // every output element: sum_s w_s * O_s.  A thread owns EPT elements and
-    // loads four splits of all of them per round, every load of a round in
-    // flight together.
-    constexpr int EPT = (G * DPL * 32 + ATT_THREADS - 1) / ATT_THREADS;  // hd <= 32*DPL
-    float O[EPT];
-#pragma unroll
-    for (int k = 0; k < EPT; k++) O[k] = 0.f;
-    for (int s0 = 0; s0 < nsplit; s0 += 4) {
-      float v[EPT][4];
-#pragma unroll
-      for (int k = 0; k < EPT; k++) {
-        const int i = t + k * ATT_THREADS, h = i / hd, d = i % hd;
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-          v[k][j] = i < G * hd && s0 + j < nsplit ? __ldcg(pall + ((size_t)(s0 + j) * G + h) * (hd + 2) + d) : 0.f;
-      }
-#pragma unroll
-      for (int k = 0; k < EPT; k++) {
-        const int i = t + k * ATT_THREADS, h = i / hd;
-        if (i < G * hd) {
-#pragma unroll
-          for (int j = 0; j < 4; j++)
-            if (s0 + j < nsplit) O[k] = fmaf(s_w[s0 + j][h], v[k][j], O[k]);
-        }
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < EPT; k++) {
-      const int i = t + k * ATT_THREADS, h = i / hd, d = i % hd;
-      if (i < G * hd) out_b[(size_t)h * hd + d] = O[k];
-    }
-  } else {
-    for (int i = t; i < G * hd; i += ATT_THREADS) {
-      const int h = i / hd, d = i % hd;
-      float M = -INFINITY;
-      for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(pall + ((size_t)s * G + h) * (hd + 2) + hd));
-      float L = 0.f, O = 0.f;
-      for (int s = 0; s < nsplit; s++) {
-        const float* ps = pall + ((size_t)s * G + h) * (hd + 2);
-        const float sc = expf(__ldcg(ps + hd) - M);
-        L = fmaf(sc, __ldcg(ps + hd + 1), L);
-        O = fmaf(sc, __ldcg(ps + d), O);
-      }
-      out_b[(size_t)h * hd + d] = O / L;
-    }
-  }
-  if (t == 0) a.counters[(size_t)b * a.n_kv_heads + kvh] = 0u;
-  group_sync(bar);  // the group's shared memory is reused by its next unit
+  attn_merge_tail<DPL, G>(a, b, kvh, nsplit, out_b, s_w, s_last, t, [&] { group_sync(bar); });
 }
 
 }  // namespace rf

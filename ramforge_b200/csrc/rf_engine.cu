@@ -849,6 +849,7 @@ AttnArgs attn_args(rf_engine* e, int l) {
   aa.counters = e->attn_counters;
   aa.out = e->att;
   aa.kv_f32 = e->rt.kv_f32;
+  aa.max_ctx = (int)e->max_seq;
   return aa;
 }
 
@@ -861,6 +862,12 @@ int tp_sum(rf_engine* e, const Launch& La, int site) {
     RF_NCCL(nccl()->allReduce(e->partial, e->hidden, e->cfg.n_embd, ncclFloat32, ncclSum, e->comm, e->stream));
   }
   return RF_OK;
+}
+
+bool all_resident(const rf_engine* e) {
+  for (auto& L : e->layers)
+    if (!L.resident) return false;
+  return true;
 }
 
 int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
@@ -896,11 +903,6 @@ int enqueue_layer(rf_engine* e, int l, bool pdl) {
   return RF_OK;
 }
 
-bool all_resident(const rf_engine* e) {
-  for (auto& L : e->layers)
-    if (!L.resident) return false;
-  return true;
-}
 
 // embedding -> every layer -> output RMSNorm into final_hidden.
 int enqueue_forward(rf_engine* e, bool pdl) {
@@ -1566,14 +1568,29 @@ int rf_bench_layer_kernels(rf_engine* e, uint32_t iters, float* avg_ms5) {
   RF_CUDA(cudaEventCreate(&a));
   RF_CUDA(cudaEventCreate(&b));
   int rc = RF_OK;
+  // Each kernel class over all layers, `iters` times, captured into one graph and
+  // replayed: the launches are serialised on the device with no host time between
+  // them, so the average is the kernel's own device time (plus the graph's
+  // kernel-to-kernel gap), not the host's launch rate.
   for (int k = 0; k < 5 && !rc; k++) {
-    cudaEventRecord(a, e->stream);
-    for (uint32_t it = 0; it < iters && !rc; it++)
-      for (uint32_t l = 0; l < e->cfg.n_layers && !rc; l++) rc = enqueue_layer_kernel(e, (int)l, k);
-    cudaEventRecord(b, e->stream);
-    cudaError_t ce = cudaEventSynchronize(b);
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaError_t ce = cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal);
+    if (ce == cudaSuccess) {
+      for (uint32_t it = 0; it < iters && !rc; it++)
+        for (uint32_t l = 0; l < e->cfg.n_layers && !rc; l++) rc = enqueue_layer_kernel(e, (int)l, k);
+      ce = cudaStreamEndCapture(e->stream, &g);
+    }
+    if (ce == cudaSuccess && !rc) ce = cudaGraphInstantiate(&ge, g, 0);
+    if (ce == cudaSuccess && !rc) ce = cudaGraphLaunch(ge, e->stream);  // warm-up
+    if (ce == cudaSuccess && !rc) ce = cudaEventRecord(a, e->stream);
+    if (ce == cudaSuccess && !rc) ce = cudaGraphLaunch(ge, e->stream);
+    if (ce == cudaSuccess && !rc) ce = cudaEventRecord(b, e->stream);
+    if (ce == cudaSuccess && !rc) ce = cudaEventSynchronize(b);
     float ms = 0.f;
-    if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, a, b);
+    if (ce == cudaSuccess && !rc) ce = cudaEventElapsedTime(&ms, a, b);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
     if (ce != cudaSuccess && !rc) rc = set_error(RF_ECUDA, "kernel timing failed: %s", cudaGetErrorString(ce));
     avg_ms5[k] = ms / (float)(iters * e->cfg.n_layers);
   }

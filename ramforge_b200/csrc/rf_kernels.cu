@@ -15,6 +15,7 @@
 #include <algorithm>
 
 #include "rf_attn.cuh"
+#include "rf_attn_stream.cuh"
 #include "rf_device.cuh"
 
 namespace rf {
@@ -273,9 +274,55 @@ static cudaError_t attn_dispatch_g(const Launch& L, const AttnArgs& a, int G) {
   }
 }
 
+// The streaming kernel (f16 cache, head_dim 32/64/128): as many splits as fill
+// the CTAs that fit on the GPU at once (occupancy of this instance x SMs).
+template <int G, int HD>
+static cudaError_t attn_stream_launch(const Launch& L, const AttnArgs& a) {
+  auto k = attn_stream_kernel<G, HD>;
+  constexpr size_t smem = as_smem_bytes<G, HD>();
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  static int per_sm = 0;
+  if (!per_sm) {
+    int nb = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, AS_THREADS, smem);
+    if (e != cudaSuccess) return e;
+    per_sm = nb > 0 ? nb : 1;
+  }
+  const int slots = per_sm * num_sms();
+  const int units = a.n_kv_heads * a.batch;
+  const int gy = std::max(1, std::min(a.max_splits, slots / std::max(1, units)));
+  return launch_k(L, k, dim3(a.n_kv_heads, gy, a.batch), dim3(AS_THREADS), smem, a, slots);
+}
+template <int HD>
+static cudaError_t attn_stream_g(const Launch& L, const AttnArgs& a, int G) {
+  switch (G) {
+    case 1: return attn_stream_launch<1, HD>(L, a);
+    case 2: return attn_stream_launch<2, HD>(L, a);
+    case 4: return attn_stream_launch<4, HD>(L, a);
+    case 8: return attn_stream_launch<8, HD>(L, a);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 cudaError_t launch_attention(const Launch& L, const AttnArgs& a) {
   if (a.n_kv_heads <= 0 || a.n_heads % a.n_kv_heads) return cudaErrorInvalidValue;
   const int G = a.n_heads / a.n_kv_heads;
+  // bulk copies need 16-byte aligned rows: an f16 cache whose base and strides are
+  // multiples of 16 bytes
+  const bool aligned = ((uintptr_t)a.kc % 16 == 0) && ((uintptr_t)a.vc % 16 == 0) && (a.head_stride * 2) % 16 == 0 &&
+                       (a.batch_stride * 2) % 16 == 0;
+  // Streaming pays from about a thousand positions: below that the unit is one
+  // latency-bound pass either way, and inside the decode step the register kernel
+  // measured faster (ctx ~530: 418 vs 411 tokens/s), while at 32768 positions the
+  // streaming kernel takes half the time.  The engine's hint is its KV capacity
+  // (the graph serves every context up to it); a standalone call's is its context.
+  const int ctx_hint = a.d_nhist ? a.max_ctx : a.nhist + (a.k_cur ? 1 : 0);
+  if (ctx_hint >= kAttnStreamMinCtx && !a.kv_f32 && aligned && (G == 1 || G == 2 || G == 4 || G == 8)) {
+    if (a.head_dim == 128) return attn_stream_g<128>(L, a, G);
+    if (a.head_dim == 64) return attn_stream_g<64>(L, a, G);
+    if (a.head_dim == 32) return attn_stream_g<32>(L, a, G);
+  }
   if (a.head_dim <= 32) return attn_dispatch_g<1>(L, a, G);
   if (a.head_dim <= 64) return attn_dispatch_g<2>(L, a, G);
   if (a.head_dim <= 128) return attn_dispatch_g<4>(L, a, G);

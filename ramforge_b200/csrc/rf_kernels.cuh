@@ -423,7 +423,11 @@ struct AttnArgs {
   unsigned* counters;      // [batch][KV], zero at rest
   float* out;              // [batch][H][hd]
   int kv_f32;
+  unsigned* err;           // bit 1 set when a bounded wait gave up (may be NULL)
+  int max_ctx;             // with d_nhist: the longest context the launch may serve (kernel choice)
 };
+// Contexts from which launch_attention streams the history through shared memory.
+constexpr int kAttnStreamMinCtx = 1024;
 size_t attn_part_floats(int batch, int n_kv_heads, int max_splits, int G, int hd);
 cudaError_t launch_attention(const Launch& L, const AttnArgs& a);
 

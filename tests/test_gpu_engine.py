@@ -109,12 +109,15 @@ def test_gqa_fixture_greedy_generation():
     assert eng.generate([1, 3], 12).tolist() == ref.tolist()  # deterministic (inference.rs:2567-2571)
 
 
+# KV capacity 1024 makes the engine use the streaming attention kernel (the
+# register-load kernel serves engines whose capacity is below 1024 positions)
+@pytest.mark.parametrize("max_seq", [256, 1024])
 @pytest.mark.parametrize("name", ["small-q4k", "small-q8", "small-q40", "small-q6k"])
-def test_small_models_stepwise_parity(models, name):
+def test_small_models_stepwise_parity(models, name, max_seq):
     g = models[name]
     rng = np.random.default_rng(5)
     prompt = rng.integers(0, orc.OracleModel(g, max_seq=4).config["vocab_size"], 6).tolist()
-    toks, worst = check_stepwise(g, prompt, 10)
+    toks, worst = check_stepwise(g, prompt, 10, max_seq=max_seq)
     assert len(toks) == 10
 
 
@@ -123,13 +126,14 @@ def test_kv_f32_mode_matches_reference_cache(models):
     check_stepwise(g, [1, 2, 3], 6, kv_f32=True)
 
 
+@pytest.mark.parametrize("max_seq", [128, 1024])
 @pytest.mark.parametrize("graphs", [True, False])
-def test_generate_matches_oracle_greedy(models, graphs):
+def test_generate_matches_oracle_greedy(models, graphs, max_seq):
     g = models["small-q4k"]
     prompt = [5, 17, 99, 3]
-    ref = orc.OracleModel(g, kv_f16=True, max_seq=128, threads=THREADS)
+    ref = orc.OracleModel(g, kv_f16=True, max_seq=max_seq, threads=THREADS)
     want, _, margins = ref.generate(prompt, 40)
-    eng = DecodeEngine(g, max_seq_len=128, disable_graphs=not graphs)
+    eng = DecodeEngine(g, max_seq_len=max_seq, disable_graphs=not graphs)
     got = eng.generate(prompt, 40)
     assert got.tolist() == want.tolist(), (got, want, margins)
     assert eng.kv_seq_len == len(prompt) + 40 - 1

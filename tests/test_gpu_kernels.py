@@ -211,6 +211,49 @@ def test_decode_attention_config3(ctx, batch):
             assert err <= tol, (ctx, b, err)
 
 
+@pytest.mark.parametrize("H,KV,hd", [(8, 8, 128), (16, 8, 128), (32, 4, 128), (64, 8, 128), (4, 4, 64),
+                                     (8, 4, 64), (32, 8, 64), (16, 2, 64), (2, 2, 32), (4, 2, 32), (8, 2, 32),
+                                     (16, 2, 32)])
+@pytest.mark.parametrize("ctx,batch", [(1024, 1), (1025, 2), (1039, 1), (1087, 3), (2065, 2), (4099, 1)])
+def test_decode_attention_streamed_kernel_shapes(H, KV, hd, ctx, batch):
+    """Every instance of the streaming kernel (GQA group 1/2/4/8, head_dim
+    32/64/128; it serves contexts from 1024 positions) at contexts whose splits
+    end inside a tile or on a tile edge, against an fp32 torch restatement of
+    attention_reference."""
+    torch = torch_mod()
+    g = torch.Generator(device="cuda").manual_seed(H * 1000 + KV * 10 + hd + ctx)
+    q = torch.randn(batch, H, hd, device="cuda", generator=g)
+    k = torch.randn(batch, KV, ctx, hd, device="cuda", generator=g).half()
+    v = torch.randn(batch, KV, ctx, hd, device="cuda", generator=g).half()
+    o = torch.full((batch, H, hd), float("nan"), device="cuda")
+    decode_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ctx, H, KV, hd, batch, o.data_ptr())
+    G = H // KV
+    s = (q.view(batch, KV, G, hd) @ k.float().transpose(-1, -2)) / hd ** 0.5
+    ref = (torch.softmax(s, -1) @ v.float()).view(batch, H, hd)
+    torch.cuda.synchronize()
+    tol = 1e-4 * ref.abs().max().item() + 1e-6
+    assert (o - ref).abs().max().item() <= tol
+
+
+def test_decode_attention_unaligned_cache_takes_register_path():
+    """A cache that starts 8 bytes past a 16-byte boundary cannot be bulk-copied;
+    the register-load kernel serves it with the same results."""
+    torch = torch_mod()
+    H, KV, hd, ctx = 32, 8, 128, 700
+    g = torch.Generator(device="cuda").manual_seed(7)
+    q = torch.randn(1, H, hd, device="cuda", generator=g)
+    kbuf = torch.randn(KV * ctx * hd + 4, device="cuda", generator=g).half()
+    vbuf = torch.randn(KV * ctx * hd + 4, device="cuda", generator=g).half()
+    k, v = kbuf[4:].view(1, KV, ctx, hd), vbuf[4:].view(1, KV, ctx, hd)
+    assert k.data_ptr() % 16 == 8
+    o = torch.empty(1, H, hd, device="cuda")
+    decode_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ctx, H, KV, hd, 1, o.data_ptr())
+    s = (q.view(1, KV, H // KV, hd) @ k.float().transpose(-1, -2)) / hd ** 0.5
+    ref = (torch.softmax(s, -1) @ v.float()).view(1, H, hd)
+    torch.cuda.synchronize()
+    assert (o - ref).abs().max().item() <= 1e-4 * ref.abs().max().item() + 1e-6
+
+
 def test_decode_attention_repeated_calls_reuse_workspace():
     torch = torch_mod()
     H, KV, hd, ctx = 32, 8, 128, 3000
