@@ -460,6 +460,30 @@ def json_only_stdout():
     os.dup2(2, 1)
 
 
+def batched_prefill(eng, spec, prompt, first_tbt, tbt_s):
+    """The 512-token prompt through rf_prefill (tensor-core GEMMs in 256-token
+    chunks) against the token-by-token prompt of rf_generate (one decode-graph
+    forward per token, the reference's loop): host time around the synchronous
+    calls, best of 3 after one warm-up; `tflops` counts 2 flops per layer weight
+    and prompt token (the three split-bf16 products are not counted)."""
+    n = len(prompt)
+    times = []
+    for _ in range(4):
+        eng.kv_reset()
+        t0 = time.perf_counter()
+        eng.prefill(prompt)
+        times.append(time.perf_counter() - t0)
+    _, first = eng.compute_logits(want_logits=False)
+    best = min(times[1:])
+    d, q, kv, ff = spec.n_embd, spec.n_embd, spec.n_kv_heads * spec.head_dim, spec.n_ff
+    layer_params = spec.n_layers * ((q + 2 * kv) * d + d * q + 2 * ff * d + d * ff)
+    return {"api": "rf_prefill", "prompt_tokens": n, "tokens_per_s": n / best, "ms": best * 1e3,
+            "token_by_token_tokens_per_s": n / tbt_s, "speedup": tbt_s / best,
+            "tflops": 2.0 * layer_params * n / best / 1e12,
+            "first_token_equals_token_by_token": int(first) == int(first_tbt),
+            "timing": "host clock around the synchronous call (best of 3 after a warm-up)"}
+
+
 def main():
     json_only_stdout()
     ap = argparse.ArgumentParser()
@@ -538,7 +562,9 @@ def main():
         return float(t.item())
 
     # prefill (token by token, like the reference: inference.rs:578-592) + warm-up
+    t0 = time.perf_counter()
     first = int(eng.generate(prompt, 1)[0])
+    tbt_s = time.perf_counter() - t0
     toks, _ = eng.decode_timed(first, args.warmup)
     nxt = int(toks[-1])
     barrier()
@@ -572,6 +598,8 @@ def main():
               "timed_first8": timed_tokens[:8].tolist(), "first_after_prompt": first,
               "timed_equals_e2e": bool(np.array_equal(timed_tokens, e2e_tokens))}
 
+    prefill = batched_prefill(eng, spec, prompt, first, tbt_s) if world == 1 else None
+
     # dominant kernel: gate/up + SwiGLU GEMV, timed over every layer (weights >> L2)
     kms = eng.bench_layer_kernels(iters=3)
     kms = [max_over_ranks(k) for k in kms]
@@ -595,7 +623,7 @@ def main():
         "gpu_launches": args.steps * eng.step_kernel_count, "roofline": roofline,
         "step_roofline": {"bytes_per_token_per_gpu": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak},
         "kernel_ms": dict(zip(["qkv_rope", "attention", "wo_residual", "gateup_swiglu", "down_residual"], kms)),
-        "tokens": tokens, "tp_peer_sum": eng.tp_peer_sum if world > 1 else None,
+        "tokens": tokens, "tp_peer_sum": eng.tp_peer_sum if world > 1 else None, "prefill": prefill,
         "setup_s": {"model_generation": gen_s, "engine_load": load_s},
     }
     eng.close()

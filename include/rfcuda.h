@@ -110,6 +110,9 @@ typedef struct rf_residency_stats {
   uint64_t peak_bytes, h2d_bytes;
   uint64_t ring_copies;      /* layer images copied into ring slots */
   uint64_t host_image_bytes; /* pinned host images of streamed layers (not charged to the VRAM budget) */
+  /* engines created from a file: coalesced reads of streamed layers' tensors
+   * (layer_read.rs:50 plans), the bytes they read and the gap bytes among them */
+  uint64_t file_reads, file_read_bytes, file_gap_bytes;
 } rf_residency_stats;
 
 /* One rank's slice of a tensor-parallel engine: Q/K/V and gate/up are split by
@@ -131,6 +134,40 @@ int rf_gguf_read_config(const void* gguf, uint64_t len, rf_model_config* out);
 /* The shard an engine of tp_size ranks gives rank tp_rank (RF_EINVAL when the
  * model does not split evenly or a slice would cut a quant block of `ggml_type`). */
 int rf_tp_shard_plan(const rf_model_config* cfg, int tp_size, int tp_rank, int ggml_type, rf_tp_shard* out);
+
+/* should_keep_resident (persistent.rs:468): 1 when a persistent tensor of
+ * resident_bytes stays resident under a budget of budget_total bytes (at most a
+ * quarter of it), else 0.  Overflow-free for any inputs. */
+int rf_should_keep_resident(uint64_t resident_bytes, uint64_t budget_total);
+
+/* A tensor's bytes in a GGUF file. */
+typedef struct rf_tensor_extent {
+  uint64_t file_offset, byte_length;
+} rf_tensor_extent;
+/* One read of a layer's plan: a contiguous file range holding `count` tensors
+ * (entries first..first+count-1 of the plan's placements); gap_bytes are the
+ * alignment/metadata bytes between them that the read carries along. */
+typedef struct rf_read_range {
+  uint64_t file_offset, byte_length, logical_bytes, gap_bytes;
+  uint32_t first, count;
+} rf_read_range;
+/* Where tensor `index` (of the extents given) lands: range `range`, at
+ * offset_in_range bytes into it. */
+typedef struct rf_planned_tensor {
+  uint32_t index, range;
+  uint64_t offset_in_range;
+} rf_planned_tensor;
+typedef struct rf_read_plan_totals {
+  uint64_t logical_tensor_count, logical_bytes, physical_bytes, gap_bytes;
+  uint64_t reusable_group_buffer_bytes; /* 0: none (LayerReadPlan::reusable_group_buffer_bytes) */
+} rf_read_plan_totals;
+/* build_layer_read_plan (layer_read.rs:50-132): tensors sorted by file offset
+ * (ties by index) are merged into one read while the gap to the previous tensor
+ * is at most 4 KiB and the merged span at most 64 MiB.  Overlapping or overflowing
+ * extents are RF_EINVAL; RF_ENOMEM when range_cap is too small.  placed has n
+ * entries, in the reads' order. */
+int rf_layer_read_plan(const rf_tensor_extent* tensors, uint32_t n, rf_read_range* ranges, uint32_t range_cap,
+                       uint32_t* n_ranges, rf_planned_tensor* placed, rf_read_plan_totals* totals);
 
 /* ---- engine lifecycle -------------------------------------------------- */
 /* Empty engine for explicit layer/persistent loads (StreamingLlamaModel::load
@@ -177,6 +214,18 @@ int rf_kv_commit(rf_engine* e);
  * length (else RF_EINVAL, streaming_model.rs:921); final_hidden (n_embd floats,
  * output-normed) may be NULL. */
 int rf_forward_token(rf_engine* e, uint32_t token, uint32_t pos, float* final_hidden);
+/* The prompt-token loop of generate_impl (inference.rs:578-592, one
+ * forward_single_streaming per prompt token) as batched passes: tokens at
+ * positions [KV length, KV length + n_tokens) go through every layer in chunks of
+ * 256 as tensor-core GEMMs (Q4_K and Q8_0 weights dequantized in shared memory,
+ * activations split into bf16 high and low parts, f32 accumulation) with one
+ * attention launch per layer and chunk.  Their K/V are committed, and the last
+ * token's hidden state is left as rf_forward_token leaves it (rf_compute_logits
+ * then gives its logits).  Results match the token-by-token forward within the
+ * GEMM's about 2^-16 relative error per product.  RF_EUNSUPPORTED (nothing
+ * changed) under tensor parallelism, with streamed layers, or when a layer matrix
+ * is not Q4_K/Q8_0; RF_ETIMEOUT when a GEMM's bounded wait gave up. */
+int rf_prefill(rf_engine* e, const uint32_t* tokens, uint32_t n_tokens);
 /* compute_logits (streaming_model.rs:1334-1371) on the last forward's hidden plus the
  * greedy pick (Sampler::sample_checked greedy branch, sampling.rs:45-56: first
  * maximum wins).  logits (vocab floats) and argmax may each be NULL. */

@@ -5,6 +5,8 @@ include/rfcuda.h); this package holds its Python host mirror (engine.py),
 ctypes bindings (_lib.py), the synthetic model generator (synth.py) and the
 build script (build.py).
 """
-from .engine import DecodeEngine, QMatrix, RfError, decode_attention, selftest_wait, tp_unique_id  # noqa: F401
+from .engine import (DecodeEngine, QMatrix, RfError, decode_attention, layer_read_plan,  # noqa: F401
+                     selftest_wait, should_keep_resident, tp_unique_id)
 
-__all__ = ["DecodeEngine", "QMatrix", "RfError", "decode_attention", "selftest_wait", "tp_unique_id"]
+__all__ = ["DecodeEngine", "QMatrix", "RfError", "decode_attention", "layer_read_plan", "selftest_wait",
+           "should_keep_resident", "tp_unique_id"]

@@ -31,12 +31,14 @@ EXPORTS = [
     "rf_last_error", "rf_abi_version", "rf_gguf_read_config", "rf_tp_shard_plan", "rf_engine_create", "rf_engine_create_from_gguf",
     "rf_engine_create_from_file", "rf_engine_destroy", "rf_engine_config", "rf_persistent_load",
     "rf_layer_load", "rf_layer_load_gguf", "rf_layer_release", "rf_layer_is_resident", "rf_layer_compute",
-    "rf_embed", "rf_hidden_write", "rf_hidden_read", "rf_kv_commit", "rf_forward_token", "rf_compute_logits",
+    "rf_embed", "rf_hidden_write", "rf_hidden_read", "rf_kv_commit", "rf_forward_token", "rf_prefill",
+    "rf_compute_logits",
     "rf_decode_step", "rf_generate", "rf_kv_reset", "rf_kv_seq_len", "rf_kv_read", "rf_budget_total",
     "rf_budget_used", "rf_budget_available", "rf_set_residency_plan", "rf_residency_stats_get",
     "rf_step_kernel_count", "rf_selftest_wait", "rf_decode_timed",
     "rf_bench_layer_kernels", "rf_tp_unique_id", "rf_tp_peer_sum", "rf_matrix_create", "rf_matrix_destroy", "rf_matrix_device_bytes",
     "rf_qmatvec", "rf_qgemm", "rf_qgemm_error_word", "rf_decode_attention", "rf_decode_attention_noalloc",
+    "rf_should_keep_resident", "rf_layer_read_plan",
 ]
 
 
@@ -72,10 +74,29 @@ class TpShard(ctypes.Structure):
                                                "ff_offset", "vocab_rows", "vocab_offset")]
 
 
+class TensorExtent(ctypes.Structure):
+    _fields_ = [("file_offset", ctypes.c_uint64), ("byte_length", ctypes.c_uint64)]
+
+
+class ReadRange(ctypes.Structure):
+    _fields_ = [("file_offset", ctypes.c_uint64), ("byte_length", ctypes.c_uint64), ("logical_bytes", ctypes.c_uint64),
+                ("gap_bytes", ctypes.c_uint64), ("first", ctypes.c_uint32), ("count", ctypes.c_uint32)]
+
+
+class PlannedTensor(ctypes.Structure):
+    _fields_ = [("index", ctypes.c_uint32), ("range", ctypes.c_uint32), ("offset_in_range", ctypes.c_uint64)]
+
+
+class ReadPlanTotals(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in ("logical_tensor_count", "logical_bytes", "physical_bytes", "gap_bytes",
+                                               "reusable_group_buffer_bytes")]
+
+
 class ResidencyStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("layer_loads", "layer_releases", "cache_hits", "cache_misses",
                                                "evictions", "peak_bytes", "h2d_bytes", "ring_copies",
-                                               "host_image_bytes")]
+                                               "host_image_bytes", "file_reads", "file_read_bytes",
+                                               "file_gap_bytes")]
 
 
 _lib = None
@@ -111,6 +132,7 @@ def lib():
             "rf_hidden_read": (c_int, [vp, f32p, c_u32]),
             "rf_kv_commit": (c_int, [vp]),
             "rf_forward_token": (c_int, [vp, c_u32, c_u32, f32p]),
+            "rf_prefill": (c_int, [vp, u32p, c_u32]),
             "rf_compute_logits": (c_int, [vp, f32p, u32p]),
             "rf_decode_step": (c_int, [vp, c_u32, u32p]),
             "rf_generate": (c_int, [vp, u32p, c_u32, c_u32, u32p]),
@@ -123,6 +145,9 @@ def lib():
             "rf_set_residency_plan": (c_int, [vp, ctypes.POINTER(ctypes.c_uint8), c_int, c_u64]),
             "rf_residency_stats_get": (c_int, [vp, ctypes.POINTER(ResidencyStats)]),
             "rf_tp_unique_id": (c_int, [ctypes.POINTER(ctypes.c_uint8)]),
+            "rf_should_keep_resident": (c_int, [c_u64, c_u64]),
+            "rf_layer_read_plan": (c_int, [ctypes.POINTER(TensorExtent), c_u32, ctypes.POINTER(ReadRange), c_u32, u32p,
+                                           ctypes.POINTER(PlannedTensor), ctypes.POINTER(ReadPlanTotals)]),
             "rf_tp_peer_sum": (c_int, [vp, ctypes.POINTER(c_int)]),
             "rf_step_kernel_count": (c_int, [vp, u32p]),
             "rf_selftest_wait": (c_int, [c_int, u32p]),

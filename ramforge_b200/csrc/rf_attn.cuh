@@ -249,7 +249,7 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kvh, int split,
   const int t = threadIdx.x % ATT_THREADS;
   const int lane = t & 31, warp = t >> 5;
   const int hd = a.head_dim;
-  const int nhist = a.d_nhist ? __ldcg(a.d_nhist) : a.nhist;
+  const int nhist = (a.d_nhist ? __ldcg(a.d_nhist) : a.nhist) + b * a.nhist_step;
   const bool has_cur = a.k_cur != nullptr;
   const int ctx = nhist + (has_cur ? 1 : 0);
   const int nsplit = attn_nsplit(ctx, a.max_splits);
@@ -271,8 +271,8 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kvh, int split,
   // the current position, when this chunk holds it
   float kcur[DPL], vcur[DPL];
   const bool with_cur = has_cur && nhist >= p0 && nhist < p1;
-  cur_load<DPL>(with_cur ? a.k_cur + (size_t)kvh * hd : nullptr, d0, hd, kcur);
-  cur_load<DPL>(with_cur ? a.v_cur + (size_t)kvh * hd : nullptr, d0, hd, vcur);
+  cur_load<DPL>(with_cur ? a.k_cur + b * a.cur_stride + (size_t)kvh * hd : nullptr, d0, hd, kcur);
+  cur_load<DPL>(with_cur ? a.v_cur + b * a.cur_stride + (size_t)kvh * hd : nullptr, d0, hd, vcur);
   if (t < G) {
     sm[t] = -INFINITY;
     sl[t] = 0.f;

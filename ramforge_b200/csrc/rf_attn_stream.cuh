@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(AttnArgs a, int
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
   // The history length is the step position, written by an earlier step.
-  const int nhist = a.d_nhist ? __ldcg(a.d_nhist) : a.nhist;
+  const int nhist = (a.d_nhist ? __ldcg(a.d_nhist) : a.nhist) + b * a.nhist_step;
   const bool has_cur = a.k_cur != nullptr;
   const int ctx = nhist + (has_cur ? 1 : 0);
   const int nsplit = as_nsplit(ctx, a.max_splits, slots, a.n_kv_heads * a.batch);
@@ -128,8 +128,8 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(AttnArgs a, int
     for (int i = 0; i < DPL; i++) qr[h][i] = __ldcg(qb + (size_t)h * HD + d0 + i);
   const bool with_cur = has_cur && nhist >= p0 && nhist < p1;
   float kcur[DPL], vcur[DPL];
-  cur_load<DPL>(with_cur ? a.k_cur + (size_t)kvh * HD : nullptr, d0, HD, kcur);
-  cur_load<DPL>(with_cur ? a.v_cur + (size_t)kvh * HD : nullptr, d0, HD, vcur);
+  cur_load<DPL>(with_cur ? a.k_cur + b * a.cur_stride + (size_t)kvh * HD : nullptr, d0, HD, kcur);
+  cur_load<DPL>(with_cur ? a.v_cur + b * a.cur_stride + (size_t)kvh * HD : nullptr, d0, HD, vcur);
   const float div = sqrtf((float)HD);  // score = dot / sqrt(hd)  (compute.rs:530)
 
   float m_run = -INFINITY, l_run = 0.f;  // softmax state of head lane % G

@@ -356,3 +356,77 @@ int expand_rows_f32(int type, const uint8_t* src, uint64_t src_row_bytes, uint64
 }
 
 }  // namespace rf
+
+namespace rf {
+
+// Tensors sorted by (file offset, index); each joins the current read when the
+// gap to it is at most kMaxCoalescedGap and the grown span at most
+// kMaxCoalescedSpan, else it starts a new read (layer_read.rs:50-132).
+int build_read_plan(const rf_tensor_extent* t, uint32_t n, ReadPlan* out) {
+  *out = ReadPlan{};
+  std::vector<uint32_t> order(n);
+  uint64_t logical = 0;
+  for (uint32_t i = 0; i < n; i++) {
+    order[i] = i;
+    if (t[i].file_offset + t[i].byte_length < t[i].file_offset)
+      return set_error(RF_EINVAL, "tensor %u file range overflows", i);
+    if (logical + t[i].byte_length < logical) return set_error(RF_EINVAL, "layer logical byte count overflows");
+    logical += t[i].byte_length;
+  }
+  std::sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) {
+    return t[a].file_offset != t[b].file_offset ? t[a].file_offset < t[b].file_offset : a < b;
+  });
+  for (uint32_t idx : order) {
+    const uint64_t start = t[idx].file_offset, end = start + t[idx].byte_length;
+    if (!out->ranges.empty()) {
+      rf_read_range& cur = out->ranges.back();
+      const uint64_t cur_end = cur.file_offset + cur.byte_length;
+      if (start < cur_end) return set_error(RF_EINVAL, "tensor ranges overlap at index %u", idx);
+      const uint64_t gap = start - cur_end, span = end - cur.file_offset;
+      if (gap <= kMaxCoalescedGap && span <= kMaxCoalescedSpan) {
+        out->placed.push_back({idx, (uint32_t)(out->ranges.size() - 1), start - cur.file_offset});
+        cur.byte_length = span;
+        cur.logical_bytes += t[idx].byte_length;
+        cur.gap_bytes += gap;
+        cur.count++;
+        continue;
+      }
+    }
+    out->ranges.push_back({start, t[idx].byte_length, t[idx].byte_length, 0, (uint32_t)out->placed.size(), 1});
+    out->placed.push_back({idx, (uint32_t)(out->ranges.size() - 1), 0});
+  }
+  rf_read_plan_totals& tot = out->totals;
+  tot.logical_tensor_count = n;
+  tot.logical_bytes = logical;
+  bool grouped = out->ranges.size() > 1;
+  uint64_t max_span = 0;
+  for (const rf_read_range& r : out->ranges) {
+    tot.physical_bytes += r.byte_length;
+    tot.gap_bytes += r.gap_bytes;
+    grouped = grouped && r.count > 1;
+    max_span = std::max(max_span, r.byte_length);
+  }
+  tot.reusable_group_buffer_bytes = grouped ? max_span : 0;
+  return RF_OK;
+}
+
+}  // namespace rf
+
+extern "C" int rf_should_keep_resident(uint64_t resident_bytes, uint64_t budget_total) {
+  return resident_bytes <= budget_total / 4 ? 1 : 0;
+}
+
+extern "C" int rf_layer_read_plan(const rf_tensor_extent* tensors, uint32_t n, rf_read_range* ranges,
+                                  uint32_t range_cap, uint32_t* n_ranges, rf_planned_tensor* placed,
+                                  rf_read_plan_totals* totals) {
+  if ((n && !tensors) || !n_ranges) return rf::set_error(RF_EINVAL, "null argument");
+  rf::ReadPlan plan;
+  RF_TRY(rf::build_read_plan(tensors, n, &plan));
+  *n_ranges = (uint32_t)plan.ranges.size();
+  if (plan.ranges.size() > range_cap || (plan.ranges.size() && !ranges))
+    return rf::set_error(RF_ENOMEM, "the plan has %zu reads, room for %u", plan.ranges.size(), range_cap);
+  std::copy(plan.ranges.begin(), plan.ranges.end(), ranges);
+  if (placed) std::copy(plan.placed.begin(), plan.placed.end(), placed);
+  if (totals) *totals = plan.totals;
+  return RF_OK;
+}

@@ -83,6 +83,16 @@ int parse_gguf(const uint8_t* p, uint64_t len, Gguf* out);
 // LlamaConfig::from_gguf (runtime/src/model.rs:40-161)
 int llama_config_from_gguf(const Gguf& g, rf_model_config* cfg);
 
+// ---- coalesced layer reads (runtime/src/layer_read.rs:6-132) -------------------
+constexpr uint64_t kMaxCoalescedGap = 4 * 1024;           // MAX_COALESCED_GAP_BYTES
+constexpr uint64_t kMaxCoalescedSpan = 64ull * 1024 * 1024;  // MAX_COALESCED_SPAN_BYTES
+struct ReadPlan {
+  std::vector<rf_read_range> ranges;
+  std::vector<rf_planned_tensor> placed;
+  rf_read_plan_totals totals{};
+};
+int build_read_plan(const rf_tensor_extent* t, uint32_t n, ReadPlan* out);
+
 // ---- host packing: GGUF rows -> PackedMat byte streams --------------------
 struct HostPacked {
   PackedMat geo;  // geometry (pointers unused)

@@ -9,6 +9,7 @@
 // LM head with argmax and the token/position advance - is one CUDA graph that
 // is replayed unchanged for every token.
 #include <dlfcn.h>
+#include <errno.h>
 #include <fcntl.h>
 #include <math.h>
 #include <nccl.h>
@@ -73,6 +74,10 @@ const char* kRoleNames[9] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_ou
 // Q/K/V biases (roles 9-11, StreamingLayerWeights::attn_{q,k,v}_bias,
 // model_executor.rs:33-48).
 constexpr int kLayerViews = 12;
+// Prompt tokens one batched pass handles (two 128-token column blocks of the
+// tensor-core GEMM), and the context splits of its attention.
+constexpr uint32_t kPrefillChunk = 256;
+constexpr int kPrefillSplits = 4;
 const char* kBiasNames[3] = {"attn_q", "attn_k", "attn_v"};
 
 struct Layer {
@@ -126,6 +131,10 @@ struct rf_engine {
   uint64_t src_len = 0;
   void* map_addr = nullptr;
   uint64_t map_len = 0;
+  int src_fd = -1;  // the GGUF file, when the engine was created from a path: streamed layers are read from it
+  bool created = false;  // creation (and its initial layer loads) finished
+  uint8_t* read_stage = nullptr;  // pinned staging of a streamed layer's coalesced reads (reused)
+  uint64_t read_stage_bytes = 0;
   // persistent weights
   PackedMat embd{}, out{};
   bool tied = false, have_embd = false, have_out = false, have_onorm = false;
@@ -169,6 +178,14 @@ struct rf_engine {
   bool ps_ok = false;
   void* ps_area = nullptr;
   std::vector<void*> ps_peer;  // peer areas mapped through cudaIpc
+  // batched prompt (rf_prefill): buffers of one chunk of kPrefillChunk tokens,
+  // allocated on the first call and charged as "scratch:prefill"
+  void* pf_block = nullptr;
+  float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_att = nullptr, *pf_act = nullptr,
+        *pf_part = nullptr;
+  unsigned *pf_cnt = nullptr, *pf_err = nullptr;
+  uint32_t* pf_tok = nullptr;
+  void* pf_xt = nullptr;
   rf_residency_stats stats{};
 };
 
@@ -795,10 +812,15 @@ int gguf_layer_views(rf_engine* e, int l, View* v /*[kLayerViews]*/) {
   return RF_OK;
 }
 
+int read_layer_views(rf_engine* e, int l, View* v);
+
 int load_layer_gguf(rf_engine* e, int l) {
   if (!e->src) return set_error(RF_ESTATE, "engine has no GGUF source");
   View v[kLayerViews];
   RF_TRY(gguf_layer_views(e, l, v));
+  // engines created from a path read a loaded layer through its coalesced read
+  // plan; the first load of every layer at creation uses the mapped file
+  if (e->src_fd >= 0 && e->created) RF_TRY(read_layer_views(e, l, v));
   return load_layer_views(e, l, v);
 }
 
@@ -941,6 +963,109 @@ int ensure_ready(rf_engine* e) {
   return RF_OK;
 }
 
+// ---- batched prompt (rf_prefill) ----------------------------------------------------
+// A prompt chunk of T tokens goes through each layer as four tensor-core GEMMs
+// (rf_prefill.cu) with the decode step's epilogues, and one attention launch whose
+// sequence b is token b over the cache positions before it plus its own K/V.  The
+// results equal the token-by-token forward (inference.rs:578-592) up to the
+// GEMM's split-bf16 products (about 2^-16 relative per product).
+
+// Why the engine cannot prefill in batches (RF_OK when it can).
+int prefill_check(rf_engine* e) {
+  if (e->tp > 1) return set_error(RF_EUNSUPPORTED, "batched prefill runs on one GPU (tp_size %d)", e->tp);
+  if (!all_resident(e)) return set_error(RF_EUNSUPPORTED, "batched prefill needs every layer resident");
+  for (size_t l = 0; l < e->layers.size(); l++) {
+    const Layer& L = e->layers[l];
+    const PackedMat* ms[5] = {&L.qkv, &L.wo, &L.gateup, &L.down, &L.vmat};
+    for (int i = 0; i < 5; i++) {
+      if (i == 4 && !ms[i]->M) continue;
+      if (!prefill_supported(ms[i]->type))
+        return set_error(RF_EUNSUPPORTED, "layer %zu holds a matrix of type %d; batched prefill covers Q4_K and Q8_0",
+                         l, ms[i]->type);
+    }
+  }
+  return RF_OK;
+}
+
+int ensure_prefill_buffers(rf_engine* e) {
+  if (e->pf_block) return RF_OK;
+  const rf_model_config& c = e->cfg;
+  const uint64_t T = kPrefillChunk, G = c.n_heads / c.n_kv_heads;
+  uint32_t kp = 0;
+  for (const Layer& L : e->layers)
+    for (const PackedMat* m : {&L.qkv, &L.wo, &L.gateup, &L.down, &L.vmat}) kp = std::max(kp, m->Kp);
+  struct Item { void** p; uint64_t bytes; };
+  std::vector<Item> items = {
+      {(void**)&e->pf_x, 4 * T * c.n_embd},          {(void**)&e->pf_q, 4 * T * e->q_local},
+      {(void**)&e->pf_k, 4 * T * e->kv_local},       {(void**)&e->pf_v, 4 * T * e->kv_local},
+      {(void**)&e->pf_att, 4 * T * e->q_local},      {(void**)&e->pf_act, 4 * T * e->ff_local},
+      {(void**)&e->pf_part, 4 * attn_part_floats((int)T, (int)e->kvh_local, kPrefillSplits, (int)G, (int)c.head_dim)},
+      {(void**)&e->pf_cnt, 4 * T * e->kvh_local},    {(void**)&e->pf_err, 4},
+      {(void**)&e->pf_tok, 4 * T},                   {(void**)&e->pf_xt, prefill_xt_bytes((uint32_t)T, kp)}};
+  uint64_t total = 0;
+  for (auto& it : items) total += align256(it.bytes);
+  RF_TRY(dev_alloc(e, "scratch:prefill", total, &e->pf_block));
+  RF_CUDA(cudaMemsetAsync(e->pf_block, 0, total, e->stream));  // attention counters start at zero
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  uint64_t off = 0;
+  for (auto& it : items) {
+    *it.p = (uint8_t*)e->pf_block + off;
+    off += align256(it.bytes);
+  }
+  return RF_OK;
+}
+
+// Tokens at positions [pos0, pos0 + T) (already in pf_tok) through every layer;
+// their K/V go into the cache, the hidden states stay in pf_x.
+int enqueue_prefill_chunk(rf_engine* e, uint32_t T, uint32_t pos0) {
+  const rf_model_config& c = e->cfg;
+  const Launch La{e->stream, false};
+  const uint32_t d = c.n_embd;
+  RF_CUDA(launch_embed_rows(La, e->embd, e->pf_tok, T, e->pf_x));
+  for (uint32_t l = 0; l < c.n_layers; l++) {
+    Layer& L = e->layers[l];
+    // RMSNorm(attn_norm) -> [Q;K;V] -> bias, RoPE, K/V append (model_executor.rs:147-196)
+    RF_CUDA(prefill_split(La, e->pf_x, d, T, d, L.qkv.Kp, L.attn_norm, c.rms_eps, e->pf_xt));
+    RopeQKVArgs ra = rope_args(e, (int)l);
+    ra.q_out = e->pf_q;
+    ra.k_cur = e->pf_k;
+    ra.v_cur = e->pf_v;
+    RF_CUDA(prefill_gemm_rope(La, L.qkv, e->pf_xt, T, e->pf_err, ra, pos0, e->q_local, e->kv_local));
+    if (L.vmat.M) {  // V of its own type: the same epilogue from the V rows on
+      if (L.vmat.Kp != L.qkv.Kp)
+        RF_CUDA(prefill_split(La, e->pf_x, d, T, d, L.vmat.Kp, L.attn_norm, c.rms_eps, e->pf_xt));
+      ra.row_base = e->q_local + e->kv_local;
+      RF_CUDA(prefill_gemm_rope(La, L.vmat, e->pf_xt, T, e->pf_err, ra, pos0, e->q_local, e->kv_local));
+    }
+    // attention: token b over cache positions [0, pos0 + b) and its own K/V
+    AttnArgs aa = attn_args(e, (int)l);
+    aa.q = e->pf_q;
+    aa.k_cur = e->pf_k;
+    aa.v_cur = e->pf_v;
+    aa.cur_stride = e->kv_local;
+    aa.d_nhist = nullptr;
+    aa.nhist = (int)pos0;
+    aa.nhist_step = 1;
+    aa.batch = (int)T;
+    aa.batch_stride = 0;
+    aa.max_splits = kPrefillSplits;
+    aa.part = e->pf_part;
+    aa.counters = e->pf_cnt;
+    aa.out = e->pf_att;
+    RF_CUDA(launch_attention(La, aa));
+    // W_o + residual
+    RF_CUDA(prefill_split(La, e->pf_att, e->q_local, T, e->q_local, L.wo.Kp, nullptr, 0.f, e->pf_xt));
+    RF_CUDA(prefill_gemm_residual(La, L.wo, e->pf_xt, T, e->pf_err, e->pf_x, d));
+    // RMSNorm(ffn_norm) -> [gate;up] -> SwiGLU
+    RF_CUDA(prefill_split(La, e->pf_x, d, T, d, L.gateup.Kp, L.ffn_norm, c.rms_eps, e->pf_xt));
+    RF_CUDA(prefill_gemm_swiglu(La, L.gateup, e->pf_xt, T, e->pf_err, e->pf_act, e->ff_local));
+    // W_down + residual
+    RF_CUDA(prefill_split(La, e->pf_act, e->ff_local, T, e->ff_local, L.down.Kp, nullptr, 0.f, e->pf_xt));
+    RF_CUDA(prefill_gemm_residual(La, L.down, e->pf_xt, T, e->pf_err, e->pf_x, d));
+  }
+  return RF_OK;
+}
+
 // Make every layer resident, loading from the GGUF source where needed.
 // Layers the residency plan marks non-resident are loaded for the step and
 // released afterwards (load -> compute -> release, streaming_model.rs:1081-1270).
@@ -979,12 +1104,59 @@ int run_stepwise(rf_engine* e, bool decode) {
 // issued as soon as a layer's kernels are queued, so transfers overlap the
 // compute of the layers in between.  The slots are charged to the byte budget
 // ("ring:slot:<i>"), the pinned images are host memory and are not.
+// A streamed layer's tensors read from the GGUF file (GgufDataSource::
+// read_coalesced_tensor_range_into, datasource.rs:411, over build_layer_read_plan,
+// layer_read.rs:50): the plan's coalesced ranges are pread into one reused pinned
+// staging buffer and the views are pointed into it.
+int read_layer_views(rf_engine* e, int l, View* v /*[kLayerViews], from gguf_layer_views*/) {
+  std::vector<rf_tensor_extent> ext;
+  std::vector<int> role;
+  for (int j = 0; j < kLayerViews; j++)
+    if (v[j].host) {
+      ext.push_back({(uint64_t)(v[j].host - e->src), v[j].bytes});
+      role.push_back(j);
+    }
+  ReadPlan plan;
+  RF_TRY(build_read_plan(ext.data(), (uint32_t)ext.size(), &plan));
+  const uint64_t need = plan.totals.physical_bytes;
+  if (need > e->read_stage_bytes) {
+    if (e->read_stage) cudaFreeHost(e->read_stage);
+    e->read_stage = nullptr;
+    e->read_stage_bytes = 0;
+    RF_CUDA(cudaHostAlloc((void**)&e->read_stage, need, cudaHostAllocDefault));
+    e->read_stage_bytes = need;
+  }
+  std::vector<uint64_t> base(plan.ranges.size());
+  uint64_t off = 0;
+  for (size_t r = 0; r < plan.ranges.size(); r++) {
+    const rf_read_range& rr = plan.ranges[r];
+    base[r] = off;
+    uint64_t done = 0;
+    while (done < rr.byte_length) {
+      const ssize_t got = pread(e->src_fd, e->read_stage + off + done, (size_t)(rr.byte_length - done),
+                                (off_t)(rr.file_offset + done));
+      if (got < 0 && errno == EINTR) continue;
+      if (got <= 0)
+        return set_error(RF_EFORMAT, "reading layer %d: %llu bytes at file offset %llu failed", l,
+                         (unsigned long long)rr.byte_length, (unsigned long long)rr.file_offset);
+      done += (uint64_t)got;
+    }
+    off += rr.byte_length;
+  }
+  for (const rf_planned_tensor& p : plan.placed) v[role[p.index]].host = e->read_stage + base[p.range] + p.offset_in_range;
+  e->stats.file_reads += plan.ranges.size();
+  e->stats.file_read_bytes += plan.totals.physical_bytes;
+  e->stats.file_gap_bytes += plan.totals.gap_bytes;
+  return RF_OK;
+}
+
 int ensure_stream_image(rf_engine* e, int l) {
   StreamImage& si = e->simg[l];
   if (si.host) return RF_OK;
   if (!e->src) return set_error(RF_ESTATE, "layer %d is not resident and the engine has no GGUF source", l);
   View v[kLayerViews];
   RF_TRY(gguf_layer_views(e, l, v));
+  if (e->src_fd >= 0) RF_TRY(read_layer_views(e, l, v));
   LayerImage img;
   RF_TRY(build_layer_image(e, l, v, &img));
   RF_CUDA(cudaHostAlloc((void**)&si.host, img.tmpl.bytes, cudaHostAllocDefault));
@@ -1219,6 +1391,7 @@ void destroy(rf_engine* e) {
   if (e->out_norm) cudaFree(e->out_norm);
   if (e->kv_block) cudaFree(e->kv_block);
   if (e->scratch) cudaFree(e->scratch);
+  if (e->pf_block) cudaFree(e->pf_block);
   if (e->copy_stream) cudaStreamSynchronize(e->copy_stream);
   for (auto p : e->ring)
     if (p) cudaFree(p);
@@ -1237,6 +1410,8 @@ void destroy(rf_engine* e) {
   if (e->comm && nccl()) nccl()->commDestroy(e->comm);
   if (e->stream) cudaStreamDestroy(e->stream);
   if (e->map_addr) munmap(e->map_addr, e->map_len);
+  if (e->src_fd >= 0) close(e->src_fd);
+  if (e->read_stage) cudaFreeHost(e->read_stage);
   delete e;
 }
 
@@ -1340,13 +1515,17 @@ int rf_engine_create_from_file(const char* path, const rf_runtime_config* rt, rf
   struct stat st;
   if (fstat(fd, &st) != 0 || st.st_size <= 0) { close(fd); return set_error(RF_EFORMAT, "cannot stat '%s'", path); }
   void* m = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
-  close(fd);
-  if (m == MAP_FAILED) return set_error(RF_EFORMAT, "cannot map '%s'", path);
+  if (m == MAP_FAILED) {
+    close(fd);
+    return set_error(RF_EFORMAT, "cannot map '%s'", path);
+  }
   rf_engine* e = new rf_engine();
   e->map_addr = m;
   e->map_len = (uint64_t)st.st_size;
+  e->src_fd = fd;
   int rc = create_from_image((const uint8_t*)m, (uint64_t)st.st_size, rt, e);
   if (rc) { destroy(e); return rc; }
+  e->created = true;
   *out = e;
   return RF_OK;
 }
@@ -1467,6 +1646,43 @@ int rf_forward_token(rf_engine* e, uint32_t token, uint32_t pos, float* final_hi
     RF_CUDA(cudaMemcpyAsync(final_hidden, e->final_hidden, 4ull * e->cfg.n_embd, cudaMemcpyDeviceToHost, e->stream));
   }
   RF_CUDA(cudaStreamSynchronize(e->stream));
+  return check_async_errors(e);
+}
+
+int rf_prefill(rf_engine* e, const uint32_t* tokens, uint32_t n_tokens) {
+  ENGINE_GUARD(e);
+  if (!tokens || n_tokens == 0) return set_error(RF_EINVAL, "empty prompt");
+  if ((uint64_t)e->seq_len + n_tokens > e->max_seq)
+    return set_error(RF_ESTATE, "prompt of %u tokens at position %u exceeds the KV capacity %u", n_tokens, e->seq_len,
+                     e->max_seq);
+  for (uint32_t i = 0; i < n_tokens; i++)
+    if (tokens[i] >= e->cfg.vocab_size) return set_error(RF_EINVAL, "token_id %u out of bounds", tokens[i]);
+  RF_TRY(ensure_ready(e));
+  RF_TRY(prefill_check(e));
+  RF_TRY(ensure_prefill_buffers(e));
+  const uint32_t d = e->cfg.n_embd;
+  uint32_t last = 0;
+  for (uint32_t c0 = 0; c0 < n_tokens; c0 += kPrefillChunk) {
+    const uint32_t T = std::min(kPrefillChunk, n_tokens - c0);
+    RF_CUDA(h2d_sync(e, e->pf_tok, tokens + c0, 4ull * T));
+    RF_TRY(enqueue_prefill_chunk(e, T, e->seq_len));
+    e->seq_len += T;
+    last = T - 1;
+  }
+  // the last token's state, as rf_forward_token leaves it: hidden and the
+  // output-normed final_hidden that rf_compute_logits reads
+  const Launch La{e->stream, false};
+  RF_CUDA(cudaMemcpyAsync(e->hidden, e->pf_x + (size_t)last * d, 4ull * d, cudaMemcpyDeviceToDevice, e->stream));
+  RF_CUDA(launch_rmsnorm(La, e->pf_x + (size_t)last * d, e->out_norm, e->cfg.rms_eps, d, e->final_hidden));
+  // the GEMMs' bounded waits report through pf_err (bit 0)
+  RF_CUDA(cudaMemcpyAsync(&e->h_err[1], e->pf_err, 4, cudaMemcpyDeviceToHost, e->stream));
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  const unsigned err = e->h_err[1];
+  if (err) {
+    RF_CUDA(cudaMemsetAsync(e->pf_err, 0, 4, e->stream));
+    RF_CUDA(cudaStreamSynchronize(e->stream));
+    return set_error(RF_ETIMEOUT, "a tensor-core GEMM of the batched prefill gave up waiting (error word 0x%x)", err);
+  }
   return check_async_errors(e);
 }
 

@@ -182,6 +182,16 @@ cudaError_t launch_embed(const Launch& L, const PackedMat& E, const uint32_t* d_
   return launch_k(L, embed_kernel, dim3(1), dim3(512), 0, E, d_token, hidden, key);
 }
 
+__global__ void embed_rows_kernel(PackedMat E, const uint32_t* __restrict__ tokens, float* __restrict__ x) {
+  const uint32_t tok = min(tokens[blockIdx.x], E.M - 1);
+  float* row = x + (size_t)blockIdx.x * E.K;
+  for (uint32_t e = threadIdx.x; e < E.K; e += blockDim.x) row[e] = dequant_elem(E, tok, e);
+}
+cudaError_t launch_embed_rows(const Launch& L, const PackedMat& E, const uint32_t* tokens, uint32_t T, float* x) {
+  if (T == 0) return cudaSuccess;
+  return launch_k(L, embed_rows_kernel, dim3(T), dim3(256), 0, E, tokens, x);
+}
+
 __global__ void dequant_rows_kernel(PackedMat W, uint32_t r0, uint32_t n, float* out) {
   const uint64_t total = (uint64_t)n * W.K;
   for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x)
@@ -317,7 +327,8 @@ cudaError_t launch_attention(const Launch& L, const AttnArgs& a) {
   // measured faster (ctx ~530: 418 vs 411 tokens/s), while at 32768 positions the
   // streaming kernel takes half the time.  The engine's hint is its KV capacity
   // (the graph serves every context up to it); a standalone call's is its context.
-  const int ctx_hint = a.d_nhist ? a.max_ctx : a.nhist + (a.k_cur ? 1 : 0);
+  const int ctx_hint =
+      a.d_nhist ? a.max_ctx : a.nhist + (a.batch - 1) * a.nhist_step + (a.k_cur ? 1 : 0);
   if (ctx_hint >= kAttnStreamMinCtx && !a.kv_f32 && aligned && (G == 1 || G == 2 || G == 4 || G == 8)) {
     if (a.head_dim == 128) return attn_stream_g<128>(L, a, G);
     if (a.head_dim == 64) return attn_stream_g<64>(L, a, G);

@@ -378,6 +378,20 @@ cudaError_t prefill_split(const Launch& L, const float* X, uint32_t ldx, uint32_
 // bit 0 when a bounded wait gave up.
 cudaError_t prefill_gemm_store(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
                                float* y, uint32_t ldy);
+// The same GEMM with the decode step's epilogues, for a prompt chunk of T tokens:
+//  rope: Q/K/V rows (packed order, a.row_base as in the step) of token t at
+//        position pos0 + t: bias, RoPE, K/V into the cache; Q, K, V rows into
+//        a.q_out / a.k_cur / a.v_cur + t * (q_stride or kv_stride);
+//  residual: x[t][row] += (W . x_t)[row];
+//  swiglu: act[t][j] = silu(gate_j) * up_j over the interleaved gate/up rows.
+cudaError_t prefill_gemm_rope(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
+                              const RopeQKVArgs& a, uint32_t pos0, uint32_t q_stride, uint32_t kv_stride);
+cudaError_t prefill_gemm_residual(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
+                                  float* x, uint32_t ldx);
+cudaError_t prefill_gemm_swiglu(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
+                                float* act, uint32_t ld);
+// x[t] <- the dequantized embedding row of tokens[t] (device array), t < T.
+cudaError_t launch_embed_rows(const Launch& L, const PackedMat& E, const uint32_t* tokens, uint32_t T, float* x);
 
 // ---- tensor-parallel sum over NVLink peer memory ------------------------------
 // The sum of the ranks' partial vectors after a row-parallel projection, as one
@@ -425,6 +439,10 @@ struct AttnArgs {
   int kv_f32;
   unsigned* err;           // bit 1 set when a bounded wait gave up (may be NULL)
   int max_ctx;             // with d_nhist: the longest context the launch may serve (kernel choice)
+  // Prompt chunks: sequence b's history is nhist + b * nhist_step positions of one
+  // shared cache (batch_stride 0) and its current K/V row is k_cur/v_cur + b * cur_stride.
+  int nhist_step;
+  uint64_t cur_stride;
 };
 // Contexts from which launch_attention streams the history through shared memory.
 constexpr int kAttnStreamMinCtx = 1024;

@@ -26,6 +26,7 @@
 #include <cuda_bf16.h>
 
 #include "rf_attn.cuh"
+#include "rf_gemv.cuh"
 #include "rf_tc.cuh"
 
 namespace rf {
@@ -280,6 +281,47 @@ struct PgEpiStore {  // y[t][row]
   __device__ void operator()(uint32_t row, uint32_t t, float v, float) const { y[(size_t)t * ldy + row] = v; }
 };
 
+// Q/K/V of token t at position pos0 + t (the decode step's rope_store, so the
+// same bias, rotation and f16 rounding): the even row of a Q/K pair rotates both
+// values (its partner's arrives as vp), V rows are stored one by one; Q and the
+// step's K/V rows go to [t][rows] buffers, K/V also into the cache.
+struct PgEpiRope {
+  RopeQKVArgs a;       // q_out/k_cur/v_cur: token 0's rows
+  uint32_t pos0;
+  uint32_t q_stride, kv_stride;  // floats per token of q_out and of k_cur/v_cur
+  __device__ void operator()(uint32_t row, uint32_t t, float v, float vp) const {
+    RopeQKVArgs b = a;
+    b.q_out = a.q_out + (size_t)t * q_stride;
+    b.k_cur = a.k_cur + (size_t)t * kv_stride;
+    b.v_cur = a.v_cur + (size_t)t * kv_stride;
+    const uint32_t p = row + a.row_base;
+    if (p < a.q_rows + a.kv_rows) {
+      if (row & 1) return;
+      const float v2[2] = {v, vp};
+      rope_store(b, (int)row, v2, 2, nullptr, (int)(pos0 + t));
+    } else {
+      rope_store(b, (int)row, &v, 1, nullptr, (int)(pos0 + t));
+    }
+  }
+};
+// x[t][row] += v: the residual add after W_o and W_down (model_executor.rs:213-215, 231-233).
+struct PgEpiResidual {
+  float* x;
+  uint32_t ldx;
+  __device__ void operator()(uint32_t row, uint32_t t, float v, float) const { x[(size_t)t * ldx + row] += v; }
+};
+// Rows (2j, 2j+1) = (gate_j, up_j): act[t][j] = silu(g) * u, silu(g) = g / (1 + exp(-g))
+// (compute.rs:337-350), the decode step's EpiSwiGLU arithmetic.
+struct PgEpiSwiGLU {
+  float* act;
+  uint32_t ld;
+  __device__ void operator()(uint32_t row, uint32_t t, float v, float vp) const {
+    if (row & 1) return;
+    const float s = v / (1.0f + expf(-v));
+    act[(size_t)t * ld + (row >> 1)] = __fmul_rn(s, vp);
+  }
+};
+
 size_t prefill_xt_bytes(uint32_t T, uint32_t Kp) {
   return (size_t)((T + PG_N - 1) / PG_N) * (Kp / PG_KS) * 2 * PG_B_BYTES;
 }
@@ -312,6 +354,18 @@ static cudaError_t run_prefill_gemm(const Launch& L, const PackedMat& W, const v
 cudaError_t prefill_gemm_store(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
                                float* y, uint32_t ldy) {
   return run_prefill_gemm(L, W, Xt, T, err, PgEpiStore{y, ldy});
+}
+cudaError_t prefill_gemm_rope(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
+                              const RopeQKVArgs& a, uint32_t pos0, uint32_t q_stride, uint32_t kv_stride) {
+  return run_prefill_gemm(L, W, Xt, T, err, PgEpiRope{a, pos0, q_stride, kv_stride});
+}
+cudaError_t prefill_gemm_residual(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
+                                  float* x, uint32_t ldx) {
+  return run_prefill_gemm(L, W, Xt, T, err, PgEpiResidual{x, ldx});
+}
+cudaError_t prefill_gemm_swiglu(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
+                                float* act, uint32_t ld) {
+  return run_prefill_gemm(L, W, Xt, T, err, PgEpiSwiGLU{act, ld});
 }
 
 }  // namespace rf

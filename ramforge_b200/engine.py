@@ -32,6 +32,32 @@ def tp_unique_id() -> bytes:
     return bytes(buf)
 
 
+def should_keep_resident(resident_bytes: int, budget_total: int) -> bool:
+    """should_keep_resident (persistent.rs:468): resident when at most a quarter of the budget."""
+    return bool(lib().rf_should_keep_resident(resident_bytes, budget_total))
+
+
+def layer_read_plan(extents):
+    """build_layer_read_plan (layer_read.rs:50) over [(file_offset, byte_length), ...]:
+    returns (ranges, placements, totals) as dicts; ranges hold file_offset,
+    byte_length, logical_bytes, gap_bytes and the plan indices of their tensors."""
+    from ._lib import PlannedTensor, ReadPlanTotals, ReadRange, TensorExtent
+    n = len(extents)
+    ext = (TensorExtent * max(1, n))(*[TensorExtent(o, b) for o, b in extents])
+    cap = max(1, n)
+    ranges = (ReadRange * cap)()
+    placed = (PlannedTensor * cap)()
+    tot = ReadPlanTotals()
+    nr = ctypes.c_uint32()
+    check(lib().rf_layer_read_plan(ext, n, ranges, cap, ctypes.byref(nr), placed, ctypes.byref(tot)))
+    rs = [{"file_offset": r.file_offset, "byte_length": r.byte_length, "logical_bytes": r.logical_bytes,
+           "gap_bytes": r.gap_bytes, "tensors": [placed[r.first + i].index for i in range(r.count)]}
+          for r in ranges[:nr.value]]
+    pl = [{"index": p.index, "range": p.range, "offset_in_range": p.offset_in_range} for p in placed[:n]]
+    totals = {f: getattr(tot, f) for f, _ in tot._fields_}
+    return rs, pl, totals
+
+
 class DecodeEngine:
     """One GPU (one tensor-parallel rank) running the legacy decoder.
 
@@ -143,8 +169,21 @@ class DecodeEngine:
         check(lib().rf_decode_step(self._h, token, ctypes.byref(nxt)))
         return nxt.value
 
-    def generate(self, prompt: Sequence[int], n_new: int) -> np.ndarray:
+    def prefill(self, tokens: Sequence[int]):
+        """The prompt tokens at positions [kv_seq_len, kv_seq_len + n) as batched
+        tensor-core passes (rf_prefill); afterwards compute_logits() gives the last
+        token's logits, as after forward_single_streaming of each token in turn."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        check(lib().rf_prefill(self._h, t.ctypes.data_as(_u32p), t.size))
+
+    def generate(self, prompt: Sequence[int], n_new: int, batched_prefill: bool = False) -> np.ndarray:
+        """Greedy generation (rf_generate).  With batched_prefill, every prompt token
+        but the last goes through rf_prefill first, then the last one starts the
+        decode loop."""
         p = np.ascontiguousarray(prompt, np.uint32)
+        if batched_prefill and p.size > 1:
+            self.prefill(p[:-1])
+            p = p[-1:]
         out = np.zeros(max(1, n_new), np.uint32)
         check(lib().rf_generate(self._h, p.ctypes.data_as(_u32p), p.size, n_new, out.ctypes.data_as(_u32p)))
         return out[:n_new]

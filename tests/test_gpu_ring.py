@@ -81,3 +81,26 @@ def test_ring_plan_over_budget_fails_cleanly(gguf):
     h = eng.forward_single_streaming(7, 0)
     assert np.isfinite(h).all()
     eng.close()
+
+
+@pytest.mark.parametrize("slots", [2, 0])
+def test_file_engine_reads_streamed_layers_through_coalesced_ranges(gguf, tmp_path, slots):
+    """An engine created from a path reads each streamed layer's tensors with the
+    coalesced read plan (layer_read.rs:50) into pinned staging: through the ring
+    (slots 2: once, into the layer's pinned image) or load -> compute -> release
+    (slots 0: every step).  Steps stay bit-identical to an all-resident engine."""
+    path = tmp_path / "ring.gguf"
+    path.write_bytes(np.asarray(gguf).tobytes())
+    a = DecodeEngine(gguf, max_seq_len=32)
+    b = DecodeEngine(str(path), max_seq_len=32)
+    mask = [True, False, True, False, False, True]
+    b.set_residency_plan(mask, ring_slots=slots)
+    steps = [5, 77, 301]
+    for pos, tok in enumerate(steps):
+        assert np.array_equal(a.forward_single_streaming(tok, pos), b.forward_single_streaming(tok, pos)), pos
+    st = b.residency_stats()
+    reads_per_pass = 3 if slots else 3 * len(steps)
+    assert st["file_reads"] >= reads_per_pass  # at least one read per streamed layer and pass
+    assert st["file_read_bytes"] > 0 and st["file_gap_bytes"] < st["file_read_bytes"] // 100
+    a.close()
+    b.close()
