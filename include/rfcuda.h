@@ -113,6 +113,10 @@ typedef struct rf_residency_stats {
   /* engines created from a file: coalesced reads of streamed layers' tensors
    * (layer_read.rs:50 plans), the bytes they read and the gap bytes among them */
   uint64_t file_reads, file_read_bytes, file_gap_bytes;
+  /* persistent tensors (token_embd, output) that should_keep_resident (persistent.rs:468)
+   * kept out of device memory under an explicit VRAM budget: held in mapped pinned host
+   * memory and read by the kernels over the host link */
+  uint64_t host_mapped_bytes;
 } rf_residency_stats;
 
 /* One rank's slice of a tensor-parallel engine: Q/K/V and gate/up are split by
@@ -282,6 +286,22 @@ int rf_budget_available(const rf_engine* e, uint64_t* out);
  * release in turn (load_layer/release_layer, streaming_model.rs:1081-1270). */
 int rf_set_residency_plan(rf_engine* e, const uint8_t* resident_mask, int ring_slots,
                           uint64_t vram_weight_budget_bytes);
+/* The planner's choice for a weight budget (a MemoryBudget mapped onto a resident
+ * set, the role of the reference's plan/StagingPlan, staging_plan.rs:46-77): when
+ * every layer image fits vram_weight_budget_bytes (or it is 0) all layers stay
+ * resident and no ring is used; else the first layers that fit beside ring_slots
+ * slots of the largest image stay resident and the rest stream through the ring
+ * (ring_slots 0: load, compute, release).  Applies the plan with
+ * rf_set_residency_plan; mask_out (n_layers entries, may be NULL) receives it.
+ * RF_ENOMEM when the ring slots alone exceed the budget. */
+int rf_plan_residency(rf_engine* e, uint64_t vram_weight_budget_bytes, int ring_slots, uint8_t* mask_out);
+/* LayerCache (layer_cache.rs:25-175) for layers the plan streams without a ring:
+ * after its step a loaded layer stays in device memory as the most recently used
+ * entry while the cached layers' bytes fit capacity_bytes, evicting least
+ * recently used ones first (residency stats: evictions, cache_hits); a layer
+ * larger than the capacity is released.  0 (the default) caches nothing; a new
+ * capacity or residency plan empties the cache. */
+int rf_set_layer_cache(rf_engine* e, uint64_t capacity_bytes);
 int rf_residency_stats_get(const rf_engine* e, rf_residency_stats* out);
 
 /* ---- tensor parallelism -------------------------------------------------------- */

@@ -38,7 +38,7 @@ EXPORTS = [
     "rf_step_kernel_count", "rf_selftest_wait", "rf_decode_timed",
     "rf_bench_layer_kernels", "rf_tp_unique_id", "rf_tp_peer_sum", "rf_matrix_create", "rf_matrix_destroy", "rf_matrix_device_bytes",
     "rf_qmatvec", "rf_qgemm", "rf_qgemm_error_word", "rf_decode_attention", "rf_decode_attention_noalloc",
-    "rf_should_keep_resident", "rf_layer_read_plan",
+    "rf_should_keep_resident", "rf_layer_read_plan", "rf_plan_residency", "rf_set_layer_cache",
 ]
 
 
@@ -96,7 +96,7 @@ class ResidencyStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("layer_loads", "layer_releases", "cache_hits", "cache_misses",
                                                "evictions", "peak_bytes", "h2d_bytes", "ring_copies",
                                                "host_image_bytes", "file_reads", "file_read_bytes",
-                                               "file_gap_bytes")]
+                                               "file_gap_bytes", "host_mapped_bytes")]
 
 
 _lib = None
@@ -146,6 +146,8 @@ def lib():
             "rf_residency_stats_get": (c_int, [vp, ctypes.POINTER(ResidencyStats)]),
             "rf_tp_unique_id": (c_int, [ctypes.POINTER(ctypes.c_uint8)]),
             "rf_should_keep_resident": (c_int, [c_u64, c_u64]),
+            "rf_plan_residency": (c_int, [vp, c_u64, c_int, ctypes.POINTER(ctypes.c_uint8)]),
+            "rf_set_layer_cache": (c_int, [vp, c_u64]),
             "rf_layer_read_plan": (c_int, [ctypes.POINTER(TensorExtent), c_u32, ctypes.POINTER(ReadRange), c_u32, u32p,
                                            ctypes.POINTER(PlannedTensor), ctypes.POINTER(ReadPlanTotals)]),
             "rf_tp_peer_sum": (c_int, [vp, ctypes.POINTER(c_int)]),

@@ -140,9 +140,17 @@ struct rf_engine {
   bool tied = false, have_embd = false, have_out = false, have_onorm = false;
   void* embd_block = nullptr;
   void* out_block = nullptr;
+  // persistent tensors the residency policy keeps in mapped pinned host memory
+  void* embd_host = nullptr;
+  void* out_host = nullptr;
+  uint64_t embd_host_bytes = 0, out_host_bytes = 0;
   float* out_norm = nullptr;
   std::vector<Layer> layers;
   std::vector<uint8_t> plan_resident;  // residency plan (1 = keep resident)
+  // LayerCache (layer_cache.rs:25-175): layers the plan streams that stay loaded
+  // after their step, least recently used first, within cache_capacity bytes
+  uint64_t cache_capacity = 0, cache_used = 0;
+  std::vector<int> cache_lru;
   // KV cache
   void* kv_block = nullptr;
   std::vector<void*> kc, vc;
@@ -748,18 +756,42 @@ int load_persistent(rf_engine* e, int role, const View& v0) {
     RF_TRY(pack_rows(v.host, row_bytes_of(v), 0, iota_rows(r0, rows), &hp, 0, 1));
     const std::string charge = is_embd ? "persistent:token_embd" : "persistent:output";
     void** blk = is_embd ? &e->embd_block : &e->out_block;
+    void** hblk = is_embd ? &e->embd_host : &e->out_host;
     dev_free(e, charge, blk);
-    RF_TRY(dev_alloc(e, charge, packed_bytes(hp), blk));
-    std::vector<uint8_t> img(packed_bytes(hp));
+    if (*hblk) {
+      e->stats.host_mapped_bytes -= is_embd ? e->embd_host_bytes : e->out_host_bytes;
+      cudaFreeHost(*hblk);
+      *hblk = nullptr;
+    }
+    const uint64_t pbytes = packed_bytes(hp);
+    std::vector<uint8_t> img(pbytes);
     uint64_t off = 0;
     PackedMat* dst = is_embd ? &e->embd : &e->out;
     image_put(hp, &img, &off, dst);
-    RF_CUDA(h2d_sync(e, *blk, img.data(), img.size()));
-    dst->qs = (uint8_t*)*blk + reinterpret_cast<uintptr_t>(dst->qs);
-    dst->sc = (uint8_t*)*blk + reinterpret_cast<uintptr_t>(dst->sc);
+    uint8_t* base = nullptr;
+    // PersistentWeight's policy (should_keep_resident, persistent.rs:468; applied at
+    // streaming_model.rs:1586): under an explicit VRAM budget a tensor larger than a
+    // quarter of it is not kept in device memory.  Here it stays in mapped pinned
+    // host memory and the same kernels read it over the host link (the streamed
+    // embedding row and output projection of persistent.rs:80-209, 286-466).
+    if (e->rt.vram_budget_bytes && !rf_should_keep_resident(pbytes, e->budget.total())) {
+      RF_CUDA(cudaHostAlloc(hblk, pbytes, cudaHostAllocMapped));
+      memcpy(*hblk, img.data(), pbytes);
+      void* dptr = nullptr;
+      RF_CUDA(cudaHostGetDevicePointer(&dptr, *hblk, 0));
+      base = (uint8_t*)dptr;
+      (is_embd ? e->embd_host_bytes : e->out_host_bytes) = pbytes;
+      e->stats.host_mapped_bytes += pbytes;
+    } else {
+      RF_TRY(dev_alloc(e, charge, pbytes, blk));
+      RF_CUDA(h2d_sync(e, *blk, img.data(), img.size()));
+      base = (uint8_t*)*blk;
+      e->stats.h2d_bytes += pbytes;
+    }
+    dst->qs = base + reinterpret_cast<uintptr_t>(dst->qs);
+    dst->sc = base + reinterpret_cast<uintptr_t>(dst->sc);
     if (is_embd) e->have_embd = true;
     else { e->have_out = true; e->tied = false; }
-    e->stats.h2d_bytes += packed_bytes(hp);
   } else {
     return set_error(RF_EINVAL, "unknown persistent role %d", role);
   }
@@ -789,6 +821,11 @@ int lm_head(rf_engine* e, PackedMat* W) {
 int release_layer_impl(rf_engine* e, int l) {
   Layer& L = e->layers[l];
   if (!L.resident) return set_error(RF_ESTATE, "layer %d is not loaded", l);
+  auto cached = std::find(e->cache_lru.begin(), e->cache_lru.end(), l);
+  if (cached != e->cache_lru.end()) {  // released while in the layer cache
+    e->cache_lru.erase(cached);
+    e->cache_used -= L.bytes;
+  }
   dev_free(e, "layer:" + std::to_string(l) + ":weights", &L.block);
   L = Layer{};
   e->stats.layer_releases++;
@@ -1069,6 +1106,43 @@ int enqueue_prefill_chunk(rf_engine* e, uint32_t T, uint32_t pos0) {
 // Make every layer resident, loading from the GGUF source where needed.
 // Layers the residency plan marks non-resident are loaded for the step and
 // released afterwards (load -> compute -> release, streaming_model.rs:1081-1270).
+// Layer l, which the plan streams, has just been used: keep it loaded as the
+// most recently used entry of the layer cache when its bytes fit the capacity
+// after evicting least recently used entries (LayerCache::insert_loaded,
+// layer_cache.rs:72-135); else release it (load -> compute -> release).
+int cache_layer(rf_engine* e, int l, bool loaded_now) {
+  auto it = std::find(e->cache_lru.begin(), e->cache_lru.end(), l);
+  if (it != e->cache_lru.end()) {  // a hit: move to the back
+    e->cache_lru.erase(it);
+    e->cache_lru.push_back(l);
+    return RF_OK;
+  }
+  const uint64_t bytes = e->layers[l].bytes;
+  if (!loaded_now) return RF_OK;
+  RF_CUDA(cudaStreamSynchronize(e->stream));  // the step's kernels may still read what is released below
+  if (!bytes || bytes > e->cache_capacity) return release_layer_impl(e, l);
+  while (e->cache_used + bytes > e->cache_capacity && !e->cache_lru.empty()) {
+    const int victim = e->cache_lru.front();
+    e->cache_lru.erase(e->cache_lru.begin());
+    e->cache_used -= e->layers[victim].bytes;
+    RF_TRY(release_layer_impl(e, victim));
+    e->stats.evictions++;
+  }
+  e->cache_lru.push_back(l);
+  e->cache_used += bytes;
+  return RF_OK;
+}
+
+// Drop every cached layer (capacity change, residency plan change).
+int cache_clear(rf_engine* e) {
+  RF_CUDA(cudaStreamSynchronize(e->stream));
+  for (int l : e->cache_lru)
+    if (e->layers[l].resident && !e->plan_resident[l]) RF_TRY(release_layer_impl(e, l));
+  e->cache_lru.clear();
+  e->cache_used = 0;
+  return RF_OK;
+}
+
 int run_stepwise(rf_engine* e, bool decode) {
   const Launch La{e->stream, false};
   RF_CUDA(launch_embed(La, e->embd, &e->d_io->token, e->hidden, e->d_key));
@@ -1082,10 +1156,7 @@ int run_stepwise(rf_engine* e, bool decode) {
       e->stats.cache_hits++;
     }
     RF_TRY(enqueue_layer(e, (int)l, false));
-    if (loaded_now && !e->plan_resident[l]) {
-      RF_CUDA(cudaStreamSynchronize(e->stream));
-      RF_TRY(release_layer_impl(e, (int)l));
-    }
+    if (!e->plan_resident[l]) RF_TRY(cache_layer(e, (int)l, loaded_now));
   }
   RF_CUDA(launch_rmsnorm(La, e->hidden, e->out_norm, e->cfg.rms_eps, e->cfg.n_embd, e->final_hidden));
   if (decode) {
@@ -1388,6 +1459,8 @@ void destroy(rf_engine* e) {
     if (e->layers[l].block) cudaFree(e->layers[l].block);
   if (e->embd_block) cudaFree(e->embd_block);
   if (e->out_block) cudaFree(e->out_block);
+  if (e->embd_host) cudaFreeHost(e->embd_host);
+  if (e->out_host) cudaFreeHost(e->out_host);
   if (e->out_norm) cudaFree(e->out_norm);
   if (e->kv_block) cudaFree(e->kv_block);
   if (e->scratch) cudaFree(e->scratch);
@@ -1866,6 +1939,7 @@ int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uin
   ENGINE_GUARD(e);
   if (!mask) return set_error(RF_EINVAL, "null residency mask");
   if (ring_slots < 0) return set_error(RF_EINVAL, "ring_slots must be >= 0");
+  RF_TRY(cache_clear(e));
   uint64_t resident_bytes = 0, slot_bytes = 0;
   for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
     if (mask[l] && e->layers[l].resident) resident_bytes += e->layers[l].bytes;
@@ -1885,6 +1959,44 @@ int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uin
   }
   if (ring_slots != e->rt.ring_slots) free_ring(e);
   e->rt.ring_slots = ring_slots;
+  return RF_OK;
+}
+
+int rf_plan_residency(rf_engine* e, uint64_t vram_weight_budget_bytes, int ring_slots, uint8_t* mask_out) {
+  ENGINE_GUARD(e);
+  if (ring_slots < 0) return set_error(RF_EINVAL, "ring_slots must be >= 0");
+  const uint32_t L = e->cfg.n_layers;
+  std::vector<uint64_t> img(L);
+  uint64_t slot = 0, all = 0;
+  for (uint32_t l = 0; l < L; l++) {
+    img[l] = layer_image_bytes(e, (int)l);
+    slot = std::max(slot, img[l]);
+    all += img[l];
+  }
+  std::vector<uint8_t> mask(L, 0);
+  int slots = ring_slots;
+  if (!vram_weight_budget_bytes || all <= vram_weight_budget_bytes) {
+    std::fill(mask.begin(), mask.end(), 1);  // everything fits: no ring
+    slots = 0;
+  } else {
+    const uint64_t ring = (uint64_t)ring_slots * slot;
+    if (ring > vram_weight_budget_bytes)
+      return set_error(RF_ENOMEM, "%d ring slots of %llu bytes exceed the weight budget %llu", ring_slots,
+                       (unsigned long long)slot, (unsigned long long)vram_weight_budget_bytes);
+    uint64_t used = ring;
+    for (uint32_t l = 0; l < L && used + img[l] <= vram_weight_budget_bytes; l++) {
+      mask[l] = 1;
+      used += img[l];
+    }
+  }
+  if (mask_out) std::copy(mask.begin(), mask.end(), mask_out);
+  return rf_set_residency_plan(e, mask.data(), slots, vram_weight_budget_bytes);
+}
+
+int rf_set_layer_cache(rf_engine* e, uint64_t capacity_bytes) {
+  ENGINE_GUARD(e);
+  RF_TRY(cache_clear(e));
+  e->cache_capacity = capacity_bytes;
   return RF_OK;
 }
 

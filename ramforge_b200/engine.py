@@ -254,6 +254,16 @@ class DecodeEngine:
         check(lib().rf_set_residency_plan(self._h, mask.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), ring_slots,
                                           vram_weight_budget_bytes))
 
+    def plan_residency(self, vram_weight_budget_bytes: int, ring_slots: int = 0) -> list:
+        """rf_plan_residency: resident layers chosen for the weight budget; returns the mask."""
+        mask = (ctypes.c_uint8 * self.config["n_layers"])()
+        check(lib().rf_plan_residency(self._h, vram_weight_budget_bytes, ring_slots, mask))
+        return [bool(m) for m in mask]
+
+    def set_layer_cache(self, capacity_bytes: int):
+        """rf_set_layer_cache: LRU byte capacity for streamed layers kept after their step."""
+        check(lib().rf_set_layer_cache(self._h, capacity_bytes))
+
     def residency_stats(self) -> dict:
         s = _lib.ResidencyStats()
         check(lib().rf_residency_stats_get(self._h, ctypes.byref(s)))

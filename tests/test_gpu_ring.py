@@ -104,3 +104,71 @@ def test_file_engine_reads_streamed_layers_through_coalesced_ranges(gguf, tmp_pa
     assert st["file_read_bytes"] > 0 and st["file_gap_bytes"] < st["file_read_bytes"] // 100
     a.close()
     b.close()
+
+
+def _layer_bytes(gguf):
+    eng = DecodeEngine(gguf, max_seq_len=16)
+    used_all = eng.budget_used
+    eng.set_residency_plan([False] * RING_MODEL.n_layers)
+    per_layer = (used_all - eng.budget_used) // RING_MODEL.n_layers
+    eng.close()
+    return per_layer
+
+
+def test_planner_maps_a_weight_budget_onto_a_resident_prefix(gguf):
+    per = _layer_bytes(gguf)
+    a = DecodeEngine(gguf, max_seq_len=32)
+    b = DecodeEngine(gguf, max_seq_len=32)
+    assert b.plan_residency(0) == [True] * 6  # no budget: everything resident
+    mask = b.plan_residency(int(per * 4.5), ring_slots=2)  # two slots + two layers fit
+    assert mask == [True, True, False, False, False, False]
+    for pos, tok in enumerate([5, 77, 301]):
+        assert np.array_equal(a.forward_single_streaming(tok, pos), b.forward_single_streaming(tok, pos)), pos
+    assert b.residency_stats()["ring_copies"] == 3 * 4
+    with pytest.raises(RfError, match="NOMEM"):
+        b.plan_residency(int(per * 1.5), ring_slots=2)  # the slots alone exceed the budget
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("cached_layers", [2.5, 6.5])
+def test_layer_cache_keeps_streamed_layers_least_recently_used_first(gguf, cached_layers):
+    per = _layer_bytes(gguf)
+    a = DecodeEngine(gguf, max_seq_len=32)
+    b = DecodeEngine(gguf, max_seq_len=32)
+    b.set_residency_plan([False] * 6, ring_slots=0)  # load -> compute -> release
+    b.set_layer_cache(int(per * cached_layers))
+    st0 = b.residency_stats()  # the plan's own releases count as evictions too
+    for pos, tok in enumerate([5, 77, 301, 9]):
+        assert np.array_equal(a.forward_single_streaming(tok, pos), b.forward_single_streaming(tok, pos)), pos
+    st = {k: v - st0[k] for k, v in b.residency_stats().items()}
+    if cached_layers > 6:  # every layer stays after the first step: later steps hit
+        assert st["cache_misses"] == 6 and st["evictions"] == 0
+        assert all(b.layer_is_resident(i) for i in range(6))
+    else:  # a cyclic pass over six layers through a two-layer LRU misses every time
+        assert st["cache_misses"] == 4 * 6 and st["evictions"] == 4 * 6 - 2
+        assert sum(b.layer_is_resident(i) for i in range(6)) == 2
+    a.close()
+    b.close()
+
+
+def test_persistent_tensors_over_a_quarter_of_the_budget_stay_in_host_memory():
+    """should_keep_resident (persistent.rs:468) under an explicit VRAM budget: a
+    token_embd/output larger than a quarter of it is held in mapped pinned host
+    memory and read over the host link by the same kernels; tokens are the ones an
+    unconstrained engine produces, and less device memory is charged."""
+    spec = synth.scaled(synth.LLAMA3_8B, name="host-lm", vocab_size=16000, n_embd=256, n_layers=2, n_ff=512,
+                        n_heads=4, n_kv_heads=2, seed=43, context_length=64)
+    g = synth.gguf_bytes(spec)
+    a = DecodeEngine(g, max_seq_len=32)
+    lm = 16000 * 256 * 34 // 32  # Q8_0 bytes of each of token_embd and output
+    budget = a.budget_used - 2 * lm + (1 << 20)
+    assert lm > budget // 4
+    b = DecodeEngine(g, max_seq_len=32, vram_budget_bytes=budget)
+    st = b.residency_stats()
+    assert st["host_mapped_bytes"] >= 2 * lm
+    assert b.budget_used < a.budget_used - lm
+    prompt = [3, 1000, 15000, 7]
+    assert b.generate(prompt, 16).tolist() == a.generate(prompt, 16).tolist()
+    a.close()
+    b.close()
