@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define RF_ABI_VERSION 2
+#define RF_ABI_VERSION 3
 
 /* status codes */
 #define RF_OK 0
