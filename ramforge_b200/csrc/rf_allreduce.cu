@@ -6,17 +6,6 @@
 namespace rf {
 
 namespace {
-constexpr unsigned kSpinFast = 1u << 12;   // polls before a wait starts to back off
-constexpr unsigned kSpinLimit = 1u << 24;  // then ~1 s of 64 ns sleeps before it gives up
-
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 __global__ void __launch_bounds__(PS_THREADS) peer_sum_kernel(PeerSum P, const float* __restrict__ partial,
                                                               float* __restrict__ out, int n, int site) {
@@ -40,14 +29,7 @@ __global__ void __launch_bounds__(PS_THREADS) peer_sum_kernel(PeerSum P, const f
     const int p = threadIdx.x;
     st_release_sys(P.flags[p] + ((size_t)P.rank * P.sites + site) * P.max_ctas + b, e);
     const unsigned* f = P.flags[P.rank] + ((size_t)p * P.sites + site) * P.max_ctas + b;
-    unsigned it = 0;
-    while (ld_acquire_sys(f) != e) {
-      if (++it > kSpinLimit) {
-        atomicOr(P.err, 1u);
-        break;
-      }
-      if (it > kSpinFast) __nanosleep(64);
-    }
+    if (!wait_flag_sys(f, e)) atomicOr(P.err, 1u);
   }
   __syncthreads();
   // 3. the ranks' partials in rank order
@@ -72,11 +54,13 @@ __global__ void __launch_bounds__(PS_THREADS) peer_sum_kernel(PeerSum P, const f
 }  // namespace
 
 static size_t recv_bytes(int n_ranks, int n_max) { return ((size_t)2 * n_ranks * n_max * sizeof(float) + 255) & ~size_t(255); }
-static int max_ctas_of(int n_max) { return (n_max + PS_ELEMS - 1) / PS_ELEMS; }
+// flag slots per call site: one per CTA of the sum kernel (PS_ELEMS elements) or
+// per 64-row tile of a GEMV that pushes its rows (PeerLink), whichever is more
+static int max_ctas_of(int n_max) { return (n_max + QT_ROWS - 1) / QT_ROWS; }
 static size_t flag_words(int n_ranks, int n_max, int sites) { return (size_t)n_ranks * sites * max_ctas_of(n_max); }
 
 size_t peer_sum_area_bytes(int n_ranks, int n_max, int sites) {
-  return recv_bytes(n_ranks, n_max) + 4 * (flag_words(n_ranks, n_max, sites) + 2 * (size_t)sites + 1);
+  return recv_bytes(n_ranks, n_max) + 4 * (flag_words(n_ranks, n_max, sites) + 3 * (size_t)sites + 1);
 }
 
 void peer_sum_bind(PeerSum* P, int p, void* area, bool own) {
@@ -89,6 +73,7 @@ void peer_sum_bind(PeerSum* P, int p, void* area, bool own) {
     P->epoch = w;
     P->done = w + P->sites;
     P->err = w + 2 * P->sites;
+    P->fgen = w + 2 * P->sites + 1;
   }
 }
 

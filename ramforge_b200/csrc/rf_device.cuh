@@ -14,6 +14,44 @@ namespace rf {
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// Flags of the tensor-parallel sums (written and read across GPUs).
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until *f == e: 4096 polls, then 64 ns sleeps between polls, about a second
+// in all; false when it gave up.
+__device__ __forceinline__ bool wait_flag_sys(const unsigned* f, unsigned e) {
+  constexpr unsigned kSpinFast = 1u << 12, kSpinLimit = 1u << 24;
+  unsigned it = 0;
+  while (ld_acquire_sys(f) != e) {
+    if (++it > kSpinLimit) return false;
+    if (it > kSpinFast) __nanosleep(64);
+  }
+  return true;
+}
+
+// Arrival on a (possibly peer) counter, after this thread's (and, through a
+// preceding barrier, its CTA's) stores.
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Wait until the counter *f has reached `want` (it only grows between resets;
+// compared modulo 2^32), bounded like wait_flag_sys.
+__device__ __forceinline__ bool wait_count_sys(const unsigned* f, unsigned want) {
+  constexpr unsigned kSpinFast = 1u << 12, kSpinLimit = 1u << 24;
+  unsigned it = 0;
+  while ((int)(ld_acquire_sys(f) - want) < 0) {
+    if (++it > kSpinLimit) return false;
+    if (it > kSpinFast) __nanosleep(64);
+  }
+  return true;
+}
+
 // Streaming loads of weights (read once per token: no L1 allocation).
 __device__ __forceinline__ void ldg256(const uint8_t* p, uint32_t (&w)[8]) {
   asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"

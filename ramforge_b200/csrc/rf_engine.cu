@@ -929,13 +929,41 @@ bool all_resident(const rf_engine* e) {
   return true;
 }
 
-int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
+// Whether the rank sum after W_o (k = 2) or W_down (k = 4) of layer l runs inside
+// the GEMVs on either side of it (PeerLink) instead of as its own kernel: under
+// tensor parallelism over peer memory, when the producing and the consuming
+// matrices are tiled.  The last layer's W_down keeps the sum kernel (the output
+// RMSNorm reads the sum).
+bool fuse_sum(const rf_engine* e, int l, int k) {
+  if (e->tp == 1 || !e->ps_ok) return false;
+  const Layer& L = e->layers[l];
+  if (k == 2) return is_tiled(L.wo.type) && is_tiled(L.gateup.type);
+  return l + 1 < (int)e->layers.size() && is_tiled(L.down.type) && is_tiled(e->layers[l + 1].qkv.type);
+}
+PeerLink peer_link(const rf_engine* e) {
+  PeerLink pl;
+  pl.P = e->ps;
+  pl.hidden = e->hidden;
+  return pl;
+}
+
+// Kernel class k of layer l.  `fused`: inside a whole step, where the rank sums
+// run inside the GEMVs around them (fuse_sum); every other caller (single layers,
+// per-class timing, streamed steps) gets the sum kernel after each row-parallel product.
+int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false, bool fused = false) {
   const rf_model_config& c = e->cfg;
   Layer& L = e->layers[l];
   const Launch La{e->stream, pdl, e->tp > 1};
   if (k == 0) {
     RopeQKVArgs ra = rope_args(e, l);
-    RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, ra));
+    if (fused && l > 0 && fuse_sum(e, l - 1, 4)) {
+      PeerLink pl = peer_link(e);
+      pl.pull_site = 2 * (l - 1) + 1;
+      pl.push_ctas = gemv_ctas(La, e->layers[l - 1].down, true);
+      RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, ra, &pl));
+    } else {
+      RF_CUDA(gemv_qkv_rope(La, L.qkv, &e->gws, e->hidden, L.attn_norm, c.rms_eps, ra));
+    }
     if (L.vmat.M) {  // V of its own type: the same epilogue from the V rows on
       ra.row_base = e->q_local + e->kv_local;
       RF_CUDA(gemv_qkv_rope(La, L.vmat, &e->gws, e->hidden, L.attn_norm, c.rms_eps, ra));
@@ -945,20 +973,32 @@ int enqueue_layer_kernel(rf_engine* e, int l, int k, bool pdl = false) {
   } else if (k == 2 || k == 4) {
     const PackedMat& W = k == 2 ? L.wo : L.down;
     const float* x = k == 2 ? e->att : e->act;
+    const int site = 2 * l + (k == 4 ? 1 : 0);
     if (e->tp == 1) {
       RF_CUDA(gemv_residual(La, W, &e->gws, x, e->hidden, e->hidden));
+    } else if (fused && fuse_sum(e, l, k)) {
+      PeerLink pl = peer_link(e);
+      pl.push_site = site;
+      RF_CUDA(gemv_peer_push(La, W, &e->gws, x, e->rank == 0 ? e->hidden : nullptr, pl));
     } else {
       RF_CUDA(gemv_residual(La, W, &e->gws, x, e->rank == 0 ? e->hidden : nullptr, e->partial));
-      RF_TRY(tp_sum(e, La, 2 * l + (k == 4 ? 1 : 0)));
+      RF_TRY(tp_sum(e, La, site));
     }
   } else {
-    RF_CUDA(gemv_swiglu(La, L.gateup, &e->gws, e->hidden, L.ffn_norm, c.rms_eps, e->act));
+    if (fused && fuse_sum(e, l, 2)) {
+      PeerLink pl = peer_link(e);
+      pl.pull_site = 2 * l;
+      pl.push_ctas = gemv_ctas(La, L.wo, true);
+      RF_CUDA(gemv_swiglu(La, L.gateup, &e->gws, e->hidden, L.ffn_norm, c.rms_eps, e->act, &pl));
+    } else {
+      RF_CUDA(gemv_swiglu(La, L.gateup, &e->gws, e->hidden, L.ffn_norm, c.rms_eps, e->act));
+    }
   }
   return RF_OK;
 }
 
-int enqueue_layer(rf_engine* e, int l, bool pdl) {
-  for (int k = 0; k < 5; k++) RF_TRY(enqueue_layer_kernel(e, l, k, pdl));
+int enqueue_layer(rf_engine* e, int l, bool pdl, bool fused = false) {
+  for (int k = 0; k < 5; k++) RF_TRY(enqueue_layer_kernel(e, l, k, pdl, fused));
   return RF_OK;
 }
 
@@ -967,7 +1007,7 @@ int enqueue_layer(rf_engine* e, int l, bool pdl) {
 int enqueue_forward(rf_engine* e, bool pdl) {
   const Launch La{e->stream, pdl};
   RF_CUDA(launch_embed(La, e->embd, &e->d_io->token, e->hidden, e->d_key));
-  for (uint32_t l = 0; l < e->cfg.n_layers; l++) RF_TRY(enqueue_layer(e, (int)l, pdl));
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++) RF_TRY(enqueue_layer(e, (int)l, pdl, true));
   RF_CUDA(launch_rmsnorm(La, e->hidden, e->out_norm, e->cfg.rms_eps, e->cfg.n_embd, e->final_hidden));
   return RF_OK;
 }
@@ -1829,10 +1869,14 @@ int rf_decode_timed(rf_engine* e, uint32_t token, uint32_t n_steps, uint32_t* ou
 int rf_step_kernel_count(const rf_engine* ec, uint32_t* out) {
   if (!ec || !out) return set_error(RF_EINVAL, "null argument");
   rf_engine* e = const_cast<rf_engine*>(ec);
-  // embed, 5 per layer (6 with a separate V matrix), output norm, LM head, advance, and the two peer sums
-  // a layer under tensor parallelism (NCCL's own kernels are not counted)
-  uint32_t n = 5u * e->cfg.n_layers + 4u + (e->ps_ok ? 2u * e->cfg.n_layers : 0u);
-  for (uint32_t l = 0; l < e->cfg.n_layers; l++) n += e->layers[l].vmat.M || layer_v_split(e, (int)l) ? 1u : 0u;
+  // embed, 5 per layer (6 with a separate V matrix), output norm, LM head, advance, and under tensor
+  // parallelism over peer memory the sum kernels of the rank sums not fused into the GEMVs (NCCL's own
+  // kernels are not counted)
+  uint32_t n = 5u * e->cfg.n_layers + 4u;
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
+    n += e->layers[l].vmat.M || layer_v_split(e, (int)l) ? 1u : 0u;
+    if (e->ps_ok) n += (fuse_sum(e, (int)l, 2) ? 0u : 1u) + (fuse_sum(e, (int)l, 4) ? 0u : 1u);
+  }
   *out = n;
   return RF_OK;
 }

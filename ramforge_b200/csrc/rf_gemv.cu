@@ -11,9 +11,9 @@ namespace rf {
 template <int FMT, bool QUIRK, class Epi, int NW>
 __global__ void __launch_bounds__(NW * 32, QG_WARPS / NW)
     qgemv_kernel(PackedMat W, const float* __restrict__ x, const float* __restrict__ nw, float eps,
-                 float* __restrict__ part, unsigned* __restrict__ cnt, Epi epi) {
+                 float* __restrict__ part, unsigned* __restrict__ cnt, Epi epi, PeerLink pl) {
   extern __shared__ __align__(16) float qsm[];
-  qgemv_body<FMT, QUIRK, NW>(W, x, nw, eps, part, cnt, epi, qsm, [] { griddep_wait(); });
+  qgemv_body<FMT, QUIRK, NW>(W, x, nw, eps, part, cnt, epi, qsm, [] { griddep_wait(); }, pl);
   epi.flush();
 }
 
@@ -32,7 +32,7 @@ constexpr size_t kMaxSmem = 227 * 1024;
 
 template <int FMT, class Epi, int NW>
 static cudaError_t run_qgemv_w(const Launch& L, const PackedMat& W, const GemvScratch& ws, const float* x,
-                               const float* nw, float eps, Epi epi) {
+                               const float* nw, float eps, Epi epi, const PeerLink& pl) {
   auto k = W.sub_scales ? qgemv_kernel<FMT, true, Epi, NW> : qgemv_kernel<FMT, false, Epi, NW>;
   const int grid = num_sms() * (QG_WARPS / NW);
   const size_t smem = qgemv_smem_bytes(W, grid, NW);
@@ -40,15 +40,20 @@ static cudaError_t run_qgemv_w(const Launch& L, const PackedMat& W, const GemvSc
   if (ws.part_floats < (uint64_t)W.Mp * W.nk * QT_PIECES || ws.n_cnt < W.Mp / QT_ROWS) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_k(L, k, dim3(grid), dim3(NW * 32), smem, W, x, nw, eps, ws.part, ws.cnt, epi);
+  return launch_k(L, k, dim3(grid), dim3(NW * 32), smem, W, x, nw, eps, ws.part, ws.cnt, epi, pl);
 }
 
 template <int FMT, class Epi>
 static cudaError_t run_qgemv_t(const Launch& L, const PackedMat& W, const GemvScratch& ws, const float* x,
-                               const float* nw, float eps, Epi epi) {
+                               const float* nw, float eps, Epi epi, const PeerLink& pl) {
   if constexpr (qgemv_split_ctas<Epi>())
-    if (!L.wide) return run_qgemv_w<FMT, Epi, QG_WARPS / 2>(L, W, ws, x, nw, eps, epi);
-  return run_qgemv_w<FMT, Epi, QG_WARPS>(L, W, ws, x, nw, eps, epi);
+    if (!L.wide) return run_qgemv_w<FMT, Epi, QG_WARPS / 2>(L, W, ws, x, nw, eps, epi, pl);
+  return run_qgemv_w<FMT, Epi, QG_WARPS>(L, W, ws, x, nw, eps, epi, pl);
+}
+
+int gemv_ctas(const Launch& L, const PackedMat&, bool residual_epilogue) {
+  const int nw = residual_epilogue && !L.wide ? QG_WARPS / 2 : QG_WARPS;
+  return num_sms() * (QG_WARPS / nw);
 }
 
 void gemv_scratch_need(const PackedMat& W, uint64_t* part_floats, uint32_t* n_cnt) {
@@ -120,18 +125,23 @@ static cudaError_t run_fgemv_t(const Launch& L, const PackedMat& W, const float*
   return launch_k(L, fgemv_kernel<FMT, Epi>, dim3(blocks), dim3(GEMV_THREADS), 0, W, x, nw, eps, epi);
 }
 
+// `pl`: a peer sum this GEMV pulls x from or pushes its rows into (quantized
+// matrices only; pulling needs the RMSNorm pass, which visits all of x).
 template <class Epi>
 static cudaError_t run_gemv(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
-                            const float* nw, float eps, Epi epi) {
+                            const float* nw, float eps, Epi epi, const PeerLink& pl = PeerLink{}) {
   if (is_tiled(W.type) && !ws) return cudaErrorInvalidValue;
+  if ((pl.pull_site >= 0 || pl.push_site >= 0) && !is_tiled(W.type)) return cudaErrorInvalidValue;
+  if (pl.pull_site >= 0 && (!nw || !pl.hidden || W.K % 4 || W.K > (uint32_t)pl.P.n_max)) return cudaErrorInvalidValue;
+  if (pl.push_site >= 0 && W.M > (uint32_t)pl.P.n_max) return cudaErrorInvalidValue;
   switch (W.type) {
-    case T_Q4_K: return run_qgemv_t<T_Q4_K>(L, W, *ws, x, nw, eps, epi);
-    case T_Q4_0: return run_qgemv_t<T_Q4_0>(L, W, *ws, x, nw, eps, epi);
-    case T_Q8_0: return run_qgemv_t<T_Q8_0>(L, W, *ws, x, nw, eps, epi);
-    case T_Q6_K: return run_qgemv_t<T_Q6_K>(L, W, *ws, x, nw, eps, epi);
-    case T_Q5_K: return run_qgemv_t<T_Q5_K>(L, W, *ws, x, nw, eps, epi);
-    case T_Q3_K: return run_qgemv_t<T_Q3_K>(L, W, *ws, x, nw, eps, epi);
-    case T_Q2_K: return run_qgemv_t<T_Q2_K>(L, W, *ws, x, nw, eps, epi);
+    case T_Q4_K: return run_qgemv_t<T_Q4_K>(L, W, *ws, x, nw, eps, epi, pl);
+    case T_Q4_0: return run_qgemv_t<T_Q4_0>(L, W, *ws, x, nw, eps, epi, pl);
+    case T_Q8_0: return run_qgemv_t<T_Q8_0>(L, W, *ws, x, nw, eps, epi, pl);
+    case T_Q6_K: return run_qgemv_t<T_Q6_K>(L, W, *ws, x, nw, eps, epi, pl);
+    case T_Q5_K: return run_qgemv_t<T_Q5_K>(L, W, *ws, x, nw, eps, epi, pl);
+    case T_Q3_K: return run_qgemv_t<T_Q3_K>(L, W, *ws, x, nw, eps, epi, pl);
+    case T_Q2_K: return run_qgemv_t<T_Q2_K>(L, W, *ws, x, nw, eps, epi, pl);
     case T_F16: return run_fgemv_t<T_F16>(L, W, x, nw, eps, epi);
     case T_F32: return run_fgemv_t<T_F32>(L, W, x, nw, eps, epi);
     default: return cudaErrorInvalidValue;
@@ -147,12 +157,17 @@ cudaError_t gemv_residual(const Launch& L, const PackedMat& W, const GemvScratch
   return run_gemv(L, W, ws, x, nullptr, 0.f, EpiResidual{res, out});
 }
 cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
-                          const float* nw, float eps, const RopeQKVArgs& a) {
-  return run_gemv(L, W, ws, x, nw, eps, EpiRope{a, -1});
+                          const float* nw, float eps, const RopeQKVArgs& a, const PeerLink* pull) {
+  return run_gemv(L, W, ws, x, nw, eps, EpiRope{a, -1}, pull ? *pull : PeerLink{});
 }
 cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x, const float* nw,
-                        float eps, float* act) {
-  return run_gemv(L, W, ws, x, nw, eps, EpiSwiGLU{act});
+                        float eps, float* act, const PeerLink* pull) {
+  return run_gemv(L, W, ws, x, nw, eps, EpiSwiGLU{act}, pull ? *pull : PeerLink{});
+}
+cudaError_t gemv_peer_push(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
+                           const float* res, const PeerLink& pl) {
+  if (pl.push_site < 0) return cudaErrorInvalidValue;
+  return run_gemv(L, W, ws, x, nullptr, 0.f, EpiPeerPush{res, pl}, pl);
 }
 cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x, const float* nw,
                         float eps, float* logits, unsigned long long* key, uint32_t row_offset) {

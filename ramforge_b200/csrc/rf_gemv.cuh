@@ -60,6 +60,7 @@ struct EpiStore {
   __device__ void pre_begin() {}
   __device__ float pre_load(uint32_t) { return 0.f; }
   __device__ void flush() {}
+  __device__ void tile_done(uint32_t) {}
 };
 
 struct EpiResidual {  // out = res + W.x (res may alias out: a row is read before it is written)
@@ -75,6 +76,38 @@ struct EpiResidual {  // out = res + W.x (res may alias out: a row is read befor
   __device__ void pre_begin() {}
   __device__ float pre_load(uint32_t row) { return res ? __ldcg(res + row) : 0.f; }
   __device__ void flush() {}
+  __device__ void tile_done(uint32_t) {}
+};
+
+// out = res + W.x of a row-parallel projection, pushed into a tensor-parallel sum
+// over peer memory (PeerLink): every row goes to each rank's receive area at this
+// rank's row of the site's parity half.  At the end of the kernel each CTA, after a
+// barrier behind all of its stores, adds one arrival to this rank's counter of the
+// site on every rank (a system-scope release-add); a counter grows by the
+// producer's CTA count per use of the site.
+struct EpiPeerPush {
+  static constexpr bool kPre = true;
+  const float* res;  // rank 0: the residual; other ranks: null
+  PeerLink pl;
+  __device__ void operator()(int row0, const float* v, int n, const float* pre = nullptr) {
+    const PeerSum& P = pl.P;
+    const size_t off = ((size_t)(pl.push_site & 1) * P.n_ranks + P.rank) * P.n_max;
+    for (int i = 0; i < n; i++) {
+      const float r = res ? (pre ? pre[i] : __ldcg(res + row0 + i)) : 0.f;
+      const float o = res ? r + v[i] : v[i];
+      for (int p = 0; p < P.n_ranks; p++) __stcg(P.recv[p] + off + row0 + i, o);
+    }
+  }
+  __device__ void pre_begin() {}
+  __device__ float pre_load(uint32_t row) { return res ? __ldcg(res + row) : 0.f; }
+  // every thread of the CTA, after its last row
+  __device__ void flush() {
+    __syncthreads();
+    const PeerSum& P = pl.P;
+    if ((int)threadIdx.x < P.n_ranks)
+      red_release_sys_add(P.flags[threadIdx.x] + ((size_t)P.rank * P.sites + pl.push_site + 1) * P.max_ctas - 1, 1u);
+  }
+  __device__ void tile_done(uint32_t) {}
 };
 
 // Q and K rows are packed as pairs (i, i+hd/2) of each head so that the
@@ -102,6 +135,7 @@ struct EpiRope {  // arguments held by value (a kernel parameter)
   __device__ void pre_begin() { pos = __ldcg(a.d_pos); }
   __device__ float pre_load(uint32_t row) { return rope_cs_of(a, row, pos); }
   __device__ void flush() {}
+  __device__ void tile_done(uint32_t) {}
 };
 struct EpiRopeRef {  // arguments read from memory when a row pair finishes
   static constexpr bool kPre = false;
@@ -110,6 +144,7 @@ struct EpiRopeRef {  // arguments read from memory when a row pair finishes
   __device__ void pre_begin() {}
   __device__ float pre_load(uint32_t) { return 0.f; }
   __device__ void flush() {}
+  __device__ void tile_done(uint32_t) {}
 };
 __device__ __forceinline__ void rope_store(const RopeQKVArgs& a, int row0, const float* v, int n, const float* pre,
                                            int pos) {
@@ -175,6 +210,7 @@ struct EpiSwiGLU {
     act[row0 >> 1] = __fmul_rn(s, u);
   }
   __device__ void flush() {}
+  __device__ void tile_done(uint32_t) {}
 };
 
 // Order-preserving 64-bit key: high word = float bits mapped to unsigned order,
@@ -211,6 +247,7 @@ struct EpiArgmax {
     }
     if ((threadIdx.x & 31) == 0 && b) atomicMax(key, b);
   }
+  __device__ void tile_done(uint32_t) {}
 };
 
 // ---------------------------------------------------------------------------
@@ -406,13 +443,38 @@ __device__ __forceinline__ unsigned arrive_acq_rel(unsigned* p, unsigned v) {
   return old;
 }
 
+// A GEMV that pulls its x from a tensor-parallel sum (PeerLink::pull_site): wait,
+// bounded (about a second, then bit 0 of the error word), until every rank's
+// arrival counter of the site holds this use's count (generation x the producer's
+// CTAs), then count this CTA in; the last CTA moves the call site to the next
+// generation.  One lane per rank polls; the CTA barrier after it orders the
+// receive-area reads after the arrivals.
+__device__ __forceinline__ void peer_pull_wait(const PeerLink& pl) {
+  const PeerSum& P = pl.P;
+  const int site = pl.pull_site;
+  const unsigned e = *reinterpret_cast<volatile const unsigned*>(P.fgen + site) + 1;
+  if (threadIdx.x < 32) {
+    bool ok = true;
+    if ((int)threadIdx.x < P.n_ranks)
+      ok = wait_count_sys(P.flags[P.rank] + ((size_t)threadIdx.x * P.sites + site + 1) * P.max_ctas - 1,
+                          e * (unsigned)pl.push_ctas);
+    if (!__all_sync(0xffffffffu, ok) && threadIdx.x == 0) atomicOr(P.err, 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(P.done + site, 1u) == gridDim.x - 1) {
+    P.fgen[site] = e;
+    P.done[site] = 0u;
+  }
+}
+
 // The quantized GEMV over every CTA of the grid.  `wait()` runs before the
 // first read of x (griddepcontrol.wait: the previous kernel's completion); x and
 // the residual input are read through L2.
 template <int FMT, bool QUIRK, int NW = QG_WARPS, class Epi, class Wait>
 __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __restrict__ x,
                                            const float* __restrict__ nw, float eps, float* __restrict__ part,
-                                           unsigned* __restrict__ cnt, Epi& epi, float* smem, Wait&& wait) {
+                                           unsigned* __restrict__ cnt, Epi& epi, float* smem, Wait&& wait,
+                                           const PeerLink& pl) {
   using T = QTraits<FMT>;
   constexpr int CE = T::CE, SW = T::SW, GE = T::GE, NG = CE / GE, SB = SW * 4;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -528,6 +590,23 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   }
 
   wait();
+  // x pulled from a tensor-parallel sum: the ranks' rows of the site's parity half,
+  // summed in rank order (the order of the sum kernel, so the same values)
+  const bool pull = pl.pull_site >= 0;
+  if (pull) peer_pull_wait(pl);
+  const float* rb = pull ? pl.P.recv[pl.P.rank] + (size_t)(pl.pull_site & 1) * pl.P.n_ranks * pl.P.n_max : nullptr;
+  auto ldx4 = [&](uint32_t i) -> float4 {  // x[i .. i+3]
+    if (!pull) return __ldcg(reinterpret_cast<const float4*>(x + i));
+    float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < pl.P.n_ranks; r++) {
+      const float4 t = __ldcv(reinterpret_cast<const float4*>(rb + (size_t)r * pl.P.n_max + i));
+      s4.x += t.x;
+      s4.y += t.y;
+      s4.z += t.z;
+      s4.w += t.w;
+    }
+    return s4;
+  };
   if (lane < 2) stile[2 * warp + lane] = -1;
   if (epre) epi.pre_begin();
   // One pass over x.  The window is staged as x*nw: RMSNorm's 1/rms is applied
@@ -552,15 +631,16 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       if (kc >= nk) kc -= nk;
       const uint32_t gi = kc * CE + e;
       const bool in = q < nq && gi < W.K;  // K is a multiple of 32: a float4 is wholly in or out
-      xv[u] = in ? __ldcg(reinterpret_cast<const float4*>(x + gi)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[u] = in ? ldx4(gi) : make_float4(0.f, 0.f, 0.f, 0.f);
       wv[u] = in && nw ? __ldcg(reinterpret_cast<const float4*>(nw + gi)) : make_float4(1.f, 1.f, 1.f, 1.f);
-      sv[u] = !win_is_x && q < KQ ? __ldcg(reinterpret_cast<const float4*>(x) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      sv[u] = !win_is_x && q < KQ ? ldx4(4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < SU; u++) {
       const uint32_t q = q0 + u * (NW * 32), f = 4 * q, e = f % CE;
       if (q < KQ) {
         const float4 t = win_is_x ? xv[u] : sv[u];
+        if (pull && blockIdx.x == 0) reinterpret_cast<float4*>(pl.hidden)[q] = t;  // the sum, for later residuals
         ss = fmaf(t.x, t.x, ss);
         ss = fmaf(t.y, t.y, ss);
         ss = fmaf(t.z, t.z, ss);
@@ -610,6 +690,7 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     const float v[2] = {ws[2 * lane], ws[2 * lane + 1]};
     if (r < W.M) epi((int)r, v, (int)min(2u, W.M - r), pre && epre ? sepi + (r - etl * QT_ROWS) : nullptr);
     __syncwarp();
+    epi.tile_done(tile);
   };
   // End of this warp's run of `len` pieces in `tile`: a whole tile goes to the
   // epilogue, a part (at most two per warp: the ends of its range) waits in

@@ -325,6 +325,7 @@ bool has_subnormal_scales(const PackedMat& W, const uint8_t* sc_host);
 // All take x (f32, K elements) and optionally RMSNorm it on the fly with
 // norm_w/eps (rms_norm_reference, compute.rs:291-319).  Quantized matrices need
 // the split-K scratch (gemv_scratch_need); F32/F16 ones ignore it.
+struct PeerLink;  // a GEMV's part in a tensor-parallel sum over peer memory (below)
 cudaError_t gemv_store(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x, const float* norm_w,
                        float eps, float* y);
 // out[row] = (res ? res[row] : 0) + (W.x)[row]   (residual add, model_executor.rs:213-215, 231-233)
@@ -348,11 +349,12 @@ struct RopeQKVArgs {
   const float* bias;
 };
 // Fused: RMSNorm(attn_norm) -> packed [Q;K;V] matvec -> RoPE on Q/K pairs -> K/V append.
+// With `pull`, x is the sum over ranks of a peer sum's rows instead (PeerLink).
 cudaError_t gemv_qkv_rope(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
-                          const float* norm_w, float eps, const RopeQKVArgs& a);
+                          const float* norm_w, float eps, const RopeQKVArgs& a, const PeerLink* pull = nullptr);
 // Fused: RMSNorm(ffn_norm) -> packed [gate_j; up_j] matvec -> act[j] = silu(g)*u.
 cudaError_t gemv_swiglu(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
-                        const float* norm_w, float eps, float* act);
+                        const float* norm_w, float eps, float* act, const PeerLink* pull = nullptr);
 // Fused LM head: optional RMSNorm(output_norm) -> logits (nullable) -> packed
 // argmax key (atomicMax of (ordered value, ~global_row)).
 cudaError_t gemv_argmax(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
@@ -409,6 +411,7 @@ struct PeerSum {
   unsigned* epoch;             // this rank: generation of each call site [sites]
   unsigned* done;              // this rank: CTAs finished per call site [sites]
   unsigned* err;               // this rank: bit 0 = a wait gave up
+  unsigned* fgen;              // this rank: generation of each call site's fused sum (PeerLink) [sites]
   int rank, n_ranks, n_max, sites, max_ctas;
 };
 // Bytes of one rank's area (receive | flags | epoch | done | err), and its layout.
@@ -420,6 +423,30 @@ cudaError_t launch_peer_sum(const Launch& L, const PeerSum& P, const float* part
 // One peer sum whose second rank never arrives (a local phantom area): its
 // bounded wait gives up and sets bit 0 of *err_out.
 cudaError_t peer_sum_selftest(unsigned* err_out);
+
+// The same sum fused into the GEMVs on either side of it, so no kernel runs for
+// it.  The row-parallel GEMV (push_site >= 0) stores its rows (plus the residual
+// on rank 0) into every rank's receive area, and each of its CTAs, after its
+// stores, adds one arrival to this rank's counter of the site on every rank
+// (system-scope release-add; the counter is the first flag word of the site).
+// The next GEMV (pull_site >= 0) waits, bounded, until every rank's counter holds
+// fused generation x push_ctas, stages x as the ranks' rows summed in rank order (the
+// sum kernel's order), and its CTA 0 writes that sum to `hidden` (the residual of
+// the next row-parallel product).  Generations advance as in the kernel above;
+// the counters grow by push_ctas per use and are compared modulo 2^32.  The fused
+// sum keeps its own generation per site (fgen) and its counter in the site's last
+// flag slot, apart from the sum kernel's, so an engine may use both on one site.
+struct PeerLink {
+  PeerSum P;
+  int push_site = -1, pull_site = -1;
+  int push_ctas = 0;  // CTAs of the pushing GEMV (its launch's grid)
+  float* hidden = nullptr;
+};
+// CTAs a quantized GEMV launch has on this device (the pushing GEMV's arrival count).
+int gemv_ctas(const Launch& L, const PackedMat& W, bool residual_epilogue);
+// out = res + W.x pushed into the peer sum of pl.push_site (res: rank 0's residual or null).
+cudaError_t gemv_peer_push(const Launch& L, const PackedMat& W, const GemvScratch* ws, const float* x,
+                           const float* res, const PeerLink& pl);
 
 // ---- attention -------------------------------------------------------------
 struct AttnArgs {
