@@ -470,11 +470,13 @@ __device__ __forceinline__ void peer_pull_wait(const PeerLink& pl) {
 // The quantized GEMV over every CTA of the grid.  `wait()` runs before the
 // first read of x (griddepcontrol.wait: the previous kernel's completion); x and
 // the residual input are read through L2.
-template <int FMT, bool QUIRK, int NW = QG_WARPS, class Epi, class Wait>
+// PULL: x comes from a tensor-parallel sum (PeerLink *pl), a separate instance so
+// the plain GEMV carries none of it.
+template <int FMT, bool QUIRK, int NW = QG_WARPS, bool PULL = false, class Epi, class Wait>
 __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __restrict__ x,
                                            const float* __restrict__ nw, float eps, float* __restrict__ part,
                                            unsigned* __restrict__ cnt, Epi& epi, float* smem, Wait&& wait,
-                                           const PeerLink& pl) {
+                                           const PeerLink* pl = nullptr) {
   using T = QTraits<FMT>;
   constexpr int CE = T::CE, SW = T::SW, GE = T::GE, NG = CE / GE, SB = SW * 4;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -592,14 +594,16 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
   wait();
   // x pulled from a tensor-parallel sum: the ranks' rows of the site's parity half,
   // summed in rank order (the order of the sum kernel, so the same values)
-  const bool pull = pl.pull_site >= 0;
-  if (pull) peer_pull_wait(pl);
-  const float* rb = pull ? pl.P.recv[pl.P.rank] + (size_t)(pl.pull_site & 1) * pl.P.n_ranks * pl.P.n_max : nullptr;
+  const float* rb = nullptr;
+  if constexpr (PULL) {
+    peer_pull_wait(*pl);
+    rb = pl->P.recv[pl->P.rank] + (size_t)(pl->pull_site & 1) * pl->P.n_ranks * pl->P.n_max;
+  }
   auto ldx4 = [&](uint32_t i) -> float4 {  // x[i .. i+3]
-    if (!pull) return __ldcg(reinterpret_cast<const float4*>(x + i));
+    if constexpr (!PULL) return __ldcg(reinterpret_cast<const float4*>(x + i));
     float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r = 0; r < pl.P.n_ranks; r++) {
-      const float4 t = __ldcv(reinterpret_cast<const float4*>(rb + (size_t)r * pl.P.n_max + i));
+    for (int r = 0; r < pl->P.n_ranks; r++) {
+      const float4 t = __ldcv(reinterpret_cast<const float4*>(rb + (size_t)r * pl->P.n_max + i));
       s4.x += t.x;
       s4.y += t.y;
       s4.z += t.z;
@@ -640,7 +644,8 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
       const uint32_t q = q0 + u * (NW * 32), f = 4 * q, e = f % CE;
       if (q < KQ) {
         const float4 t = win_is_x ? xv[u] : sv[u];
-        if (pull && blockIdx.x == 0) reinterpret_cast<float4*>(pl.hidden)[q] = t;  // the sum, for later residuals
+        if constexpr (PULL)
+          if (blockIdx.x == 0) reinterpret_cast<float4*>(pl->hidden)[q] = t;  // the sum, for later residuals
         ss = fmaf(t.x, t.x, ss);
         ss = fmaf(t.y, t.y, ss);
         ss = fmaf(t.z, t.z, ss);
