@@ -259,12 +259,133 @@ def run_profile(args, spec):
         spec = synth.scaled(spec, name=f"{spec.name}-{args.layers}l", n_layers=args.layers)
     torch.cuda.set_device(0)
     g = synth.gguf_bytes(spec)
+    if args.prefill:  # one batched prefill (tensor-core GEMMs) after a warm-up one
+        eng = DecodeEngine(g, device=0, max_seq_len=args.prefill + 8)
+        prompt = np.random.default_rng(3).integers(0, spec.vocab_size, args.prefill).tolist()
+        eng.prefill(prompt)
+        eng.kv_reset()
+        t0 = time.perf_counter()
+        eng.prefill(prompt)
+        emit({"profile_run": spec.name, "layers": spec.n_layers, "prefill_tokens": args.prefill,
+              "ms": (time.perf_counter() - t0) * 1e3})
+        eng.close()
+        return
     eng = DecodeEngine(g, device=0, max_seq_len=64, disable_graphs=True)
     first = int(eng.generate([11, 22, 33, 44], 1)[0])
     toks, ms = eng.decode_timed(first, 2)
     torch.cuda.synchronize()
     emit({"profile_run": spec.name, "layers": spec.n_layers, "tokens": toks.tolist(), "ms": ms})
     eng.close()
+
+
+def run_attn_profile(args):
+    """--profile-attn CTX,BATCH: benchmark configuration 3's inputs at one shape,
+    three rf_decode_attention calls (an ncu capture takes the last)."""
+    import torch
+    from ramforge_b200 import decode_attention
+    ctx, batch = (int(v) for v in args.profile_attn.split(","))
+    H, KV, hd = 32, 8, 128
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    q = torch.randn(batch, H, hd, device="cuda", generator=g)
+    k = torch.randn(batch, KV, ctx, hd, device="cuda", generator=g).half()
+    v = torch.randn(batch, KV, ctx, hd, device="cuda", generator=g).half()
+    o = torch.empty(batch, H, hd, device="cuda")
+    for _ in range(3):
+        decode_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ctx, H, KV, hd, batch, o.data_ptr())
+    torch.cuda.synchronize()
+    emit({"profile_attn": {"ctx": ctx, "batch": batch}, "finite": bool(torch.isfinite(o).all().item())})
+
+
+def pinned_h2d_gbs():
+    """Pinned host-to-device copy rate of this box (1 GiB, 5 copies, CUDA events)."""
+    import torch
+    h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    d = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    d.copy_(h, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        d.copy_(h, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    gbs = 5 * (1 << 30) / (e0.elapsed_time(e1) / 1e3) / 1e9
+    del h, d
+    return gbs
+
+
+def out_of_core(eng, spec, first_token, steps):
+    """The benchmark engine re-planned for a weight budget of three quarters of its
+    layer images plus two ring slots (rf_plan_residency): the last quarter of the
+    layers streams every step from pinned host images through the ring.  tokens/s against
+    the bound the measured pinned host-to-device rate sets for the streamed bytes."""
+    h2d = pinned_h2d_gbs()
+    d, kv, ff = spec.n_embd, spec.n_kv_heads * spec.head_dim, spec.n_ff
+    layer_est = ((d + 2 * kv) * d + d * d + 2 * ff * d + d * ff) * 144 // 256 + 8 * d  # Q4_K image, norms
+    budget = int((spec.n_layers * 3 // 4 + 2) * layer_est * 1.001)
+    mask = eng.plan_residency(budget, ring_slots=2)
+    n = mask.count(False)
+    eng.kv_reset()
+    t0 = time.perf_counter()
+    eng.generate([first_token], 1)  # builds the streamed layers' pinned images
+    setup_s = time.perf_counter() - t0
+    toks, dev_ms = eng.decode_timed(int(first_token), steps)
+    st = eng.residency_stats()
+    layer_bytes = st["host_image_bytes"] / max(1, n)
+    value = steps / (dev_ms / 1e3)
+    bound = h2d * 1e9 / (n * layer_bytes) if n else float("inf")
+    return {"api": "rf_plan_residency + rf_decode_timed", "weight_budget_bytes": budget,
+            "streamed_layers": n, "layers": spec.n_layers, "ring_slots": 2, "tokens_per_s": value,
+            "steps": steps, "layer_image_bytes": layer_bytes, "h2d_gbs": h2d,
+            "h2d_bound_tokens_per_s": bound, "frac_of_h2d_bound": value / bound, "setup_s": setup_s,
+            "ring_copies": st["ring_copies"]}
+
+
+def config5(steps):
+    """SURVEY configuration 5: the 70B shape (dim 8192, 80 layers, 64/8 heads, FFN
+    28672, vocab 128256, Q4_K layers and output, seed 4) under a 4 GiB per-GPU
+    weight budget: rf_plan_residency keeps the layers that fit beside 2 ring slots
+    and streams the rest from pinned host images every step.  Returns tokens/s
+    against the bound of the pinned host-to-device rate measured here."""
+    import torch
+    from ramforge_b200 import DecodeEngine, synth
+    spec = synth.scaled(synth.LLAMA3_8B, name="llama-70b-shape-q4k", n_embd=8192, n_layers=80, n_heads=64,
+                        n_kv_heads=8, n_ff=28672, seed=4, out_type=synth.Q4_K, context_length=4096)
+    h2d = pinned_h2d_gbs()
+    t0 = time.perf_counter()
+    g = synth.gguf_bytes(spec)
+    gen_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    eng = DecodeEngine(g, device=torch.cuda.current_device(), max_seq_len=64, ring_slots=2)
+    mask = eng.plan_residency(4 << 30, ring_slots=2)
+    load_s = time.perf_counter() - t0
+    n = mask.count(False)
+    t0 = time.perf_counter()
+    first = int(eng.generate([11, 22], 1)[0])  # also packs every streamed layer into pinned memory once
+    first_s = time.perf_counter() - t0
+    toks, dev_ms = eng.decode_timed(first, steps)
+    st = eng.residency_stats()
+    eng.close()
+    del g
+    layer_bytes = st["host_image_bytes"] / max(1, n)
+    value = steps / (dev_ms / 1e3)
+    bound = h2d * 1e9 / (n * layer_bytes)
+    return {"metric": "out-of-core decode tokens/s (70B shape Q4_K, 4 GiB weight budget)", "value": value,
+            "unit": "tokens/s", "steps": steps, "api": "rf_plan_residency + rf_decode_timed",
+            "workload": "70B-shape Q4_K greedy decode, 4 GiB of device weights, 2 ring slots",
+            "resident_layers": spec.n_layers - n, "streamed_layers": n, "layer_image_bytes": layer_bytes,
+            "roofline": {"bound": "h2d", "achieved": n * layer_bytes * value / 1e9, "peak": h2d, "unit": "GB/s",
+                         "frac": value / bound, "peak_source": "pinned host-to-device copy measured in this run"},
+            "tokens": toks.tolist(), "setup_s": {"generation": gen_s, "engine": load_s, "first_token": first_s},
+            "ring_copies": st["ring_copies"]}
+
+
+def run_config5(args):
+    """--config5: configuration 5 alone, as its own line."""
+    import torch
+    torch.cuda.set_device(0)
+    emit(config5(args.steps))
 
 
 def run_ring(args, spec):
@@ -494,6 +615,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="small eager run for ncu captures")
     ap.add_argument("--layers", type=int, default=0, help="with --profile: layer count of the model")
+    ap.add_argument("--prefill", type=int, default=0, help="with --profile: batched prefill of this many tokens")
+    ap.add_argument("--profile-attn", default="", help="CTX,BATCH: a few rf_decode_attention calls (ncu capture)")
+    ap.add_argument("--config5", action="store_true", help="70B-shape model, 4 GiB weight budget, ring (SURVEY config 5)")
+    ap.add_argument("--no-ring", action="store_true", help="leave the out-of-core measurements off the main line")
     ap.add_argument("--ring", type=int, default=0, help="out-of-core run: stream this many layers per step")
     ap.add_argument("--gemv-sweep", action="store_true", help="benchmark configuration 2: GEMV per format and shape")
     ap.add_argument("--formats", default="", help="with --gemv-sweep: comma-separated subset, e.g. Q4_K,Q6_K")
@@ -512,6 +637,12 @@ def main():
         return
     if args.profile:
         run_profile(args, spec)
+        return
+    if args.profile_attn:
+        run_attn_profile(args)
+        return
+    if args.config5:
+        run_config5(args)
         return
     if args.ring:
         run_ring(args, spec)
@@ -626,6 +757,8 @@ def main():
         "tokens": tokens, "tp_peer_sum": eng.tp_peer_sum if world > 1 else None, "prefill": prefill,
         "setup_s": {"model_generation": gen_s, "engine_load": load_s},
     }
+    if world == 1 and not args.no_ring:
+        line["out_of_core"] = out_of_core(eng, spec, first, max(4, args.steps // 4))
     eng.close()
     if world > 1:
         import torch.distributed as dist
@@ -634,6 +767,8 @@ def main():
     if rank == 0:
         if world == 1 and not args.no_attn_sweep:
             line["attention_sweep"] = attention_sweep(peak, peak_kind)
+        if world == 1 and not args.no_ring:
+            line["config5"] = config5(2)
         if world == 1 and not args.no_cpu_baseline:
             ctx = PROMPT_LEN + args.warmup
             line["cpu_baseline"] = cpu_baseline(gguf, spec, ctx, threads=1)

@@ -283,7 +283,9 @@ int rf_budget_available(const rf_engine* e, uint64_t* out);
  * ("ring:slot:<i>" budget charges), overlapping the compute of the layers before
  * it (StagingPlan's transfer/compute overlap, staging_plan.rs:46-77, which the
  * reference leaves unsupported).  With ring_slots == 0 they load, compute and
- * release in turn (load_layer/release_layer, streaming_model.rs:1081-1270). */
+ * release in turn (load_layer/release_layer, streaming_model.rs:1081-1270).  Kept
+ * layers that are not loaded (an engine created with ring_slots > 0 uploads none)
+ * are loaded from the GGUF source. */
 int rf_set_residency_plan(rf_engine* e, const uint8_t* resident_mask, int ring_slots,
                           uint64_t vram_weight_budget_bytes);
 /* The planner's choice for a weight budget (a MemoryBudget mapped onto a resident

@@ -1986,7 +1986,7 @@ int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uin
   RF_TRY(cache_clear(e));
   uint64_t resident_bytes = 0, slot_bytes = 0;
   for (uint32_t l = 0; l < e->cfg.n_layers; l++) {
-    if (mask[l] && e->layers[l].resident) resident_bytes += e->layers[l].bytes;
+    if (mask[l]) resident_bytes += e->layers[l].resident ? e->layers[l].bytes : layer_image_bytes(e, (int)l);
     if (!mask[l]) slot_bytes = std::max(slot_bytes, layer_image_bytes(e, (int)l));
   }
   const uint64_t need = resident_bytes + (uint64_t)ring_slots * slot_bytes;
@@ -2001,6 +2001,10 @@ int rf_set_residency_plan(rf_engine* e, const uint8_t* mask, int ring_slots, uin
       e->stats.evictions++;
     }
   }
+  // layers the plan keeps that are not loaded yet (an engine created with a ring
+  // uploads none) are loaded now from the GGUF source
+  for (uint32_t l = 0; l < e->cfg.n_layers; l++)
+    if (mask[l] && !e->layers[l].resident && e->src) RF_TRY(load_layer_gguf(e, (int)l));
   if (ring_slots != e->rt.ring_slots) free_ring(e);
   e->rt.ring_slots = ring_slots;
   return RF_OK;

@@ -172,3 +172,20 @@ def test_persistent_tensors_over_a_quarter_of_the_budget_stay_in_host_memory():
     assert b.generate(prompt, 16).tolist() == a.generate(prompt, 16).tolist()
     a.close()
     b.close()
+
+
+def test_plan_loads_the_resident_layers_of_an_engine_created_with_a_ring(gguf):
+    # an engine created with ring_slots > 0 uploads no layer; the plan loads the
+    # layers it keeps, and only the others stream
+    per = _layer_bytes(gguf)
+    a = DecodeEngine(gguf, max_seq_len=32)
+    b = DecodeEngine(gguf, max_seq_len=32, ring_slots=2)
+    assert not any(b.layer_is_resident(i) for i in range(6))
+    mask = b.plan_residency(int(per * 5.5), ring_slots=2)
+    assert mask == [True, True, True, False, False, False]
+    assert [b.layer_is_resident(i) for i in range(6)] == mask
+    for pos, tok in enumerate([5, 77, 301]):
+        assert np.array_equal(a.forward_single_streaming(tok, pos), b.forward_single_streaming(tok, pos)), pos
+    assert b.residency_stats()["ring_copies"] == 3 * 3
+    a.close()
+    b.close()
