@@ -438,8 +438,9 @@ GGUF_BYTES_PER_256 = {"Q8_0": 272, "Q4_0": 144, "Q4_K": 144, "Q5_K": 176, "Q6_K"
 
 def run_gemv_sweep(args):
     """--gemv-sweep: benchmark configuration 2, the standalone quantized GEMV
-    (rf_qmatvec) of every tiled format on the four config-2 shapes at batch 1, one
-    JSON line each.  Time: CUDA events on the launching stream around 100 calls
+    (rf_qmatvec) of every tiled format on the four config-2 shapes at the --batches
+    sizes (default 1), one JSON line each; past batch 1, Q4_K and Q8_0 lines also time
+    the tensor-core GEMM (rf_qgemm) on the same inputs.  Time: CUDA events on the launching stream around 100 calls
     after 3 warm-up calls, rotating over distinct copies of the matrix that
     together exceed 4x the 126 MB L2.  `gbs` is algorithmic bytes (GGUF bytes
     M*K*b plus 4K + 4M) over that time; `moved_bytes` is the packed matrix."""
@@ -451,6 +452,7 @@ def run_gemv_sweep(args):
     shapes = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
     stream = torch.cuda.current_stream()
     want = set(f for f in args.formats.split(",") if f) or set(names.values())
+    batches = [int(b) for b in args.batches.split(",") if b]
     for gtype, name in names.items():
         if name not in want:
             continue
@@ -463,24 +465,43 @@ def run_gemv_sweep(args):
             copies = [first] + [QMatrix(gtype, raw, M, K)
                                 for _ in range(min(63, -(-4 * 126_000_000 // first.device_bytes) - 1))]
             del raw
-            x = torch.randn(K, device="cuda")
-            y = torch.empty(M, device="cuda")
-            for i in range(3):
-                copies[i % len(copies)].matvec(x.data_ptr(), y.data_ptr(), 1, stream.cuda_stream)
-            n = 100
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize()
-            e0.record(stream)
-            for i in range(n):
-                copies[i % len(copies)].matvec(x.data_ptr(), y.data_ptr(), 1, stream.cuda_stream)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / n
-            alg = M * K * GGUF_BYTES_PER_256[name] / 256 + 4 * K + 4 * M
-            emit({"metric": "standalone GEMV GB/s (benchmark configuration 2)", "format": name, "M": M, "K": K,
-                  "batch": 1, "us_per_call": us, "gbs": alg / us / 1e3, "unit": "GB/s",
-                  "frac": alg / us / 1e3 / peak, "peak": peak, "peak_source": f"{peak_kind} hbm_gbs",
-                  "algorithmic_bytes": alg, "moved_bytes": first.device_bytes, "copies": len(copies), "calls": n})
+            def timed(fn, n):
+                for i in range(3):
+                    fn(i)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record(stream)
+                for i in range(n):
+                    fn(i)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                return e0.elapsed_time(e1) * 1e3 / n
+
+            for batch in batches:
+                x = torch.randn(batch, K, device="cuda")
+                y = torch.empty(batch, M, device="cuda")
+                n = max(10, 100 // batch)
+                def gemv(i):  # rf_qmatvec takes up to 8 vectors a call
+                    for b0 in range(0, batch, 8):
+                        nb = min(8, batch - b0)
+                        copies[i % len(copies)].matvec(x[b0].data_ptr(), y[b0].data_ptr(), nb, stream.cuda_stream)
+
+                us = timed(gemv, n)
+                alg = M * K * GGUF_BYTES_PER_256[name] / 256 + 4 * K * batch + 4 * M * batch
+                line = {"metric": "standalone GEMV GB/s (benchmark configuration 2)", "format": name, "M": M,
+                        "K": K, "batch": batch, "us_per_call": us, "gbs": alg / us / 1e3, "unit": "GB/s",
+                        "frac": alg / us / 1e3 / peak, "peak": peak, "peak_source": f"{peak_kind} hbm_gbs",
+                        "algorithmic_bytes": alg, "moved_bytes": first.device_bytes, "copies": len(copies),
+                        "calls": n, "api": "rf_qmatvec (CUDA cores, one pass over the weights per vector, 8 vectors a call)"}
+                if batch > 1 and gtype in (synth.Q4_K, synth.Q8_0):
+                    # the tensor-core GEMM of the prompt path on the same inputs: where it starts to pay
+                    gus = timed(lambda i: copies[i % len(copies)].gemm(x.data_ptr(), y.data_ptr(), batch,
+                                                                       stream.cuda_stream), n)
+                    line["tensor_core"] = {"api": "rf_qgemm (tcgen05, one pass per 128 vectors)", "us_per_call": gus,
+                                           "gbs": alg / gus / 1e3, "tflops": 2.0 * M * K * batch / gus / 1e6,
+                                           "faster_than_gemv": gus < us}
+                emit(line)
+                del x, y
             for m in copies:
                 m.close()
             del copies
@@ -622,6 +643,7 @@ def main():
     ap.add_argument("--ring", type=int, default=0, help="out-of-core run: stream this many layers per step")
     ap.add_argument("--gemv-sweep", action="store_true", help="benchmark configuration 2: GEMV per format and shape")
     ap.add_argument("--formats", default="", help="with --gemv-sweep: comma-separated subset, e.g. Q4_K,Q6_K")
+    ap.add_argument("--batches", default="1", help="with --gemv-sweep: batch sizes, e.g. 1,4,8,16,32")
     ap.add_argument("--attn-sweep", action="store_true", help="benchmark configuration 3: decode attention GB/s")
     ap.add_argument("--no-attn-sweep", action="store_true", help="leave the attention sweep off the main line")
     args = ap.parse_args()
