@@ -34,7 +34,7 @@ namespace rf {
 
 constexpr int AS_WARPS = ATT_WARPS;  // the merge tail's thread count
 constexpr int AS_THREADS = AS_WARPS * 32;
-constexpr int AS_STAGES = 3;
+constexpr int AS_STAGES = 2;  // two, not three: 3 CTAs share an SM (batch 8, ctx 32768: 0.70 vs 0.62 of peak)
 
 // Positions per tile: 32 (position, head) dot products a butterfly.
 template <int G>
