@@ -514,9 +514,10 @@ ATTN_SHAPES = [(b, c) for b in (1, 8) for c in (512, 2048, 8192, 32768)]
 def attention_sweep(peak: float, peak_kind: str, iters: int = 50):
     """Benchmark configuration 3: rf_decode_attention (32 query heads over 8 KV
     heads of head_dim 128, f16 K/V, one query token per sequence) at batch 1/8 x
-    context 512/2048/8192/32768.  Time: CUDA events on the launching stream around
-    `iters` calls after 3 warm-up calls, rotating over distinct K/V buffers that
-    together exceed 4x the 126 MB L2 (one buffer when a single one already does).
+    context 512/2048/8192/32768.  Time: CUDA events around the replay of one CUDA
+    graph holding `iters` calls (captured after 3 warm-up calls, so the figure is
+    device time, not the host's launch rate), rotating over distinct K/V buffers
+    that together exceed 4x the 126 MB L2 (one buffer when a single one does).
     Algorithmic bytes per call: batch*ctx*KV*hd*2*2 (K and V f16) + batch*H*hd*4*2
     (query in, output out)."""
     import torch
@@ -533,21 +534,29 @@ def attention_sweep(peak: float, peak_kind: str, iters: int = 50):
         q = torch.randn(batch, H, hd, device="cuda")
         o = torch.empty(batch, H, hd, device="cuda")
 
-        def call(i):
+        def call(i, st):
             j = i % copies
             decode_attention(q.data_ptr(), k[j].data_ptr(), v[j].data_ptr(), ctx, H, KV, hd, batch, o.data_ptr(),
-                             stream.cuda_stream)
+                             st.cuda_stream)
 
-        for i in range(3):
-            call(i)
+        for i in range(3):  # also creates the library's workspace, before the capture
+            call(i, stream)
+        torch.cuda.synchronize()
+        # the timed calls replay from one captured graph: device time, not the host's launch rate
+        side = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(iters):
+                call(i, side)
+        graph.replay()  # warm
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(stream)
-        for i in range(iters):
-            call(i)
+        graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / iters
+        del graph
         alg = per_copy + batch * H * hd * 4 * 2
         rows.append({"batch": batch, "ctx": ctx, "us_per_call": us, "gbs": alg / us / 1e3,
                      "frac": alg / us / 1e3 / peak, "algorithmic_bytes": alg, "copies": copies})

@@ -134,7 +134,7 @@ __device__ __forceinline__ void warp_transpose_sum(float* v, int lane) {
 // merges the nsplit partials (max-rescaled sums) into out_b; the others return.
 // Run by ATT_THREADS threads (t = thread index, warp/lane of t); `sync` is their
 // barrier, s_w [ATT_MERGE_SPLITS][G] and s_last shared scratch.
-template <int DPL, int G, class Sync>
+template <int DPL, int G, int MR_MAX, class Sync>
 __device__ __forceinline__ void attn_merge_tail(const AttnArgs& a, int b, int kvh, int nsplit, float* out_b,
                                                 float (*s_w)[G], int* s_last, int t, Sync&& sync) {
   const int lane = t & 31, warp = t >> 5, hd = a.head_dim;
@@ -179,20 +179,24 @@ __device__ __forceinline__ void attn_merge_tail(const AttnArgs& a, int b, int kv
       for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) s_w[lane + 32 * j][h] = ms[j] / L;
     }
     sync();
-    // every output element: sum_s w_s * O_s.  A thread owns EPT elements and
-    // loads four splits of all of them per round, every load of a round in
-    // flight together.
+    // every output element: sum_s w_s * O_s in split order.  A thread owns EPT
+    // elements and loads MR splits of all of them per round, every load of a round
+    // in flight together: each round is one L2 round trip, so a caller that merges
+    // tens of splits takes MR_MAX up to 16 (at most 64 values a thread); the
+    // register-load kernel keeps 4, which keeps its registers where its occupancy
+    // in the decode step needs them.
     constexpr int EPT = (G * DPL * 32 + ATT_THREADS - 1) / ATT_THREADS;  // hd <= 32*DPL
+    constexpr int MR = 64 / EPT < 4 ? 4 : (64 / EPT > MR_MAX ? MR_MAX : 64 / EPT);
     float O[EPT];
 #pragma unroll
     for (int k = 0; k < EPT; k++) O[k] = 0.f;
-    for (int s0 = 0; s0 < nsplit; s0 += 4) {
-      float v[EPT][4];
+    for (int s0 = 0; s0 < nsplit; s0 += MR) {
+      float v[EPT][MR];
 #pragma unroll
       for (int k = 0; k < EPT; k++) {
         const int i = t + k * ATT_THREADS, h = i / hd, d = i % hd;
 #pragma unroll
-        for (int j = 0; j < 4; j++)
+        for (int j = 0; j < MR; j++)
           v[k][j] = i < G * hd && s0 + j < nsplit ? __ldcg(pall + ((size_t)(s0 + j) * G + h) * (hd + 2) + d) : 0.f;
       }
 #pragma unroll
@@ -200,7 +204,7 @@ __device__ __forceinline__ void attn_merge_tail(const AttnArgs& a, int b, int kv
         const int i = t + k * ATT_THREADS, h = i / hd;
         if (i < G * hd) {
 #pragma unroll
-          for (int j = 0; j < 4; j++)
+          for (int j = 0; j < MR; j++)
             if (s0 + j < nsplit) O[k] = fmaf(s_w[s0 + j][h], v[k][j], O[k]);
         }
       }
@@ -407,7 +411,7 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kvh, int split,
     __stcg(part + (size_t)t * (hd + 2) + hd, sm[t]);
     __stcg(part + (size_t)t * (hd + 2) + hd + 1, sl[t]);
   }
-  attn_merge_tail<DPL, G>(a, b, kvh, nsplit, out_b, s_w, s_last, t, [&] { group_sync(bar); });
+  attn_merge_tail<DPL, G, 4>(a, b, kvh, nsplit, out_b, s_w, s_last, t, [&] { group_sync(bar); });
 }
 
 }  // namespace rf

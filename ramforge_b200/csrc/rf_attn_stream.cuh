@@ -56,10 +56,12 @@ __host__ __device__ constexpr size_t as_smem_bytes() {
          4 * ((size_t)AS_WARPS * as_tpw<G>() * G + ATT_MERGE_SPLITS * G + AS_WARPS * 2 * G + 4);
 }
 
-// Splits of a context: at most one per 64 positions... as many as fill `slots`
-// CTAs for the (sequence, KV head) pairs, and no more than the workspace holds.
+// Splits of a context: at most one per 256 positions (4 tiles a warp, so a
+// split's fixed costs, from its first copy to its partial, are spread over a
+// pipeline of tiles), as many as fill `slots` CTAs for the (sequence, KV head)
+// pairs, and no more than the workspace holds.
 __host__ __device__ inline int as_nsplit(int ctx, int max_splits, int slots, int units) {
-  int s = (ctx + AS_WARPS * 16 - 1) / (AS_WARPS * 16);
+  int s = (ctx + AS_WARPS * 64 - 1) / (AS_WARPS * 64);
   const int fill = units > 0 ? slots / units : 1;
   s = s < fill ? s : fill;
   s = s < max_splits ? s : max_splits;
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(AttnArgs a, int
     }
   }
   if (nsplit == 1) return;
-  attn_merge_tail<DPL, G>(a, b, kvh, nsplit, out_b, s_w, s_last, t, [] { __syncthreads(); });
+  attn_merge_tail<DPL, G, 16>(a, b, kvh, nsplit, out_b, s_w, s_last, t, [] { __syncthreads(); });
 }
 
 }  // namespace rf
