@@ -27,6 +27,8 @@
 // expiry the kernel sets bit 1 of *a.err (when given), waits (bounded) for its
 // own copies in flight, and finishes with the values it has.
 #pragma once
+#include <type_traits>
+
 #include "rf_attn.cuh"
 #include "rf_tc.cuh"
 
@@ -66,6 +68,26 @@ __host__ __device__ inline int as_nsplit(int ctx, int max_splits, int slots, int
   s = s < fill ? s : fill;
   s = s < max_splits ? s : max_splits;
   return s < 1 ? 1 : s;
+}
+
+// DPL consecutive f16 of a shared-memory row as f32.
+template <int DPL>
+__device__ __forceinline__ void half_row(const __half* r, float (&v)[DPL]) {
+  if constexpr (DPL == 4) {
+    const uint2 w = *reinterpret_cast<const uint2*>(r);
+    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+    v[0] = f0.x;
+    v[1 % DPL] = f0.y;
+    v[2 % DPL] = f1.x;
+    v[3 % DPL] = f1.y;
+  } else if constexpr (DPL == 2) {
+    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(r));
+    v[0] = f0.x;
+    v[1 % DPL] = f0.y;
+  } else {
+    v[0] = __half2float(r[0]);
+  }
 }
 
 template <int G, int HD>
@@ -135,11 +157,14 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(AttnArgs a, int
   const float div = sqrtf((float)HD);  // score = dot / sqrt(hd)  (compute.rs:530)
 
   float m_run = -INFINITY, l_run = 0.f;  // softmax state of head lane % G
-  float acc[G][DPL];
+  // output sums of heads (2hp, 2hp+1) as float2 pairs, so that p*v accumulates with
+  // packed fma.rn.f32x2 (each half the scalar fmaf's rounding; G = 1 leaves .y at 0)
+  constexpr int GP = (G + 1) / 2;
+  float2 acc[GP][DPL];
 #pragma unroll
-  for (int h = 0; h < G; h++)
+  for (int hp = 0; hp < GP; hp++)
 #pragma unroll
-    for (int i = 0; i < DPL; i++) acc[h][i] = 0.f;
+    for (int i = 0; i < DPL; i++) acc[hp][i] = make_float2(0.f, 0.f);
   float* ew = ew_all + warp * E;
   bool ok = true;
   int waited = 0;  // tiles whose copies have completed
@@ -151,120 +176,104 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(AttnArgs a, int
     const __half* kt = reinterpret_cast<const __half*>(wslots + (size_t)s * 2 * TB);
     const __half* vt = reinterpret_cast<const __half*>(wslots + (size_t)s * 2 * TB + TB);
     const int pa = tile_pos(i);
-    // scores: value c = j*G + h (position pa + j, head h), 32 at a time
-    float sc[NV];
+    // FULL: every position of the tile is a history row of this split (most tiles),
+    // so the per-position checks drop out
+    auto tile = [&](auto full_tag) {
+      constexpr bool FULL = decltype(full_tag)::value;
+      // scores: value c = j*G + h (position pa + j, head h), 32 at a time
+      float sc[NV];
 #pragma unroll
-    for (int c0 = 0; c0 < E; c0 += 32) {
-      float v[32];
+      for (int c0 = 0; c0 < E; c0 += 32) {
+        float v[32];
 #pragma unroll
-      for (int jj = 0; jj < 32 / G; jj++) {
-        const int j = c0 / G + jj, p = pa + j;
-        float k[DPL];
-        if (p < nhist && p < p1) {
-          const __half* kr = kt + (size_t)j * HD + d0;
-          if constexpr (DPL == 4) {
-            const uint2 w = *reinterpret_cast<const uint2*>(kr);
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
-            k[0] = f0.x;
-            k[1 % DPL] = f0.y;
-            k[2 % DPL] = f1.x;
-            k[3 % DPL] = f1.y;
-          } else if constexpr (DPL == 2) {
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(kr));
-            k[0] = f0.x;
-            k[1 % DPL] = f0.y;
+        for (int jj = 0; jj < 32 / G; jj++) {
+          const int j = c0 / G + jj, p = pa + j;
+          float k[DPL];
+          if (FULL || (p < nhist && p < p1)) {
+            half_row<DPL>(kt + (size_t)j * HD + d0, k);
           } else {
-            k[0] = __half2float(kr[0]);
+#pragma unroll
+            for (int d = 0; d < DPL; d++) k[d] = p < p1 ? kcur[d] : 0.f;
           }
+#pragma unroll
+          for (int h = 0; h < G; h++) {
+            float dot = 0.f;
+#pragma unroll
+            for (int d = 0; d < DPL; d++) dot = fmaf(qr[h][d], k[d], dot);
+            v[jj * G + h] = dot;
+          }
+        }
+        warp_transpose_sum<32, 16>(v, lane);
+        if constexpr (FULL) {
+          sc[c0 / 32] = v[0] / div;
+        } else {
+          const int p = pa + (c0 + lane) / G;
+          const bool valid = p < p1 && (p < nhist || with_cur);
+          sc[c0 / 32] = valid ? v[0] / div : -INFINITY;
+        }
+      }
+      // running softmax of head lane % G (softmax_reference, compute.rs:363-384)
+      float mx = sc[0];
+#pragma unroll
+      for (int k = 1; k < NV; k++) mx = fmaxf(mx, sc[k]);
+#pragma unroll
+      for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float m_new = fmaxf(m_run, mx);
+      float ls = 0.f;
+#pragma unroll
+      for (int k = 0; k < NV; k++) {
+        const float e = expf(sc[k] - m_new);
+        ew[32 * k + lane] = e;
+        ls += e;
+      }
+#pragma unroll
+      for (int o = G; o < 32; o <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+      const float f = expf(m_run - m_new);
+      l_run = l_run * f + ls;
+      m_run = m_new;
+      __syncwarp();
+#pragma unroll
+      for (int hp = 0; hp < GP; hp++) {
+        const float f0 = __shfl_sync(0xffffffffu, f, 2 * hp);
+        const float f1 = G > 1 ? __shfl_sync(0xffffffffu, f, 2 * hp + 1) : 0.f;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) {
+          acc[hp][d].x *= f0;
+          acc[hp][d].y *= f1;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < TPW; j++) {
+        const int p = pa + j;
+        if (!FULL && p >= p1) break;
+        float v[DPL];
+        if (FULL || p < nhist) {
+          half_row<DPL>(vt + (size_t)j * HD + d0, v);
         } else {
 #pragma unroll
-          for (int d = 0; d < DPL; d++) k[d] = p < p1 ? kcur[d] : 0.f;
+          for (int d = 0; d < DPL; d++) v[d] = vcur[d];
         }
+        float2 e2[GP];
+        if constexpr (G % 4 == 0) {
 #pragma unroll
-        for (int h = 0; h < G; h++) {
-          float dot = 0.f;
-#pragma unroll
-          for (int d = 0; d < DPL; d++) dot = fmaf(qr[h][d], k[d], dot);
-          v[jj * G + h] = dot;
-        }
-      }
-      warp_transpose_sum<32, 16>(v, lane);
-      const int p = pa + (c0 + lane) / G;
-      const bool valid = p < p1 && (p < nhist || with_cur);
-      sc[c0 / 32] = valid ? v[0] / div : -INFINITY;
-    }
-    // running softmax of head lane % G (softmax_reference, compute.rs:363-384)
-    float mx = sc[0];
-#pragma unroll
-    for (int k = 1; k < NV; k++) mx = fmaxf(mx, sc[k]);
-#pragma unroll
-    for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float m_new = fmaxf(m_run, mx);
-    float ls = 0.f;
-#pragma unroll
-    for (int k = 0; k < NV; k++) {
-      const float e = expf(sc[k] - m_new);
-      ew[32 * k + lane] = e;
-      ls += e;
-    }
-#pragma unroll
-    for (int o = G; o < 32; o <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
-    const float f = expf(m_run - m_new);
-    l_run = l_run * f + ls;
-    m_run = m_new;
-    __syncwarp();
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-      const float fh = __shfl_sync(0xffffffffu, f, h);
-#pragma unroll
-      for (int d = 0; d < DPL; d++) acc[h][d] *= fh;
-    }
-#pragma unroll
-    for (int j = 0; j < TPW; j++) {
-      const int p = pa + j;
-      if (p >= p1) break;
-      float v[DPL];
-      if (p < nhist) {
-        const __half* vr = vt + (size_t)j * HD + d0;
-        if constexpr (DPL == 4) {
-          const uint2 w = *reinterpret_cast<const uint2*>(vr);
-          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
-          const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
-          v[0] = f0.x;
-          v[1 % DPL] = f0.y;
-          v[2 % DPL] = f1.x;
-          v[3 % DPL] = f1.y;
-        } else if constexpr (DPL == 2) {
-          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(vr));
-          v[0] = f0.x;
-          v[1 % DPL] = f0.y;
+          for (int h = 0; h < G; h += 4) {
+            const float4 e4 = *reinterpret_cast<const float4*>(ew + j * G + h);
+            e2[h / 2] = make_float2(e4.x, e4.y);
+            e2[h / 2 + 1] = make_float2(e4.z, e4.w);
+          }
+        } else if constexpr (G == 2) {
+          e2[0] = *reinterpret_cast<const float2*>(ew + j * 2);
         } else {
-          v[0] = __half2float(vr[0]);
+          e2[0] = make_float2(ew[j], 0.f);
         }
-      } else {
 #pragma unroll
-        for (int d = 0; d < DPL; d++) v[d] = vcur[d];
+        for (int hp = 0; hp < GP; hp++)
+#pragma unroll
+          for (int d = 0; d < DPL; d++) acc[hp][d] = __ffma2_rn(e2[hp], make_float2(v[d], v[d]), acc[hp][d]);
       }
-      float e[G];
-      if constexpr (G % 4 == 0) {
-#pragma unroll
-        for (int h = 0; h < G; h += 4) {
-          const float4 e4 = *reinterpret_cast<const float4*>(ew + j * G + h);
-          e[h] = e4.x;
-          e[h + 1] = e4.y;
-          e[h + 2] = e4.z;
-          e[h + 3] = e4.w;
-        }
-      } else {
-#pragma unroll
-        for (int h = 0; h < G; h++) e[h] = ew[j * G + h];
-      }
-#pragma unroll
-      for (int h = 0; h < G; h++)
-#pragma unroll
-        for (int d = 0; d < DPL; d++) acc[h][d] = fmaf(e[h], v[d], acc[h][d]);
-    }
+    };
+    if (pa + TPW <= min(p1, nhist)) tile(std::true_type{});
+    else tile(std::false_type{});
     __syncwarp();  // slot s and the weights are read
     if (lane == 0 && i + AS_STAGES < nt) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -292,7 +301,7 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(AttnArgs a, int
 #pragma unroll
   for (int h = 0; h < G; h++)
 #pragma unroll
-    for (int d = 0; d < DPL; d++) wacc[h * HD + d0 + d] = acc[h][d];
+    for (int d = 0; d < DPL; d++) wacc[h * HD + d0 + d] = (h & 1) ? acc[h / 2][d].y : acc[h / 2][d].x;
   __syncthreads();
   float* out_b = a.out + ((size_t)b * a.n_heads + (size_t)kvh * G) * HD;
   const size_t slot = ((size_t)b * a.n_kv_heads + kvh) * a.max_splits;
