@@ -139,10 +139,16 @@ __device__ __forceinline__ void attn_merge_tail(const AttnArgs& a, int b, int kv
                                                 float (*s_w)[G], int* s_last, int t, Sync&& sync) {
   const int lane = t & 31, warp = t >> 5, hd = a.head_dim;
   const size_t slot = ((size_t)b * a.n_kv_heads + kvh) * a.max_splits;
-  __threadfence();
+  // the group barrier orders every thread's partial before thread 0's arrival,
+  // whose release is cumulative; its acquire, then the barrier, orders the other
+  // splits' partials before every thread's loads below
   sync();
   if (t == 0) {
-    const unsigned prev = atomicAdd(&a.counters[(size_t)b * a.n_kv_heads + kvh], 1u);
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(prev)
+                 : "l"(&a.counters[(size_t)b * a.n_kv_heads + kvh])
+                 : "memory");
     *s_last = prev == (unsigned)(nsplit - 1);
   }
   sync();
@@ -150,7 +156,6 @@ __device__ __forceinline__ void attn_merge_tail(const AttnArgs& a, int b, int kv
     sync();
     return;
   }
-  __threadfence();
   const float* pall = a.part + slot * (size_t)G * (hd + 2);
   if (nsplit <= ATT_MERGE_SPLITS) {
     // one warp per head: split weights exp(m_s - M) / sum_s exp(m_s - M) l_s in one load round

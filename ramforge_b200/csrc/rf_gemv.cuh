@@ -1010,13 +1010,16 @@ __device__ __forceinline__ void qgemv_body(const PackedMat& W, const float* __re
     float* p = part + a * QT_ROWS;
     __stcg(p + lane, s0);
     __stcg(p + 32 + lane, s1);
-    __threadfence();  // every lane's partial before the arrival (each lane fences its own stores)
+    // __syncwarp orders every lane's partial before lane 0's arrival, whose
+    // release is cumulative (the same idiom as a CTA barrier followed by one
+    // thread's release); its acquire, then __syncwarp, orders the other parts
+    // before every lane's loads below
     __syncwarp();
     unsigned old = 0;
-    if (lane == 0) old = atomicAdd(cnt + T, len_c);
+    if (lane == 0) old = arrive_acq_rel(cnt + T, len_c);
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old + len_c != tp) continue;
-    __threadfence();  // the other parts, published before their arrivals, are read after this one
+    __syncwarp();
     const uint64_t G = gridDim.x;
     float r0 = 0.f, r1 = 0.f;
     for (uint32_t k = 0; k < tp;) {
