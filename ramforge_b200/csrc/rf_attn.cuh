@@ -158,6 +158,26 @@ __device__ __forceinline__ void attn_merge_tail(const AttnArgs& a, int b, int kv
   }
   const float* pall = a.part + slot * (size_t)G * (hd + 2);
   if (nsplit <= ATT_MERGE_SPLITS) {
+    // every output element: sum_s w_s * O_s in split order.  A thread owns EPT
+    // elements and loads MR splits of all of them per round, every load of a round
+    // in flight together: each round is one L2 round trip, so a caller that merges
+    // tens of splits takes MR_MAX up to 16 (at most 64 values a thread); the
+    // register-load kernel keeps 4, which keeps its registers where its occupancy
+    // in the decode step needs them.  The first round is issued before the split
+    // weights are computed (it does not depend on them), so the two overlap.
+    constexpr int EPT = (G * DPL * 32 + ATT_THREADS - 1) / ATT_THREADS;  // hd <= 32*DPL
+    constexpr int MR = 64 / EPT < 4 ? 4 : (64 / EPT > MR_MAX ? MR_MAX : 64 / EPT);
+    float v[EPT][MR];
+    auto load_round = [&](int s0) {
+#pragma unroll
+      for (int k = 0; k < EPT; k++) {
+        const int i = t + k * ATT_THREADS, h = i / hd, d = i % hd;
+#pragma unroll
+        for (int j = 0; j < MR; j++)
+          v[k][j] = i < G * hd && s0 + j < nsplit ? __ldcg(pall + ((size_t)(s0 + j) * G + h) * (hd + 2) + d) : 0.f;
+      }
+    };
+    load_round(0);
     // one warp per head: split weights exp(m_s - M) / sum_s exp(m_s - M) l_s in one load round
     for (int h = warp; h < G; h += ATT_WARPS) {
       float ms[ATT_MERGE_SPLITS / 32], ls[ATT_MERGE_SPLITS / 32];
@@ -184,26 +204,11 @@ __device__ __forceinline__ void attn_merge_tail(const AttnArgs& a, int b, int kv
       for (int j = 0; j < ATT_MERGE_SPLITS / 32; j++) s_w[lane + 32 * j][h] = ms[j] / L;
     }
     sync();
-    // every output element: sum_s w_s * O_s in split order.  A thread owns EPT
-    // elements and loads MR splits of all of them per round, every load of a round
-    // in flight together: each round is one L2 round trip, so a caller that merges
-    // tens of splits takes MR_MAX up to 16 (at most 64 values a thread); the
-    // register-load kernel keeps 4, which keeps its registers where its occupancy
-    // in the decode step needs them.
-    constexpr int EPT = (G * DPL * 32 + ATT_THREADS - 1) / ATT_THREADS;  // hd <= 32*DPL
-    constexpr int MR = 64 / EPT < 4 ? 4 : (64 / EPT > MR_MAX ? MR_MAX : 64 / EPT);
     float O[EPT];
 #pragma unroll
     for (int k = 0; k < EPT; k++) O[k] = 0.f;
     for (int s0 = 0; s0 < nsplit; s0 += MR) {
-      float v[EPT][MR];
-#pragma unroll
-      for (int k = 0; k < EPT; k++) {
-        const int i = t + k * ATT_THREADS, h = i / hd, d = i % hd;
-#pragma unroll
-        for (int j = 0; j < MR; j++)
-          v[k][j] = i < G * hd && s0 + j < nsplit ? __ldcg(pall + ((size_t)(s0 + j) * G + h) * (hd + 2) + d) : 0.f;
-      }
+      if (s0 > 0) load_round(s0);
 #pragma unroll
       for (int k = 0; k < EPT; k++) {
         const int i = t + k * ATT_THREADS, h = i / hd;
