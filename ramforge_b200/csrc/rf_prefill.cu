@@ -79,17 +79,48 @@ __global__ void __launch_bounds__(256) prefill_split_kernel(const float* __restr
 }
 
 // ---------------------------------------------------------------------------
-// Weights of one K step -> shared memory.  Thread t dequantizes half a row's
-// step: row r = t / 2 of the CTA's 128, 32 of the step's 64 elements, with the
-// reference's decode (Q4_K: (d*sc)*q - dmin*m, quant.rs:228-254; Q8_0: q*d,
-// quant.rs:176-180), and stores hi and lo into the canonical A blocks.
+// Weights of one K step -> shared memory, in two parts so that the next step's
+// loads are in flight while this step is converted.  Thread t handles half a
+// row's step: row r = t / 2 of the CTA's 128, 32 of the step's 64 elements.
+// pg_load fetches the raw words (quant bytes and scales), pg_dequant_step
+// applies the reference's decode (Q4_K: (d*sc)*q - dmin*m, quant.rs:228-254;
+// Q8_0: q*d, quant.rs:176-180) and stores hi and lo into the canonical A blocks.
 // ---------------------------------------------------------------------------
+struct PgRaw {
+  uint4 q0, q1;  // Q4_K: q0 = 16 quant bytes, q1 = the row's 16-byte header; Q8_0: the 32 quant bytes
+  uint32_t d;    // Q8_0: the block's f16 scale bits
+};
+
 template <int FMT>
-__device__ __forceinline__ void pg_dequant_step(const PackedMat& W, uint32_t m0, uint32_t ks, __nv_bfloat16* a_hi,
-                                                __nv_bfloat16* a_lo) {
+__device__ __forceinline__ PgRaw pg_load(const PackedMat& W, uint32_t m0, uint32_t ks) {
   const uint32_t r = threadIdx.x >> 1, h = threadIdx.x & 1;
-  const uint32_t row = m0 + r;  // < W.Mp (rows padded to 64 with zero rows)
+  const uint32_t row = m0 + r;  // rows past W.Mp (the last 64-row tile) are zero rows
   const uint32_t tile = row / QT_ROWS, lr = row % QT_ROWS;
+  PgRaw raw{};
+  if (row >= W.Mp) return raw;
+  if constexpr (FMT == T_Q4_K) {
+    // step ks = chunk ks/4, piece c = ks%4: bytes 32c.. of the super-block; byte l
+    // holds element 64c + l (low nibble) and 64c + 32 + l (high nibble)
+    const uint32_t kc = ks / 4, c = ks % 4;
+    const uint64_t item = (uint64_t)tile * W.nk + kc;
+    raw.q0 = *reinterpret_cast<const uint4*>(W.qs + (item * 4 + c) * (QT_ROWS * 32) + lr * 32 + 16 * h);
+    raw.q1 = *reinterpret_cast<const uint4*>(W.sc + (item * QT_ROWS + lr) * 16);
+  } else {  // Q8_0: step ks = pieces 2(ks%2), 2(ks%2)+1 of chunk ks/2 (one 32-element block each)
+    const uint32_t kc = ks / 2, blk = 2 * (ks % 2) + h;
+    const uint64_t item = (uint64_t)tile * W.nk + kc;
+    const uint8_t* qp = W.qs + (item * 4 + blk) * (QT_ROWS * 32) + lr * 32;
+    raw.q0 = *reinterpret_cast<const uint4*>(qp);
+    raw.q1 = *reinterpret_cast<const uint4*>(qp + 16);
+    raw.d = *reinterpret_cast<const uint16_t*>(W.sc + (item * QT_ROWS + lr) * 8 + 2 * blk);
+  }
+  return raw;
+}
+
+template <int FMT>
+__device__ __forceinline__ void pg_dequant_step(const PackedMat& W, uint32_t m0, uint32_t ks, const PgRaw& raw,
+                                                __nv_bfloat16* a_hi, __nv_bfloat16* a_lo) {
+  const uint32_t r = threadIdx.x >> 1, h = threadIdx.x & 1;
+  const uint32_t row = m0 + r;
   float v[32];  // elements this thread produces, at step offsets kidx[]
   uint32_t kidx[32];
   if (row >= W.Mp) {  // past the last 64-row tile: zero rows
@@ -99,21 +130,15 @@ __device__ __forceinline__ void pg_dequant_step(const PackedMat& W, uint32_t m0,
       kidx[i] = 32 * h + i;
     }
   } else if constexpr (FMT == T_Q4_K) {
-    // step ks = chunk ks/4, piece c = ks%4: bytes 32c.. of the super-block; byte l
-    // holds element 64c + l (low nibble) and 64c + 32 + l (high nibble)
-    const uint32_t kc = ks / 4, c = ks % 4;
-    const uint64_t item = (uint64_t)tile * W.nk + kc;
-    const uint4 q = *reinterpret_cast<const uint4*>(W.qs + (item * 4 + c) * (QT_ROWS * 32) + lr * 32 + 16 * h);
-    const uint8_t* hd = W.sc + (item * QT_ROWS + lr) * 16;
-    const uint4 hw = *reinterpret_cast<const uint4*>(hd);
-    const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hw);
+    const uint32_t c = ks % 4;
+    const uint8_t* hb = reinterpret_cast<const uint8_t*>(&raw.q1);
     const float d = h2f(hb[0] | (hb[1] << 8)), dmin = h2f(hb[2] | (hb[3] << 8));
     uint32_t sc0, m0v, sc1, m1v;
     k4_scale_min(hb + 4, (int)(2 * c), &sc0, &m0v);
     k4_scale_min(hb + 4, (int)(2 * c + 1), &sc1, &m1v);
     const float d0 = __fmul_rn(d, (float)sc0), mn0 = __fmul_rn(dmin, (float)m0v);
     const float d1 = __fmul_rn(d, (float)sc1), mn1 = __fmul_rn(dmin, (float)m1v);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    const uint32_t w[4] = {raw.q0.x, raw.q0.y, raw.q0.z, raw.q0.w};
 #pragma unroll
     for (int i = 0; i < 16; i++) {
       const uint32_t byte = (w[i / 4] >> (8 * (i % 4))) & 0xFFu;
@@ -122,14 +147,9 @@ __device__ __forceinline__ void pg_dequant_step(const PackedMat& W, uint32_t m0,
       v[16 + i] = __fsub_rn(__fmul_rn(d1, (float)(byte >> 4)), mn1);
       kidx[16 + i] = 32 + 16 * h + i;
     }
-  } else {  // Q8_0: step ks = pieces 2(ks%2), 2(ks%2)+1 of chunk ks/2 (one 32-element block each)
-    const uint32_t kc = ks / 2, blk = 2 * (ks % 2) + h;
-    const uint64_t item = (uint64_t)tile * W.nk + kc;
-    const uint8_t* qp = W.qs + (item * 4 + blk) * (QT_ROWS * 32) + lr * 32;
-    const uint4 qa = *reinterpret_cast<const uint4*>(qp), qb = *reinterpret_cast<const uint4*>(qp + 16);
-    const uint8_t* sp = W.sc + (item * QT_ROWS + lr) * 8 + 2 * blk;
-    const float d = h2f(sp[0] | (sp[1] << 8));
-    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  } else {  // Q8_0
+    const float d = h2f(raw.d);
+    const uint32_t w[8] = {raw.q0.x, raw.q0.y, raw.q0.z, raw.q0.w, raw.q1.x, raw.q1.y, raw.q1.z, raw.q1.w};
 #pragma unroll
     for (int i = 0; i < 32; i++) {
       const int8_t qv = (int8_t)((w[i / 4] >> (8 * (i % 4))) & 0xFFu);
@@ -184,7 +204,9 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tslot;
-  // the activations this kernel reads were written by the previous kernel
+  // the first step's weight words (no earlier kernel writes weights), then the
+  // wait: the activations this kernel reads were written by the previous kernel
+  PgRaw nxt = nks > 0 ? pg_load<FMT>(W, m0, 0) : PgRaw{};
   griddep_wait();
 
   constexpr uint32_t idesc = tc_idesc_bf16_f32(PG_M, PG_N);
@@ -204,7 +226,11 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
                   2 * PG_B_BYTES, x_full(s));
       n_x[s]++;
     }
-    pg_dequant_step<FMT>(W, m0, ks, reinterpret_cast<__nv_bfloat16*>(st),
+    // this step's weight words arrived during the previous step; request the next
+    // step's before converting these
+    const PgRaw cur = nxt;
+    if (ks + 1 < nks) nxt = pg_load<FMT>(W, m0, ks + 1);
+    pg_dequant_step<FMT>(W, m0, ks, cur, reinterpret_cast<__nv_bfloat16*>(st),
                          reinterpret_cast<__nv_bfloat16*>(st + PG_A_BYTES));
     tc_fence_proxy_async();  // this thread's A stores, before the MMAs read them
     __syncthreads();
