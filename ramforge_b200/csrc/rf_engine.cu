@@ -194,6 +194,7 @@ struct rf_engine {
   unsigned *pf_cnt = nullptr, *pf_err = nullptr;
   uint32_t* pf_tok = nullptr;
   void* pf_xt = nullptr;
+  PrefillKSplit pf_ks;  // K split of the W_o / W_down GEMMs
   rf_residency_stats stats{};
 };
 
@@ -426,6 +427,9 @@ int engine_init_device(rf_engine* e) {
   }
   e->gws.part_floats = gpart;
   e->gws.n_cnt = gcnt;
+  // the residual GEMMs split K over CTA pairs only when their blocks fill at most
+  // half the SMs, so half the SM count bounds the blocks that need scratch
+  const uint32_t ks_tiles = (uint32_t)std::max(1, num_sms() / 2);
   struct Item { void** p; uint64_t bytes; };
   const uint64_t vl_pad = (uint64_t)e->vocab_chunk;
   std::vector<Item> items = {
@@ -1071,6 +1075,9 @@ int ensure_prefill_buffers(rf_engine* e) {
   uint32_t kp = 0;
   for (const Layer& L : e->layers)
     for (const PackedMat* m : {&L.qkv, &L.wo, &L.gateup, &L.down, &L.vmat}) kp = std::max(kp, m->Kp);
+  // the residual GEMMs split K over CTA pairs only when their blocks fill at most
+  // half the SMs, so half the SM count bounds the blocks that need scratch
+  const uint32_t ks_tiles = (uint32_t)std::max(1, num_sms() / 2);
   struct Item { void** p; uint64_t bytes; };
   std::vector<Item> items = {
       {(void**)&e->pf_x, 4 * T * c.n_embd},          {(void**)&e->pf_q, 4 * T * e->q_local},
@@ -1078,7 +1085,9 @@ int ensure_prefill_buffers(rf_engine* e) {
       {(void**)&e->pf_att, 4 * T * e->q_local},      {(void**)&e->pf_act, 4 * T * e->ff_local},
       {(void**)&e->pf_part, 4 * attn_part_floats((int)T, (int)e->kvh_local, kPrefillSplits, (int)G, (int)c.head_dim)},
       {(void**)&e->pf_cnt, 4 * T * e->kvh_local},    {(void**)&e->pf_err, 4},
-      {(void**)&e->pf_tok, 4 * T},                   {(void**)&e->pf_xt, prefill_xt_bytes((uint32_t)T, kp)}};
+      {(void**)&e->pf_tok, 4 * T},                   {(void**)&e->pf_xt, prefill_xt_bytes((uint32_t)T, kp)},
+      {(void**)&e->pf_ks.part, 4 * prefill_ksplit_floats(ks_tiles)},
+      {(void**)&e->pf_ks.cnt, 4ull * ks_tiles}};
   uint64_t total = 0;
   for (auto& it : items) total += align256(it.bytes);
   RF_TRY(dev_alloc(e, "scratch:prefill", total, &e->pf_block));
@@ -1089,6 +1098,7 @@ int ensure_prefill_buffers(rf_engine* e) {
     *it.p = (uint8_t*)e->pf_block + off;
     off += align256(it.bytes);
   }
+  e->pf_ks.tiles = ks_tiles;
   return RF_OK;
 }
 
@@ -1132,13 +1142,13 @@ int enqueue_prefill_chunk(rf_engine* e, uint32_t T, uint32_t pos0) {
     RF_CUDA(launch_attention(La, aa));
     // W_o + residual
     RF_CUDA(prefill_split(La, e->pf_att, e->q_local, T, e->q_local, L.wo.Kp, nullptr, 0.f, e->pf_xt));
-    RF_CUDA(prefill_gemm_residual(La, L.wo, e->pf_xt, T, e->pf_err, e->pf_x, d));
+    RF_CUDA(prefill_gemm_residual(La, L.wo, e->pf_xt, T, e->pf_err, e->pf_x, d, e->pf_ks));
     // RMSNorm(ffn_norm) -> [gate;up] -> SwiGLU
     RF_CUDA(prefill_split(La, e->pf_x, d, T, d, L.gateup.Kp, L.ffn_norm, c.rms_eps, e->pf_xt));
     RF_CUDA(prefill_gemm_swiglu(La, L.gateup, e->pf_xt, T, e->pf_err, e->pf_act, e->ff_local));
     // W_down + residual
     RF_CUDA(prefill_split(La, e->pf_act, e->ff_local, T, e->ff_local, L.down.Kp, nullptr, 0.f, e->pf_xt));
-    RF_CUDA(prefill_gemm_residual(La, L.down, e->pf_xt, T, e->pf_err, e->pf_x, d));
+    RF_CUDA(prefill_gemm_residual(La, L.down, e->pf_xt, T, e->pf_err, e->pf_x, d, e->pf_ks));
   }
   return RF_OK;
 }

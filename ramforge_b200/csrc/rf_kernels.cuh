@@ -388,8 +388,17 @@ cudaError_t prefill_gemm_store(const Launch& L, const PackedMat& W, const void* 
 //  swiglu: act[t][j] = silu(gate_j) * up_j over the interleaved gate/up rows.
 cudaError_t prefill_gemm_rope(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
                               const RopeQKVArgs& a, uint32_t pos0, uint32_t q_stride, uint32_t kv_stride);
+// Scratch of the residual GEMM's K split: `tiles` output blocks of two [128 x 128]
+// f32 partials (prefill_ksplit_floats(tiles) floats) and one arrival counter each
+// (zero at rest; the last arrival resets it).  Without it the GEMM runs unsplit.
+struct PrefillKSplit {
+  float* part = nullptr;
+  unsigned* cnt = nullptr;
+  uint32_t tiles = 0;
+};
+size_t prefill_ksplit_floats(uint32_t tiles);
 cudaError_t prefill_gemm_residual(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
-                                  float* x, uint32_t ldx);
+                                  float* x, uint32_t ldx, const PrefillKSplit& ks = PrefillKSplit{});
 cudaError_t prefill_gemm_swiglu(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
                                 float* act, uint32_t ld);
 // x[t] <- the dequantized embedding row of tokens[t] (device array), t < T.

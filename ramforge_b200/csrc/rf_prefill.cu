@@ -173,8 +173,10 @@ __device__ __forceinline__ void pg_dequant_step(const PackedMat& W, uint32_t m0,
 
 // ---------------------------------------------------------------------------
 // The GEMM: D[row][t] = sum_k W[row][k] * X[t][k] for the CTA's 128 rows (m0 =
-// blockIdx.x * 128) and PG_N tokens (block blockIdx.y), K = W.Kp.  Xt is the
-// tiled hi/lo activation buffer of prefill_split_kernel for K = W.Kp.
+// blockIdx.x * 128) and PG_N tokens (block blockIdx.y), K = W.Kp, or half of K
+// when gridDim.z == 2 (CTA z takes the steps [z*nks/2, (z+1)*nks/2); the pair
+// meets through kpart / kcnt, below).  Xt is the tiled hi/lo activation buffer
+// of prefill_split_kernel for K = W.Kp.
 // Shared memory: PG_STAGES x [A hi | A lo | B hi | B lo], then the barriers and
 // the tensor-memory address.
 // ---------------------------------------------------------------------------
@@ -182,12 +184,18 @@ constexpr size_t PG_SMEM = (size_t)PG_STAGES * PG_STAGE_BYTES + 128;
 
 template <int FMT, class Epi>
 __global__ void __launch_bounds__(PG_THREADS, 1)
-    prefill_gemm_kernel(PackedMat W, const __nv_bfloat16* __restrict__ Xt, uint32_t T, unsigned* err, Epi epi) {
+    prefill_gemm_kernel(PackedMat W, const __nv_bfloat16* __restrict__ Xt, uint32_t T, unsigned* err, Epi epi,
+                        float* __restrict__ kpart, unsigned* __restrict__ kcnt) {
   extern __shared__ __align__(1024) uint8_t psm[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(psm + (size_t)PG_STAGES * PG_STAGE_BYTES);  // x_full[S], mma_done[S]
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2 * PG_STAGES);
+  int* s_last = reinterpret_cast<int*>(tslot + 1);
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t m0 = blockIdx.x * PG_M, nb = blockIdx.y, nks = W.Kp / PG_KS;
+  const uint32_t m0 = blockIdx.x * PG_M, nb = blockIdx.y;
+  // K split over gridDim.z CTAs (1 or 2): this CTA's steps [kb, ke) of the Kp / 64
+  const uint32_t nks_all = W.Kp / PG_KS, kz = blockIdx.z, nz = gridDim.z;
+  const uint32_t kb = (uint32_t)((uint64_t)nks_all * kz / nz), ke = (uint32_t)((uint64_t)nks_all * (kz + 1) / nz);
+  const uint32_t nks = ke - kb;
   auto stage = [&](uint32_t s) { return psm + (size_t)s * PG_STAGE_BYTES; };
   auto x_full = [&](uint32_t s) { return tc_smem_u32(bars + s); };
   auto mma_done = [&](uint32_t s) { return tc_smem_u32(bars + PG_STAGES + s); };
@@ -206,7 +214,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
   const uint32_t tmem = *tslot;
   // the first step's weight words (no earlier kernel writes weights), then the
   // wait: the activations this kernel reads were written by the previous kernel
-  PgRaw nxt = nks > 0 ? pg_load<FMT>(W, m0, 0) : PgRaw{};
+  PgRaw nxt = nks > 0 ? pg_load<FMT>(W, m0, kb) : PgRaw{};
   griddep_wait();
 
   constexpr uint32_t idesc = tc_idesc_bf16_f32(PG_M, PG_N);
@@ -222,15 +230,15 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       break;
     }
     if (tid == 0) {
-      tc_bulk_g2s(tc_smem_u32(st + 2 * PG_A_BYTES), Xt + ((size_t)nb * nks + ks) * (2 * PG_N * PG_KS),
+      tc_bulk_g2s(tc_smem_u32(st + 2 * PG_A_BYTES), Xt + ((size_t)nb * nks_all + kb + ks) * (2 * PG_N * PG_KS),
                   2 * PG_B_BYTES, x_full(s));
       n_x[s]++;
     }
     // this step's weight words arrived during the previous step; request the next
     // step's before converting these
     const PgRaw cur = nxt;
-    if (ks + 1 < nks) nxt = pg_load<FMT>(W, m0, ks + 1);
-    pg_dequant_step<FMT>(W, m0, ks, cur, reinterpret_cast<__nv_bfloat16*>(st),
+    if (ks + 1 < nks) nxt = pg_load<FMT>(W, m0, kb + ks + 1);
+    pg_dequant_step<FMT>(W, m0, kb + ks, cur, reinterpret_cast<__nv_bfloat16*>(st),
                          reinterpret_cast<__nv_bfloat16*>(st + PG_A_BYTES));
     tc_fence_proxy_async();  // this thread's A stores, before the MMAs read them
     __syncthreads();
@@ -273,21 +281,58 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
         if (n_m[s]) tc_mbar_wait(mma_done(s), (n_m[s] - 1) & 1);
       }
     }
-  } else {
+  }
+  // warp w holds lanes 32*(w%4).. of D (rows) and tokens 64*(w/4).. of it
+  const uint32_t q = warp % 4, half = warp / 4;
+  const uint32_t row = m0 + 32 * q + lane;
+  float v[2][32];
+  if (!bad) {
     tc_fence_after_sync();
-    // epilogue: warp w reads lanes 32*(w%4).. (rows) and tokens 64*(w/4).. of D
-    const uint32_t q = warp % 4, half = warp / 4;
-    const uint32_t row = m0 + 32 * q + lane;
+#pragma unroll
+    for (int part = 0; part < 2; part++) tc_ld_32cols(tmem + ((32 * q) << 16) + 64 * half + 32 * part, v[part]);
+  }
+  bool emit = !bad;
+  if (nz > 1) {
+    // K split: each CTA publishes its [128 x PG_N] partial; the last of the pair to
+    // arrive adds the other's (two terms, so the sum does not depend on which
+    // arrives last) and runs the epilogue.  The barrier orders every thread's
+    // stores before thread 0's arrival, whose release is cumulative; its acquire,
+    // then the barrier, orders the other partial before the loads.
+    const uint32_t tile = nb * gridDim.x + blockIdx.x;
+    float* mine = kpart + ((size_t)tile * 2 + kz) * (PG_M * PG_N);
+    const float* other = kpart + ((size_t)tile * 2 + (1 - kz)) * (PG_M * PG_N);
+    if (!bad) {
+#pragma unroll
+      for (int part = 0; part < 2; part++)
+#pragma unroll
+        for (int j = 0; j < 32; j++) __stcg(mine + (size_t)(64 * half + 32 * part + j) * PG_M + 32 * q + lane, v[part][j]);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      unsigned old;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(kcnt + tile) : "memory");
+      *s_last = old == nz - 1;
+      if (old == nz - 1) kcnt[tile] = 0u;
+    }
+    __syncthreads();
+    emit = emit && *s_last;
+    if (emit) {
+#pragma unroll
+      for (int part = 0; part < 2; part++)
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          v[part][j] += __ldcg(other + (size_t)(64 * half + 32 * part + j) * PG_M + 32 * q + lane);
+    }
+  }
+  if (emit) {
 #pragma unroll
     for (int part = 0; part < 2; part++) {
       const uint32_t c0 = 64 * half + 32 * part;
-      float v[32];
-      tc_ld_32cols(tmem + ((32 * q) << 16) + c0, v);
 #pragma unroll
       for (int j = 0; j < 32; j++) {
-        const float vp = __shfl_xor_sync(0xffffffffu, v[j], 1);
+        const float vp = __shfl_xor_sync(0xffffffffu, v[part][j], 1);
         const uint32_t t = nb * PG_N + c0 + j;
-        if (t < T && row < W.M) epi(row, t, v[j], vp);
+        if (t < T && row < W.M) epi(row, t, v[part][j], vp);
       }
     }
   }
@@ -361,10 +406,12 @@ cudaError_t prefill_split(const Launch& L, const float* X, uint32_t ldx, uint32_
                   static_cast<__nv_bfloat16*>(Xt));
 }
 
+// The K split: a pair of CTAs per output block when the blocks alone fill at most
+// half the SMs and the scratch (`ks` with room for `ks_tiles` blocks) is given.
 template <class Epi>
 static cudaError_t run_prefill_gemm(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
-                                    Epi epi) {
-  void (*k)(PackedMat, const __nv_bfloat16*, uint32_t, unsigned*, Epi) = nullptr;
+                                    Epi epi, const PrefillKSplit& ks = PrefillKSplit{}) {
+  void (*k)(PackedMat, const __nv_bfloat16*, uint32_t, unsigned*, Epi, float*, unsigned*) = nullptr;
   switch (W.type) {
     case T_Q4_K: k = prefill_gemm_kernel<T_Q4_K, Epi>; break;
     case T_Q8_0: k = prefill_gemm_kernel<T_Q8_0, Epi>; break;
@@ -373,8 +420,13 @@ static cudaError_t run_prefill_gemm(const Launch& L, const PackedMat& W, const v
   if (W.Kp % PG_KS || T == 0) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PG_SMEM);
   if (e != cudaSuccess) return e;
-  const dim3 grid((W.Mp + PG_M - 1) / PG_M, (T + PG_N - 1) / PG_N);
-  return launch_k(L, k, grid, dim3(PG_THREADS), PG_SMEM, W, static_cast<const __nv_bfloat16*>(Xt), T, err, epi);
+  dim3 grid((W.Mp + PG_M - 1) / PG_M, (T + PG_N - 1) / PG_N, 1);
+  const uint32_t blocks = grid.x * grid.y;
+  if (ks.part && ks.cnt && blocks <= ks.tiles && 2 * blocks <= (uint32_t)num_sms() &&
+      W.Kp / PG_KS >= 2 * PG_STAGES)
+    grid.z = 2;
+  return launch_k(L, k, grid, dim3(PG_THREADS), PG_SMEM, W, static_cast<const __nv_bfloat16*>(Xt), T, err, epi,
+                  grid.z > 1 ? ks.part : nullptr, grid.z > 1 ? ks.cnt : nullptr);
 }
 
 cudaError_t prefill_gemm_store(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
@@ -386,9 +438,10 @@ cudaError_t prefill_gemm_rope(const Launch& L, const PackedMat& W, const void* X
   return run_prefill_gemm(L, W, Xt, T, err, PgEpiRope{a, pos0, q_stride, kv_stride});
 }
 cudaError_t prefill_gemm_residual(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
-                                  float* x, uint32_t ldx) {
-  return run_prefill_gemm(L, W, Xt, T, err, PgEpiResidual{x, ldx});
+                                  float* x, uint32_t ldx, const PrefillKSplit& ks) {
+  return run_prefill_gemm(L, W, Xt, T, err, PgEpiResidual{x, ldx}, ks);
 }
+size_t prefill_ksplit_floats(uint32_t tiles) { return (size_t)tiles * 2 * PG_M * PG_N; }
 cudaError_t prefill_gemm_swiglu(const Launch& L, const PackedMat& W, const void* Xt, uint32_t T, unsigned* err,
                                 float* act, uint32_t ld) {
   return run_prefill_gemm(L, W, Xt, T, err, PgEpiSwiGLU{act, ld});
