@@ -116,6 +116,21 @@ __device__ __forceinline__ PgRaw pg_load(const PackedMat& W, uint32_t m0, uint32
   return raw;
 }
 
+// Scale and min j (0..7) of a Q4_K row header held in registers (hw.y, hw.z, hw.w
+// = the 12 packed scale bytes): the fields k4_scale_min reads, taken by shifts so
+// that the header never leaves registers.
+__device__ __forceinline__ void k4_scale_min_w(const uint4& hw, uint32_t j, uint32_t* sc, uint32_t* m) {
+  const uint32_t sh = 8 * (j & 3u);
+  const uint32_t by = (hw.y >> sh) & 0xFFu, bz = (hw.z >> sh) & 0xFFu, bw = (hw.w >> sh) & 0xFFu;
+  if (j < 4) {
+    *sc = by & 63u;
+    *m = bz & 63u;
+  } else {
+    *sc = (bw & 0xFu) | ((by >> 6) << 4);
+    *m = (bw >> 4) | ((bz >> 6) << 4);
+  }
+}
+
 template <int FMT>
 __device__ __forceinline__ void pg_dequant_step(const PackedMat& W, uint32_t m0, uint32_t ks, const PgRaw& raw,
                                                 __nv_bfloat16* a_hi, __nv_bfloat16* a_lo) {
@@ -131,11 +146,10 @@ __device__ __forceinline__ void pg_dequant_step(const PackedMat& W, uint32_t m0,
     }
   } else if constexpr (FMT == T_Q4_K) {
     const uint32_t c = ks % 4;
-    const uint8_t* hb = reinterpret_cast<const uint8_t*>(&raw.q1);
-    const float d = h2f(hb[0] | (hb[1] << 8)), dmin = h2f(hb[2] | (hb[3] << 8));
+    const float d = h2f(raw.q1.x & 0xFFFFu), dmin = h2f(raw.q1.x >> 16);
     uint32_t sc0, m0v, sc1, m1v;
-    k4_scale_min(hb + 4, (int)(2 * c), &sc0, &m0v);
-    k4_scale_min(hb + 4, (int)(2 * c + 1), &sc1, &m1v);
+    k4_scale_min_w(raw.q1, 2 * c, &sc0, &m0v);
+    k4_scale_min_w(raw.q1, 2 * c + 1, &sc1, &m1v);
     const float d0 = __fmul_rn(d, (float)sc0), mn0 = __fmul_rn(dmin, (float)m0v);
     const float d1 = __fmul_rn(d, (float)sc1), mn1 = __fmul_rn(dmin, (float)m1v);
     const uint32_t w[4] = {raw.q0.x, raw.q0.y, raw.q0.z, raw.q0.w};
