@@ -343,7 +343,7 @@ def out_of_core(eng, spec, first_token, steps):
 
 
 def config5(steps):
-    """SURVEY configuration 5: the 70B shape (dim 8192, 80 layers, 64/8 heads, FFN
+    """Benchmark configuration 5: the 70B shape (dim 8192, 80 layers, 64/8 heads, FFN
     28672, vocab 128256, Q4_K layers and output, seed 4) under a 4 GiB per-GPU
     weight budget: rf_plan_residency keeps the layers that fit beside 2 ring slots
     and streams the rest from pinned host images every step.  Returns tokens/s
@@ -647,7 +647,7 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="with --profile: layer count of the model")
     ap.add_argument("--prefill", type=int, default=0, help="with --profile: batched prefill of this many tokens")
     ap.add_argument("--profile-attn", default="", help="CTX,BATCH: a few rf_decode_attention calls (ncu capture)")
-    ap.add_argument("--config5", action="store_true", help="70B-shape model, 4 GiB weight budget, ring (SURVEY config 5)")
+    ap.add_argument("--config5", action="store_true", help="70B-shape model, 4 GiB weight budget, ring (benchmark configuration 5)")
     ap.add_argument("--no-ring", action="store_true", help="leave the out-of-core measurements off the main line")
     ap.add_argument("--ring", type=int, default=0, help="out-of-core run: stream this many layers per step")
     ap.add_argument("--gemv-sweep", action="store_true", help="benchmark configuration 2: GEMV per format and shape")
