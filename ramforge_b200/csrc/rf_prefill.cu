@@ -191,8 +191,8 @@ __device__ __forceinline__ void pg_dequant_step(const PackedMat& W, uint32_t m0,
 // when gridDim.z == 2 (CTA z takes the steps [z*nks/2, (z+1)*nks/2); the pair
 // meets through kpart / kcnt, below).  Xt is the tiled hi/lo activation buffer
 // of prefill_split_kernel for K = W.Kp.
-// Shared memory: PG_STAGES x [A hi | A lo | B hi | B lo], then the barriers and
-// the tensor-memory address.
+// Shared memory: PG_STAGES x [A hi | A lo | B hi | B lo], then the barriers, the
+// tensor-memory address and the K-split pair's last-arrival flag.
 // ---------------------------------------------------------------------------
 constexpr size_t PG_SMEM = (size_t)PG_STAGES * PG_STAGE_BYTES + 128;
 
